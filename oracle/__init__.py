@@ -1,0 +1,9 @@
+"""CPU oracle for the DSpark draft-layer MoE block.
+
+Test infrastructure only: the checker the CUDA path is compared against. Only ``tests/``,
+``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` import this package;
+the product package (``dsm``) never does and has no CPU fallback.
+"""
+
+from .moe_oracle import *  # noqa: F401,F403
+from .formats import *  # noqa: F401,F403
