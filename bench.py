@@ -1,0 +1,467 @@
+"""Benchmark of the DSpark draft-layer MoE block on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl reference]
+
+One step = one MoE-layer call (router, permutation, grouped fp8 expert SwiGLU, combine,
+shared expert) on one draft block of synthetic tokens: by default the fp8 decode workload
+(hidden 4096, 256 experts, top-6, inter 2048, e4m3 experts with 128x128 fp32 block
+scales, 8 sequences x 7 draft tokens). The routed expert weights touched per step
+(~4.7 GB) are far larger than L2, and steps rotate over several token batches, so no step
+is served from cache.
+
+Prints one JSON line (rank 0). ``value`` is whole-job tokens/s with inputs resident in HBM;
+``e2e`` is the same metric through the public ``dsm.MoE`` call with the tokens copied from
+pinned host memory and the output copied back inside the timed region.
+``--impl reference`` times the CPU restatement of the reference block on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "dspark-mlx_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE-layer tokens/s & draft-block latency; HBM GB/s vs 8 TB/s at 1/2/4/8 B200"
+SPEC_HBM_GBS = 8000.0
+KERNELS_PER_STEP = 14  # router 2, permute 3, stage 1, gate/up 1, down 1, shared 4, combine 1
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons with NVML while the timed region runs."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x1: "gpu_idle", 0x2: "applications_clocks_setting"}
+
+    def __init__(self, index: int, period: float = 0.05):
+        self.index, self.period = index, period
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._h = None
+            try:
+                import torch
+
+                pr = torch.cuda.get_device_properties(self.index)
+                bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+                self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self._nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        except Exception:
+            self._nv = None
+        return self
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                get = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                r = get(self._h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def _barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def _max_over_ranks(v: float, ws: int, device) -> float:
+    if ws == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class CpuReference:
+    """The CPU restatement of the reference block on a sample of the workload's tokens.
+
+    Routed experts are dequantised to fp32 once, before timing, as the reference's loader
+    does at load time (``dspark_mlx/loading.py:7-18``); each timed call is ``MoE.__call__``
+    restated (router, per-(token, slot) expert products, fp32 combine, shared expert).
+    ``t`` holds the small tensors (x, router, shared expert); ``experts(ids)`` returns the
+    routed expert stacks of the given experts, in that order.
+    """
+
+    def __init__(self, wl, t, experts, sample_tokens: int, threads: int):
+        import torch
+
+        import oracle
+
+        torch.set_num_threads(threads)
+        self.oracle, self.threads = oracle, threads
+        a = t["args"]
+        self.a = a
+        self.sample = sample_tokens
+        self.x = t["x"][:sample_tokens].cpu()
+        self.gw = t["gate_weight"].cpu()
+        self.gb = t["gate_bias"].cpu() if "gate_bias" in t else None
+        self.t2e = t["tid2eid"].cpu() if "tid2eid" in t else None
+        self.ids = t["input_ids"][:sample_tokens].cpu() if "input_ids" in t else None
+        self.kw = dict(topk=a["n_activated_experts"], score_func=a["score_func"], route_scale=a["route_scale"])
+        _, idx = oracle.gate_forward(self.x, self.gw, bias=self.gb, tid2eid=self.t2e, input_ids=self.ids, **self.kw)
+        used = sorted(set(idx.flatten().tolist()))
+        self.remap = torch.full((a["n_routed_experts"],), -1, dtype=torch.int64)
+        self.remap[used] = torch.arange(len(used))
+        st = experts(used)
+        self.w = {}
+        for n in ("w1", "w3", "w2"):
+            mats = []
+            for j in range(len(used)):
+                if wl.wfmt == "fp8":
+                    mats.append(oracle.fp8_weight_dequant(st[n + "_codes"][j].cpu(), st[n + "_scale"][j].cpu()))
+                elif wl.wfmt == "fp4":
+                    mats.append(oracle.fp4_weight_dequant(st[n + "_codes"][j].cpu(), st[n + "_scale"][j].cpu(),
+                                                          st[n + "_tensor_scale"][j].cpu()))
+                else:
+                    mats.append(st[n][j].cpu())
+            self.w[n] = oracle.OracleWeights("dense", torch.stack(mats))
+        self.shared = (t["shared_w1"].cpu(), t["shared_w2"].cpu(), t["shared_w3"].cpu())
+
+    def call(self):
+        import torch
+
+        o = self.oracle
+        weights, ind = o.gate_forward(self.x, self.gw, bias=self.gb, tid2eid=self.t2e, input_ids=self.ids, **self.kw)
+        out = o.route_experts(self.x, self.remap[ind.long()].to(torch.int32), self.w["w1"], self.w["w3"],
+                              self.w["w2"], self.a["swiglu_limit"])
+        y = (out.float() * weights[..., None]).sum(-2)
+        y = y + o.expert_forward(self.x, *self.shared, self.a["swiglu_limit"]).float()
+        return y.to(self.x.dtype)
+
+    def timed(self, budget_s: float, max_calls: int = 1000):
+        """tokens/s over repeated calls for about ``budget_s`` seconds."""
+        self.call()
+        n, t0 = 0, time.perf_counter()
+        while True:
+            self.call()
+            n += 1
+            el = time.perf_counter() - t0
+            if el > budget_s or n >= max_calls:
+                return self.sample * n / el, n, el
+
+
+def run_reference(args):
+    ws, rank, _ = _dist()
+    if rank != 0:
+        return
+    from dsm import workloads as W
+
+    wl = W.WORKLOADS[args.workload]
+    t = W.make_moe_tensors(wl, device="cpu", routed=False)
+    threads = os.cpu_count() or 1
+    sample = min(8, wl.n_tokens)
+    ref = CpuReference(wl, t, lambda ids: W.expert_tensors(wl, ids), sample, threads)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        ref.call()
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            vals.append(sample / dt)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wl.n_tokens / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (bf16 in/out)",
+        "data": "synthetic",
+        "config": {"workload": wl.name, "tokens_per_step": wl.n_tokens, "dim": wl.args["dim"],
+                   "n_experts": wl.args["n_routed_experts"], "topk": wl.args["n_activated_experts"],
+                   "inter": wl.args["moe_inter_dim"], "weights": wl.wfmt},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"one call per step on {sample} of the {wl.n_tokens} tokens, experts dequantised "
+                                   f"to fp32 before timing (the reference dequantises at load); CPU restatement of "
+                                   f"MoE.__call__ in PyTorch (mlx is not installable here)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def run_gpu(args):
+    import ctypes
+
+    import torch
+
+    from dsm import _lib, workloads as W
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    wl = W.WORKLOADS[args.workload]
+    if args.experts:
+        # a smaller expert pool with every per-expert shape unchanged (profiling captures)
+        import dataclasses
+
+        wl = dataclasses.replace(wl, args=dict(wl.args, n_routed_experts=args.experts))
+    t = W.make_moe_tensors(wl, device=dev, seed=wl.seed + 1000 * rank)
+    moe = W.build_moe(wl, t, dev)
+    N, dim = wl.n_tokens, wl.args["dim"]
+    # several distinct token batches (different routing per step)
+    n_batches = 4
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    xs = [t["x"]] + [torch.randn(N, dim, generator=gen, device=dev).to(torch.bfloat16) for _ in range(n_batches - 1)]
+    ids = t.get("input_ids")
+    L = _lib.lib()
+    desc, keep = moe.describe(N, torch.bfloat16)
+    wsb = L.dsm_moe_workspace_bytes(ctypes.byref(desc))
+    wsp = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    y = torch.empty(N, dim, dtype=torch.bfloat16, device=dev)
+    rw = torch.empty(N, wl.args["n_activated_experts"], dtype=torch.float32, device=dev)
+    ri = torch.empty(N, wl.args["n_activated_experts"], dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    ids_p = ids.data_ptr() if ids is not None else None
+
+    def step(i):
+        x = xs[i % n_batches]
+        _lib.check(L.dsm_moe_forward(ctypes.byref(desc), x.data_ptr(), _lib.DT_BF16, ids_p, _lib.DT_I32,
+                                     N if ids is not None else 0, y.data_ptr(), rw.data_ptr(), ri.data_ptr(),
+                                     wsp.data_ptr(), wsb, sp))
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    # routing statistics of the measured batches (for the algorithmic byte count)
+    touched_bytes = []
+    for i in range(n_batches):
+        step(i)
+        c = torch.bincount(ri.flatten().long(), minlength=wl.args["n_routed_experts"]).cpu()
+        touched_bytes.append(W.routed_weight_bytes(wl, c))
+    torch.cuda.synchronize()
+    _barrier(ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms = _max_over_ranks(ms, ws, dev)
+    _barrier(ws)
+
+    # ---- dominant kernel: the fused gate/up expert kernel, timed alone with events
+    sh_bytes = 3 * wl.args["moe_inter_dim"] * dim * 2
+    gate_bytes = wl.args["n_routed_experts"] * dim * 4
+    per_step_bytes = [b + sh_bytes + gate_bytes + 2 * N * dim * 2 for b in touched_bytes]
+    avg_step_bytes = sum(per_step_bytes[i % n_batches] for i in range(args.steps)) / args.steps
+    hbm_peak, _, peak_kind = _peaks()
+    if args.no_kernel_timing:
+        k_ms, k_bytes, achieved = None, None, None
+    else:
+        k_ms, k_bytes = time_gate_up(moe, xs[0], ids, args, L, dev)
+        achieved = k_bytes / (k_ms * 1e-3) / 1e9
+
+    # ---- end to end through the public API: pinned host tokens in, host result out
+    e2e_ms = None
+    if not args.no_e2e:
+        xh = [x.cpu().pin_memory() for x in xs]
+        yh = torch.empty(N, dim, dtype=torch.bfloat16).pin_memory()
+        ids_d = ids
+        for i in range(3):
+            yh.copy_(moe(xh[i % n_batches].to(dev, non_blocking=True), ids_d), non_blocking=True)
+        torch.cuda.synchronize()
+        _barrier(ws)
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2.record(stream)
+        for i in range(args.steps):
+            xd = xh[i % n_batches].to(dev, non_blocking=True)
+            yh.copy_(moe(xd, ids_d), non_blocking=True)
+        e3.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = _max_over_ranks(e2.elapsed_time(e3) / args.steps, ws, dev)
+
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            traffic = json.load(f).get(f"gate_up/{wl.name}")
+    except Exception:
+        traffic = None
+
+    if rank == 0:
+        cpu = None
+        if ws == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+
+            def experts(ids, t=t):
+                keys = [k for k in t if k[:2] in ("w1", "w2", "w3")]
+                return {k: t[k][ids].cpu() for k in keys}
+
+            v, n, el = CpuReference(wl, t, experts, min(8, N), threads).timed(args.cpu_seconds)
+            cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                   "sample": f"{min(8, N)} of the {N} tokens, {n} calls in {el:.1f} s; experts dequantised to fp32 "
+                             f"before timing; CPU restatement of MoE.__call__ in PyTorch"}
+        value = ws * N / (ms * 1e-3)
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp8 e4m3 weights x bf16 activations (f16 MMA, fp32 accumulate)",
+            "data": "synthetic",
+            "config": {"workload": wl.name, "tokens_per_step_per_gpu": N, "batch": wl.batch, "draft_block": wl.block,
+                       "dim": dim, "n_experts": wl.args["n_routed_experts"], "topk": wl.args["n_activated_experts"],
+                       "inter": wl.args["moe_inter_dim"], "weights": wl.wfmt,
+                       "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                       "l2": "inputs larger than L2 (touched expert weights ~GB per step, 4 rotating token batches)"},
+            "draft_block_latency_ms": ms,
+            "hbm_gbs_step": avg_step_bytes / (ms * 1e-3) / 1e9,
+            "hbm_frac_of_8tbs_step": avg_step_bytes / (ms * 1e-3) / 1e9 / SPEC_HBM_GBS,
+            "roofline": None if achieved is None else {
+                "bound": "hbm", "kernel": "expert_kernel<fp8, gate_up>", "achieved": achieved, "peak": hbm_peak,
+                "unit": "GB/s", "frac": achieved / hbm_peak, "peak_kind": peak_kind,
+                "frac_of_8tbs": achieved / SPEC_HBM_GBS, "algorithmic_bytes_per_launch": k_bytes,
+                "launch_ms": k_ms, "traffic": traffic},
+            "cpu_baseline": cpu,
+            "e2e": None if e2e_ms is None else {
+                "value": ws * N / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": N * dim * 2,
+                "d2h_bytes_per_step": N * dim * 2, "ms_per_step": e2e_ms},
+            "gpu_launches": KERNELS_PER_STEP * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line))
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def time_gate_up(moe, x, ids, args, L, dev):
+    """Average duration of the fused gate/up expert kernel (CUDA events) and its algorithmic bytes."""
+    import ctypes
+
+    import torch
+
+    from dsm import _lib
+
+    N = x.shape[0]
+    desc, keep = moe.describe(N, torch.bfloat16)
+    p1, p3 = keep[0], keep[1]
+    E, topk = desc.n_experts, desc.topk
+    P = N * topk
+    s = torch.cuda.current_stream().cuda_stream
+    w, idx = moe.gate(x, ids)
+    counts = torch.empty(E, dtype=torch.int32, device=dev)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    perm = torch.empty(P, dtype=torch.int32, device=dev)
+    inv = torch.empty(P, dtype=torch.int32, device=dev)
+    pwsb = L.dsm_permute_workspace_bytes(P, E)
+    pws = torch.empty(pwsb, dtype=torch.uint8, device=dev)
+    _lib.check(L.dsm_permute(idx.data_ptr(), P, E, counts.data_ptr(), offsets.data_ptr(), perm.data_ptr(),
+                             inv.data_ptr(), pws.data_ptr(), pwsb, s))
+    cap = L.dsm_stage_rows_cap(P)
+    xs = torch.empty(L.dsm_stage_bytes(cap, desc.dim), dtype=torch.uint8, device=dev)
+    xsc = torch.empty(cap, dtype=torch.float32, device=dev)
+    hs = torch.empty(L.dsm_stage_bytes(cap, desc.inter), dtype=torch.uint8, device=dev)
+    _lib.check(L.dsm_stage_rows(x.data_ptr(), _lib.DT_BF16, N, desc.dim, perm.data_ptr(), P, topk, xs.data_ptr(), cap,
+                                xsc.data_ptr(), s))
+
+    def launch():
+        _lib.check(L.dsm_expert_gate_up(xs.data_ptr(), xsc.data_ptr(), cap, desc.dim, offsets.data_ptr(), E, p1.wfmt,
+                                        p1.group_size, p1.packed.data_ptr(), p3.packed.data_ptr(), desc.inter,
+                                        desc.act, desc.swiglu_limit, desc.round_gu, hs.data_ptr(), 1.0, P, s))
+
+    for _ in range(5):
+        launch()
+    torch.cuda.synchronize()
+    n = max(20, min(args.steps, 500))
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    for _ in range(n):
+        launch()
+    a1.record()
+    torch.cuda.synchronize()
+    k_ms = a0.elapsed_time(a1) / n
+    c = counts.cpu()
+    touched = int((c > 0).sum())
+    header = -(-E * 4 // 256) * 256
+    per_expert = (p1.packed.numel() - header) // E  # packed tile bytes (codes + scales) of one expert
+    w13 = 2 * touched * per_expert
+    act = (P * desc.dim * 2) + (P * desc.inter * 2)
+    return k_ms, w13 + act
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--workload", default="fp8_decode")
+    ap.add_argument("--impl", default="dsm", choices=["dsm", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-kernel-timing", action="store_true")
+    ap.add_argument("--experts", type=int, default=0, help="shrink the routed expert pool (profiling)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

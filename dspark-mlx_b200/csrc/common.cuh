@@ -1,0 +1,214 @@
+// Shared device/host helpers of libdsm (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "dsm.h"
+
+namespace dsm {
+
+// ------------------------------------------------------------------------------------------
+// host-side status plumbing
+// ------------------------------------------------------------------------------------------
+void set_error(const std::string& msg);
+int fail(int status, const std::string& msg);
+int check_launch(const char* what);
+
+#define DSM_REQUIRE(cond, msg)                                   \
+  do {                                                           \
+    if (!(cond)) return ::dsm::fail(DSM_ERR_INVALID_ARGUMENT, msg); \
+  } while (0)
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+int num_sms();
+
+// ------------------------------------------------------------------------------------------
+// geometry shared by staging, packing and the expert kernels
+// ------------------------------------------------------------------------------------------
+constexpr int kTileRows = 128;   // weight rows (output features) per work unit
+constexpr int kChunkK = 128;     // K elements per pipeline stage / staging chunk
+constexpr int kStagePitch = DSM_STAGE_PITCH;  // halves per staged row (128 + 32 pad)
+constexpr int kPackHeader = 256; // bytes before the tiles in a packed weight buffer (>= 4*E)
+
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// bytes of one packed 128x128 tile (codes + per-tile metadata) per format
+__host__ __device__ constexpr int tile_code_bytes(int wfmt) {
+  return wfmt == DSM_WFMT_F16 ? 32768
+         : (wfmt == DSM_WFMT_FP8_B128 || wfmt == DSM_WFMT_AFFINE8) ? 16384
+                                                                     : 8192;
+}
+__host__ __device__ constexpr int tile_meta_bytes(int wfmt, int group_size) {
+  return wfmt == DSM_WFMT_FP8_B128   ? 16
+         : wfmt == DSM_WFMT_FP4_G32  ? 512
+         : (wfmt == DSM_WFMT_AFFINE8 || wfmt == DSM_WFMT_AFFINE4)
+             ? kTileRows * (kChunkK / (group_size > 0 ? group_size : 64)) * 4
+             : 0;
+}
+__host__ __device__ constexpr int tile_bytes(int wfmt, int group_size) {
+  return tile_code_bytes(wfmt) + tile_meta_bytes(wfmt, group_size);
+}
+inline int64_t packed_header_bytes(int n_experts) {
+  return ceil_div(int64_t(n_experts) * 4, kPackHeader) * kPackHeader;
+}
+
+// ------------------------------------------------------------------------------------------
+// device error word
+// ------------------------------------------------------------------------------------------
+extern __device__ int g_device_error;
+__device__ __forceinline__ void raise_device_error(int code) { atomicCAS(&g_device_error, 0, code); }
+
+// ------------------------------------------------------------------------------------------
+// PTX helpers: shared-memory addresses, mbarriers, bulk async copies, cache policies
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait for the phase with the given parity to complete, for at most ~2 s of wall time.
+// Returns false (and records DSM_DEV_ERR_PIPELINE_TIMEOUT) if the budget ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (global_timer_ns() - t0 > 2000000000ull) {
+      raise_device_error(DSM_DEV_ERR_PIPELINE_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// 1-D bulk copy global -> shared, completing `bytes` transaction bytes on `bar`.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// ------------------------------------------------------------------------------------------
+// code conversions (hardware cvt on sm_100a: exact for e4m3 / e2m1 into f16)
+// ------------------------------------------------------------------------------------------
+// 4 e4m3 bytes -> two f16x2: lo = (byte0, byte1), hi = (byte2, byte3) (low byte -> low half)
+__device__ __forceinline__ void e4m3x4_to_f16(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n .reg .b16 a, b;\n mov.b32 {a, b}, %2;\n cvt.rn.f16x2.e4m3x2 %0, a;\n cvt.rn.f16x2.e4m3x2 %1, b;\n}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
+// 8 e2m1 nibbles -> four f16x2: o[j] = (low nibble of byte j, high nibble of byte j)
+__device__ __forceinline__ void e2m1x8_to_f16(uint32_t w, uint32_t (&o)[4]) {
+  asm("{\n .reg .b8 a, b, c, d;\n mov.b32 {a, b, c, d}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, a;\n cvt.rn.f16x2.e2m1x2 %1, b;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, c;\n cvt.rn.f16x2.e2m1x2 %3, d;\n}"
+      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+      : "r"(w));
+}
+// one e4m3 byte -> f16 (bits in the low half)
+__device__ __forceinline__ uint32_t e4m3_to_f16_bits(uint32_t byte) {
+  uint32_t lo, hi;
+  e4m3x4_to_f16(byte & 0xFFu, lo, hi);
+  return lo & 0xFFFFu;
+}
+// bytes 0,1 (resp. 2,3) of w placed as f16 (1024 + byte): magic-number conversion of uint8
+__device__ __forceinline__ void u8x4_to_f16_plus1024(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  lo = __byte_perm(w, 0x64646464u, 0x4140);
+  hi = __byte_perm(w, 0x64646464u, 0x4342);
+}
+// nibbles (j, j+4) of w as f16 (1024 + nibble), j = 0..3
+__device__ __forceinline__ void u4x8_to_f16_plus1024(uint32_t w, uint32_t (&o)[4]) {
+  o[0] = (w & 0x000F000Fu) | 0x64006400u;
+  o[1] = ((w >> 4) & 0x000F000Fu) | 0x64006400u;
+  o[2] = ((w >> 8) & 0x000F000Fu) | 0x64006400u;
+  o[3] = ((w >> 12) & 0x000F000Fu) | 0x64006400u;
+}
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// D = A(16x16 f16, row) * B(16x8 f16, col) + C, fp32 accumulate
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+template <typename T>
+__device__ __forceinline__ float load_as_float(const T* p, int64_t i);
+template <>
+__device__ __forceinline__ float load_as_float<float>(const float* p, int64_t i) {
+  return p[i];
+}
+template <>
+__device__ __forceinline__ float load_as_float<__nv_bfloat16>(const __nv_bfloat16* p, int64_t i) {
+  return __bfloat162float(p[i]);
+}
+
+}  // namespace dsm

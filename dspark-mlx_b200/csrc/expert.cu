@@ -1,0 +1,601 @@
+// Grouped expert products at decode token counts: the routed experts' gather_mm /
+// gather_qmm calls and the SwiGLU between them (dspark_mlx/model/moe.py:37-44, 132-149).
+//
+// Work unit = (expert e, 128-row tile of the output features, chunk of BN = 8*NT of the
+// expert's staged rows). A persistent grid (one CTA per SM) walks the units; every CTA
+// computes the unit list from the expert offsets itself, so no host round trip is needed.
+//
+// Per CTA: one producer warp issues, per pipeline stage (K chunk of 128), one bulk copy of
+// the packed weight tile (two for the fused gate/up pair) and one of the BN staged
+// activation rows into a ring of shared-memory stages (mbarrier complete_tx); four
+// consumer warps each own 32 weight rows, load their A fragments with one ld.shared.v4 per
+// m16 tile (the packer stored them in fragment order), dequantise in registers (hardware
+// e4m3/e2m1 -> f16 conversions, magic-number uint8/uint4 -> f16), and run
+// mma.sync m16n8k16 f16 x f16 -> fp32 against the activations. Weight streams are read
+// with an L2 evict-first policy, activations with evict-last.
+//
+// Scales: fp8 128x128 block scales and affine group scale/bias are applied to fp32
+// partial sums at group boundaries (the affine bias term uses the activation group sums,
+// obtained with an all-ones MMA); e2m1 codes are multiplied by their e4m3 group scale in
+// f16 (exact: at most 6 significant bits); the per-expert multiplier from the packed
+// header (f16 prescale, fp4 per-tensor scale) and the activation row scale are applied in
+// the epilogue.
+//
+// Epilogue of the gate/up kernel: g, u -> (optional bf16 rounding, as bf16 / affine
+// weights give bf16 products in the reference) -> activation -> bf16 rounding (the
+// reference casts h to x.dtype) -> staged f16 rows for the down kernel. Epilogue of the
+// down kernel: fp32 rows of o (optionally rounded to bf16).
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace dsm {
+namespace {
+
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+
+struct ExpertArgs {
+  const uint8_t* wa;  // packed weights (gate or down)
+  const uint8_t* wb;  // packed up weights (gate/up kernel) or nullptr
+  const __half* xin;  // staged activation rows
+  const float* act_scale;  // per staged row, or nullptr -> act_scale_const
+  float act_scale_const;
+  int64_t rows_cap;
+  const int32_t* offsets;
+  int n_experts;
+  int out_rows;
+  int rt_count;
+  int kc_count;
+  int group_size;
+  int act;
+  float limit;
+  int round_gu;
+  float h_scale;
+  __half* h_out;
+  int64_t h_rows_cap;
+  float* o_out;
+  int ldo;
+  int round_o;
+};
+
+__device__ __forceinline__ float sigmoidf_(float v) { return 1.f / (1.f + expf(-v)); }
+
+__device__ __forceinline__ float apply_act(float g, float u, int act, float limit) {
+  if (act == DSM_ACT_SILU_MUL_BF16) {
+    // nn.silu(g) * u with bf16 arrays: every elementwise op rounds to bf16
+    const float sig = bf16_round(sigmoidf_(g));
+    const float s = bf16_round(g * sig);
+    return s * u;
+  }
+  if (limit > 0.f) {
+    u = fminf(fmaxf(u, -limit), limit);
+    g = fminf(g, limit);
+  }
+  return g * sigmoidf_(g) * u;
+}
+
+// expert e owning unit u: the largest e with pre[e] <= u (pre[0] = 0, pre[E] = total)
+__device__ __forceinline__ int find_expert(const int* pre, int n_experts, int u) {
+  int lo = 0, hi = n_experts - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (pre[mid] <= u)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+template <int FMT, bool DUAL, int NT>
+__global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a, int n_stages) {
+  constexpr int BN = 8 * NT;
+  constexpr int NM = DUAL ? 2 : 1;
+  constexpr bool kBlockScaled = FMT == DSM_WFMT_FP8_B128;
+  constexpr bool kAffine = FMT == DSM_WFMT_AFFINE8 || FMT == DSM_WFMT_AFFINE4;
+  constexpr bool kTmp = kBlockScaled || kAffine;
+  extern __shared__ __align__(1024) uint8_t smem[];
+
+  const int tile_b = tile_bytes(FMT, a.group_size);
+  constexpr int act_b = BN * kStagePitch * 2;
+  const int stage_b = NM * tile_b + act_b;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + int64_t(n_stages) * stage_b);
+  uint64_t* empty = full + n_stages;
+  int* pre = reinterpret_cast<int*>(empty + n_stages);
+  volatile int* abort_flag = pre + a.n_experts + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = a.n_experts;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < n_stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {  // units per expert, inclusive scan -> pre[1..E]
+    int carry = 0;
+    if (lane == 0) pre[0] = 0;
+    for (int base = 0; base < E; base += 32) {
+      const int e = base + lane;
+      int v = 0;
+      if (e < E) {
+        const int cnt = a.offsets[e + 1] - a.offsets[e];
+        v = cnt > 0 ? a.rt_count * ((cnt + BN - 1) / BN) : 0;
+      }
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      if (e < E) pre[e + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  __syncthreads();
+  const int total = pre[E];
+  const float* hdr_a = reinterpret_cast<const float*>(a.wa);
+  const float* hdr_b = DUAL ? reinterpret_cast<const float*>(a.wb) : nullptr;
+  const int64_t hdr_bytes = ceil_div(int64_t(E) * 4, kPackHeader) * kPackHeader;
+  const uint8_t* tiles_a = a.wa + hdr_bytes;
+  const uint8_t* tiles_b = DUAL ? a.wb + hdr_bytes : nullptr;
+
+  if (warp == kConsumerWarps) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        const int e = find_expert(pre, E, u);
+        const int cnt = a.offsets[e + 1] - a.offsets[e];
+        const int nch = (cnt + BN - 1) / BN;
+        const int local = u - pre[e];
+        const int rt = local / nch, chunk = local % nch;
+        const int64_t row0 = int64_t(a.offsets[e]) + int64_t(chunk) * BN;
+        const int64_t tile0 = (int64_t(e) * a.rt_count + rt) * a.kc_count;
+        for (int kc = 0; kc < a.kc_count; ++kc) {
+          if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + int64_t(s) * stage_b;
+          mbar_arrive_expect_tx(&full[s], uint32_t(stage_b));
+          bulk_g2s(st, tiles_a + (tile0 + kc) * tile_b, uint32_t(tile_b), &full[s], pol_w);
+          if (DUAL) bulk_g2s(st + tile_b, tiles_b + (tile0 + kc) * tile_b, uint32_t(tile_b), &full[s], pol_w);
+          bulk_g2s(st + NM * tile_b, a.xin + (int64_t(kc) * a.rows_cap + row0) * kStagePitch, uint32_t(act_b),
+                   &full[s], pol_x);
+          if (++s == n_stages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // let copies already in flight land before the CTA retires (bounded: ~100 us)
+        for (int i = 0; i < 100; ++i) __nanosleep(1000);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumers
+  const int g = lane >> 2, q = lane & 3;
+  int s = 0;
+  uint32_t ph = 0;
+  const uint32_t ones = 0x3C003C00u;  // f16x2 (1, 1)
+  const uint32_t ones_a[4] = {ones, ones, ones, ones};
+  for (int u = blockIdx.x; u < total; u += gridDim.x) {
+    const int e = find_expert(pre, E, u);
+    const int off = a.offsets[e];
+    const int cnt = a.offsets[e + 1] - off;
+    const int nch = (cnt + BN - 1) / BN;
+    const int local = u - pre[e];
+    const int rt = local / nch, chunk = local % nch;
+
+    float acc[NM][2][NT][4];
+    float tmp[kTmp ? NM : 1][2][NT][4];
+    float xsum[kAffine ? NT : 1][4];
+#pragma unroll
+    for (int m = 0; m < NM; ++m)
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            acc[m][i][j][c] = 0.f;
+            if (kTmp) tmp[m < (kTmp ? NM : 1) ? m : 0][i][j][c] = 0.f;
+          }
+#pragma unroll
+    for (int j = 0; j < (kAffine ? NT : 1); ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) xsum[j][c] = 0.f;
+
+    bool ok = true;
+    for (int kc = 0; kc < a.kc_count; ++kc) {
+      if (*abort_flag || !mbar_wait(&full[s], ph)) {
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      const uint32_t st = smem_u32(smem + int64_t(s) * stage_b);
+      const uint32_t sx = st + NM * tile_b;
+      // ---- per-format stage compute
+      if constexpr (FMT == DSM_WFMT_F16) {
+#pragma unroll
+        for (int sl = 0; sl < 8; ++sl) {
+          uint32_t A[NM][2][4];
+#pragma unroll
+          for (int m = 0; m < NM; ++m)
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const uint4 v = lds128(st + m * tile_b + ((sl * 8 + 2 * warp + i) * 32 + lane) * 16);
+              A[m][i][0] = v.x;
+              A[m][i][1] = v.z;
+              A[m][i][2] = v.y;
+              A[m][i][3] = v.w;
+            }
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            const uint2 xb = lds64(sx + (j * 8 + g) * (kStagePitch * 2) + sl * 32 + q * 8);
+#pragma unroll
+            for (int m = 0; m < NM; ++m)
+#pragma unroll
+              for (int i = 0; i < 2; ++i) mma_f16(acc[m][i][j], A[m][i], xb.x, xb.y);
+          }
+        }
+      } else if constexpr (FMT == DSM_WFMT_FP8_B128 || FMT == DSM_WFMT_AFFINE8) {
+        const int slabs_per_group = kAffine ? a.group_size / 32 : 4;
+#pragma unroll
+        for (int sl = 0; sl < 4; ++sl) {
+          uint32_t A[NM][2][2][4];  // [matrix][m16 tile][mma 0/1][regs]
+#pragma unroll
+          for (int m = 0; m < NM; ++m)
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const uint4 v = lds128(st + m * tile_b + ((sl * 8 + 2 * warp + i) * 32 + lane) * 16);
+              if constexpr (FMT == DSM_WFMT_FP8_B128) {
+                e4m3x4_to_f16(v.x, A[m][i][0][0], A[m][i][0][2]);
+                e4m3x4_to_f16(v.y, A[m][i][1][0], A[m][i][1][2]);
+                e4m3x4_to_f16(v.z, A[m][i][0][1], A[m][i][0][3]);
+                e4m3x4_to_f16(v.w, A[m][i][1][1], A[m][i][1][3]);
+              } else {
+                u8x4_to_f16_plus1024(v.x, A[m][i][0][0], A[m][i][0][2]);
+                u8x4_to_f16_plus1024(v.y, A[m][i][1][0], A[m][i][1][2]);
+                u8x4_to_f16_plus1024(v.z, A[m][i][0][1], A[m][i][0][3]);
+                u8x4_to_f16_plus1024(v.w, A[m][i][1][1], A[m][i][1][3]);
+              }
+            }
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            const uint4 xb = lds128(sx + (j * 8 + g) * (kStagePitch * 2) + sl * 64 + q * 16);
+#pragma unroll
+            for (int m = 0; m < NM; ++m)
+#pragma unroll
+              for (int i = 0; i < 2; ++i) {
+                mma_f16(tmp[m][i][j], A[m][i][0], xb.x, xb.y);
+                mma_f16(tmp[m][i][j], A[m][i][1], xb.z, xb.w);
+              }
+            if constexpr (kAffine) {
+              mma_f16(xsum[j < (kAffine ? NT : 1) ? j : 0], ones_a, xb.x, xb.y);
+              mma_f16(xsum[j < (kAffine ? NT : 1) ? j : 0], ones_a, xb.z, xb.w);
+            }
+          }
+          if constexpr (kAffine) {
+            if ((sl + 1) % slabs_per_group == 0) {
+              const int grp = (sl + 1) / slabs_per_group - 1;
+              const int gpt = kChunkK / a.group_size;
+#pragma unroll
+              for (int m = 0; m < NM; ++m)
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                  const int r0 = 32 * warp + 16 * i + g;
+                  const uint32_t sb0 = lds32(st + m * tile_b + tile_code_bytes(FMT) + (r0 * gpt + grp) * 4);
+                  const uint32_t sb1 = lds32(st + m * tile_b + tile_code_bytes(FMT) + ((r0 + 8) * gpt + grp) * 4);
+                  const float s0 = __uint_as_float(sb0 << 16), b0 = __uint_as_float(sb0 & 0xFFFF0000u);
+                  const float s1 = __uint_as_float(sb1 << 16), b1 = __uint_as_float(sb1 & 0xFFFF0000u);
+                  const float c0 = fmaf(-1024.f, s0, b0), c1 = fmaf(-1024.f, s1, b1);
+#pragma unroll
+                  for (int j = 0; j < NT; ++j) {
+                    acc[m][i][j][0] += s0 * tmp[m][i][j][0] + c0 * xsum[j][0];
+                    acc[m][i][j][1] += s0 * tmp[m][i][j][1] + c0 * xsum[j][1];
+                    acc[m][i][j][2] += s1 * tmp[m][i][j][2] + c1 * xsum[j][2];
+                    acc[m][i][j][3] += s1 * tmp[m][i][j][3] + c1 * xsum[j][3];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) tmp[m][i][j][c] = 0.f;
+                  }
+                }
+#pragma unroll
+              for (int j = 0; j < NT; ++j)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) xsum[j][c] = 0.f;
+            }
+          }
+        }
+        if constexpr (kBlockScaled) {
+#pragma unroll
+          for (int m = 0; m < NM; ++m) {
+            const float sc = __uint_as_float(lds32(st + m * tile_b + tile_code_bytes(FMT)));
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+              for (int j = 0; j < NT; ++j)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  acc[m][i][j][c] = fmaf(sc, tmp[m][i][j][c], acc[m][i][j][c]);
+                  tmp[m][i][j][c] = 0.f;
+                }
+          }
+        }
+      } else {  // 4-bit formats: FP4_G32, AFFINE4 (slab = 64 K)
+        const int slabs_per_group = kAffine ? a.group_size / 64 : 1;
+        uint32_t gsc[NM][2][2];  // fp4 group-scale words of rows r0, r0+8 per m16 tile
+        if constexpr (FMT == DSM_WFMT_FP4_G32) {
+#pragma unroll
+          for (int m = 0; m < NM; ++m)
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const int r0 = 32 * warp + 16 * i + g;
+              gsc[m][i][0] = lds32(st + m * tile_b + tile_code_bytes(FMT) + r0 * 4);
+              gsc[m][i][1] = lds32(st + m * tile_b + tile_code_bytes(FMT) + (r0 + 8) * 4);
+            }
+        }
+#pragma unroll
+        for (int sl = 0; sl < 2; ++sl) {
+          uint32_t A[NM][2][4][4];  // [matrix][m16][mma t][regs]
+#pragma unroll
+          for (int m = 0; m < NM; ++m)
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const uint4 v = lds128(st + m * tile_b + ((sl * 8 + 2 * warp + i) * 32 + lane) * 16);
+              uint32_t c0[4], c1[4], c2[4], c3[4];
+              if constexpr (FMT == DSM_WFMT_FP4_G32) {
+                e2m1x8_to_f16(v.x, c0);
+                e2m1x8_to_f16(v.y, c1);
+                e2m1x8_to_f16(v.z, c2);
+                e2m1x8_to_f16(v.w, c3);
+                const int sh = 8 * (2 * sl + (q >> 1));
+                const uint32_t f0 = e4m3_to_f16_bits((gsc[m][i][0] >> sh) & 0xFFu);
+                const uint32_t f1 = e4m3_to_f16_bits((gsc[m][i][1] >> sh) & 0xFFu);
+                const uint32_t s0 = f0 | (f0 << 16), s1 = f1 | (f1 << 16);
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                  c0[t] = hmul2_bits(c0[t], s0);
+                  c1[t] = hmul2_bits(c1[t], s0);
+                  c2[t] = hmul2_bits(c2[t], s1);
+                  c3[t] = hmul2_bits(c3[t], s1);
+                }
+              } else {
+                u4x8_to_f16_plus1024(v.x, c0);
+                u4x8_to_f16_plus1024(v.y, c1);
+                u4x8_to_f16_plus1024(v.z, c2);
+                u4x8_to_f16_plus1024(v.w, c3);
+              }
+              // mma t covers K 4t..4t+3 of this lane's 16: regs (k 4t,4t+1) and (k 4t+2,4t+3)
+              A[m][i][0][0] = c0[0]; A[m][i][0][1] = c2[0]; A[m][i][0][2] = c0[1]; A[m][i][0][3] = c2[1];
+              A[m][i][1][0] = c0[2]; A[m][i][1][1] = c2[2]; A[m][i][1][2] = c0[3]; A[m][i][1][3] = c2[3];
+              A[m][i][2][0] = c1[0]; A[m][i][2][1] = c3[0]; A[m][i][2][2] = c1[1]; A[m][i][2][3] = c3[1];
+              A[m][i][3][0] = c1[2]; A[m][i][3][1] = c3[2]; A[m][i][3][2] = c1[3]; A[m][i][3][3] = c3[3];
+            }
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            const int n = j * 8 + g;
+            const uint32_t base = sx + n * (kStagePitch * 2) + sl * 128 + q * 32;
+            const uint32_t odd = uint32_t(n & 1) * 16u;  // odd rows load their halves swapped
+            const uint4 p0 = lds128(base + odd);
+            const uint4 p1 = lds128(base + (16u - odd));
+            const uint4 lo = (n & 1) ? p1 : p0;
+            const uint4 hi = (n & 1) ? p0 : p1;
+            const uint32_t xr[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+#pragma unroll
+              for (int m = 0; m < NM; ++m)
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                  if constexpr (kAffine)
+                    mma_f16(tmp[m][i][j], A[m][i][t], xr[2 * t], xr[2 * t + 1]);
+                  else
+                    mma_f16(acc[m][i][j], A[m][i][t], xr[2 * t], xr[2 * t + 1]);
+                }
+              if constexpr (kAffine) mma_f16(xsum[j < (kAffine ? NT : 1) ? j : 0], ones_a, xr[2 * t], xr[2 * t + 1]);
+            }
+          }
+          if constexpr (kAffine) {
+            if ((sl + 1) % slabs_per_group == 0) {
+              const int grp = (sl + 1) / slabs_per_group - 1;
+              const int gpt = kChunkK / a.group_size;
+#pragma unroll
+              for (int m = 0; m < NM; ++m)
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                  const int r0 = 32 * warp + 16 * i + g;
+                  const uint32_t sb0 = lds32(st + m * tile_b + tile_code_bytes(FMT) + (r0 * gpt + grp) * 4);
+                  const uint32_t sb1 = lds32(st + m * tile_b + tile_code_bytes(FMT) + ((r0 + 8) * gpt + grp) * 4);
+                  const float s0 = __uint_as_float(sb0 << 16), b0 = __uint_as_float(sb0 & 0xFFFF0000u);
+                  const float s1 = __uint_as_float(sb1 << 16), b1 = __uint_as_float(sb1 & 0xFFFF0000u);
+                  const float c0 = fmaf(-1024.f, s0, b0), c1 = fmaf(-1024.f, s1, b1);
+#pragma unroll
+                  for (int j = 0; j < NT; ++j) {
+                    acc[m][i][j][0] += s0 * tmp[m][i][j][0] + c0 * xsum[j][0];
+                    acc[m][i][j][1] += s0 * tmp[m][i][j][1] + c0 * xsum[j][1];
+                    acc[m][i][j][2] += s1 * tmp[m][i][j][2] + c1 * xsum[j][2];
+                    acc[m][i][j][3] += s1 * tmp[m][i][j][3] + c1 * xsum[j][3];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) tmp[m][i][j][c] = 0.f;
+                  }
+                }
+#pragma unroll
+              for (int j = 0; j < NT; ++j)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) xsum[j][c] = 0.f;
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == n_stages) {
+        s = 0;
+        ph ^= 1u;
+      }
+    }
+    if (!ok) break;
+
+    // ---------------------------------------------------------------- epilogue
+    const float wmul_a = hdr_a[e];
+    const float wmul_b = DUAL ? hdr_b[e] : 1.f;
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int col = chunk * BN + j * 8 + 2 * q + (c & 1);
+          if (col >= cnt) continue;
+          const int rloc = 32 * warp + 16 * i + g + ((c & 2) ? 8 : 0);
+          const int64_t r = int64_t(off) + col;
+          const float xs = a.act_scale ? a.act_scale[r] : a.act_scale_const;
+          if constexpr (DUAL) {
+            float gv = acc[0][i][j][c] * xs * wmul_a;
+            float uv = acc[DUAL ? 1 : 0][i][j][c] * xs * wmul_b;
+            if (a.round_gu & 1) {
+              gv = bf16_round(gv);
+              uv = bf16_round(uv);
+            }
+            float h = apply_act(gv, uv, a.act, a.limit);
+            if (a.round_gu & 2) h = bf16_round(h);
+            a.h_out[(int64_t(rt) * a.h_rows_cap + r) * kStagePitch + rloc] = __float2half_rn(h * a.h_scale);
+          } else {
+            const int d = rt * kTileRows + rloc;
+            if (d >= a.out_rows) continue;
+            float v = acc[0][i][j][c] * xs * wmul_a;
+            if (a.round_o) v = bf16_round(v);
+            a.o_out[r * a.ldo + d] = v;
+          }
+        }
+  }
+}
+
+template <int FMT, bool DUAL, int NT>
+int launch_expert(const ExpertArgs& a, cudaStream_t stream) {
+  const int tile_b = tile_bytes(FMT, a.group_size);
+  const int act_b = 8 * NT * kStagePitch * 2;
+  const int stage_b = (DUAL ? 2 : 1) * tile_b + act_b;
+  const int budget = 200 * 1024;
+  int n_stages = std::min(8, budget / stage_b);
+  if (n_stages < 2) return fail(DSM_ERR_UNSUPPORTED, "expert kernel: tile too large for the shared-memory ring");
+  const size_t smem = size_t(n_stages) * stage_b + size_t(2 * n_stages) * 8 + size_t(a.n_experts + 2) * 4;
+  auto kern = expert_kernel<FMT, DUAL, NT>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return check_launch("expert kernel smem attribute");
+  kern<<<num_sms(), kThreads, smem, stream>>>(a, n_stages);
+  return check_launch("expert kernel");
+}
+
+template <bool DUAL>
+int dispatch(int wfmt, int nt, const ExpertArgs& a, cudaStream_t s) {
+#define DSM_NT_CASES(F)                                    \
+  if (nt == 1) return launch_expert<F, DUAL, 1>(a, s);     \
+  if (nt == 2) return launch_expert<F, DUAL, 2>(a, s);     \
+  return launch_expert<F, DUAL, 4>(a, s);
+  switch (wfmt) {
+    case DSM_WFMT_F16: { DSM_NT_CASES(DSM_WFMT_F16) }
+    case DSM_WFMT_FP8_B128: { DSM_NT_CASES(DSM_WFMT_FP8_B128) }
+    case DSM_WFMT_FP4_G32: { DSM_NT_CASES(DSM_WFMT_FP4_G32) }
+    case DSM_WFMT_AFFINE8: { DSM_NT_CASES(DSM_WFMT_AFFINE8) }
+    case DSM_WFMT_AFFINE4: { DSM_NT_CASES(DSM_WFMT_AFFINE4) }
+    default: return fail(DSM_ERR_INVALID_ARGUMENT, "expert kernel: unknown weight format");
+  }
+#undef DSM_NT_CASES
+}
+
+// n-tile count from the average rows per expert: decode draft blocks put one or two rows
+// on most experts, so one n8 tile keeps the tensor-core work per weight byte minimal.
+int pick_nt(int64_t n_rows, int n_experts) {
+  const int64_t busy = std::max<int64_t>(1, std::min<int64_t>(n_rows, n_experts));
+  const double avg = double(n_rows) / double(busy);
+  return avg <= 8.0 ? 1 : (avg <= 16.0 ? 2 : 4);
+}
+
+int check_common(int wfmt, int group_size, const int32_t* offsets, int n_experts) {
+  DSM_REQUIRE(wfmt >= DSM_WFMT_F16 && wfmt <= DSM_WFMT_AFFINE4, "expert: unknown weight format");
+  DSM_REQUIRE(n_experts >= 1 && n_experts <= 4096, "expert: n_experts out of range");
+  DSM_REQUIRE(offsets != nullptr, "expert: offsets is NULL");
+  if (wfmt == DSM_WFMT_AFFINE8)
+    DSM_REQUIRE(group_size == 32 || group_size == 64 || group_size == 128, "expert: affine8 group_size 32/64/128");
+  if (wfmt == DSM_WFMT_AFFINE4) DSM_REQUIRE(group_size == 64 || group_size == 128, "expert: affine4 group_size 64/128");
+  return DSM_OK;
+}
+
+}  // namespace
+}  // namespace dsm
+
+extern "C" int dsm_expert_gate_up(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int dim,
+                                  const int32_t* offsets, int n_experts, int wfmt, int group_size,
+                                  const void* w1_packed, const void* w3_packed, int inter, int act,
+                                  float swiglu_limit, int round_gu, void* h_staged, float h_scale, int64_t n_rows,
+                                  void* stream) {
+  using namespace dsm;
+  if (int rc = check_common(wfmt, group_size, offsets, n_experts)) return rc;
+  DSM_REQUIRE(dim > 0 && inter > 0 && n_rows >= 0, "dsm_expert_gate_up: bad shape");
+  DSM_REQUIRE(rows_cap >= dsm_stage_rows_cap(n_rows), "dsm_expert_gate_up: rows_cap too small");
+  DSM_REQUIRE(act == DSM_ACT_SWIGLU_CLAMP || act == DSM_ACT_SILU_MUL_BF16, "dsm_expert_gate_up: bad act");
+  DSM_REQUIRE(x_staged && x_row_scale && w1_packed && w3_packed && h_staged, "dsm_expert_gate_up: NULL pointer");
+  if (n_rows == 0) return DSM_OK;
+  ExpertArgs a{};
+  a.wa = static_cast<const uint8_t*>(w1_packed);
+  a.wb = static_cast<const uint8_t*>(w3_packed);
+  a.xin = static_cast<const __half*>(x_staged);
+  a.act_scale = x_row_scale;
+  a.act_scale_const = 1.f;
+  a.rows_cap = rows_cap;
+  a.offsets = offsets;
+  a.n_experts = n_experts;
+  a.out_rows = inter;
+  a.rt_count = int(ceil_div(inter, kTileRows));
+  a.kc_count = int(ceil_div(dim, kChunkK));
+  a.group_size = group_size > 0 ? group_size : 64;
+  a.act = act;
+  a.limit = swiglu_limit;
+  a.round_gu = round_gu;
+  a.h_scale = h_scale;
+  a.h_out = static_cast<__half*>(h_staged);
+  a.h_rows_cap = rows_cap;
+  return dispatch<true>(wfmt, pick_nt(n_rows, n_experts), a, as_stream(stream));
+}
+
+extern "C" int dsm_expert_down(const void* h_staged, float h_scale, int64_t rows_cap, int inter,
+                               const int32_t* offsets, int n_experts, int wfmt, int group_size, const void* w2_packed,
+                               int dim, int round_o, float* o_rows, int ldo, int64_t n_rows, void* stream) {
+  using namespace dsm;
+  if (int rc = check_common(wfmt, group_size, offsets, n_experts)) return rc;
+  DSM_REQUIRE(dim > 0 && inter > 0 && n_rows >= 0 && ldo >= dim, "dsm_expert_down: bad shape");
+  DSM_REQUIRE(rows_cap >= dsm_stage_rows_cap(n_rows), "dsm_expert_down: rows_cap too small");
+  DSM_REQUIRE(h_scale > 0.f, "dsm_expert_down: h_scale must be positive");
+  DSM_REQUIRE(h_staged && w2_packed && o_rows, "dsm_expert_down: NULL pointer");
+  if (n_rows == 0) return DSM_OK;
+  ExpertArgs a{};
+  a.wa = static_cast<const uint8_t*>(w2_packed);
+  a.wb = nullptr;
+  a.xin = static_cast<const __half*>(h_staged);
+  a.act_scale = nullptr;
+  a.act_scale_const = 1.f / h_scale;
+  a.rows_cap = rows_cap;
+  a.offsets = offsets;
+  a.n_experts = n_experts;
+  a.out_rows = dim;
+  a.rt_count = int(ceil_div(dim, kTileRows));
+  a.kc_count = int(ceil_div(inter, kChunkK));
+  a.group_size = group_size > 0 ? group_size : 64;
+  a.o_out = o_rows;
+  a.ldo = ldo;
+  a.round_o = round_o;
+  return dispatch<false>(wfmt, pick_nt(n_rows, n_experts), a, as_stream(stream));
+}

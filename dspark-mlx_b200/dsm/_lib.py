@@ -1,0 +1,137 @@
+"""ctypes bindings of ``libdsm.so`` (the C ABI declared in ``include/dsm.h``).
+
+The library is loaded from this directory; there is no fallback: if it is missing or was
+not built for this GPU, every entry point raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_float, c_int, c_int64, c_size_t, c_void_p
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libdsm.so")
+
+# status / enums (mirror include/dsm.h)
+DSM_OK = 0
+DT_F32, DT_BF16, DT_F16, DT_I32, DT_I64 = 0, 1, 2, 3, 4
+SCORE = {"softmax": 0, "sigmoid": 1, "sqrtsoftplus": 2}
+WFMT_F16, WFMT_FP8_B128, WFMT_FP4_G32, WFMT_AFFINE8, WFMT_AFFINE4 = 0, 1, 2, 3, 4
+ACT_SWIGLU_CLAMP, ACT_SILU_MUL_BF16 = 0, 1
+STAGE_PITCH = 160
+DEVICE_ERRORS = {0x10: "expert id out of range", 0x11: "token id out of range",
+                 0x12: "pipeline wait ran out of its time budget"}
+
+EXPORTED = (
+    "dsm_abi_version", "dsm_status_string", "dsm_last_error_message", "dsm_device_error",
+    "dsm_router", "dsm_permute_workspace_bytes", "dsm_permute", "dsm_stage_bytes",
+    "dsm_stage_rows_cap", "dsm_stage_rows", "dsm_packed_bytes", "dsm_pack_weights",
+    "dsm_affine_quantize", "dsm_expert_gate_up", "dsm_expert_down", "dsm_combine",
+    "dsm_moe_workspace_bytes", "dsm_moe_forward",
+)
+
+
+class MoEDesc(ctypes.Structure):
+    """``dsm_moe_desc`` (field order and types follow the C struct)."""
+
+    _fields_ = [
+        ("n_tokens", c_int64),
+        ("dim", c_int), ("inter", c_int), ("n_experts", c_int), ("topk", c_int),
+        ("score_func", c_int),
+        ("route_scale", c_float), ("swiglu_limit", c_float),
+        ("gate_weight", c_void_p), ("gate_bias", c_void_p), ("tid2eid", c_void_p),
+        ("vocab", c_int64),
+        ("wfmt", c_int), ("group_size", c_int),
+        ("w1", c_void_p), ("w3", c_void_p), ("w2", c_void_p),
+        ("round_gu", c_int), ("round_o", c_int),
+        ("shared_wfmt", c_int), ("shared_group_size", c_int),
+        ("s1", c_void_p), ("s3", c_void_p), ("s2", c_void_p),
+        ("shared_inter", c_int), ("shared_round_gu", c_int), ("shared_round_o", c_int),
+        ("act", c_int),
+    ]
+
+
+class DsmError(RuntimeError):
+    pass
+
+
+_lib = None
+
+
+def _declare(lib):
+    V, I, I64, F, S = c_void_p, c_int, c_int64, c_float, c_size_t
+    sig = {
+        "dsm_abi_version": (I, []),
+        "dsm_status_string": (ctypes.c_char_p, [I]),
+        "dsm_last_error_message": (ctypes.c_char_p, []),
+        "dsm_device_error": (I, [POINTER(c_int), I, V]),
+        "dsm_router": (I, [V, I, I64, I, V, I, V, V, I64, V, I, I64, I, I, F, V, V, V, V]),
+        "dsm_permute_workspace_bytes": (S, [I64, I]),
+        "dsm_permute": (I, [V, I64, I, V, V, V, V, V, S, V]),
+        "dsm_stage_bytes": (S, [I64, I]),
+        "dsm_stage_rows_cap": (I64, [I64]),
+        "dsm_stage_rows": (I, [V, I, I64, I, V, I64, I, V, I64, V, V]),
+        "dsm_packed_bytes": (S, [I, I, I, I, I]),
+        "dsm_pack_weights": (I, [I, I, I, I, I, I, V, V, V, V, V, V]),
+        "dsm_affine_quantize": (I, [V, I, I64, I, I, I, V, V, V, V]),
+        "dsm_expert_gate_up": (I, [V, V, I64, I, V, I, I, I, V, V, I, I, F, I, V, F, I64, V]),
+        "dsm_expert_down": (I, [V, F, I64, I, V, I, I, I, V, I, I, V, I, I64, V]),
+        "dsm_combine": (I, [V, V, V, I64, I, I, V, V, I, V]),
+        "dsm_moe_workspace_bytes": (S, [POINTER(MoEDesc)]),
+        "dsm_moe_forward": (I, [POINTER(MoEDesc), V, I, V, I, I64, V, V, V, V, S, V]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+
+
+def lib():
+    """The loaded library (raises if ``libdsm.so`` is missing: there is no CPU fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise DsmError(f"{LIB_PATH} is missing; build it with `python -m dsm.build`")
+        handle = ctypes.CDLL(LIB_PATH)
+        _declare(handle)
+        if handle.dsm_abi_version() != 1:
+            raise DsmError("libdsm ABI version mismatch")
+        _lib = handle
+    return _lib
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != DSM_OK:
+        L = lib()
+        msg = L.dsm_last_error_message().decode() or L.dsm_status_string(rc).decode()
+        raise DsmError(f"{what}: {msg}" if what else msg)
+
+
+def device_error(clear: bool = True, stream=None) -> int:
+    """Read the device-side error word (synchronises the stream)."""
+    code = c_int(0)
+    check(lib().dsm_device_error(ctypes.byref(code), int(clear), stream_ptr(stream)), "dsm_device_error")
+    return code.value
+
+
+def raise_device_error(stream=None) -> None:
+    code = device_error(True, stream)
+    if code:
+        raise DsmError(f"device error 0x{code:x}: {DEVICE_ERRORS.get(code, 'unknown')}")
+
+
+def stream_ptr(stream=None) -> int:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return int(stream.cuda_stream)
+
+
+def ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    return {torch.float32: DT_F32, torch.bfloat16: DT_BF16, torch.float16: DT_F16,
+            torch.int32: DT_I32, torch.int64: DT_I64}[dt]

@@ -1,0 +1,219 @@
+"""Seeded synthetic MoE workloads (the shapes the DSpark draft MoE is measured on).
+
+No dataset is involved: every tensor is drawn from a seeded ``torch.Generator``.
+
+* ``tiny_hash``    hidden 256, 16 routed + 1 shared expert, top-2 hash routing over a
+                   1024-token vocabulary (seeded map, 2 distinct experts per id), expert
+                   inter 128, bf16 weights N(0, 0.02), x N(0, 1) [7, 256].
+* ``fp8_decode``   hidden 4096, 256 experts, top-6 sigmoid + bias N(0, 0.02), route scale
+                   2.5, inter 2048; e4m3 codes of N(0, 1) draws with fp32 128x128 block
+                   scales log-uniform in [2^-10, 2^-4]; bf16 shared expert N(0, 0.02);
+                   x bf16 N(0, 1) [56, 4096] (8 sequences x 7 draft tokens).
+* ``fp4_decode``   as fp8_decode with e2m1 codes (uniform over the 16 codes), e4m3 group-32
+                   scales 2^U(-3, 3) and an fp32 per-expert scale 2^U(-9, -7); 448 tokens
+                   (64 x 7); Zipf(1.1) routing skew.
+* ``qwen3_mlp_q8`` dense SwiGLU hidden 2560 / inter 9728, MLX affine 8-bit group 64,
+                   x [112, 2560] (16 x 7), no clamp.
+* ``prefill_fp8``  16384 tokens, 256 experts, top-8, fp8 experts, Zipf(1.2) skew.
+
+Zipf skew: expert ``e`` with popularity rank ``r_e`` (a seeded permutation) gets a selection
+offset ``-alpha * beta * ln(r_e)`` added to its gate bias, with ``beta = 0.2`` (the spread of
+the sigmoid scores of N(0, 1.64) logits); with Gumbel-like score noise of that spread the
+top-1 choice frequency falls off as ``r^-alpha``. The bias steers selection only, as in the
+reference gate (``dspark_mlx/model/moe.py:74-75``).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Dict, Optional
+
+import torch
+
+ZIPF_BETA = 0.2
+
+
+@dataclass
+class Workload:
+    name: str
+    args: Dict
+    n_tokens: int
+    wfmt: str  # "bf16" | "fp8" | "fp4" | "affine8"
+    layer_id: int = 0
+    zipf_alpha: Optional[float] = None
+    seed: int = 0
+    batch: int = 1
+    block: int = 7
+    notes: str = ""
+    extra: Dict = field(default_factory=dict)
+
+
+def _args(**kw):
+    base = dict(n_shared_experts=1, swiglu_limit=10.0, n_hash_layers=0)
+    base.update(kw)
+    return base
+
+
+WORKLOADS = {
+    "tiny_hash": Workload(
+        "tiny_hash", _args(vocab_size=1024, dim=256, moe_inter_dim=128, n_routed_experts=16, n_activated_experts=2,
+                           n_hash_layers=1, score_func="sqrtsoftplus", route_scale=1.5),
+        n_tokens=7, wfmt="bf16", layer_id=0, batch=1),
+    "fp8_decode": Workload(
+        "fp8_decode", _args(vocab_size=129280, dim=4096, moe_inter_dim=2048, n_routed_experts=256,
+                            n_activated_experts=6, score_func="sigmoid", route_scale=2.5),
+        n_tokens=56, wfmt="fp8", batch=8),
+    "fp4_decode": Workload(
+        "fp4_decode", _args(vocab_size=129280, dim=4096, moe_inter_dim=2048, n_routed_experts=256,
+                            n_activated_experts=6, score_func="sigmoid", route_scale=2.5),
+        n_tokens=448, wfmt="fp4", zipf_alpha=1.1, batch=64),
+    "qwen3_mlp_q8": Workload(
+        "qwen3_mlp_q8", dict(hidden_size=2560, intermediate_size=9728), n_tokens=112, wfmt="affine8", batch=16),
+    "prefill_fp8": Workload(
+        "prefill_fp8", _args(vocab_size=129280, dim=4096, moe_inter_dim=2048, n_routed_experts=256,
+                             n_activated_experts=8, score_func="sigmoid", route_scale=2.5),
+        n_tokens=16384, wfmt="fp8", zipf_alpha=1.2, batch=1, block=16384),
+}
+
+
+def zipf_offsets(n_experts: int, alpha: float, gen: torch.Generator) -> torch.Tensor:
+    ranks = torch.randperm(n_experts, generator=gen).to(torch.float64) + 1.0
+    return (-alpha * ZIPF_BETA * torch.log(ranks)).to(torch.float32)
+
+
+def _randn(shape, gen, device, std=1.0, dtype=torch.float32):
+    return (torch.randn(shape, generator=gen, device=device) * std).to(dtype)
+
+
+def e4m3_codes(shape, gen, device) -> torch.Tensor:
+    v = torch.randn(shape, generator=gen, device=device).clamp_(-448, 448)
+    return v.to(torch.float8_e4m3fn).view(torch.uint8)
+
+
+def make_moe_tensors(wl: Workload, device="cpu", seed: Optional[int] = None, n_tokens: Optional[int] = None,
+                     experts_subset: Optional[int] = None, routed: bool = True) -> Dict[str, torch.Tensor]:
+    """All tensors of one MoE call of workload ``wl``, generated on ``device``.
+
+    ``experts_subset`` shrinks the routed expert count (keeping every other shape) for
+    tests that must fit a CPU oracle; ``n_tokens`` overrides the token count;
+    ``routed=False`` skips the routed expert stacks (see :func:`expert_tensors`).
+    """
+    a = dict(wl.args)
+    if experts_subset:
+        a["n_routed_experts"] = experts_subset
+    E, dim, inter, k = a["n_routed_experts"], a["dim"], a["moe_inter_dim"], a["n_activated_experts"]
+    N = n_tokens or wl.n_tokens
+    gen = torch.Generator(device=device)
+    gen.manual_seed(wl.seed if seed is None else seed)
+    out: Dict[str, torch.Tensor] = {"args": a}
+    out["x"] = _randn((N, dim), gen, device, dtype=torch.bfloat16)
+    out["gate_weight"] = _randn((E, dim), gen, device, std=0.02)
+    if wl.layer_id < a.get("n_hash_layers", 0):
+        vocab = a["vocab_size"]
+        keys = torch.rand((vocab, E), generator=gen, device=device)
+        out["tid2eid"] = keys.argsort(dim=1)[:, :k].to(torch.int32)
+        out["input_ids"] = torch.randint(0, vocab, (N,), generator=gen, device=device, dtype=torch.int32)
+    else:
+        bias = _randn((E,), gen, device, std=0.02)
+        if wl.zipf_alpha:
+            g2 = torch.Generator(device="cpu")
+            g2.manual_seed((wl.seed if seed is None else seed) + 7919)
+            bias = bias + zipf_offsets(E, wl.zipf_alpha, g2).to(device)
+        out["gate_bias"] = bias
+    shapes = {"w1": (E, inter, dim), "w3": (E, inter, dim), "w2": (E, dim, inter)}
+    for n, shp in (shapes.items() if routed else ()):
+        if wl.wfmt == "bf16":
+            out[n] = _randn(shp, gen, device, std=0.02, dtype=torch.bfloat16)
+        elif wl.wfmt == "fp8":
+            out[n + "_codes"] = e4m3_codes(shp, gen, device)
+            sb = (shp[0], -(-shp[1] // 128), -(-shp[2] // 128))
+            out[n + "_scale"] = torch.exp2(torch.rand(sb, generator=gen, device=device) * 6.0 - 10.0)
+        elif wl.wfmt == "fp4":
+            nib = torch.randint(0, 16, shp, generator=gen, device=device, dtype=torch.int32)
+            out[n + "_codes"] = (nib[..., 0::2] | (nib[..., 1::2] << 4)).to(torch.uint8)
+            gsh = (shp[0], shp[1], shp[2] // 32)
+            gs = torch.exp2(torch.rand(gsh, generator=gen, device=device) * 6.0 - 3.0)
+            out[n + "_scale"] = gs.to(torch.float8_e4m3fn).view(torch.uint8)
+            out[n + "_tensor_scale"] = torch.exp2(torch.rand((shp[0],), generator=gen, device=device) * 2.0 - 9.0)
+        else:
+            raise ValueError(wl.wfmt)
+    for n, shp in (("shared_w1", (inter, dim)), ("shared_w2", (dim, inter)), ("shared_w3", (inter, dim))):
+        out[n] = _randn(shp, gen, device, std=0.02, dtype=torch.bfloat16)
+    return out
+
+
+def build_moe(wl: Workload, t: Dict[str, torch.Tensor], device="cuda"):
+    """A ``dsm.MoE`` holding the tensors of ``make_moe_tensors``."""
+    from .config import DSparkArgs
+    from .moe import MoE
+
+    args = DSparkArgs.from_dict(t["args"])
+    moe = MoE(args, wl.layer_id)
+    moe.gate.weight = t["gate_weight"].to(device)
+    if "tid2eid" in t:
+        moe.gate.tid2eid = t["tid2eid"].to(device)
+    else:
+        moe.gate.bias = t["gate_bias"].to(device)
+    if wl.wfmt == "bf16":
+        for n in ("w1", "w3", "w2"):
+            setattr(moe, n, t[n].to(device))
+    elif wl.wfmt == "fp8":
+        moe.load_fp8_experts(**{n: (t[n + "_codes"].to(device), t[n + "_scale"].to(device)) for n in ("w1", "w3", "w2")})
+    elif wl.wfmt == "fp4":
+        moe.load_fp4_experts(**{n: (t[n + "_codes"].to(device), t[n + "_scale"].to(device),
+                                    t[n + "_tensor_scale"].to(device)) for n in ("w1", "w3", "w2")})
+    for n in ("w1", "w2", "w3"):
+        getattr(moe.shared_experts, n).weight = torch.nn.Parameter(t["shared_" + n].to(device), requires_grad=False)
+    return moe.to(device)
+
+
+def routed_weight_bytes(wl: Workload, counts: torch.Tensor, args: Optional[Dict] = None) -> int:
+    """Bytes of routed expert weights a call must read: every expert with a nonzero count."""
+    a = args or wl.args
+    dim, inter = a["dim"], a["moe_inter_dim"]
+    touched = int((counts > 0).sum())
+    per = 3 * inter * dim
+    if wl.wfmt == "fp8":
+        per_b = per + 3 * math.ceil(inter / 128) * math.ceil(dim / 128) * 4
+    elif wl.wfmt == "fp4":
+        per_b = per // 2 + 3 * inter * dim // 32 + 3 * 4
+    elif wl.wfmt == "bf16":
+        per_b = per * 2
+    else:
+        per_b = per + 3 * inter * (dim // 64) * 4
+    return touched * per_b
+
+
+def expert_tensors(wl: Workload, experts, seed: Optional[int] = None) -> Dict[str, torch.Tensor]:
+    """Routed expert weights for the listed experts only, stacked in that order, on the CPU.
+
+    Each expert comes from its own generator (seeded by the workload seed and the expert
+    id), so any subset can be produced without materialising the whole stack.
+    """
+    a = wl.args
+    dim, inter = a["dim"], a["moe_inter_dim"]
+    base = (wl.seed if seed is None else seed) * 1_000_003 + 17
+    parts: Dict[str, list] = {}
+    for e in experts:
+        gen = torch.Generator()
+        gen.manual_seed(base + int(e))
+        one = Workload(wl.name, dict(a, n_routed_experts=1), n_tokens=1, wfmt=wl.wfmt)
+        shapes = {"w1": (1, inter, dim), "w3": (1, inter, dim), "w2": (1, dim, inter)}
+        for n, shp in shapes.items():
+            if wl.wfmt == "bf16":
+                vals = {n: _randn(shp, gen, "cpu", std=0.02, dtype=torch.bfloat16)}
+            elif wl.wfmt == "fp8":
+                sb = (1, -(-shp[1] // 128), -(-shp[2] // 128))
+                vals = {n + "_codes": e4m3_codes(shp, gen, "cpu"),
+                        n + "_scale": torch.exp2(torch.rand(sb, generator=gen) * 6.0 - 10.0)}
+            else:
+                nib = torch.randint(0, 16, shp, generator=gen, dtype=torch.int32)
+                gs = torch.exp2(torch.rand((1, shp[1], shp[2] // 32), generator=gen) * 6.0 - 3.0)
+                vals = {n + "_codes": (nib[..., 0::2] | (nib[..., 1::2] << 4)).to(torch.uint8),
+                        n + "_scale": gs.to(torch.float8_e4m3fn).view(torch.uint8),
+                        n + "_tensor_scale": torch.exp2(torch.rand((1,), generator=gen) * 2.0 - 9.0)}
+            for k, v in vals.items():
+                parts.setdefault(k, []).append(v)
+        del one
+    return {k: torch.cat(v, 0) for k, v in parts.items()}

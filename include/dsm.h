@@ -1,0 +1,189 @@
+/*
+ * dsm.h -- C ABI of libdsm, a B200 (sm_100a) implementation of the DeepSeek-V4 DSpark
+ * draft-layer Mixture-of-Experts block (router, token permutation, grouped quantised
+ * expert SwiGLU products, weighted combine and shared expert).
+ *
+ * Conventions
+ *   - Every pointer argument is a device pointer unless stated otherwise; all buffers are
+ *     owned by the caller. No entry point allocates device memory: scratch space comes
+ *     from a caller-provided workspace whose size a *_workspace_bytes query returns.
+ *   - Every call is ordered on the given CUDA stream (passed as void*, a cudaStream_t;
+ *     NULL is the legacy default stream) and returns immediately.
+ *   - Return value: DSM_OK (0) or a nonzero dsm status. No C++ exception crosses the ABI.
+ *     dsm_last_error_message() gives a description of the last failure on this thread.
+ *   - Data-dependent faults that can only be seen on the device (an expert id outside
+ *     [0, n_experts), a token id outside the hash table, a pipeline wait that ran out of
+ *     its time budget) are recorded in a device-side error word that
+ *     dsm_device_error() reads; the kernel skips the offending access instead of faulting.
+ *
+ * Reference interface each entry point replaces (dspark_mlx, file:line):
+ *   dsm_router          Gate.__call__                       model/moe.py:62-79
+ *   dsm_permute         (implicit in gather_mm rhs_indices)  model/moe.py:145-148
+ *   dsm_stage_rows      gather_mm lhs broadcast x[N,1,1,dim]  model/moe.py:158
+ *   dsm_expert_gate_up  gather_mm / gather_qmm w1, w3 + _swiglu  model/moe.py:37-44,138-147
+ *   dsm_expert_down     gather_mm / gather_qmm w2             model/moe.py:143,148
+ *   dsm_combine         sum_k o * weights + shared, cast      model/moe.py:159-161
+ *   dsm_moe_forward     MoE.__call__                          model/moe.py:151-161
+ *   dsm_affine_quantize mx.quantize in MoE.quantize           model/moe.py:124-130
+ *   dsm_pack_weights    stacked [E,out,in] expert weights      loading.py:88-100 (+103-114)
+ */
+#ifndef DSM_H_
+#define DSM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSM_ABI_VERSION 1
+
+/* status codes */
+#define DSM_OK 0
+#define DSM_ERR_INVALID_ARGUMENT 1
+#define DSM_ERR_UNSUPPORTED 2
+#define DSM_ERR_WORKSPACE 3
+#define DSM_ERR_CUDA 4
+/* device-side error word values */
+#define DSM_DEV_ERR_EXPERT_RANGE 0x10
+#define DSM_DEV_ERR_TOKEN_RANGE 0x11
+#define DSM_DEV_ERR_PIPELINE_TIMEOUT 0x12
+
+/* element types */
+#define DSM_DT_F32 0
+#define DSM_DT_BF16 1
+#define DSM_DT_F16 2
+#define DSM_DT_I32 3
+#define DSM_DT_I64 4
+
+/* Gate.score_func (model/config.py:33) */
+#define DSM_SCORE_SOFTMAX 0
+#define DSM_SCORE_SIGMOID 1
+#define DSM_SCORE_SQRTSOFTPLUS 2
+
+/* expert weight storage formats */
+#define DSM_WFMT_F16 0      /* bf16/fp32 weights held as f16 with a per-expert power-of-two scale */
+#define DSM_WFMT_FP8_B128 1 /* e4m3 codes, fp32 scale per 128x128 block (loading.py:103-107) */
+#define DSM_WFMT_FP4_G32 2  /* e2m1 codes, e4m3 scale per 32 along K, fp32 per expert (loading.py:110-114) */
+#define DSM_WFMT_AFFINE8 3  /* MLX affine 8-bit: q*scale+bias per group (moe.py:124-130) */
+#define DSM_WFMT_AFFINE4 4  /* MLX affine 4-bit */
+
+/* activation applied between the gate/up and down products */
+#define DSM_ACT_SWIGLU_CLAMP 0 /* _swiglu, fp32, asymmetric clamp at swiglu_limit (moe.py:37-44) */
+#define DSM_ACT_SILU_MUL_BF16 1 /* silu(g)*u with every op rounded to bf16 (arch/qwen3.py:153-154) */
+
+int dsm_abi_version(void);
+const char* dsm_status_string(int status);
+const char* dsm_last_error_message(void);
+
+/* Read (and optionally clear) the device-side error word of the current device.
+ * Synchronises the stream. *code receives 0 or a DSM_DEV_ERR_* value. */
+int dsm_device_error(int* code, int clear, void* stream);
+
+/* ---- router: Gate.__call__ (model/moe.py:62-79) ---------------------------------------
+ * x [n_tokens, dim] (x_dtype F32 or BF16); gate_weight [n_experts, dim] fp32.
+ * Score mode: gate_bias [n_experts] fp32, tid2eid = NULL. Hash mode: gate_bias = NULL,
+ * tid2eid [vocab, topk] int32 and input_ids (I32 or I64) of length n_ids == n_tokens or 1.
+ * scores_ws: [n_tokens, n_experts] fp32 scratch. Outputs weights [n_tokens, topk] fp32 and
+ * indices [n_tokens, topk] int32 (ascending by biased score: best expert in the last slot). */
+int dsm_router(const void* x, int x_dtype, int64_t n_tokens, int dim, const float* gate_weight,
+               int n_experts, const float* gate_bias, const int32_t* tid2eid, int64_t vocab,
+               const void* input_ids, int ids_dtype, int64_t n_ids, int topk, int score_func,
+               float route_scale, float* scores_ws, float* weights_out, int32_t* indices_out,
+               void* stream);
+
+/* ---- permutation (defines per-expert token lists) ------------------------------------
+ * indices [n_pairs] int32 (the flattened [n_tokens, topk] routing). Outputs counts [E],
+ * offsets [E+1], perm [n_pairs] (sorted position -> pair id, stable), inv [n_pairs]. */
+size_t dsm_permute_workspace_bytes(int64_t n_pairs, int n_experts);
+int dsm_permute(const int32_t* indices, int64_t n_pairs, int n_experts, int32_t* counts,
+                int32_t* offsets, int32_t* perm, int32_t* inv, void* workspace,
+                size_t workspace_bytes, void* stream);
+
+/* ---- activation staging ---------------------------------------------------------------
+ * Writes rows of x (row r = token perm[r] / topk, or token r when perm is NULL) into the
+ * K-chunked f16 layout the expert kernels stream: chunk c holds columns [128c, 128c+128)
+ * of every row, rows_cap rows of DSM_STAGE_PITCH halves each. Each row is scaled by a
+ * power of two so its largest magnitude lies in [2^14, 2^15); row_scale[r] receives the
+ * inverse (exact) factor. Columns past k_dim are written as zeros. */
+#define DSM_STAGE_PITCH 160
+size_t dsm_stage_bytes(int64_t rows_cap, int k_dim);
+int64_t dsm_stage_rows_cap(int64_t n_rows);
+int dsm_stage_rows(const void* x, int x_dtype, int64_t n_tokens, int dim, const int32_t* perm,
+                   int64_t n_rows, int topk, void* staged, int64_t rows_cap, float* row_scale,
+                   void* stream);
+
+/* ---- expert weight packing (load time) ------------------------------------------------
+ * Converts stacked expert weights [n_experts, rows, cols] (nn.Linear [out, in] layout)
+ * into the tile stream the expert kernels read. Source arrays per format:
+ *   F16:      codes = weights (src_dtype F32 or BF16)
+ *   FP8_B128: codes uint8 e4m3 [E,rows,cols]; scales fp32 [E,ceil(rows/128),ceil(cols/128)]
+ *   FP4_G32:  codes uint8 [E,rows,cols/2] (element 2j low nibble); scales uint8 e4m3
+ *             [E,rows,cols/32]; tensor_scale fp32 [E]
+ *   AFFINE8/4: codes uint8 [E,rows,cols*bits/8] (byte view of MLX's uint32 packing);
+ *             scales, biases bf16 [E,rows,cols/group_size]
+ * The packed buffer must not alias the sources. */
+size_t dsm_packed_bytes(int wfmt, int n_experts, int rows, int cols, int group_size);
+int dsm_pack_weights(int wfmt, int n_experts, int rows, int cols, int group_size, int src_dtype,
+                     const void* codes, const void* scales, const void* biases,
+                     const float* tensor_scale, void* packed, void* stream);
+
+/* ---- affine quantisation (mx.quantize restated) ---------------------------------------
+ * w [n_rows, cols] (F32 or BF16) -> codes uint8 [n_rows, cols*bits/8], scales and biases
+ * [n_rows, cols/group_size] in w's dtype. bits 4 or 8; group_size 32, 64 or 128. */
+int dsm_affine_quantize(const void* w, int w_dtype, int64_t n_rows, int cols, int group_size,
+                        int bits, uint8_t* codes, void* scales, void* biases, void* stream);
+
+/* ---- grouped expert products ----------------------------------------------------------
+ * Rows of expert e are the staged rows [offsets[e], offsets[e+1]).
+ * gate_up: h = act(x W1^T, x W3^T) for every row, written to the staged layout of h
+ *   (k_dim = inter) scaled by h_scale (power of two). round_gu bit 0: round the two
+ *   products to bf16 before the activation (the reference's products are bf16 for bf16 or
+ *   affine weights with bf16 x); bit 1: round h to bf16 (the reference casts h to x's dtype).
+ * down: o = h W2^T (h read with scale 1/h_scale), fp32 rows [n_rows, ldo];
+ *   round_o: round o to bf16 first. */
+int dsm_expert_gate_up(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int dim,
+                       const int32_t* offsets, int n_experts, int wfmt, int group_size,
+                       const void* w1_packed, const void* w3_packed, int inter, int act,
+                       float swiglu_limit, int round_gu, void* h_staged, float h_scale,
+                       int64_t n_rows, void* stream);
+int dsm_expert_down(const void* h_staged, float h_scale, int64_t rows_cap, int inter,
+                    const int32_t* offsets, int n_experts, int wfmt, int group_size,
+                    const void* w2_packed, int dim, int round_o, float* o_rows, int ldo,
+                    int64_t n_rows, void* stream);
+
+/* ---- combine: y = sum_s o[inv[t*k+s]] * w[t,s] (+ shared[t]) -> y_dtype --------------- */
+int dsm_combine(const float* o_sorted, const int32_t* inv, const float* route_weights,
+                int64_t n_tokens, int topk, int dim, const float* shared_rows, void* y,
+                int y_dtype, void* stream);
+
+/* ---- whole MoE.__call__ -----------------------------------------------------------------*/
+typedef struct dsm_moe_desc {
+  int64_t n_tokens; /* tokens of x (after flattening) */
+  int dim, inter, n_experts, topk;
+  int score_func;
+  float route_scale, swiglu_limit;
+  const float* gate_weight; /* [E, dim] */
+  const float* gate_bias;   /* [E] (score mode) or NULL */
+  const int32_t* tid2eid;   /* [vocab, topk] (hash mode) or NULL */
+  int64_t vocab;
+  int wfmt, group_size;     /* routed experts */
+  const void *w1, *w3, *w2; /* packed */
+  int round_gu, round_o;
+  int shared_wfmt, shared_group_size; /* shared expert; s1 == NULL: none */
+  const void *s1, *s3, *s2;
+  int shared_inter, shared_round_gu, shared_round_o;
+  int act;
+} dsm_moe_desc;
+
+size_t dsm_moe_workspace_bytes(const dsm_moe_desc* d);
+int dsm_moe_forward(const dsm_moe_desc* d, const void* x, int x_dtype, const void* input_ids,
+                    int ids_dtype, int64_t n_ids, void* y, float* route_weights_out,
+                    int32_t* route_indices_out, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DSM_H_ */

@@ -1,0 +1,86 @@
+"""The C-ABI library loads, exports every entry point ``include/dsm.h`` declares, and
+answers size queries / rejects bad arguments on the host (no GPU work)."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from dsm import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "dsm.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(dsm_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert "dsm_moe_forward" in names and "dsm_router" in names
+    assert set(names) == set(_lib.EXPORTED), set(names) ^ set(_lib.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol():
+    raw = ctypes.CDLL(_lib.LIB_PATH)
+    for name in _declared():
+        assert hasattr(raw, name), f"{name} not exported"
+
+
+def test_abi_version_and_status_strings():
+    L = _lib.lib()
+    assert L.dsm_abi_version() == 1
+    assert L.dsm_status_string(0) == b"ok"
+    assert L.dsm_status_string(1) == b"invalid argument"
+
+
+def test_size_queries():
+    L = _lib.lib()
+    # fp8 tile: 16 KB codes + 16 B scale; 256 B header for <= 64 experts
+    assert L.dsm_packed_bytes(_lib.WFMT_FP8_B128, 2, 128, 256, 128) == 256 + 2 * 2 * (16384 + 16)
+    assert L.dsm_packed_bytes(_lib.WFMT_FP4_G32, 1, 128, 128, 32) == 256 + 8192 + 512
+    assert L.dsm_packed_bytes(_lib.WFMT_F16, 1, 100, 100, 0) == 256 + 32768  # padded to one tile
+    assert L.dsm_packed_bytes(_lib.WFMT_AFFINE8, 1, 128, 128, 64) == 256 + 16384 + 1024
+    assert L.dsm_packed_bytes(99, 1, 128, 128, 64) == 0
+    cap = L.dsm_stage_rows_cap(336)
+    assert cap >= 336 + 32 and cap % 8 == 0
+    assert L.dsm_stage_bytes(cap, 4096) == 32 * cap * 160 * 2
+    assert L.dsm_permute_workspace_bytes(131072, 256) == 128 * 256 * 4
+    d = _lib.MoEDesc(n_tokens=56, dim=4096, inter=2048, n_experts=256, topk=6)
+    d.s1 = 1
+    assert L.dsm_moe_workspace_bytes(ctypes.byref(d)) > 56 * 6 * 4096 * 4
+
+
+@pytest.mark.parametrize("call", ["router", "permute", "combine", "quantize"])
+def test_bad_arguments_are_rejected_on_the_host(call):
+    L = _lib.lib()
+    if call == "router":
+        rc = L.dsm_router(None, _lib.DT_BF16, 4, 0, None, 8, None, None, 0, None, _lib.DT_I32, 0, 2, 1, 1.0,
+                          None, None, None, None)
+    elif call == "permute":
+        rc = L.dsm_permute(None, 10, 0, None, None, None, None, None, 0, None)
+    elif call == "combine":
+        rc = L.dsm_combine(None, None, None, 4, 0, 16, None, None, _lib.DT_BF16, None)
+    else:
+        rc = L.dsm_affine_quantize(None, _lib.DT_BF16, 4, 100, 64, 8, None, None, None, None)
+    assert rc == 1
+    assert L.dsm_last_error_message().decode()
+
+
+def test_desc_struct_layout_matches_header():
+    # field offsets of the ctypes mirror must follow the C struct (8-byte pointers, int64 first)
+    assert _lib.MoEDesc.n_tokens.offset == 0
+    assert _lib.MoEDesc.gate_weight.offset % 8 == 0
+    assert ctypes.sizeof(_lib.MoEDesc) % 8 == 0
+    names = [f for f, _ in _lib.MoEDesc._fields_]
+    text = open(HEADER).read()
+    body = text[text.index("typedef struct dsm_moe_desc"):text.index("} dsm_moe_desc;")]
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    c_fields = re.findall(r"\*?\s*([a-z_0-9]+)\s*[,;]", body)
+    assert c_fields == names
