@@ -31,7 +31,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "MoE-layer tokens/s & draft-block latency; HBM GB/s vs 8 TB/s at 1/2/4/8 B200"
 SPEC_HBM_GBS = 8000.0
-KERNELS_PER_STEP = 14  # router 2, permute 3, stage 1, gate/up 1, down 1, shared 4, combine 1
+KERNELS_PER_STEP = 10  # router 3, permute 1, staging 1, routed gate/up + down 2, shared gate/up + down 2, combine 1
 
 
 def _peaks():

@@ -10,10 +10,11 @@ template <typename YT>
 __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ o, const int32_t* __restrict__ inv,
                                                       const float* __restrict__ w, int64_t n_tokens, int topk,
                                                       int dim, const float* __restrict__ shared, YT* __restrict__ y) {
+  // grid (tokens, column blocks): one thread per 4 consecutive columns of one token
   const int64_t t = blockIdx.x;
   const int32_t* it = inv + t * topk;
   const float* wt = w + t * topk;
-  for (int d = threadIdx.x * 4; d < dim; d += blockDim.x * 4) {
+  for (int d = (blockIdx.y * blockDim.x + threadIdx.x) * 4; d < dim; d += gridDim.y * blockDim.x * 4) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int s = 0; s < topk; ++s) {
       const float ws = wt[s];
@@ -51,13 +52,14 @@ extern "C" int dsm_combine(const float* o_sorted, const int32_t* inv, const floa
   DSM_REQUIRE(o_sorted && inv && route_weights && y, "dsm_combine: NULL pointer");
   DSM_REQUIRE(n_tokens < (int64_t(1) << 31), "dsm_combine: too many tokens");
   cudaStream_t s = as_stream(stream);
-  const int threads = dim >= 1024 ? 256 : 128;
+  const int threads = 128;
+  const dim3 grid(unsigned(n_tokens), unsigned(ceil_div(ceil_div(dim, 4), threads)));
   if (y_dtype == DSM_DT_BF16)
-    combine_kernel<__nv_bfloat16><<<unsigned(n_tokens), threads, 0, s>>>(o_sorted, inv, route_weights, n_tokens, topk,
+    combine_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(o_sorted, inv, route_weights, n_tokens, topk,
                                                                          dim, shared_rows,
                                                                          static_cast<__nv_bfloat16*>(y));
   else
-    combine_kernel<float><<<unsigned(n_tokens), threads, 0, s>>>(o_sorted, inv, route_weights, n_tokens, topk, dim,
+    combine_kernel<float><<<grid, threads, 0, s>>>(o_sorted, inv, route_weights, n_tokens, topk, dim,
                                                                  shared_rows, static_cast<float*>(y));
   return check_launch("combine");
 }

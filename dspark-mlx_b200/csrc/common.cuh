@@ -27,6 +27,12 @@ int check_launch(const char* what);
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 int num_sms();
 
+// Stage two row sets of the same x in one launch: rows of x in perm order (job a) and, when
+// n_rows_b > 0, the first n_rows_b tokens in order (job b). Arguments as dsm_stage_rows.
+int stage_rows_pair(const void* x, int x_dtype, int64_t n_tokens, int dim, const int32_t* perm, int64_t n_rows,
+                    int topk, void* staged, int64_t rows_cap, float* row_scale, int64_t n_rows_b, void* staged_b,
+                    int64_t rows_cap_b, float* row_scale_b, void* stream);
+
 // ------------------------------------------------------------------------------------------
 // geometry shared by staging, packing and the expert kernels
 // ------------------------------------------------------------------------------------------

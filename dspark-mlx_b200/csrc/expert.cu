@@ -26,6 +26,7 @@
 // reference casts h to x.dtype) -> staged f16 rows for the down kernel. Epilogue of the
 // down kernel: fp32 rows of o (optionally rounded to bf16).
 #include <algorithm>
+#include <cmath>
 
 #include "common.cuh"
 
@@ -57,7 +58,14 @@ struct ExpertArgs {
   float* o_out;
   int ldo;
   int round_o;
+  int64_t n_rows;  // rows of the single group when offsets is NULL
 };
+
+// rows [first, first + count) of group e (offsets == NULL: one group holding every row)
+__device__ __forceinline__ int group_first(const ExpertArgs& a, int e) { return a.offsets ? a.offsets[e] : 0; }
+__device__ __forceinline__ int group_count(const ExpertArgs& a, int e) {
+  return a.offsets ? a.offsets[e + 1] - a.offsets[e] : int(a.n_rows);
+}
 
 __device__ __forceinline__ float sigmoidf_(float v) { return 1.f / (1.f + expf(-v)); }
 
@@ -122,7 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
       const int e = base + lane;
       int v = 0;
       if (e < E) {
-        const int cnt = a.offsets[e + 1] - a.offsets[e];
+        const int cnt = group_count(a, e);
         v = cnt > 0 ? a.rt_count * ((cnt + BN - 1) / BN) : 0;
       }
 #pragma unroll
@@ -152,11 +160,11 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
       bool ok = true;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
         const int e = find_expert(pre, E, u);
-        const int cnt = a.offsets[e + 1] - a.offsets[e];
+        const int cnt = group_count(a, e);
         const int nch = (cnt + BN - 1) / BN;
         const int local = u - pre[e];
         const int rt = local / nch, chunk = local % nch;
-        const int64_t row0 = int64_t(a.offsets[e]) + int64_t(chunk) * BN;
+        const int64_t row0 = int64_t(group_first(a, e)) + int64_t(chunk) * BN;
         const int64_t tile0 = (int64_t(e) * a.rt_count + rt) * a.kc_count;
         for (int kc = 0; kc < a.kc_count; ++kc) {
           if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u)) {
@@ -192,8 +200,8 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
   const uint32_t ones_a[4] = {ones, ones, ones, ones};
   for (int u = blockIdx.x; u < total; u += gridDim.x) {
     const int e = find_expert(pre, E, u);
-    const int off = a.offsets[e];
-    const int cnt = a.offsets[e + 1] - off;
+    const int off = group_first(a, e);
+    const int cnt = group_count(a, e);
     const int nch = (cnt + BN - 1) / BN;
     const int local = u - pre[e];
     const int rt = local / nch, chunk = local % nch;
@@ -517,17 +525,26 @@ int dispatch(int wfmt, int nt, const ExpertArgs& a, cudaStream_t s) {
 }
 
 // n-tile count from the average rows per expert: decode draft blocks put one or two rows
-// on most experts, so one n8 tile keeps the tensor-core work per weight byte minimal.
-int pick_nt(int64_t n_rows, int n_experts) {
+// on most experts, so one n8 tile keeps the tensor-core work per weight byte minimal. A
+// wider tile re-reads each weight tile less often, but only while the grid stays full:
+// with few busy experts (the shared expert is one group holding every token) narrower
+// tiles give more work units, and the re-reads of a tile are served from L2.
+int pick_nt(int64_t n_rows, int n_experts, int rt_count) {
   const int64_t busy = std::max<int64_t>(1, std::min<int64_t>(n_rows, n_experts));
   const double avg = double(n_rows) / double(busy);
-  return avg <= 8.0 ? 1 : (avg <= 16.0 ? 2 : 4);
+  int nt = avg <= 8.0 ? 1 : (avg <= 16.0 ? 2 : 4);
+  while (nt > 1) {
+    const int64_t units = busy * int64_t(std::ceil(avg / (8.0 * nt))) * rt_count;
+    if (units >= 2 * int64_t(num_sms())) break;
+    nt >>= 1;
+  }
+  return nt;
 }
 
 int check_common(int wfmt, int group_size, const int32_t* offsets, int n_experts) {
   DSM_REQUIRE(wfmt >= DSM_WFMT_F16 && wfmt <= DSM_WFMT_AFFINE4, "expert: unknown weight format");
   DSM_REQUIRE(n_experts >= 1 && n_experts <= 4096, "expert: n_experts out of range");
-  DSM_REQUIRE(offsets != nullptr, "expert: offsets is NULL");
+  DSM_REQUIRE(offsets != nullptr || n_experts == 1, "expert: offsets may be NULL only for a single group");
   if (wfmt == DSM_WFMT_AFFINE8)
     DSM_REQUIRE(group_size == 32 || group_size == 64 || group_size == 128, "expert: affine8 group_size 32/64/128");
   if (wfmt == DSM_WFMT_AFFINE4) DSM_REQUIRE(group_size == 64 || group_size == 128, "expert: affine4 group_size 64/128");
@@ -557,6 +574,7 @@ extern "C" int dsm_expert_gate_up(const void* x_staged, const float* x_row_scale
   a.act_scale_const = 1.f;
   a.rows_cap = rows_cap;
   a.offsets = offsets;
+  a.n_rows = n_rows;
   a.n_experts = n_experts;
   a.out_rows = inter;
   a.rt_count = int(ceil_div(inter, kTileRows));
@@ -568,7 +586,7 @@ extern "C" int dsm_expert_gate_up(const void* x_staged, const float* x_row_scale
   a.h_scale = h_scale;
   a.h_out = static_cast<__half*>(h_staged);
   a.h_rows_cap = rows_cap;
-  return dispatch<true>(wfmt, pick_nt(n_rows, n_experts), a, as_stream(stream));
+  return dispatch<true>(wfmt, pick_nt(n_rows, n_experts, a.rt_count), a, as_stream(stream));
 }
 
 extern "C" int dsm_expert_down(const void* h_staged, float h_scale, int64_t rows_cap, int inter,
@@ -589,6 +607,7 @@ extern "C" int dsm_expert_down(const void* h_staged, float h_scale, int64_t rows
   a.act_scale_const = 1.f / h_scale;
   a.rows_cap = rows_cap;
   a.offsets = offsets;
+  a.n_rows = n_rows;
   a.n_experts = n_experts;
   a.out_rows = dim;
   a.rt_count = int(ceil_div(dim, kTileRows));
@@ -597,5 +616,5 @@ extern "C" int dsm_expert_down(const void* h_staged, float h_scale, int64_t rows
   a.o_out = o_rows;
   a.ldo = ldo;
   a.round_o = round_o;
-  return dispatch<false>(wfmt, pick_nt(n_rows, n_experts), a, as_stream(stream));
+  return dispatch<false>(wfmt, pick_nt(n_rows, n_experts, a.rt_count), a, as_stream(stream));
 }

@@ -7,11 +7,6 @@
 namespace dsm {
 namespace {
 
-__global__ void set_shared_offsets_kernel(int32_t* off, int32_t n) {
-  off[0] = 0;
-  off[1] = n;
-}
-
 struct Carve {
   uint8_t* base;
   size_t used = 0;
@@ -29,7 +24,7 @@ float h_scale_for(int act, float limit) {
 }
 
 struct Layout {
-  float* scores;
+  void* scores;
   float* weights;
   int32_t* indices;
   int32_t *counts, *offsets, *perm, *inv;
@@ -50,7 +45,7 @@ size_t carve(const dsm_moe_desc* d, void* ws, Layout* L, bool own_routing) {
   const int64_t N = d->n_tokens, P = N * d->topk;
   L->cap_r = dsm_stage_rows_cap(P);
   L->cap_s = dsm_stage_rows_cap(N);
-  L->scores = static_cast<float*>(c.take(size_t(N) * d->n_experts * 4));
+  L->scores = c.take(dsm_router_workspace_bytes(N, d->dim, d->n_experts));
   if (own_routing) {
     L->weights = static_cast<float*>(c.take(size_t(P) * 4));
     L->indices = static_cast<int32_t*>(c.take(size_t(P) * 4));
@@ -103,7 +98,6 @@ extern "C" int dsm_moe_forward(const dsm_moe_desc* d, const void* x, int x_dtype
   carve(d, workspace, &L, true);
   if (route_weights_out) L.weights = route_weights_out;
   if (route_indices_out) L.indices = route_indices_out;
-  cudaStream_t s = as_stream(stream);
   const int64_t N = d->n_tokens, P = N * d->topk;
   int rc = dsm_router(x, x_dtype, N, d->dim, d->gate_weight, d->n_experts, d->tid2eid ? nullptr : d->gate_bias,
                       d->tid2eid, d->vocab, input_ids, ids_dtype, n_ids, d->topk, d->score_func, d->route_scale,
@@ -111,7 +105,9 @@ extern "C" int dsm_moe_forward(const dsm_moe_desc* d, const void* x, int x_dtype
   if (rc) return rc;
   rc = dsm_permute(L.indices, P, d->n_experts, L.counts, L.offsets, L.perm, L.inv, L.perm_ws, L.perm_ws_bytes, stream);
   if (rc) return rc;
-  rc = dsm_stage_rows(x, x_dtype, N, d->dim, L.perm, P, d->topk, L.xs_r, L.cap_r, L.xscale_r, stream);
+  // routed rows (expert order) and, for the shared expert, every token in order: one launch
+  rc = stage_rows_pair(x, x_dtype, N, d->dim, L.perm, P, d->topk, L.xs_r, L.cap_r, L.xscale_r, d->s1 ? N : 0, L.xs_s,
+                       L.cap_s, L.xscale_s, stream);
   if (rc) return rc;
   const float hs = h_scale_for(d->act, d->swiglu_limit);
   rc = dsm_expert_gate_up(L.xs_r, L.xscale_r, L.cap_r, d->dim, L.offsets, d->n_experts, d->wfmt, d->group_size, d->w1,
@@ -121,15 +117,11 @@ extern "C" int dsm_moe_forward(const dsm_moe_desc* d, const void* x, int x_dtype
                        d->round_o, L.o_r, d->dim, P, stream);
   if (rc) return rc;
   if (d->s1) {
-    set_shared_offsets_kernel<<<1, 1, 0, s>>>(L.off_s, int32_t(N));
-    if ((rc = check_launch("shared offsets"))) return rc;
-    rc = dsm_stage_rows(x, x_dtype, N, d->dim, nullptr, N, 1, L.xs_s, L.cap_s, L.xscale_s, stream);
-    if (rc) return rc;
-    rc = dsm_expert_gate_up(L.xs_s, L.xscale_s, L.cap_s, d->dim, L.off_s, 1, d->shared_wfmt, d->shared_group_size,
+    rc = dsm_expert_gate_up(L.xs_s, L.xscale_s, L.cap_s, d->dim, nullptr, 1, d->shared_wfmt, d->shared_group_size,
                             d->s1, d->s3, d->shared_inter, d->act, d->swiglu_limit, d->shared_round_gu, L.hs_s, hs, N,
                             stream);
     if (rc) return rc;
-    rc = dsm_expert_down(L.hs_s, hs, L.cap_s, d->shared_inter, L.off_s, 1, d->shared_wfmt, d->shared_group_size, d->s2,
+    rc = dsm_expert_down(L.hs_s, hs, L.cap_s, d->shared_inter, nullptr, 1, d->shared_wfmt, d->shared_group_size, d->s2,
                          d->dim, d->shared_round_o, L.o_s, d->dim, N, stream);
     if (rc) return rc;
   }

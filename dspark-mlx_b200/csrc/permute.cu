@@ -95,6 +95,91 @@ __global__ void __launch_bounds__(kPermBlock) scatter_kernel(const int32_t* __re
   }
 }
 
+// Decode-sized inputs: the whole permutation in one CTA (histogram, scan, then a stable
+// scatter of 1024-pair chunks with running per-expert cursors).
+constexpr int64_t kSmallPairs = 16384;
+
+__global__ void __launch_bounds__(kPermBlock) permute_small_kernel(const int32_t* __restrict__ idx, int64_t n_pairs,
+                                                                   int n_experts, int32_t* __restrict__ counts,
+                                                                   int32_t* __restrict__ offsets,
+                                                                   int32_t* __restrict__ perm,
+                                                                   int32_t* __restrict__ inv) {
+  extern __shared__ int32_t sm[];
+  int32_t* cursor = sm;                  // [n_experts]
+  int32_t* wsum = sm + n_experts;        // [32]
+  int32_t* wh = wsum + 32;               // [32][n_experts]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int k = tid; k < n_experts; k += kPermBlock) cursor[k] = 0;
+  for (int k = tid; k < 32 * n_experts; k += kPermBlock) wh[k] = 0;
+  __syncthreads();
+  for (int64_t i = tid; i < n_pairs; i += kPermBlock) {
+    const int e = idx[i];
+    if (e >= 0 && e < n_experts)
+      atomicAdd(&cursor[e], 1);
+    else
+      raise_device_error(DSM_DEV_ERR_EXPERT_RANGE);
+  }
+  __syncthreads();
+  // exclusive scan of the counts (n_experts <= 1024: one expert per thread)
+  const int c = tid < n_experts ? cursor[tid] : 0;
+  int v = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  if (lane == 31) wsum[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    int wv = wsum[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, wv, o);
+      if (lane >= o) wv += t;
+    }
+    wsum[lane] = wv;  // inclusive over warps
+  }
+  __syncthreads();
+  const int excl = v - c + (warp > 0 ? wsum[warp - 1] : 0);
+  if (tid < n_experts) {
+    counts[tid] = c;
+    offsets[tid] = excl;
+    cursor[tid] = excl;
+  }
+  if (tid == 0) offsets[n_experts] = wsum[31];
+  __syncthreads();
+  for (int64_t base = 0; base < n_pairs; base += kPermBlock) {
+    const int64_t i = base + tid;
+    int e = -1;
+    if (i < n_pairs) {
+      e = idx[i];
+      if (e < 0 || e >= n_experts) e = -1;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (e >= 0 && rank == 0) wh[warp * n_experts + e] = __popc(peers);
+    __syncthreads();
+    if (e >= 0) {
+      int pos = cursor[e] + rank;
+      for (int w = 0; w < warp; ++w) pos += wh[w * n_experts + e];
+      perm[pos] = int32_t(i);
+      inv[i] = pos;
+    } else if (i < n_pairs) {
+      inv[i] = 0;
+    }
+    __syncthreads();
+    for (int k = tid; k < n_experts; k += kPermBlock) {
+      int add = 0;
+      for (int w = 0; w < 32; ++w) {
+        add += wh[w * n_experts + k];
+        wh[w * n_experts + k] = 0;
+      }
+      cursor[k] += add;
+    }
+    __syncthreads();
+  }
+}
+
 }  // namespace
 }  // namespace dsm
 
@@ -114,6 +199,14 @@ extern "C" int dsm_permute(const int32_t* indices, int64_t n_pairs, int n_expert
   if (workspace_bytes < dsm_permute_workspace_bytes(n_pairs, n_experts))
     return fail(DSM_ERR_WORKSPACE, "dsm_permute: workspace too small");
   cudaStream_t s = as_stream(stream);
+  if (n_pairs > 0 && n_pairs <= kSmallPairs) {
+    const size_t sm = size_t(n_experts + 32 + 32 * n_experts) * sizeof(int32_t);
+    if (sm > 48 * 1024 &&
+        cudaFuncSetAttribute(permute_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm)) != cudaSuccess)
+      return check_launch("permute_small smem attribute");
+    permute_small_kernel<<<1, kPermBlock, sm, s>>>(indices, n_pairs, n_experts, counts, offsets, perm, inv);
+    return check_launch("permute_small");
+  }
   const int blocks = int(ceil_div(n_pairs > 0 ? n_pairs : 1, kPermBlock));
   int32_t* hist = static_cast<int32_t*>(workspace);
   const size_t wh_bytes = size_t(32) * n_experts * sizeof(int32_t);

@@ -16,24 +16,76 @@
 namespace dsm {
 namespace {
 
+constexpr int kStageThreads = 128;
+
+// 8 consecutive elements of a row (k multiple of 8) as floats; zeros past dim
 template <typename XT>
-__global__ void __launch_bounds__(256) stage_rows_kernel(const XT* __restrict__ x, int64_t n_tokens, int dim,
-                                                         const int32_t* __restrict__ perm, int64_t n_rows, int topk,
-                                                         __half* __restrict__ staged, int64_t rows_cap,
-                                                         float* __restrict__ row_scale, int k_chunks) {
-  const int lane = threadIdx.x & 31;
-  const int64_t r = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (r >= n_rows) return;
+__device__ __forceinline__ void load8(const XT* row, int k, int dim, bool vec_ok, float (&v)[8]) {
+  if (vec_ok && k + 8 <= dim) {
+    if constexpr (sizeof(XT) == 2) {
+      const uint4 u = *reinterpret_cast<const uint4*>(row + k);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+      }
+    } else {
+      const float4 a = *reinterpret_cast<const float4*>(row + k);
+      const float4 b = *reinterpret_cast<const float4*>(row + k + 4);
+      v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = (k + i < dim) ? load_as_float(row, k + i) : 0.f;
+  }
+}
+
+struct StageJob {
+  const int32_t* perm;  // NULL: row r is token r
+  int topk;
+  __half* staged;
+  int64_t rows_cap;
+  float* row_scale;
+};
+
+// One CTA per staged row: 16-byte loads, block max, one 16-byte store per 8 columns.
+// Blocks [0, n_rows) serve job a; blocks [n_rows, n_rows + n_rows_b) serve job b.
+template <typename XT>
+__global__ void __launch_bounds__(kStageThreads) stage_rows_kernel(const XT* __restrict__ x, int64_t n_tokens, int dim,
+                                                                   int64_t n_rows, StageJob ja, StageJob jb,
+                                                                   int k_chunks) {
+  __shared__ float red[kStageThreads / 32];
+  const bool second = int64_t(blockIdx.x) >= n_rows;
+  const StageJob& j = second ? jb : ja;
+  const int32_t* __restrict__ perm = j.perm;
+  const int topk = j.topk;
+  __half* __restrict__ staged = j.staged;
+  const int64_t rows_cap = j.rows_cap;
+  float* __restrict__ row_scale = j.row_scale;
+  const int64_t r = second ? int64_t(blockIdx.x) - n_rows : int64_t(blockIdx.x);
   int64_t t = perm ? int64_t(perm[r]) / topk : r;
   if (t < 0 || t >= n_tokens) {
-    if (lane == 0) raise_device_error(DSM_DEV_ERR_TOKEN_RANGE);
+    if (threadIdx.x == 0) raise_device_error(DSM_DEV_ERR_TOKEN_RANGE);
     t = 0;
   }
   const XT* row = x + t * dim;
+  const bool vec_ok = (dim % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  const int kpad = k_chunks * kChunkK;
   float amax = 0.f;
-  for (int k = lane; k < dim; k += 32) amax = fmaxf(amax, fabsf(load_as_float(row, k)));
+  for (int k = threadIdx.x * 8; k < dim; k += kStageThreads * 8) {
+    float v[8];
+    load8(row, k, dim, vec_ok, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  }
 #pragma unroll
   for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int i = 1; i < kStageThreads / 32; ++i) amax = fmaxf(amax, red[i]);
   int s = 0;
   if (amax > 0.f && isfinite(amax)) {
     int ex;
@@ -42,15 +94,18 @@ __global__ void __launch_bounds__(256) stage_rows_kernel(const XT* __restrict__ 
     s = s < -100 ? -100 : (s > 100 ? 100 : s);
   }
   const float up = ldexpf(1.f, s);
-  if (lane == 0) row_scale[r] = ldexpf(1.f, -s);
-  const int kpad = k_chunks * kChunkK;
-  for (int k = lane * 2; k < kpad; k += 64) {
-    float v0 = 0.f, v1 = 0.f;
-    if (k < dim) v0 = load_as_float(row, k) * up;
-    if (k + 1 < dim) v1 = load_as_float(row, k + 1) * up;
+  if (threadIdx.x == 0) row_scale[r] = ldexpf(1.f, -s);
+  for (int k = threadIdx.x * 8; k < kpad; k += kStageThreads * 8) {
+    float v[8];
+    load8(row, k, dim, vec_ok, v);
+    uint32_t h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 p = __floats2half2_rn(v[2 * i] * up, v[2 * i + 1] * up);
+      h[i] = *reinterpret_cast<const uint32_t*>(&p);
+    }
     const int c = k / kChunkK, col = k % kChunkK;
-    __half2* dst = reinterpret_cast<__half2*>(staged + (int64_t(c) * rows_cap + r) * kStagePitch + col);
-    *dst = __floats2half2_rn(v0, v1);
+    *reinterpret_cast<uint4*>(staged + (int64_t(c) * rows_cap + r) * kStagePitch + col) = make_uint4(h[0], h[1], h[2], h[3]);
   }
 }
 
@@ -74,15 +129,27 @@ extern "C" int dsm_stage_rows(const void* x, int x_dtype, int64_t n_tokens, int 
   if (n_rows == 0) return DSM_OK;
   DSM_REQUIRE(x && staged && row_scale, "dsm_stage_rows: NULL pointer");
   DSM_REQUIRE((reinterpret_cast<uintptr_t>(staged) & 15) == 0, "dsm_stage_rows: staged must be 16-byte aligned");
+  DSM_REQUIRE(n_rows < (int64_t(1) << 31), "dsm_stage_rows: too many rows");
+  return stage_rows_pair(x, x_dtype, n_tokens, dim, perm, n_rows, topk, staged, rows_cap, row_scale, 0, nullptr, 0,
+                         nullptr, stream);
+}
+
+namespace dsm {
+int stage_rows_pair(const void* x, int x_dtype, int64_t n_tokens, int dim, const int32_t* perm, int64_t n_rows,
+                    int topk, void* staged, int64_t rows_cap, float* row_scale, int64_t n_rows_b, void* staged_b,
+                    int64_t rows_cap_b, float* row_scale_b, void* stream) {
   const int kc = int(ceil_div(dim, kChunkK));
-  const unsigned blocks = unsigned(ceil_div(n_rows, 8));
+  const StageJob ja{perm, topk, static_cast<__half*>(staged), rows_cap, row_scale};
+  const StageJob jb{nullptr, 1, static_cast<__half*>(staged_b), rows_cap_b, row_scale_b};
+  const unsigned blocks = unsigned(n_rows + n_rows_b);
+  if (blocks == 0) return DSM_OK;
   cudaStream_t s = as_stream(stream);
   if (x_dtype == DSM_DT_BF16)
-    stage_rows_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), n_tokens, dim, perm,
-                                                            n_rows, topk, static_cast<__half*>(staged), rows_cap,
-                                                            row_scale, kc);
+    stage_rows_kernel<__nv_bfloat16><<<blocks, kStageThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(x), n_tokens,
+                                                                      dim, n_rows, ja, jb, kc);
   else
-    stage_rows_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), n_tokens, dim, perm, n_rows, topk,
-                                                    static_cast<__half*>(staged), rows_cap, row_scale, kc);
+    stage_rows_kernel<float><<<blocks, kStageThreads, 0, s>>>(static_cast<const float*>(x), n_tokens, dim, n_rows, ja,
+                                                              jb, kc);
   return check_launch("stage_rows");
 }
+}  // namespace dsm

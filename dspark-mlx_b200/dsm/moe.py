@@ -79,7 +79,7 @@ class Gate(nn.Module):
         ids, ids_p, ids_dt, n_ids = _ids_arg(input_ids)
         if self.hash and ids is None:
             raise ValueError("hash routing needs input_ids")
-        scores = torch.empty(n, w.shape[0], dtype=torch.float32, device=x.device)
+        scores = torch.empty(lib().dsm_router_workspace_bytes(n, dim, w.shape[0]), dtype=torch.uint8, device=x.device)
         weights = torch.empty(n, self.topk, dtype=torch.float32, device=x.device)
         indices = torch.empty(n, self.topk, dtype=torch.int32, device=x.device)
         check(lib().dsm_router(ptr(x), dtype_code(x.dtype), n, dim, ptr(w), w.shape[0], ptr(b), ptr(t2e),

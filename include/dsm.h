@@ -85,12 +85,14 @@ int dsm_device_error(int* code, int clear, void* stream);
  * x [n_tokens, dim] (x_dtype F32 or BF16); gate_weight [n_experts, dim] fp32.
  * Score mode: gate_bias [n_experts] fp32, tid2eid = NULL. Hash mode: gate_bias = NULL,
  * tid2eid [vocab, topk] int32 and input_ids (I32 or I64) of length n_ids == n_tokens or 1.
- * scores_ws: [n_tokens, n_experts] fp32 scratch. Outputs weights [n_tokens, topk] fp32 and
- * indices [n_tokens, topk] int32 (ascending by biased score: best expert in the last slot). */
+ * workspace: dsm_router_workspace_bytes() of scratch (fp64 logit partial sums). Outputs
+ * weights [n_tokens, topk] fp32 and indices [n_tokens, topk] int32 (ascending by biased
+ * score: best expert in the last slot). Logits are accumulated in fp64 and rounded once. */
+size_t dsm_router_workspace_bytes(int64_t n_tokens, int dim, int n_experts);
 int dsm_router(const void* x, int x_dtype, int64_t n_tokens, int dim, const float* gate_weight,
                int n_experts, const float* gate_bias, const int32_t* tid2eid, int64_t vocab,
                const void* input_ids, int ids_dtype, int64_t n_ids, int topk, int score_func,
-               float route_scale, float* scores_ws, float* weights_out, int32_t* indices_out,
+               float route_scale, void* workspace, float* weights_out, int32_t* indices_out,
                void* stream);
 
 /* ---- permutation (defines per-expert token lists) ------------------------------------
@@ -136,7 +138,8 @@ int dsm_affine_quantize(const void* w, int w_dtype, int64_t n_rows, int cols, in
                         int bits, uint8_t* codes, void* scales, void* biases, void* stream);
 
 /* ---- grouped expert products ----------------------------------------------------------
- * Rows of expert e are the staged rows [offsets[e], offsets[e+1]).
+ * Rows of expert e are the staged rows [offsets[e], offsets[e+1]); offsets may be NULL when
+ * n_experts == 1 (one group holding rows [0, n_rows), e.g. the shared expert).
  * gate_up: h = act(x W1^T, x W3^T) for every row, written to the staged layout of h
  *   (k_dim = inter) scaled by h_scale (power of two). round_gu bit 0: round the two
  *   products to bf16 before the activation (the reference's products are bf16 for bf16 or
