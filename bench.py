@@ -310,9 +310,9 @@ def run_gpu(args):
     avg_step_bytes = sum(per_step_bytes[i % n_batches] for i in range(args.steps)) / args.steps
     hbm_peak, _, peak_kind = _peaks()
     if args.no_kernel_timing:
-        k_ms, k_bytes, achieved = None, None, None
+        k_ms, k_bytes, k_touched, achieved = None, None, None, None
     else:
-        k_ms, k_bytes = time_gate_up(moe, xs[0], ids, args, L, dev)
+        k_ms, k_bytes, k_touched = time_gate_up(moe, xs[0], ids, args, L, dev)
         achieved = k_bytes / (k_ms * 1e-3) / 1e9
 
     # ---- end to end through the public API: pinned host tokens in, host result out
@@ -334,10 +334,14 @@ def run_gpu(args):
         torch.cuda.synchronize()
         e2e_ms = _max_over_ranks(e2.elapsed_time(e3) / args.steps, ws, dev)
 
+    # DRAM traffic of the dominant kernel from the committed ncu capture (a smaller expert
+    # pool), scaled to this launch by the experts it streams
     traffic = None
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            traffic = json.load(f).get(f"gate_up/{wl.name}")
+            per = json.load(f).get(f"gate_up/{wl.name}")
+        if per and k_touched:
+            traffic = per["bytes_per_touched_expert"] * k_touched
     except Exception:
         traffic = None
 
@@ -372,7 +376,8 @@ def run_gpu(args):
                 "bound": "hbm", "kernel": "expert_kernel<fp8, gate_up>", "achieved": achieved, "peak": hbm_peak,
                 "unit": "GB/s", "frac": achieved / hbm_peak, "peak_kind": peak_kind,
                 "frac_of_8tbs": achieved / SPEC_HBM_GBS, "algorithmic_bytes_per_launch": k_bytes,
-                "launch_ms": k_ms, "traffic": traffic},
+                "launch_ms": k_ms, "touched_experts": k_touched, "traffic": traffic,
+                "traffic_over_algorithmic": (traffic / k_bytes) if traffic else None},
             "cpu_baseline": cpu,
             "e2e": None if e2e_ms is None else {
                 "value": ws * N / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": N * dim * 2,
@@ -439,7 +444,7 @@ def time_gate_up(moe, x, ids, args, L, dev):
     per_expert = (p1.packed.numel() - header) // E  # packed tile bytes (codes + scales) of one expert
     w13 = 2 * touched * per_expert
     act = (P * desc.dim * 2) + (P * desc.inter * 2)
-    return k_ms, w13 + act
+    return k_ms, w13 + act, touched
 
 
 def main():
