@@ -26,7 +26,7 @@ DEVICE_ERRORS = {0x10: "expert id out of range", 0x11: "token id out of range",
 
 EXPORTED = (
     "dsm_abi_version", "dsm_status_string", "dsm_last_error_message", "dsm_device_error",
-    "dsm_router_workspace_bytes", "dsm_router", "dsm_permute_workspace_bytes", "dsm_permute", "dsm_stage_bytes",
+    "dsm_router_workspace_bytes", "dsm_router", "dsm_router_noalloc", "dsm_permute_workspace_bytes", "dsm_permute", "dsm_stage_bytes",
     "dsm_stage_rows_cap", "dsm_stage_rows", "dsm_packed_bytes", "dsm_pack_weights",
     "dsm_affine_quantize", "dsm_expert_gate_up", "dsm_expert_down", "dsm_combine",
     "dsm_moe_workspace_bytes", "dsm_moe_forward",
@@ -69,6 +69,7 @@ def _declare(lib):
         "dsm_device_error": (I, [POINTER(c_int), I, V]),
         "dsm_router_workspace_bytes": (S, [I64, I, I]),
         "dsm_router": (I, [V, I, I64, I, V, I, V, V, I64, V, I, I64, I, I, F, V, V, V, V]),
+        "dsm_router_noalloc": (I, [V, I, I64, I, V, I, V, V, I64, V, I, I64, I, I, F, V, V, V]),
         "dsm_permute_workspace_bytes": (S, [I64, I]),
         "dsm_permute": (I, [V, I64, I, V, V, V, V, V, S, V]),
         "dsm_stage_bytes": (S, [I64, I]),

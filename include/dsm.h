@@ -95,6 +95,21 @@ int dsm_router(const void* x, int x_dtype, int64_t n_tokens, int dim, const floa
                float route_scale, void* workspace, float* weights_out, int32_t* indices_out,
                void* stream);
 
+/* ---- router without a workspace ---------------------------------------------------------
+ * No counterpart in the reference. For callers that cannot allocate device memory -- an
+ * engine whose memory arena owns the whole GPU and cannot grant per-call buffers, or a
+ * latency-critical loop that must not touch an allocator. Same arguments and results as
+ * dsm_router minus the workspace: the scratch is a fixed array of
+ * DSM_ROUTER_NOALLOC_MAX_SCRATCH_BYTES inside the library, held on every GPU that loads it
+ * until exit. Calls needing more (dsm_router_workspace_bytes) fail with DSM_ERR_WORKSPACE.
+ * The first call on a device resolves the array's address there: make it before any stream
+ * capture. All calls share the array: calls that can overlap on the GPU race on it. */
+#define DSM_ROUTER_NOALLOC_MAX_SCRATCH_BYTES (8u << 20)
+int dsm_router_noalloc(const void* x, int x_dtype, int64_t n_tokens, int dim, const float* gate_weight,
+                       int n_experts, const float* gate_bias, const int32_t* tid2eid, int64_t vocab,
+                       const void* input_ids, int ids_dtype, int64_t n_ids, int topk, int score_func,
+                       float route_scale, float* weights_out, int32_t* indices_out, void* stream);
+
 /* ---- permutation (defines per-expert token lists) ------------------------------------
  * indices [n_pairs] int32 (the flattened [n_tokens, topk] routing). Outputs counts [E],
  * offsets [E+1], perm [n_pairs] (sorted position -> pair id, stable), inv [n_pairs]. */
