@@ -32,6 +32,8 @@ sys.path.insert(0, ROOT)
 METRIC = "MoE-layer tokens/s & draft-block latency; HBM GB/s vs 8 TB/s at 1/2/4/8 B200"
 SPEC_HBM_GBS = 8000.0
 KERNELS_PER_STEP = 10  # router 3, permute 1, staging 1, routed gate/up + down 2, shared gate/up + down 2, combine 1
+# expert-parallel step: router 3, permute 2, gather 1, shared 3, segment ids 1, staging 1, gate/up + down 2, combine 1
+KERNELS_PER_STEP_EP = 14
 
 
 def _peaks():
@@ -254,66 +256,97 @@ def run_gpu(args):
         import dataclasses
 
         wl = dataclasses.replace(wl, args=dict(wl.args, n_routed_experts=args.experts))
-    t = W.make_moe_tensors(wl, device=dev, seed=wl.seed + 1000 * rank)
+    # every rank holds the same weights; each rank routes its own tokens
+    t = W.make_moe_tensors(wl, device=dev, seed=wl.seed)
     moe = W.build_moe(wl, t, dev)
-    N, dim = wl.n_tokens, wl.args["dim"]
+    N, dim, E = wl.n_tokens, wl.args["dim"], wl.args["n_routed_experts"]
     # several distinct token batches (different routing per step)
     n_batches = 4
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
-    xs = [t["x"]] + [torch.randn(N, dim, generator=gen, device=dev).to(torch.bfloat16) for _ in range(n_batches - 1)]
+    xs = [t["x"] if ws == 1 else torch.randn(N, dim, generator=gen, device=dev).to(torch.bfloat16)]
+    xs += [torch.randn(N, dim, generator=gen, device=dev).to(torch.bfloat16) for _ in range(n_batches - 1)]
     ids = t.get("input_ids")
     L = _lib.lib()
-    desc, keep = moe.describe(N, torch.bfloat16)
-    wsb = L.dsm_moe_workspace_bytes(ctypes.byref(desc))
-    wsp = torch.empty(wsb, dtype=torch.uint8, device=dev)
-    y = torch.empty(N, dim, dtype=torch.bfloat16, device=dev)
-    rw = torch.empty(N, wl.args["n_activated_experts"], dtype=torch.float32, device=dev)
-    ri = torch.empty(N, wl.args["n_activated_experts"], dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
-    sp = stream.cuda_stream
-    ids_p = ids.data_ptr() if ids is not None else None
+    topk = wl.args["n_activated_experts"]
+    if ws == 1:
+        model = moe
+        desc, keep = moe.describe(N, torch.bfloat16)
+        wsb = L.dsm_moe_workspace_bytes(ctypes.byref(desc))
+        wsp = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        y = torch.empty(N, dim, dtype=torch.bfloat16, device=dev)
+        rw = torch.empty(N, topk, dtype=torch.float32, device=dev)
+        ri = torch.empty(N, topk, dtype=torch.int32, device=dev)
+        sp = stream.cuda_stream
+        ids_p = ids.data_ptr() if ids is not None else None
 
-    def step(i):
-        x = xs[i % n_batches]
-        _lib.check(L.dsm_moe_forward(ctypes.byref(desc), x.data_ptr(), _lib.DT_BF16, ids_p, _lib.DT_I32,
-                                     N if ids is not None else 0, y.data_ptr(), rw.data_ptr(), ri.data_ptr(),
-                                     wsp.data_ptr(), wsb, sp))
+        def step(i):
+            x = xs[i % n_batches]
+            _lib.check(L.dsm_moe_forward(ctypes.byref(desc), x.data_ptr(), _lib.DT_BF16, ids_p, _lib.DT_I32,
+                                         N if ids is not None else 0, y.data_ptr(), rw.data_ptr(), ri.data_ptr(),
+                                         wsp.data_ptr(), wsb, sp))
+
+        def routing(i):
+            step(i)
+            return ri
+    else:
+        from dsm.config import DSparkArgs
+        from dsm.ep import ExpertParallelMoE
+
+        model = ExpertParallelMoE.from_moe(moe, DSparkArgs.from_dict(t["args"]), wl.layer_id)
+        del moe
+        t = {k: v for k, v in t.items() if not (k[:2] in ("w1", "w2", "w3"))}
+        torch.cuda.empty_cache()
+
+        def step(i):
+            model(xs[i % n_batches], ids)
+
+        def routing(i):
+            return model(xs[i % n_batches], ids, return_routing=True)[2]
 
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
-    # routing statistics of the measured batches (for the algorithmic byte count)
+    # routing statistics of the measured batches (for the algorithmic byte count): the routed
+    # expert bytes this rank streams are those of its experts that any rank's tokens touch
     touched_bytes = []
     for i in range(n_batches):
-        step(i)
-        c = torch.bincount(ri.flatten().long(), minlength=wl.args["n_routed_experts"]).cpu()
-        touched_bytes.append(W.routed_weight_bytes(wl, c))
+        idx = routing(i).flatten().long()
+        c = torch.bincount(idx, minlength=E)
+        if ws > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(c)
+            e0, el = model.e0, model.e_local
+            c = c[e0:e0 + el]
+        touched_bytes.append(W.routed_weight_bytes(wl, c.cpu()))
     torch.cuda.synchronize()
     _barrier(ws)
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0_, e1_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
-        e0.record(stream)
+        e0_.record(stream)
         for i in range(args.steps):
             step(i)
-        e1.record(stream)
+        e1_.record(stream)
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
+    ms = e0_.elapsed_time(e1_) / args.steps
     ms = _max_over_ranks(ms, ws, dev)
     _barrier(ws)
 
-    # ---- dominant kernel: the fused gate/up expert kernel, timed alone with events
+    # ---- dominant kernel: the fused gate/up expert kernel, timed alone with events (1 GPU)
     sh_bytes = 3 * wl.args["moe_inter_dim"] * dim * 2
-    gate_bytes = wl.args["n_routed_experts"] * dim * 4
+    gate_bytes = E * dim * 4
     per_step_bytes = [b + sh_bytes + gate_bytes + 2 * N * dim * 2 for b in touched_bytes]
     avg_step_bytes = sum(per_step_bytes[i % n_batches] for i in range(args.steps)) / args.steps
     hbm_peak, _, peak_kind = _peaks()
-    if args.no_kernel_timing:
+    if args.no_kernel_timing or ws > 1:
         k_ms, k_bytes, k_touched, achieved = None, None, None, None
     else:
-        k_ms, k_bytes, k_touched = time_gate_up(moe, xs[0], ids, args, L, dev)
+        k_ms, k_bytes, k_touched = time_gate_up(model, xs[0], ids, args, L, dev)
         achieved = k_bytes / (k_ms * 1e-3) / 1e9
+    moe = model
 
     # ---- end to end through the public API: pinned host tokens in, host result out
     e2e_ms = None
@@ -367,12 +400,16 @@ def run_gpu(args):
             "config": {"workload": wl.name, "tokens_per_step_per_gpu": N, "batch": wl.batch, "draft_block": wl.block,
                        "dim": dim, "n_experts": wl.args["n_routed_experts"], "topk": wl.args["n_activated_experts"],
                        "inter": wl.args["moe_inter_dim"], "weights": wl.wfmt,
-                       "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                       "parallelism": f"ep{ws} (experts sharded, NCCL all-to-all)" if ws > 1 else "single",
                        "l2": "inputs larger than L2 (touched expert weights ~GB per step, 4 rotating token batches)"},
             "draft_block_latency_ms": ms,
             "hbm_gbs_step": avg_step_bytes / (ms * 1e-3) / 1e9,
             "hbm_frac_of_8tbs_step": avg_step_bytes / (ms * 1e-3) / 1e9 / SPEC_HBM_GBS,
-            "roofline": None if achieved is None else {
+            "roofline": {
+                "bound": "hbm", "kernel": "whole step per rank (expert-parallel)",
+                "achieved": avg_step_bytes / (ms * 1e-3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                "frac": avg_step_bytes / (ms * 1e-3) / 1e9 / hbm_peak, "peak_kind": peak_kind,
+                "traffic": None} if achieved is None and ws > 1 else None if achieved is None else {
                 "bound": "hbm", "kernel": "expert_kernel<fp8, gate_up>", "achieved": achieved, "peak": hbm_peak,
                 "unit": "GB/s", "frac": achieved / hbm_peak, "peak_kind": peak_kind,
                 "frac_of_8tbs": achieved / SPEC_HBM_GBS, "algorithmic_bytes_per_launch": k_bytes,
@@ -382,7 +419,7 @@ def run_gpu(args):
             "e2e": None if e2e_ms is None else {
                 "value": ws * N / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": N * dim * 2,
                 "d2h_bytes_per_step": N * dim * 2, "ms_per_step": e2e_ms},
-            "gpu_launches": KERNELS_PER_STEP * args.steps,
+            "gpu_launches": (KERNELS_PER_STEP if ws == 1 else KERNELS_PER_STEP_EP) * args.steps,
             "clocks": clk.summary(),
         }
         print(json.dumps(line))

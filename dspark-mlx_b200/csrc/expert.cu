@@ -56,6 +56,7 @@ struct ExpertArgs {
   __half* h_out;
   int64_t h_rows_cap;
   float* o_out;
+  const int32_t* o_row_map;  // down: staged row r is written to output row o_row_map[r] (NULL: r)
   int ldo;
   int round_o;
   int64_t n_rows;  // rows of the single group when offsets is NULL
@@ -485,7 +486,8 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
             if (d >= a.out_rows) continue;
             float v = acc[0][i][j][c] * xs * wmul_a;
             if (a.round_o) v = bf16_round(v);
-            a.o_out[r * a.ldo + d] = v;
+            const int64_t orow = a.o_row_map ? int64_t(a.o_row_map[r]) : r;
+            a.o_out[orow * a.ldo + d] = v;
           }
         }
   }
@@ -591,7 +593,8 @@ extern "C" int dsm_expert_gate_up(const void* x_staged, const float* x_row_scale
 
 extern "C" int dsm_expert_down(const void* h_staged, float h_scale, int64_t rows_cap, int inter,
                                const int32_t* offsets, int n_experts, int wfmt, int group_size, const void* w2_packed,
-                               int dim, int round_o, float* o_rows, int ldo, int64_t n_rows, void* stream) {
+                               int dim, int round_o, float* o_rows, int ldo, const int32_t* o_row_map,
+                               int64_t n_rows, void* stream) {
   using namespace dsm;
   if (int rc = check_common(wfmt, group_size, offsets, n_experts)) return rc;
   DSM_REQUIRE(dim > 0 && inter > 0 && n_rows >= 0 && ldo >= dim, "dsm_expert_down: bad shape");
@@ -614,6 +617,7 @@ extern "C" int dsm_expert_down(const void* h_staged, float h_scale, int64_t rows
   a.kc_count = int(ceil_div(inter, kChunkK));
   a.group_size = group_size > 0 ? group_size : 64;
   a.o_out = o_rows;
+  a.o_row_map = o_row_map;
   a.ldo = ldo;
   a.round_o = round_o;
   return dispatch<false>(wfmt, pick_nt(n_rows, n_experts, a.rt_count), a, as_stream(stream));

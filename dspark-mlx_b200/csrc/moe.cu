@@ -114,7 +114,7 @@ extern "C" int dsm_moe_forward(const dsm_moe_desc* d, const void* x, int x_dtype
                           d->w3, d->inter, d->act, d->swiglu_limit, d->round_gu, L.hs_r, hs, P, stream);
   if (rc) return rc;
   rc = dsm_expert_down(L.hs_r, hs, L.cap_r, d->inter, L.offsets, d->n_experts, d->wfmt, d->group_size, d->w2, d->dim,
-                       d->round_o, L.o_r, d->dim, P, stream);
+                       d->round_o, L.o_r, d->dim, nullptr, P, stream);
   if (rc) return rc;
   if (d->s1) {
     rc = dsm_expert_gate_up(L.xs_s, L.xscale_s, L.cap_s, d->dim, nullptr, 1, d->shared_wfmt, d->shared_group_size,
@@ -122,7 +122,7 @@ extern "C" int dsm_moe_forward(const dsm_moe_desc* d, const void* x, int x_dtype
                             stream);
     if (rc) return rc;
     rc = dsm_expert_down(L.hs_s, hs, L.cap_s, d->shared_inter, nullptr, 1, d->shared_wfmt, d->shared_group_size, d->s2,
-                         d->dim, d->shared_round_o, L.o_s, d->dim, N, stream);
+                         d->dim, d->shared_round_o, L.o_s, d->dim, nullptr, N, stream);
     if (rc) return rc;
   }
   const int y_dtype = x_dtype;

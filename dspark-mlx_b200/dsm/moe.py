@@ -141,7 +141,7 @@ class Expert(nn.Module):
                                    ptr(p1.packed), ptr(p3.packed), p1.rows, _lib.ACT_SWIGLU_CLAMP,
                                    float(self.swiglu_limit), rgu, ptr(hs), hsc, n, s), "dsm_expert_gate_up")
         check(L.dsm_expert_down(ptr(hs), hsc, cap, p2.cols, ptr(offsets), 1, p2.wfmt, p2.group_size, ptr(p2.packed),
-                                p2.rows, rgo, ptr(o), p2.rows, n, s), "dsm_expert_down")
+                                p2.rows, rgo, ptr(o), p2.rows, None, n, s), "dsm_expert_down")
         out_dt = torch.promote_types(dt, self.w2.weight.dtype)
         return o.to(out_dt).reshape(*shape[:-1], p2.rows)
 
@@ -158,14 +158,28 @@ class MoE(nn.Module):
         self.swiglu_limit = args.swiglu_limit
         self.gate = Gate(args, layer_id)
         E, dim, inter = args.n_routed_experts, args.dim, args.moe_inter_dim
-        self.register_buffer("w1", torch.zeros(E, inter, dim, dtype=torch.float32))
-        self.register_buffer("w3", torch.zeros(E, inter, dim, dtype=torch.float32))
-        self.register_buffer("w2", torch.zeros(E, dim, inter, dtype=torch.float32))
+        # Shape-only placeholders until weights are assigned (the reference's mx.zeros is
+        # lazy; eager fp32 zeros would cost 25 GB at DeepSeek-V4 sizes).
+        self.register_buffer("w1", torch.empty(E, inter, dim, dtype=torch.float32, device="meta"))
+        self.register_buffer("w3", torch.empty(E, inter, dim, dtype=torch.float32, device="meta"))
+        self.register_buffer("w2", torch.empty(E, dim, inter, dtype=torch.float32, device="meta"))
         self.shared_experts = Expert(dim, inter, args.swiglu_limit)
         self.quant: Optional[Tuple[int, int]] = None
         self.expert_format = "dense"
         self._packed = None
         self._ws: Optional[torch.Tensor] = None
+
+    def _apply(self, fn, recurse=True):
+        # unassigned (meta) expert stacks stay placeholders through .to() / .cuda()
+        meta = {k: v for k, v in self._buffers.items() if v is not None and v.is_meta}
+        for k in meta:
+            self._buffers[k] = None
+        try:
+            return super()._apply(fn, recurse)
+        finally:
+            for k, v in meta.items():
+                if self._buffers.get(k) is None:
+                    self._buffers[k] = v
 
     # ------------------------------------------------------------------ weight formats
     def _sources(self):
@@ -231,6 +245,8 @@ class MoE(nn.Module):
 
     def packed_experts(self) -> Tuple[PackedMatrix, PackedMatrix, PackedMatrix]:
         srcs = self._sources()
+        if any(t.is_meta for t in srcs):
+            raise ValueError("routed expert weights are not assigned (w1/w3/w2 are placeholders)")
         key = (self.expert_format,) + tuple((t.data_ptr(), t._version, t.dtype, t.device) for t in srcs)
         if self._packed is None or self._packed[0] != key:
             f = self.expert_format
@@ -251,7 +267,8 @@ class MoE(nn.Module):
         return self._packed[1]
 
     # ------------------------------------------------------------------ forward
-    def _round_flags(self, x_dtype: torch.dtype):
+    def routed_round_flags(self, x_dtype: torch.dtype) -> Tuple[int, int]:
+        """(gate/up flags, down flag) following the reference's dtypes for the routed experts."""
         bf16x = x_dtype == torch.bfloat16
         f = self.expert_format
         if f == "dense":
@@ -261,11 +278,16 @@ class MoE(nn.Module):
             prod_bf16 = o_bf16 = bf16x  # gather_qmm returns the activation dtype
         else:
             prod_bf16 = o_bf16 = False  # fp8/fp4 weights are dequantised to fp32 by the reference
+        return int(prod_bf16) | (2 if bf16x else 0), int(o_bf16)
+
+    def _round_flags(self, x_dtype: torch.dtype):
+        bf16x = x_dtype == torch.bfloat16
+        rgu, ro = self.routed_round_flags(x_dtype)
         sh = self.shared_experts
         s_gu = bf16x and sh.w1.weight.dtype == torch.bfloat16
         s_o = bf16x and sh.w2.weight.dtype == torch.bfloat16
         hbit = 2 if bf16x else 0
-        return int(prod_bf16) | hbit, int(o_bf16), int(s_gu) | hbit, int(s_o)
+        return rgu, ro, int(s_gu) | hbit, int(s_o)
 
     def describe(self, n_tokens: int, x_dtype: torch.dtype) -> Tuple[MoEDesc, tuple]:
         """The C descriptor for a call on ``n_tokens`` tokens (and the tensors it points into)."""

@@ -26,6 +26,9 @@
  *   dsm_moe_forward     MoE.__call__                          model/moe.py:151-161
  *   dsm_affine_quantize mx.quantize in MoE.quantize           model/moe.py:124-130
  *   dsm_pack_weights    stacked [E,out,in] expert weights      loading.py:88-100 (+103-114)
+ *   dsm_gather_rows, dsm_segment_ids: expert-parallel plumbing; the reference runs on one
+ *                       device (tests/reference_model.py:55-56 forces world_size 1) and has
+ *                       no counterpart.
  */
 #ifndef DSM_H_
 #define DSM_H_
@@ -160,7 +163,8 @@ int dsm_affine_quantize(const void* w, int w_dtype, int64_t n_rows, int cols, in
  *   products to bf16 before the activation (the reference's products are bf16 for bf16 or
  *   affine weights with bf16 x); bit 1: round h to bf16 (the reference casts h to x's dtype).
  * down: o = h W2^T (h read with scale 1/h_scale), fp32 rows [n_rows, ldo];
- *   round_o: round o to bf16 first. */
+ *   round_o: round o to bf16 first; o_row_map (NULL = identity) sends staged row r to
+ *   output row o_row_map[r] (e.g. back to the order the rows arrived in). */
 int dsm_expert_gate_up(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int dim,
                        const int32_t* offsets, int n_experts, int wfmt, int group_size,
                        const void* w1_packed, const void* w3_packed, int inter, int act,
@@ -169,7 +173,18 @@ int dsm_expert_gate_up(const void* x_staged, const float* x_row_scale, int64_t r
 int dsm_expert_down(const void* h_staged, float h_scale, int64_t rows_cap, int inter,
                     const int32_t* offsets, int n_experts, int wfmt, int group_size,
                     const void* w2_packed, int dim, int round_o, float* o_rows, int ldo,
-                    int64_t n_rows, void* stream);
+                    const int32_t* o_row_map, int64_t n_rows, void* stream);
+
+/* ---- expert-parallel helpers -----------------------------------------------------------
+ * gather_rows: out[r] = x[perm[r] / topk] (perm NULL: x[r]), same dtype (F32/BF16), the
+ *   rows a rank sends to the owners of its routed experts (expert order = owner order).
+ * segment_ids: rows arriving from W sources, each source's rows grouped by the receiver's
+ *   E_local experts with counts[s * E_local + e] rows; ids[row] = e (the local expert).
+ *   n_segments = W * E_local <= 4096; n_rows = sum(counts). */
+int dsm_gather_rows(const void* x, int x_dtype, int64_t n_tokens, int dim, const int32_t* perm,
+                    int64_t n_rows, int topk, void* out, void* stream);
+int dsm_segment_ids(const int32_t* counts, int n_segments, int e_local, int32_t* ids, int64_t n_rows,
+                    void* stream);
 
 /* ---- combine: y = sum_s o[inv[t*k+s]] * w[t,s] (+ shared[t]) -> y_dtype --------------- */
 int dsm_combine(const float* o_sorted, const int32_t* inv, const float* route_weights,
