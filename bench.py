@@ -340,11 +340,12 @@ def run_gpu(args):
     gate_bytes = E * dim * 4
     per_step_bytes = [b + sh_bytes + gate_bytes + 2 * N * dim * 2 for b in touched_bytes]
     avg_step_bytes = sum(per_step_bytes[i % n_batches] for i in range(args.steps)) / args.steps
-    hbm_peak, _, peak_kind = _peaks()
+    hbm_peak, tc_peak, peak_kind = _peaks()
+    k_tc = False
     if args.no_kernel_timing or ws > 1:
-        k_ms, k_bytes, k_touched, achieved = None, None, None, None
+        k_ms, k_bytes, k_touched, k_flops, achieved = None, None, None, None, None
     else:
-        k_ms, k_bytes, k_touched = time_gate_up(model, xs[0], ids, args, L, dev)
+        k_ms, k_bytes, k_touched, k_flops, k_tc = time_gate_up(model, xs[0], ids, args, L, dev)
         achieved = k_bytes / (k_ms * 1e-3) / 1e9
     moe = model
 
@@ -405,16 +406,8 @@ def run_gpu(args):
             "draft_block_latency_ms": ms,
             "hbm_gbs_step": avg_step_bytes / (ms * 1e-3) / 1e9,
             "hbm_frac_of_8tbs_step": avg_step_bytes / (ms * 1e-3) / 1e9 / SPEC_HBM_GBS,
-            "roofline": {
-                "bound": "hbm", "kernel": "whole step per rank (expert-parallel)",
-                "achieved": avg_step_bytes / (ms * 1e-3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
-                "frac": avg_step_bytes / (ms * 1e-3) / 1e9 / hbm_peak, "peak_kind": peak_kind,
-                "traffic": None} if achieved is None and ws > 1 else None if achieved is None else {
-                "bound": "hbm", "kernel": "expert_kernel<fp8, gate_up>", "achieved": achieved, "peak": hbm_peak,
-                "unit": "GB/s", "frac": achieved / hbm_peak, "peak_kind": peak_kind,
-                "frac_of_8tbs": achieved / SPEC_HBM_GBS, "algorithmic_bytes_per_launch": k_bytes,
-                "launch_ms": k_ms, "touched_experts": k_touched, "traffic": traffic,
-                "traffic_over_algorithmic": (traffic / k_bytes) if traffic else None},
+            "roofline": roofline_entry(ws, k_ms, k_bytes, k_touched, k_flops, k_tc, achieved, avg_step_bytes, ms,
+                                       hbm_peak, tc_peak, peak_kind, traffic),
             "cpu_baseline": cpu,
             "e2e": None if e2e_ms is None else {
                 "value": ws * N / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": N * dim * 2,
@@ -427,6 +420,28 @@ def run_gpu(args):
         import torch.distributed as dist
 
         dist.destroy_process_group()
+
+
+def roofline_entry(ws, k_ms, k_bytes, k_touched, k_flops, k_tc, achieved, step_bytes, ms, hbm_peak, tc_peak,
+                   peak_kind, traffic):
+    """The roofline figure of the dominant kernel (or, for expert parallelism, of the step)."""
+    if ws > 1:
+        gbs = step_bytes / (ms * 1e-3) / 1e9
+        return {"bound": "hbm", "kernel": "whole step per rank (expert-parallel)", "achieved": gbs, "peak": hbm_peak,
+                "unit": "GB/s", "frac": gbs / hbm_peak, "peak_kind": peak_kind, "traffic": None}
+    if achieved is None:
+        return None
+    if k_tc:  # many rows per expert: the tcgen05 kernel, bound by the tensor pipe
+        tflops = k_flops / (k_ms * 1e-3) / 1e12
+        return {"bound": "tensor", "kernel": "expert_tc_kernel<gate_up> (tcgen05 kind::f16, TMEM)",
+                "achieved": tflops, "peak": tc_peak, "unit": "TFLOP/s", "frac": tflops / tc_peak,
+                "peak_kind": peak_kind + " (dense bf16/f16 burst)", "algorithmic_flops_per_launch": k_flops,
+                "launch_ms": k_ms, "hbm_gbs": achieved, "traffic": None}
+    return {"bound": "hbm", "kernel": "expert_kernel<fp8, gate_up>", "achieved": achieved, "peak": hbm_peak,
+            "unit": "GB/s", "frac": achieved / hbm_peak, "peak_kind": peak_kind,
+            "frac_of_8tbs": achieved / SPEC_HBM_GBS, "algorithmic_bytes_per_launch": k_bytes, "launch_ms": k_ms,
+            "touched_experts": k_touched, "traffic": traffic,
+            "traffic_over_algorithmic": (traffic / k_bytes) if traffic else None}
 
 
 def time_gate_up(moe, x, ids, args, L, dev):
@@ -481,7 +496,10 @@ def time_gate_up(moe, x, ids, args, L, dev):
     per_expert = (p1.packed.numel() - header) // E  # packed tile bytes (codes + scales) of one expert
     w13 = 2 * touched * per_expert
     act = (P * desc.dim * 2) + (P * desc.inter * 2)
-    return k_ms, w13 + act, touched
+    flops = 2 * 2 * P * desc.dim * desc.inter  # gate and up products over every (token, slot) pair
+    busy = max(1, min(P, E))
+    tc = p1.wfmt == _lib.WFMT_FP8_B128 and P >= 64 * busy  # the dispatch rule of the expert kernels
+    return k_ms, w13 + act, touched, flops, tc
 
 
 def main():

@@ -27,6 +27,17 @@ int check_launch(const char* what);
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 int num_sms();
 
+// tcgen05 grouped products at large token counts (expert_tc.cu): fp8 block-scaled and f16
+bool tc_supports(int wfmt);
+int expert_tc_gate_up(int wfmt, const void* x_staged, const float* x_row_scale, int64_t rows_cap, int dim,
+                      const int32_t* offsets, int n_experts, const void* w1, const void* w3, int inter, int act,
+                      float limit, int round_gu, void* h_staged, float h_scale, int64_t n_rows, void* stream);
+int expert_tc_down(int wfmt, const void* h_staged, float h_scale, int64_t rows_cap, int inter, const int32_t* offsets,
+                   int n_experts, const void* w2, int dim, int round_o, float* o_rows, int ldo,
+                   const int32_t* o_row_map, int64_t n_rows, void* stream);
+// 0 = choose by rows per expert, 1 = always the decode kernel, 2 = tcgen05 where supported
+int expert_regime();
+
 // Stage two row sets of the same x in one launch: rows of x in perm order (job a) and, when
 // n_rows_b > 0, the first n_rows_b tokens in order (job b). Arguments as dsm_stage_rows.
 int stage_rows_pair(const void* x, int x_dtype, int64_t n_tokens, int dim, const int32_t* perm, int64_t n_rows,

@@ -26,6 +26,7 @@
 // reference casts h to x.dtype) -> staged f16 rows for the down kernel. Epilogue of the
 // down kernel: fp32 rows of o (optionally rounded to bf16).
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 
 #include "common.cuh"
@@ -543,6 +544,19 @@ int pick_nt(int64_t n_rows, int n_experts, int rt_count) {
   return nt;
 }
 
+std::atomic<int> g_regime{0};
+
+// The tcgen05 kernel pays off once an expert's weight tile is reused by many rows: with
+// 128-row MMA tiles, from about 64 rows per busy expert on average.
+bool use_tc(int wfmt, int64_t n_rows, int n_experts) {
+  if (!tc_supports(wfmt)) return false;
+  const int r = g_regime.load(std::memory_order_relaxed);
+  if (r == 1) return false;
+  if (r == 2) return true;
+  const int64_t busy = std::max<int64_t>(1, std::min<int64_t>(n_rows, n_experts));
+  return n_rows >= 64 * busy;
+}
+
 int check_common(int wfmt, int group_size, const int32_t* offsets, int n_experts) {
   DSM_REQUIRE(wfmt >= DSM_WFMT_F16 && wfmt <= DSM_WFMT_AFFINE4, "expert: unknown weight format");
   DSM_REQUIRE(n_experts >= 1 && n_experts <= 4096, "expert: n_experts out of range");
@@ -588,6 +602,9 @@ extern "C" int dsm_expert_gate_up(const void* x_staged, const float* x_row_scale
   a.h_scale = h_scale;
   a.h_out = static_cast<__half*>(h_staged);
   a.h_rows_cap = rows_cap;
+  if (use_tc(wfmt, n_rows, n_experts))
+    return expert_tc_gate_up(wfmt, x_staged, x_row_scale, rows_cap, dim, offsets, n_experts, w1_packed, w3_packed, inter,
+                             act, swiglu_limit, round_gu, h_staged, h_scale, n_rows, stream);
   return dispatch<true>(wfmt, pick_nt(n_rows, n_experts, a.rt_count), a, as_stream(stream));
 }
 
@@ -620,5 +637,18 @@ extern "C" int dsm_expert_down(const void* h_staged, float h_scale, int64_t rows
   a.o_row_map = o_row_map;
   a.ldo = ldo;
   a.round_o = round_o;
+  if (use_tc(wfmt, n_rows, n_experts))
+    return expert_tc_down(wfmt, h_staged, h_scale, rows_cap, inter, offsets, n_experts, w2_packed, dim, round_o, o_rows, ldo,
+                          o_row_map, n_rows, stream);
   return dispatch<false>(wfmt, pick_nt(n_rows, n_experts, a.rt_count), a, as_stream(stream));
+}
+
+namespace dsm {
+int expert_regime() { return g_regime.load(); }
+}  // namespace dsm
+
+extern "C" int dsm_set_expert_regime(int regime) {
+  DSM_REQUIRE(regime >= 0 && regime <= 2, "dsm_set_expert_regime: regime must be 0, 1 or 2");
+  dsm::g_regime.store(regime);
+  return DSM_OK;
 }

@@ -1,0 +1,569 @@
+// Grouped expert products at large token counts (prefill): tcgen05 MMA with TMEM
+// accumulators, for fp8 128x128 block-scaled experts and f16-packed (bf16/fp32) experts --
+// the shared expert among them.
+//
+// Work unit = (expert e, 128 weight rows, BN staged rows of the expert). Persistent CTAs,
+// warp-specialised:
+//   warp 0      producer: per 64-wide K stage, bulk-copies the unit's fp8 codes (half of a
+//               packed 128x128 tile, already in the layout the decode kernel reads) plus the
+//               tile's fp32 block scale, and TMA-loads the BN x 64 f16 activation box (128B
+//               swizzle) from the staged rows;
+//   warp 1      MMA issuer (one elected thread): tcgen05.mma kind::f16, M=128, N = the
+//               unit's rows rounded to 16, K=16 x 4 per stage, D in TMEM (double-buffered so
+//               the epilogue of one unit overlaps the main loop of the next); tcgen05.commit
+//               releases smem stages and hands accumulators to the epilogue;
+//   warps 2-9   converters: e4m3 -> f16 (hardware cvt) times the block scale (f16 multiply),
+//               written as the K-major SWIZZLE_128B f16 A operand;
+//   warps 10-13 epilogue: tcgen05.ld of the accumulators (each warp its 32-lane TMEM
+//               sub-partition), activation row scale, SwiGLU (gate/up) or output rows (down).
+//
+// A and B of one kind::f16 MMA must share a type, and the bf16 activations rule out the fp8
+// MMA kinds (fp8 activations would cost ~2% relative error), so the weights are widened to
+// f16 in shared memory; the block scale is folded in there (one extra f16 rounding of the
+// weight, 2^-11 relative) because it changes every 128 K and a TMEM accumulator cannot be
+// rescaled between K blocks without reading it out.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace dsm {
+namespace {
+
+constexpr int kTcM = 128;            // weight rows per unit = one scale row block
+constexpr int kTcK = 64;             // K per stage = one 128-byte swizzle row of f16
+constexpr int kTcConvWarps = 8;
+constexpr int kTcEpiWarps = 4;
+constexpr int kTcConvWarp0 = 2;
+constexpr int kTcEpiWarp0 = kTcConvWarp0 + kTcConvWarps;  // 10
+constexpr int kTcThreads = 32 * (kTcEpiWarp0 + kTcEpiWarps);  // 448
+constexpr int kABytes = kTcM * kTcK * 2;
+
+// FMT: DSM_WFMT_FP8_B128 (codes widened and block-scaled by the converters) or DSM_WFMT_F16
+// (f16 codes reshuffled into the swizzled layout; the per-expert prescale is undone in the
+// epilogue). The raw stage holds the packed tile's codes for 64 K: slabs 2h, 2h+1 (fp8, 8 KB)
+// or 4h .. 4h+3 (f16, 16 KB) of the 128-K tile.
+template <int FMT, bool DUAL>
+struct TcCfg {
+  static constexpr bool kFp8 = FMT == DSM_WFMT_FP8_B128;
+  static constexpr int NM = DUAL ? 2 : 1;
+  static constexpr int BN = DUAL ? 128 : 256;
+  static constexpr int kRawBytes = kFp8 ? 8192 : 16384;
+  static constexpr int kMetaBytes = kFp8 ? 16 : 0;
+  static constexpr int kBBytes = BN * kTcK * 2;
+  // stage: [A x NM][B][raw x NM][meta x NM], 1024-aligned operand pieces
+  static constexpr int kOffB = NM * kABytes;
+  static constexpr int kOffRaw = kOffB + kBBytes;
+  static constexpr int kOffMeta = kOffRaw + NM * kRawBytes;
+  static constexpr int kStageBytes = ((kOffMeta + NM * 16) + 1023) / 1024 * 1024;
+  static constexpr int kStages = (3 * kStageBytes <= 204 * 1024) ? 3 : 2;
+  static constexpr int kTxBytes = NM * (kRawBytes + kMetaBytes) + kBBytes;
+  static constexpr int kTmemCols = 2 * NM * BN;  // double-buffered accumulators = 512
+};
+
+struct TcArgs {
+  const uint8_t* wa;
+  const uint8_t* wb;
+  const float* act_scale;
+  float act_scale_const;
+  const int32_t* offsets;
+  int64_t n_rows;
+  int n_experts;
+  int out_rows;
+  int rt_count;
+  int kc_count;
+  int act;
+  float limit;
+  int round_gu;
+  float h_scale;
+  __half* h_out;
+  int64_t h_rows_cap;
+  float* o_out;
+  const int32_t* o_row_map;
+  int ldo;
+  int round_o;
+};
+
+__device__ __forceinline__ int tc_group_first(const TcArgs& a, int e) { return a.offsets ? a.offsets[e] : 0; }
+__device__ __forceinline__ int tc_group_count(const TcArgs& a, int e) {
+  return a.offsets ? a.offsets[e + 1] - a.offsets[e] : int(a.n_rows);
+}
+
+__device__ __forceinline__ int tc_find_expert(const int* pre, int n_experts, int u) {
+  int lo = 0, hi = n_experts - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (pre[mid] <= u)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ float tc_sigmoid(float v) { return 1.f / (1.f + expf(-v)); }
+
+__device__ __forceinline__ float tc_act(float g, float u, int act, float limit) {
+  if (act == DSM_ACT_SILU_MUL_BF16) {
+    const float sig = bf16_round(tc_sigmoid(g));
+    return bf16_round(g * sig) * u;
+  }
+  if (limit > 0.f) {
+    u = fminf(fmaxf(u, -limit), limit);
+    g = fminf(g, limit);
+  }
+  return g * tc_sigmoid(g) * u;
+}
+
+// ---- tcgen05 / TMA wrappers -----------------------------------------------------------
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major, SWIZZLE_128B operand: rows at 128 B, 8-row groups at 1024 B (SBO), LBO field 1.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+         (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+// kind::f16: D f32, A = B = f16, both K-major, N and M as given.
+__device__ __forceinline__ uint32_t umma_idesc_f16(int m, int n) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  const uint32_t no_mask = 0u;  // disable-output-lane mask: every lane written
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(no_mask)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+template <int FMT, bool DUAL>
+__global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a,
+                                                                  const __grid_constant__ CUtensorMap xmap) {
+  using C = TcCfg<FMT, DUAL>;
+  constexpr int kTcStages = C::kStages;
+  constexpr int NM = C::NM, BN = C::BN;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw0 = smem_u32(smem_raw);
+  const uint32_t base = (raw0 + 1023u) & ~1023u;
+  uint8_t* sbase = smem_raw + (base - raw0);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sbase + kTcStages * C::kStageBytes);
+  uint64_t* conv = full + kTcStages;
+  uint64_t* empty = conv + kTcStages;
+  uint64_t* tfull = empty + kTcStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* pre = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_slot + 2));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = a.n_experts;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], kTcConvWarps);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kTcEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {  // TMEM: 512 columns (two accumulator buffers)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (warp == 0) {  // units per expert: rt_count x ceil(count / BN)
+    int carry = 0;
+    if (lane == 0) pre[0] = 0;
+    for (int b0 = 0; b0 < E; b0 += 32) {
+      const int e = b0 + lane;
+      int v = 0;
+      if (e < E) {
+        const int cnt = tc_group_count(a, e);
+        v = cnt > 0 ? a.rt_count * ((cnt + BN - 1) / BN) : 0;
+      }
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      if (e < E) pre[e + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int total = pre[E];
+  const int64_t hdr_bytes = ceil_div(int64_t(E) * 4, kPackHeader) * kPackHeader;
+  const int tile_b = tile_bytes(FMT, 0);
+  const uint8_t* tiles[2] = {a.wa + hdr_bytes, DUAL ? a.wb + hdr_bytes : nullptr};
+  const int nks = 2 * a.kc_count;  // 64-wide K stages per unit
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        const int e = tc_find_expert(pre, E, u);
+        const int cnt = tc_group_count(a, e);
+        const int nch = (cnt + BN - 1) / BN;
+        const int local = u - pre[e];
+        const int rt = local / nch, chunk = local % nch;
+        const int row0 = tc_group_first(a, e) + chunk * BN;
+        const int64_t tile0 = (int64_t(e) * a.rt_count + rt) * a.kc_count;
+        for (int ks = 0; ks < nks; ++ks) {
+          if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          uint8_t* st = sbase + s * C::kStageBytes;
+          const int kc = ks >> 1, half = ks & 1;
+          mbar_arrive_expect_tx(&full[s], uint32_t(C::kTxBytes));
+#pragma unroll
+          for (int m = 0; m < NM; ++m) {
+            const uint8_t* tile = tiles[m] + (tile0 + kc) * tile_b;
+            bulk_g2s(st + C::kOffRaw + m * C::kRawBytes, tile + half * C::kRawBytes, C::kRawBytes, &full[s], pol_w);
+            if (C::kFp8) bulk_g2s(st + C::kOffMeta + m * 16, tile + 16384, 16, &full[s], pol_w);
+          }
+          tma_load_3d(smem_u32(st + C::kOffB), &xmap, half * kTcK, row0, kc, &full[s]);
+          if (++s == kTcStages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (!ok)
+        for (int i = 0; i < 100; ++i) __nanosleep(1000);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      int j = 0;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++j) {
+        const int e = tc_find_expert(pre, E, u);
+        const int cnt = tc_group_count(a, e);
+        const int nch = (cnt + BN - 1) / BN;
+        const int chunk = (u - pre[e]) % nch;
+        const int rows = min(BN, cnt - chunk * BN);
+        const int n_mma = min(BN, (rows + 15) / 16 * 16);
+        const uint32_t idesc = umma_idesc_f16(kTcM, n_mma);
+        const int buf = j & 1;
+        if (*abort_flag || !mbar_wait(&tempty[buf], ((j >> 1) & 1) ^ 1u)) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int ks = 0; ks < nks; ++ks) {
+          if (*abort_flag || !mbar_wait(&conv[s], ph) || !mbar_wait(&full[s], ph)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(sbase + s * C::kStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < kTcK / 16; ++kk) {
+            const uint64_t bdesc = umma_desc_sw128(st + C::kOffB) + uint64_t(kk * 2);
+#pragma unroll
+            for (int m = 0; m < NM; ++m) {
+              const uint64_t adesc = umma_desc_sw128(st + m * kABytes) + uint64_t(kk * 2);
+              const uint32_t d = tmem + uint32_t((buf * NM + m) * BN);
+              umma_f16(d, adesc, bdesc, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty[s]);  // smem stage free once these MMAs have read it
+          if (++s == kTcStages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[buf]);  // accumulator ready for the epilogue
+      }
+      // all MMAs issued by this thread complete before TMEM is released
+      umma_commit(drain);
+      mbar_wait(drain, 0);
+    }
+  } else if (warp < kTcEpiWarp0) {
+    // ------------------------------------------------------------------ converters
+    const int cw = warp - kTcConvWarp0;  // 0..7
+    const int g = lane >> 2, q = lane & 3;
+    int s = 0;
+    uint32_t ph = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x) {
+      bool ok = true;
+      for (int ks = 0; ks < nks; ++ks) {
+        if (*abort_flag || !mbar_wait(&full[s], ph)) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        uint8_t* st = sbase + s * C::kStageBytes;
+#pragma unroll
+        for (int m = 0; m < NM; ++m) {
+          const uint32_t rawm = smem_u32(st + C::kOffRaw + m * C::kRawBytes);
+          const uint32_t am = smem_u32(st + m * kABytes);
+          if constexpr (!C::kFp8) {
+            // f16 codes: 4 k16 slabs x 8 m16 tiles of 512 B; lane holds rows r0, r0+8 at k 4q..4q+3
+#pragma unroll
+            for (int bi = 0; bi < 4; ++bi) {
+              const int blk = cw + 8 * bi;
+              const int sl = blk >> 3, mt = blk & 7;
+              const uint4 v = lds128(rawm + (blk * 32 + lane) * 16);
+              const int r0 = mt * 16 + g, r1 = r0 + 8;
+              const int k = sl * 16 + q * 4;
+              const int ch = k >> 3, sub = (k & 7) * 2;
+              const uint32_t p0 = am + r0 * 128 + ((ch ^ (r0 & 7)) << 4) + sub;
+              const uint32_t p1 = am + r1 * 128 + ((ch ^ (r1 & 7)) << 4) + sub;
+              asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(p0), "r"(v.x), "r"(v.y) : "memory");
+              asm volatile("st.shared.v2.b32 [%0], {%1,%2};" ::"r"(p1), "r"(v.z), "r"(v.w) : "memory");
+            }
+            continue;
+          }
+          const float sc = *reinterpret_cast<const float*>(st + C::kOffMeta + m * 16);
+          const __half2 s2 = __float2half2_rn(sc);
+          const uint32_t sbits = *reinterpret_cast<const uint32_t*>(&s2);
+          // 16 blocks of 512 B (2 slabs x 8 m16 tiles); warp cw converts blocks cw and cw + 8
+#pragma unroll
+          for (int bi = 0; bi < 2; ++bi) {
+            const int blk = cw + 8 * bi;
+            const int sl = blk >> 3, mt = blk & 7;
+            const uint4 v = lds128(rawm + (blk * 32 + lane) * 16);
+            uint32_t h[8];
+            e4m3x4_to_f16(v.x, h[0], h[1]);  // row r0, k 8q..8q+3
+            e4m3x4_to_f16(v.y, h[2], h[3]);  // row r0, k 8q+4..8q+7
+            e4m3x4_to_f16(v.z, h[4], h[5]);  // row r0+8
+            e4m3x4_to_f16(v.w, h[6], h[7]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) h[i] = hmul2_bits(h[i], sbits);
+            const int r0 = mt * 16 + g, r1 = r0 + 8;
+            const int ch = sl * 4 + q;  // 16-byte chunk (8 halves) of the 128-byte row
+            const uint32_t p0 = am + r0 * 128 + ((ch ^ (r0 & 7)) << 4);
+            const uint32_t p1 = am + r1 * 128 + ((ch ^ (r1 & 7)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(p0), "r"(h[0]), "r"(h[1]), "r"(h[2]),
+                         "r"(h[3])
+                         : "memory");
+            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(p1), "r"(h[4]), "r"(h[5]), "r"(h[6]),
+                         "r"(h[7])
+                         : "memory");
+          }
+        }
+        fence_async_smem();  // generic-proxy writes -> visible to the tensor core's async proxy
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
+        if (++s == kTcStages) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+      if (!ok) break;
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int sp = warp & 3;  // TMEM sub-partition of this warp: lanes 32*sp .. 32*sp+31
+    const int rloc = 32 * sp + lane;
+    int j = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++j) {
+      const int e = tc_find_expert(pre, E, u);
+      const int off = tc_group_first(a, e);
+      const int cnt = tc_group_count(a, e);
+      const int nch = (cnt + BN - 1) / BN;
+      const int local = u - pre[e];
+      const int rt = local / nch, chunk = local % nch;
+      const int rows = min(BN, cnt - chunk * BN);
+      const int buf = j & 1;
+      if (*abort_flag || !mbar_wait(&tfull[buf], (j >> 1) & 1)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const float wmul_a = reinterpret_cast<const float*>(a.wa)[e];
+      const float wmul_b = DUAL ? reinterpret_cast<const float*>(a.wb)[e] : 1.f;
+      const uint32_t lane_base = tmem + (uint32_t(32 * sp) << 16);
+      for (int cb = 0; cb < rows; cb += 16) {
+        uint32_t gv[16], uv[16];
+        tmem_ld16(lane_base + uint32_t(buf * NM * BN + cb), gv);
+        if (DUAL) tmem_ld16(lane_base + uint32_t((buf * NM + 1) * BN + cb), uv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int col = cb + i;
+          if (col >= rows) break;
+          const int64_t r = int64_t(off) + chunk * BN + col;
+          const float xs = a.act_scale ? a.act_scale[r] : a.act_scale_const;
+          if constexpr (DUAL) {
+            float gg = __uint_as_float(gv[i]) * xs * wmul_a;
+            float uu = __uint_as_float(uv[i]) * xs * wmul_b;
+            if (a.round_gu & 1) {
+              gg = bf16_round(gg);
+              uu = bf16_round(uu);
+            }
+            float h = tc_act(gg, uu, a.act, a.limit);
+            if (a.round_gu & 2) h = bf16_round(h);
+            a.h_out[(int64_t(rt) * a.h_rows_cap + r) * kStagePitch + rloc] = __float2half_rn(h * a.h_scale);
+          } else {
+            const int d = rt * kTcM + rloc;
+            if (d < a.out_rows) {
+              float v = __uint_as_float(gv[i]) * xs * wmul_a;
+              if (a.round_o) v = bf16_round(v);
+              const int64_t orow = a.o_row_map ? int64_t(a.o_row_map[r]) : r;
+              a.o_out[orow * a.ldo + d] = v;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
+  }
+}
+
+// ---- host side ------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// staged rows [chunks][rows_cap][160 halves] -> boxes of 64 halves x bn rows (128B swizzle)
+int make_stage_map(CUtensorMap* map, const void* staged, int64_t rows_cap, int k_chunks, int bn) {
+  auto enc = encode_fn();
+  if (!enc) return fail(DSM_ERR_CUDA, "expert_tc: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {cuuint64_t(kStagePitch), cuuint64_t(rows_cap), cuuint64_t(k_chunks)};
+  const cuuint64_t strides[2] = {cuuint64_t(kStagePitch) * 2, cuuint64_t(rows_cap) * kStagePitch * 2};
+  const cuuint32_t box[3] = {cuuint32_t(kTcK), cuuint32_t(bn), 1};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(staged), dims, strides, box, estride,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DSM_ERR_CUDA, "expert_tc: cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  return DSM_OK;
+}
+
+template <int FMT, bool DUAL>
+int launch_tc(const TcArgs& a, const void* staged, int64_t rows_cap, cudaStream_t stream) {
+  using C = TcCfg<FMT, DUAL>;
+  constexpr int kTcStages = C::kStages;
+  CUtensorMap map;
+  if (int rc = make_stage_map(&map, staged, rows_cap, a.kc_count, C::BN)) return rc;
+  const size_t smem = 1024 + size_t(kTcStages) * C::kStageBytes + 8 * (3 * kTcStages + 5) + 16 +
+                      size_t(a.n_experts + 1) * 4;
+  auto kern = expert_tc_kernel<FMT, DUAL>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return check_launch("expert_tc smem attribute");
+  kern<<<num_sms(), kTcThreads, smem, stream>>>(a, map);
+  return check_launch("expert_tc");
+}
+
+}  // namespace
+
+// Entry points used by the expert dispatch (expert.cu) for the fp8 large-token regime.
+bool tc_supports(int wfmt) { return wfmt == DSM_WFMT_FP8_B128 || wfmt == DSM_WFMT_F16; }
+
+int expert_tc_gate_up(int wfmt, const void* x_staged, const float* x_row_scale, int64_t rows_cap, int dim,
+                      const int32_t* offsets, int n_experts, const void* w1, const void* w3, int inter, int act,
+                      float limit, int round_gu, void* h_staged, float h_scale, int64_t n_rows, void* stream) {
+  TcArgs a{};
+  a.wa = static_cast<const uint8_t*>(w1);
+  a.wb = static_cast<const uint8_t*>(w3);
+  a.act_scale = x_row_scale;
+  a.act_scale_const = 1.f;
+  a.offsets = offsets;
+  a.n_rows = n_rows;
+  a.n_experts = n_experts;
+  a.out_rows = inter;
+  a.rt_count = int(ceil_div(inter, kTcM));
+  a.kc_count = int(ceil_div(dim, kChunkK));
+  a.act = act;
+  a.limit = limit;
+  a.round_gu = round_gu;
+  a.h_scale = h_scale;
+  a.h_out = static_cast<__half*>(h_staged);
+  a.h_rows_cap = rows_cap;
+  if (wfmt == DSM_WFMT_F16) return launch_tc<DSM_WFMT_F16, true>(a, x_staged, rows_cap, as_stream(stream));
+  return launch_tc<DSM_WFMT_FP8_B128, true>(a, x_staged, rows_cap, as_stream(stream));
+}
+
+int expert_tc_down(int wfmt, const void* h_staged, float h_scale, int64_t rows_cap, int inter, const int32_t* offsets,
+                   int n_experts, const void* w2, int dim, int round_o, float* o_rows, int ldo,
+                   const int32_t* o_row_map, int64_t n_rows, void* stream) {
+  TcArgs a{};
+  a.wa = static_cast<const uint8_t*>(w2);
+  a.wb = nullptr;
+  a.act_scale = nullptr;
+  a.act_scale_const = 1.f / h_scale;
+  a.offsets = offsets;
+  a.n_rows = n_rows;
+  a.n_experts = n_experts;
+  a.out_rows = dim;
+  a.rt_count = int(ceil_div(dim, kTcM));
+  a.kc_count = int(ceil_div(inter, kChunkK));
+  a.o_out = o_rows;
+  a.o_row_map = o_row_map;
+  a.ldo = ldo;
+  a.round_o = round_o;
+  if (wfmt == DSM_WFMT_F16) return launch_tc<DSM_WFMT_F16, false>(a, h_staged, rows_cap, as_stream(stream));
+  return launch_tc<DSM_WFMT_FP8_B128, false>(a, h_staged, rows_cap, as_stream(stream));
+}
+
+}  // namespace dsm

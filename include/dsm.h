@@ -175,6 +175,12 @@ int dsm_expert_down(const void* h_staged, float h_scale, int64_t rows_cap, int i
                     const void* w2_packed, int dim, int round_o, float* o_rows, int ldo,
                     const int32_t* o_row_map, int64_t n_rows, void* stream);
 
+/* Kernel regime of the grouped expert products: 0 (default) picks by rows per busy
+ * expert -- the mma.sync weight-streaming kernel at decode sizes, the tcgen05/TMEM kernel
+ * (fp8 block-scaled experts) from ~64 rows per expert; 1 forces the streaming kernel;
+ * 2 forces tcgen05 wherever the format supports it. Process-wide. */
+int dsm_set_expert_regime(int regime);
+
 /* ---- expert-parallel helpers -----------------------------------------------------------
  * gather_rows: out[r] = x[perm[r] / topk] (perm NULL: x[r]), same dtype (F32/BF16), the
  *   rows a rank sends to the owners of its routed experts (expert order = owner order).
