@@ -407,7 +407,7 @@ def run_gpu(args):
             "hbm_gbs_step": avg_step_bytes / (ms * 1e-3) / 1e9,
             "hbm_frac_of_8tbs_step": avg_step_bytes / (ms * 1e-3) / 1e9 / SPEC_HBM_GBS,
             "roofline": roofline_entry(ws, k_ms, k_bytes, k_touched, k_flops, k_tc, achieved, avg_step_bytes, ms,
-                                       hbm_peak, tc_peak, peak_kind, traffic),
+                                       hbm_peak, tc_peak, peak_kind, traffic, wl.wfmt),
             "cpu_baseline": cpu,
             "e2e": None if e2e_ms is None else {
                 "value": ws * N / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": N * dim * 2,
@@ -423,7 +423,7 @@ def run_gpu(args):
 
 
 def roofline_entry(ws, k_ms, k_bytes, k_touched, k_flops, k_tc, achieved, step_bytes, ms, hbm_peak, tc_peak,
-                   peak_kind, traffic):
+                   peak_kind, traffic, wfmt="fp8"):
     """The roofline figure of the dominant kernel (or, for expert parallelism, of the step)."""
     if ws > 1:
         gbs = step_bytes / (ms * 1e-3) / 1e9
@@ -437,7 +437,7 @@ def roofline_entry(ws, k_ms, k_bytes, k_touched, k_flops, k_tc, achieved, step_b
                 "achieved": tflops, "peak": tc_peak, "unit": "TFLOP/s", "frac": tflops / tc_peak,
                 "peak_kind": peak_kind + " (dense bf16/f16 burst)", "algorithmic_flops_per_launch": k_flops,
                 "launch_ms": k_ms, "hbm_gbs": achieved, "traffic": None}
-    return {"bound": "hbm", "kernel": "expert_kernel<fp8, gate_up>", "achieved": achieved, "peak": hbm_peak,
+    return {"bound": "hbm", "kernel": f"expert_kernel<{wfmt}, gate_up>", "achieved": achieved, "peak": hbm_peak,
             "unit": "GB/s", "frac": achieved / hbm_peak, "peak_kind": peak_kind,
             "frac_of_8tbs": achieved / SPEC_HBM_GBS, "algorithmic_bytes_per_launch": k_bytes, "launch_ms": k_ms,
             "touched_experts": k_touched, "traffic": traffic,

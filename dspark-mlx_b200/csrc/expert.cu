@@ -34,7 +34,10 @@
 namespace dsm {
 namespace {
 
-constexpr int kConsumerWarps = 4;
+// Consumer warps share a 128-row tile as 8 m16 tiles; more warps give the in-register
+// dequantisation (2 cvt + 1 multiply per 4 e2m1 codes) more issue slots.
+constexpr int kConsumerWarps = 8;
+constexpr int kMt = 8 / kConsumerWarps;  // m16 tiles per consumer warp
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 
 struct ExpertArgs {
@@ -208,13 +211,13 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
     const int local = u - pre[e];
     const int rt = local / nch, chunk = local % nch;
 
-    float acc[NM][2][NT][4];
-    float tmp[kTmp ? NM : 1][2][NT][4];
+    float acc[NM][kMt][NT][4];
+    float tmp[kTmp ? NM : 1][kMt][NT][4];
     float xsum[kAffine ? NT : 1][4];
 #pragma unroll
     for (int m = 0; m < NM; ++m)
 #pragma unroll
-      for (int i = 0; i < 2; ++i)
+      for (int i = 0; i < kMt; ++i)
 #pragma unroll
         for (int j = 0; j < NT; ++j)
 #pragma unroll
@@ -240,12 +243,12 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
       if constexpr (FMT == DSM_WFMT_F16) {
 #pragma unroll
         for (int sl = 0; sl < 8; ++sl) {
-          uint32_t A[NM][2][4];
+          uint32_t A[NM][kMt][4];
 #pragma unroll
           for (int m = 0; m < NM; ++m)
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              const uint4 v = lds128(st + m * tile_b + ((sl * 8 + 2 * warp + i) * 32 + lane) * 16);
+            for (int i = 0; i < kMt; ++i) {
+              const uint4 v = lds128(st + m * tile_b + ((sl * 8 + kMt * warp + i) * 32 + lane) * 16);
               A[m][i][0] = v.x;
               A[m][i][1] = v.z;
               A[m][i][2] = v.y;
@@ -257,19 +260,19 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
 #pragma unroll
             for (int m = 0; m < NM; ++m)
 #pragma unroll
-              for (int i = 0; i < 2; ++i) mma_f16(acc[m][i][j], A[m][i], xb.x, xb.y);
+              for (int i = 0; i < kMt; ++i) mma_f16(acc[m][i][j], A[m][i], xb.x, xb.y);
           }
         }
       } else if constexpr (FMT == DSM_WFMT_FP8_B128 || FMT == DSM_WFMT_AFFINE8) {
         const int slabs_per_group = kAffine ? a.group_size / 32 : 4;
 #pragma unroll
         for (int sl = 0; sl < 4; ++sl) {
-          uint32_t A[NM][2][2][4];  // [matrix][m16 tile][mma 0/1][regs]
+          uint32_t A[NM][kMt][2][4];  // [matrix][m16 tile][mma 0/1][regs]
 #pragma unroll
           for (int m = 0; m < NM; ++m)
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              const uint4 v = lds128(st + m * tile_b + ((sl * 8 + 2 * warp + i) * 32 + lane) * 16);
+            for (int i = 0; i < kMt; ++i) {
+              const uint4 v = lds128(st + m * tile_b + ((sl * 8 + kMt * warp + i) * 32 + lane) * 16);
               if constexpr (FMT == DSM_WFMT_FP8_B128) {
                 e4m3x4_to_f16(v.x, A[m][i][0][0], A[m][i][0][2]);
                 e4m3x4_to_f16(v.y, A[m][i][1][0], A[m][i][1][2]);
@@ -288,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
 #pragma unroll
             for (int m = 0; m < NM; ++m)
 #pragma unroll
-              for (int i = 0; i < 2; ++i) {
+              for (int i = 0; i < kMt; ++i) {
                 mma_f16(tmp[m][i][j], A[m][i][0], xb.x, xb.y);
                 mma_f16(tmp[m][i][j], A[m][i][1], xb.z, xb.w);
               }
@@ -304,8 +307,8 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
 #pragma unroll
               for (int m = 0; m < NM; ++m)
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                  const int r0 = 32 * warp + 16 * i + g;
+                for (int i = 0; i < kMt; ++i) {
+                  const int r0 = 16 * (kMt * warp + i) + g;
                   const uint32_t sb0 = lds32(st + m * tile_b + tile_code_bytes(FMT) + (r0 * gpt + grp) * 4);
                   const uint32_t sb1 = lds32(st + m * tile_b + tile_code_bytes(FMT) + ((r0 + 8) * gpt + grp) * 4);
                   const float s0 = __uint_as_float(sb0 << 16), b0 = __uint_as_float(sb0 & 0xFFFF0000u);
@@ -333,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
           for (int m = 0; m < NM; ++m) {
             const float sc = __uint_as_float(lds32(st + m * tile_b + tile_code_bytes(FMT)));
 #pragma unroll
-            for (int i = 0; i < 2; ++i)
+            for (int i = 0; i < kMt; ++i)
 #pragma unroll
               for (int j = 0; j < NT; ++j)
 #pragma unroll
@@ -345,25 +348,25 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
         }
       } else {  // 4-bit formats: FP4_G32, AFFINE4 (slab = 64 K)
         const int slabs_per_group = kAffine ? a.group_size / 64 : 1;
-        uint32_t gsc[NM][2][2];  // fp4 group-scale words of rows r0, r0+8 per m16 tile
+        uint32_t gsc[NM][kMt][2];  // fp4 group-scale words of rows r0, r0+8 per m16 tile
         if constexpr (FMT == DSM_WFMT_FP4_G32) {
 #pragma unroll
           for (int m = 0; m < NM; ++m)
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              const int r0 = 32 * warp + 16 * i + g;
+            for (int i = 0; i < kMt; ++i) {
+              const int r0 = 16 * (kMt * warp + i) + g;
               gsc[m][i][0] = lds32(st + m * tile_b + tile_code_bytes(FMT) + r0 * 4);
               gsc[m][i][1] = lds32(st + m * tile_b + tile_code_bytes(FMT) + (r0 + 8) * 4);
             }
         }
 #pragma unroll
         for (int sl = 0; sl < 2; ++sl) {
-          uint32_t A[NM][2][4][4];  // [matrix][m16][mma t][regs]
+          uint32_t A[NM][kMt][4][4];  // [matrix][m16][mma t][regs]
 #pragma unroll
           for (int m = 0; m < NM; ++m)
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              const uint4 v = lds128(st + m * tile_b + ((sl * 8 + 2 * warp + i) * 32 + lane) * 16);
+            for (int i = 0; i < kMt; ++i) {
+              const uint4 v = lds128(st + m * tile_b + ((sl * 8 + kMt * warp + i) * 32 + lane) * 16);
               uint32_t c0[4], c1[4], c2[4], c3[4];
               if constexpr (FMT == DSM_WFMT_FP4_G32) {
                 e2m1x8_to_f16(v.x, c0);
@@ -408,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
 #pragma unroll
               for (int m = 0; m < NM; ++m)
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
+                for (int i = 0; i < kMt; ++i) {
                   if constexpr (kAffine)
                     mma_f16(tmp[m][i][j], A[m][i][t], xr[2 * t], xr[2 * t + 1]);
                   else
@@ -424,8 +427,8 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
 #pragma unroll
               for (int m = 0; m < NM; ++m)
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                  const int r0 = 32 * warp + 16 * i + g;
+                for (int i = 0; i < kMt; ++i) {
+                  const int r0 = 16 * (kMt * warp + i) + g;
                   const uint32_t sb0 = lds32(st + m * tile_b + tile_code_bytes(FMT) + (r0 * gpt + grp) * 4);
                   const uint32_t sb1 = lds32(st + m * tile_b + tile_code_bytes(FMT) + ((r0 + 8) * gpt + grp) * 4);
                   const float s0 = __uint_as_float(sb0 << 16), b0 = __uint_as_float(sb0 & 0xFFFF0000u);
@@ -462,14 +465,14 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
     const float wmul_a = hdr_a[e];
     const float wmul_b = DUAL ? hdr_b[e] : 1.f;
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < kMt; ++i)
 #pragma unroll
       for (int j = 0; j < NT; ++j)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int col = chunk * BN + j * 8 + 2 * q + (c & 1);
           if (col >= cnt) continue;
-          const int rloc = 32 * warp + 16 * i + g + ((c & 2) ? 8 : 0);
+          const int rloc = 16 * (kMt * warp + i) + g + ((c & 2) ? 8 : 0);
           const int64_t r = int64_t(off) + col;
           const float xs = a.act_scale ? a.act_scale[r] : a.act_scale_const;
           if constexpr (DUAL) {

@@ -255,6 +255,22 @@ def test_fp8_decode_full_size_sampled_tokens():
     assert max_rel_err(y[sample], ref_y) < MOE_TOL
 
 
+def test_fp4_decode_full_size_sampled_tokens():
+    """The 448-token fp4 block (Zipf-skewed routing) at full size; the oracle checks a sample."""
+    wl = W.WORKLOADS["fp4_decode"]
+    t = W.make_moe_tensors(wl, device=DEV)
+    moe = W.build_moe(wl, t, DEV)
+    y, rw, ri = moe(t["x"], None, return_routing=True)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    counts = torch.bincount(ri.flatten().long(), minlength=256)
+    assert int(counts.max()) > 4 * int(counts.float().mean())  # the skew is there
+    sample = [1, 100, 333, 447]
+    ref_y, _, ref_i = oracle_moe(wl, t, tokens=sample)
+    assert torch.equal(ri.cpu()[sample], ref_i)
+    assert max_rel_err(y[sample], ref_y) < MOE_TOL
+
+
 def test_fp8_decode_batch_invariance():
     """Size-independent property: a token's output does not depend on its batch neighbours."""
     wl = W.WORKLOADS["fp8_decode"]
