@@ -35,6 +35,13 @@ int expert_tc_gate_up(int wfmt, const void* x_staged, const float* x_row_scale, 
 int expert_tc_down(int wfmt, const void* h_staged, float h_scale, int64_t rows_cap, int inter, const int32_t* offsets,
                    int n_experts, const void* w2, int dim, int round_o, float* o_rows, int ldo,
                    const int32_t* o_row_map, int64_t n_rows, void* stream);
+// fp4 experts at every token count (expert_tm.cu): weights dequantised into tensor memory
+int expert_tm_gate_up(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int dim, const int32_t* offsets,
+                      int n_experts, const void* w1, const void* w3, int inter, int act, float limit, int round_gu,
+                      void* h_staged, float h_scale, int64_t n_rows, void* stream);
+int expert_tm_down(const void* h_staged, float h_scale, int64_t rows_cap, int inter, const int32_t* offsets,
+                   int n_experts, const void* w2, int dim, int round_o, float* o_rows, int ldo,
+                   const int32_t* o_row_map, int64_t n_rows, void* stream);
 // 0 = choose by rows per expert, 1 = always the decode kernel, 2 = tcgen05 where supported
 int expert_regime();
 

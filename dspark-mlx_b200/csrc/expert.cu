@@ -10,16 +10,15 @@
 // activation rows into a ring of shared-memory stages (mbarrier complete_tx); four
 // consumer warps each own 32 weight rows, load their A fragments with one ld.shared.v4 per
 // m16 tile (the packer stored them in fragment order), dequantise in registers (hardware
-// e4m3/e2m1 -> f16 conversions, magic-number uint8/uint4 -> f16), and run
+// e4m3 -> f16 conversions, magic-number uint8/uint4 -> f16), and run
 // mma.sync m16n8k16 f16 x f16 -> fp32 against the activations. Weight streams are read
 // with an L2 evict-first policy, activations with evict-last.
 //
 // Scales: fp8 128x128 block scales and affine group scale/bias are applied to fp32
 // partial sums at group boundaries (the affine bias term uses the activation group sums,
-// obtained with an all-ones MMA); e2m1 codes are multiplied by their e4m3 group scale in
-// f16 (exact: at most 6 significant bits); the per-expert multiplier from the packed
-// header (f16 prescale, fp4 per-tensor scale) and the activation row scale are applied in
-// the epilogue.
+// obtained with an all-ones MMA); the per-expert multiplier from the packed header (f16
+// prescale) and the activation row scale are applied in the epilogue. fp4 experts are
+// multiplied by the tensor-memory kernel (expert_tm.cu) at every token count.
 //
 // Epilogue of the gate/up kernel: g, u -> (optional bf16 rounding, as bf16 / affine
 // weights give bf16 products in the reference) -> activation -> bf16 rounding (the
@@ -346,19 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
                 }
           }
         }
-      } else {  // 4-bit formats: FP4_G32, AFFINE4 (slab = 64 K)
-        const int slabs_per_group = kAffine ? a.group_size / 64 : 1;
-        uint32_t gsc[NM][kMt][2];  // fp4 group-scale words of rows r0, r0+8 per m16 tile
-        if constexpr (FMT == DSM_WFMT_FP4_G32) {
-#pragma unroll
-          for (int m = 0; m < NM; ++m)
-#pragma unroll
-            for (int i = 0; i < kMt; ++i) {
-              const int r0 = 16 * (kMt * warp + i) + g;
-              gsc[m][i][0] = lds32(st + m * tile_b + tile_code_bytes(FMT) + r0 * 4);
-              gsc[m][i][1] = lds32(st + m * tile_b + tile_code_bytes(FMT) + (r0 + 8) * 4);
-            }
-        }
+      } else {  // AFFINE4 (slab = 64 K); fp4 experts run in expert_tm.cu
+        const int slabs_per_group = a.group_size / 64;
 #pragma unroll
         for (int sl = 0; sl < 2; ++sl) {
           uint32_t A[NM][kMt][4][4];  // [matrix][m16][mma t][regs]
@@ -368,28 +356,10 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
             for (int i = 0; i < kMt; ++i) {
               const uint4 v = lds128(st + m * tile_b + ((sl * 8 + kMt * warp + i) * 32 + lane) * 16);
               uint32_t c0[4], c1[4], c2[4], c3[4];
-              if constexpr (FMT == DSM_WFMT_FP4_G32) {
-                e2m1x8_to_f16(v.x, c0);
-                e2m1x8_to_f16(v.y, c1);
-                e2m1x8_to_f16(v.z, c2);
-                e2m1x8_to_f16(v.w, c3);
-                const int sh = 8 * (2 * sl + (q >> 1));
-                const uint32_t f0 = e4m3_to_f16_bits((gsc[m][i][0] >> sh) & 0xFFu);
-                const uint32_t f1 = e4m3_to_f16_bits((gsc[m][i][1] >> sh) & 0xFFu);
-                const uint32_t s0 = f0 | (f0 << 16), s1 = f1 | (f1 << 16);
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                  c0[t] = hmul2_bits(c0[t], s0);
-                  c1[t] = hmul2_bits(c1[t], s0);
-                  c2[t] = hmul2_bits(c2[t], s1);
-                  c3[t] = hmul2_bits(c3[t], s1);
-                }
-              } else {
-                u4x8_to_f16_plus1024(v.x, c0);
-                u4x8_to_f16_plus1024(v.y, c1);
-                u4x8_to_f16_plus1024(v.z, c2);
-                u4x8_to_f16_plus1024(v.w, c3);
-              }
+              u4x8_to_f16_plus1024(v.x, c0);
+              u4x8_to_f16_plus1024(v.y, c1);
+              u4x8_to_f16_plus1024(v.z, c2);
+              u4x8_to_f16_plus1024(v.w, c3);
               // mma t covers K 4t..4t+3 of this lane's 16: regs (k 4t,4t+1) and (k 4t+2,4t+3)
               A[m][i][0][0] = c0[0]; A[m][i][0][1] = c2[0]; A[m][i][0][2] = c0[1]; A[m][i][0][3] = c2[1];
               A[m][i][1][0] = c0[2]; A[m][i][1][1] = c2[2]; A[m][i][1][2] = c0[3]; A[m][i][1][3] = c2[3];
@@ -522,7 +492,6 @@ int dispatch(int wfmt, int nt, const ExpertArgs& a, cudaStream_t s) {
   switch (wfmt) {
     case DSM_WFMT_F16: { DSM_NT_CASES(DSM_WFMT_F16) }
     case DSM_WFMT_FP8_B128: { DSM_NT_CASES(DSM_WFMT_FP8_B128) }
-    case DSM_WFMT_FP4_G32: { DSM_NT_CASES(DSM_WFMT_FP4_G32) }
     case DSM_WFMT_AFFINE8: { DSM_NT_CASES(DSM_WFMT_AFFINE8) }
     case DSM_WFMT_AFFINE4: { DSM_NT_CASES(DSM_WFMT_AFFINE4) }
     default: return fail(DSM_ERR_INVALID_ARGUMENT, "expert kernel: unknown weight format");
@@ -605,6 +574,9 @@ extern "C" int dsm_expert_gate_up(const void* x_staged, const float* x_row_scale
   a.h_scale = h_scale;
   a.h_out = static_cast<__half*>(h_staged);
   a.h_rows_cap = rows_cap;
+  if (wfmt == DSM_WFMT_FP4_G32)
+    return expert_tm_gate_up(x_staged, x_row_scale, rows_cap, dim, offsets, n_experts, w1_packed, w3_packed, inter, act,
+                             swiglu_limit, round_gu, h_staged, h_scale, n_rows, stream);
   if (use_tc(wfmt, n_rows, n_experts))
     return expert_tc_gate_up(wfmt, x_staged, x_row_scale, rows_cap, dim, offsets, n_experts, w1_packed, w3_packed, inter,
                              act, swiglu_limit, round_gu, h_staged, h_scale, n_rows, stream);
@@ -640,6 +612,9 @@ extern "C" int dsm_expert_down(const void* h_staged, float h_scale, int64_t rows
   a.o_row_map = o_row_map;
   a.ldo = ldo;
   a.round_o = round_o;
+  if (wfmt == DSM_WFMT_FP4_G32)
+    return expert_tm_down(h_staged, h_scale, rows_cap, inter, offsets, n_experts, w2_packed, dim, round_o, o_rows, ldo,
+                          o_row_map, n_rows, stream);
   if (use_tc(wfmt, n_rows, n_experts))
     return expert_tc_down(wfmt, h_staged, h_scale, rows_cap, inter, offsets, n_experts, w2_packed, dim, round_o, o_rows, ldo,
                           o_row_map, n_rows, stream);

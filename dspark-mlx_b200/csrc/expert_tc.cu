@@ -22,16 +22,15 @@
 // f16 in shared memory; the block scale is folded in there (one extra f16 rounding of the
 // weight, 2^-11 relative) because it changes every 128 K and a TMEM accumulator cannot be
 // rescaled between K blocks without reading it out.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <algorithm>
 #include <mutex>
 
-#include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace dsm {
 namespace {
+
+using namespace tc;
 
 constexpr int kTcM = 128;            // weight rows per unit = one scale row block
 constexpr int kTcK = 64;             // K per stage = one 128-byte swizzle row of f16
@@ -103,69 +102,6 @@ __device__ __forceinline__ int tc_find_expert(const int* pre, int n_experts, int
   }
   return lo;
 }
-
-__device__ __forceinline__ float tc_sigmoid(float v) { return 1.f / (1.f + expf(-v)); }
-
-__device__ __forceinline__ float tc_act(float g, float u, int act, float limit) {
-  if (act == DSM_ACT_SILU_MUL_BF16) {
-    const float sig = bf16_round(tc_sigmoid(g));
-    return bf16_round(g * sig) * u;
-  }
-  if (limit > 0.f) {
-    u = fminf(fmaxf(u, -limit), limit);
-    g = fminf(g, limit);
-  }
-  return g * tc_sigmoid(g) * u;
-}
-
-// ---- tcgen05 / TMA wrappers -----------------------------------------------------------
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
-          dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// K-major, SWIZZLE_128B operand: rows at 128 B, 8-row groups at 1024 B (SBO), LBO field 1.
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
-  return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
-         (uint64_t(1) << 46) | (uint64_t(2) << 61);
-}
-
-// kind::f16: D f32, A = B = f16, both K-major, N and M as given.
-__device__ __forceinline__ uint32_t umma_idesc_f16(int m, int n) {
-  return (1u << 4) | (0u << 7) | (0u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  const uint32_t no_mask = 0u;  // disable-output-lane mask: every lane written
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(no_mask)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 template <int FMT, bool DUAL>
 __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a,
@@ -471,35 +407,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
   }
 }
 
-// ---- host side ------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-// staged rows [chunks][rows_cap][160 halves] -> boxes of 64 halves x bn rows (128B swizzle)
-int make_stage_map(CUtensorMap* map, const void* staged, int64_t rows_cap, int k_chunks, int bn) {
-  auto enc = encode_fn();
-  if (!enc) return fail(DSM_ERR_CUDA, "expert_tc: cuTensorMapEncodeTiled unavailable");
-  const cuuint64_t dims[3] = {cuuint64_t(kStagePitch), cuuint64_t(rows_cap), cuuint64_t(k_chunks)};
-  const cuuint64_t strides[2] = {cuuint64_t(kStagePitch) * 2, cuuint64_t(rows_cap) * kStagePitch * 2};
-  const cuuint32_t box[3] = {cuuint32_t(kTcK), cuuint32_t(bn), 1};
-  const cuuint32_t estride[3] = {1, 1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(staged), dims, strides, box, estride,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(DSM_ERR_CUDA, "expert_tc: cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
-  return DSM_OK;
-}
-
 template <int FMT, bool DUAL>
 int launch_tc(const TcArgs& a, const void* staged, int64_t rows_cap, cudaStream_t stream) {
   using C = TcCfg<FMT, DUAL>;
@@ -516,6 +423,34 @@ int launch_tc(const TcArgs& a, const void* staged, int64_t rows_cap, cudaStream_
 }
 
 }  // namespace
+
+// ---- host side ------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int make_stage_map(CUtensorMap* map, const void* staged, int64_t rows_cap, int k_chunks, int box_rows) {
+  auto enc = encode_fn();
+  if (!enc) return fail(DSM_ERR_CUDA, "expert_tc: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {cuuint64_t(kStagePitch), cuuint64_t(rows_cap), cuuint64_t(k_chunks)};
+  const cuuint64_t strides[2] = {cuuint64_t(kStagePitch) * 2, cuuint64_t(rows_cap) * kStagePitch * 2};
+  const cuuint32_t box[3] = {cuuint32_t(kTcK), cuuint32_t(box_rows), 1};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(staged), dims, strides, box, estride,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DSM_ERR_CUDA, "expert_tc: cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  return DSM_OK;
+}
 
 // Entry points used by the expert dispatch (expert.cu) for the fp8 large-token regime.
 bool tc_supports(int wfmt) { return wfmt == DSM_WFMT_FP8_B128 || wfmt == DSM_WFMT_F16; }

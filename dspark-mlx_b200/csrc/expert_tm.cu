@@ -1,0 +1,479 @@
+// Grouped expert products for fp4 experts (e2m1 codes, e4m3 scale per 32 K, fp32 per-expert
+// tensor scale; dspark_mlx/loading.py:110-114 dequantisation, applied inside the products of
+// dspark_mlx/model/moe.py:132-149) at every token count: the weights are dequantised in
+// registers straight into tensor memory and multiplied there by tcgen05.
+//
+// Work unit = (expert e, 128 weight rows, up to BN of the expert's staged rows). Persistent
+// CTAs (one per SM), warp-specialised:
+//   warps 0-3   epilogue: tcgen05.ld of the accumulators (warp w reads TMEM lanes 32w..),
+//               per-expert tensor scale and activation row scale, SwiGLU (gate/up) or
+//               output rows (down);
+//   warp 4      producer: per 128-K stage, one bulk copy of each packed 8.5 KB weight tile
+//               (codes + group scales) and TMA loads of the unit's activation rows (16-row
+//               boxes of 64 f16, 128-byte swizzle) into a ring of shared-memory stages;
+//   warps 8-15  converters: each thread owns one weight row (its TMEM lane) and a K range of
+//               the stage: ld.shared.v4 of 32 codes, hardware e2m1 -> f16 conversion, one f16
+//               multiply by the group scale (exact: at most 6 significant bits), tcgen05.st
+//               into the A buffer;
+//   warps 16..  P MMA issuers (one thread each): tcgen05.mma kind::f16, M = 128, N = the
+//               unit's rows rounded up to 16, A read from TMEM, B (activations) from shared
+//               memory. One thread issues at most one such MMA every ~46 cycles whatever N
+//               is, so the 8 x (gate, up) MMAs of a stage are split over P threads, each
+//               accumulating its share of the k16 steps of one matrix into its own partial
+//               D in TMEM (two buffers, so an epilogue overlaps the next unit); the epilogue
+//               adds the partials.
+// The activations are read by the tensor core from shared memory, so no register traffic or
+// legacy MMA pipe is spent on them; the ALU work per weight byte is the conversion alone.
+//
+// Packed fp4 tile (128 rows x 128 K, written by dsm_pack_weights): codes [32-K chunk c][row]
+// [16 bytes], byte j of a chunk holding K 32c+2j (low nibble) and 32c+2j+1 (high nibble),
+// then the e4m3 group scales [row][chunk]. A warp's ld.shared.v4 of one chunk covers 32
+// consecutive rows: 512 contiguous bytes, no bank conflicts.
+#include <algorithm>
+
+#include "tcgen05.cuh"
+
+namespace dsm {
+namespace {
+
+using namespace tc;
+
+constexpr int kTmM = 128;
+constexpr int kTmEpiWarps = 4;    // warps 0-3
+constexpr int kTmProducer = 4;
+constexpr int kTmConv0 = 8;       // first converter warp (a multiple of 4: warp % 4 = TMEM sub-partition)
+constexpr int kTmBoxRows = 16;
+constexpr int kFp4CodeBytes = 8192;
+constexpr int kFp4TileBytes = 8192 + 512;
+
+template <bool DUAL, int BN, int CW, int P>
+struct TmCfg {
+  static constexpr int NM = DUAL ? 2 : 1;
+  static constexpr int kMma0 = kTmConv0 + CW;  // first MMA issuer warp
+  static constexpr int kThreads = 32 * (kMma0 + P);
+  static constexpr int kKkStride = P / NM;     // issuer p: matrix p % NM, k16 steps p / NM + j * kKkStride
+  static constexpr int kBHalf = BN * 128;  // one 64-K half of the activation rows
+  static constexpr int kOffRaw = 2 * kBHalf;
+  static constexpr int kStageBytes = (kOffRaw + NM * kFp4TileBytes + 1023) / 1024 * 1024;
+  static constexpr int kStages = std::min(8, (200 * 1024) / kStageBytes);
+  static constexpr int kDCols = 2 * P * BN;  // two buffers of P partial accumulators
+  static constexpr int kACols = NM * 64;      // one A buffer: 128 K of f16 per matrix
+  static constexpr int kABufs = std::min(4, (512 - kDCols) / kACols);
+  static constexpr int kParts = CW / 4;           // converter warps per TMEM sub-partition
+  static constexpr int kChunks = 4 / kParts;      // 32-K chunks per converter thread per matrix
+  static_assert(CW == 8 || CW == 16, "converter warps");
+  static_assert(P % NM == 0 && 8 % (P / NM) == 0, "issuers split the k16 steps evenly");
+  static_assert(kABufs >= 2, "TMEM budget");
+};
+
+struct TmArgs {
+  const uint8_t* wa;
+  const uint8_t* wb;
+  const float* act_scale;
+  float act_scale_const;
+  const int32_t* offsets;
+  int64_t n_rows;
+  int n_experts;
+  int out_rows;
+  int rt_count;
+  int kc_count;
+  int act;
+  float limit;
+  int round_gu;
+  float h_scale;
+  __half* h_out;
+  int64_t h_rows_cap;
+  float* o_out;
+  const int32_t* o_row_map;
+  int ldo;
+  int round_o;
+};
+
+__device__ __forceinline__ int tm_first(const TmArgs& a, int e) { return a.offsets ? a.offsets[e] : 0; }
+__device__ __forceinline__ int tm_count(const TmArgs& a, int e) {
+  return a.offsets ? a.offsets[e + 1] - a.offsets[e] : int(a.n_rows);
+}
+__device__ __forceinline__ int tm_find(const int* pre, int n, int u) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (pre[mid] <= u)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+template <bool DUAL, int BN, int CW, int P>
+__global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
+    expert_tm_kernel(const TmArgs a, const __grid_constant__ CUtensorMap xmap) {
+  using C = TmCfg<DUAL, BN, CW, P>;
+  constexpr int NM = C::NM, S = C::kStages, NA = C::kABufs;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw0 = smem_u32(smem_raw);
+  const uint32_t base = (raw0 + 1023u) & ~1023u;
+  uint8_t* sbase = smem_raw + (base - raw0);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sbase + S * C::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* afull = empty + S;
+  uint64_t* aempty = afull + NA;
+  uint64_t* tfull = aempty + NA;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* pre = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_slot + 2));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = a.n_experts;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], CW + P);  // converters done reading the codes + MMAs done reading B
+    }
+    for (int b = 0; b < NA; ++b) {
+      mbar_init(&afull[b], CW);
+      mbar_init(&aempty[b], P);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], P);
+      mbar_init(&tempty[b], kTmEpiWarps);
+    }
+    mbar_init(drain, P);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == C::kMma0) tmem_alloc(tmem_slot, 512);
+  if (warp == kTmProducer) {  // units per expert: rt_count x ceil(count / BN), scanned into pre[1..E]
+    int carry = 0;
+    if (lane == 0) pre[0] = 0;
+    for (int b0 = 0; b0 < E; b0 += 32) {
+      const int e = b0 + lane;
+      int v = 0;
+      if (e < E) {
+        const int cnt = tm_count(a, e);
+        v = cnt > 0 ? a.rt_count * ((cnt + BN - 1) / BN) : 0;
+      }
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      if (e < E) pre[e + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int total = pre[E];
+  const int64_t hdr_bytes = ceil_div(int64_t(E) * 4, kPackHeader) * kPackHeader;
+  const uint8_t* tiles_a = a.wa + hdr_bytes;
+  const uint8_t* tiles_b = DUAL ? a.wb + hdr_bytes : nullptr;
+  const int kcs = a.kc_count;
+
+  if (warp == kTmProducer) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        const int e = tm_find(pre, E, u);
+        const int cnt = tm_count(a, e);
+        const int nch = (cnt + BN - 1) / BN;
+        const int local = u - pre[e];
+        const int rt = local / nch, chunk = local % nch;
+        const int row0 = tm_first(a, e) + chunk * BN;
+        const int nbox = (min(BN, cnt - chunk * BN) + kTmBoxRows - 1) / kTmBoxRows;
+        const int64_t tile0 = (int64_t(e) * a.rt_count + rt) * kcs;
+        const uint32_t tx = uint32_t(NM * kFp4TileBytes + 2 * nbox * kTmBoxRows * 128);
+        for (int kc = 0; kc < kcs; ++kc) {
+          if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          uint8_t* st = sbase + s * C::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], tx);
+          bulk_g2s(st + C::kOffRaw, tiles_a + (tile0 + kc) * kFp4TileBytes, kFp4TileBytes, &full[s], pol_w);
+          if (DUAL)
+            bulk_g2s(st + C::kOffRaw + kFp4TileBytes, tiles_b + (tile0 + kc) * kFp4TileBytes, kFp4TileBytes,
+                     &full[s], pol_w);
+          for (int h = 0; h < 2; ++h)
+            for (int b = 0; b < nbox; ++b)
+              tma_load_3d(smem_u32(st + h * C::kBHalf + b * kTmBoxRows * 128), &xmap, h * 64, row0 + b * kTmBoxRows,
+                          kc, &full[s]);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (!ok)
+        for (int i = 0; i < 100; ++i) __nanosleep(1000);
+    }
+  } else if (warp >= C::kMma0) {
+    // ------------------------------------------------------------------ MMA issuers
+    const int p = warp - C::kMma0;
+    const int m = p % NM, kk0 = p / NM;
+    if (lane == 0) {
+      int s = 0, ab = 0;
+      uint32_t ph = 0, aph = 0;
+      bool ok = true;
+      int j = 0;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++j) {
+        const int e = tm_find(pre, E, u);
+        const int cnt = tm_count(a, e);
+        const int nch = (cnt + BN - 1) / BN;
+        const int chunk = (u - pre[e]) % nch;
+        const int n_mma = (min(BN, cnt - chunk * BN) + 15) / 16 * 16;
+        const uint32_t idesc = umma_idesc_f16(kTmM, n_mma);
+        const int buf = j & 1;
+        if (*abort_flag || !mbar_wait(&tempty[buf], ((j >> 1) & 1) ^ 1u)) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kc = 0; kc < kcs; ++kc) {
+          if (*abort_flag || !mbar_wait(&afull[ab], aph) || !mbar_wait(&full[s], ph)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(sbase + s * C::kStageBytes);
+          const uint32_t dcol = uint32_t((buf * P + p) * BN);
+#pragma unroll
+          for (int kk = kk0; kk < 8; kk += C::kKkStride) {
+            const uint64_t bdesc = umma_desc_sw128(st + (kk >> 2) * C::kBHalf) + uint64_t((kk & 3) * 2);
+            const uint32_t acol = uint32_t(C::kDCols + (ab * NM + m) * 64 + kk * 8);
+            umma_f16_tmem_a(tmem + dcol, tmem + acol, bdesc, idesc, (kc > 0 || kk > kk0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);   // activation rows read
+          umma_commit(&aempty[ab]);  // A buffer read
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+          if (++ab == NA) {
+            ab = 0;
+            aph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[buf]);
+      }
+      umma_commit(drain);  // every MMA of this thread completes before TMEM is released
+      mbar_wait(drain, 0);
+    }
+  } else if (warp >= kTmConv0) {
+    // ------------------------------------------------------------------ converters
+    const int sp = warp & 3;                     // TMEM sub-partition: lanes 32*sp ..
+    const int part = (warp - kTmConv0) >> 2;     // K range of the stage: chunks part*kChunks ..
+    const int row = 32 * sp + lane;              // weight row = TMEM lane
+    const uint32_t lane_base = tmem + (uint32_t(32 * sp) << 16);
+    int s = 0, ab = 0;
+    uint32_t ph = 0, aph = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+      for (int kc = 0; kc < kcs; ++kc) {
+        if (*abort_flag || !mbar_wait(&full[s], ph) || !mbar_wait(&aempty[ab], aph ^ 1u)) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t st = smem_u32(sbase + s * C::kStageBytes) + C::kOffRaw;
+#pragma unroll
+        for (int m = 0; m < NM; ++m) {
+          const uint32_t raw = st + m * kFp4TileBytes;
+          const uint32_t sw = lds32(raw + kFp4CodeBytes + row * 4);  // e4m3 scales of the 4 chunks
+          uint32_t out[16 * C::kChunks];
+#pragma unroll
+          for (int c = 0; c < C::kChunks; ++c) {
+            const int cc = part * C::kChunks + c;
+            const uint4 v = lds128(raw + (cc * kTmM + row) * 16);
+            const uint32_t sf = e4m3_to_f16_bits((sw >> (8 * cc)) & 0xFFu);
+            const uint32_t s2 = sf | (sf << 16);
+            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+              uint32_t o[4];
+              e2m1x8_to_f16(w4[wi], o);
+#pragma unroll
+              for (int t = 0; t < 4; ++t) out[16 * c + 4 * wi + t] = hmul2_bits(o[t], s2);
+            }
+          }
+          const uint32_t col = uint32_t(C::kDCols + (ab * NM + m) * 64 + part * 16 * C::kChunks);
+          if constexpr (C::kChunks == 2)
+            tmem_st32(lane_base + col, out);
+          else
+            tmem_st16(lane_base + col, out);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&afull[ab]);
+          mbar_arrive(&empty[s]);
+        }
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
+        }
+        if (++ab == NA) {
+          ab = 0;
+          aph ^= 1u;
+        }
+      }
+    }
+  } else if (warp < kTmEpiWarps) {
+    // ------------------------------------------------------------------ epilogue
+    const int rloc = 32 * warp + lane;
+    const uint32_t lane_base = tmem + (uint32_t(32 * warp) << 16);
+    int j = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++j) {
+      const int e = tm_find(pre, E, u);
+      const int off = tm_first(a, e);
+      const int cnt = tm_count(a, e);
+      const int nch = (cnt + BN - 1) / BN;
+      const int local = u - pre[e];
+      const int rt = local / nch, chunk = local % nch;
+      const int rows = min(BN, cnt - chunk * BN);
+      const int buf = j & 1;
+      if (*abort_flag || !mbar_wait(&tfull[buf], (j >> 1) & 1)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const float wmul_a = reinterpret_cast<const float*>(a.wa)[e];
+      const float wmul_b = DUAL ? reinterpret_cast<const float*>(a.wb)[e] : 1.f;
+      for (int cb = 0; cb < rows; cb += 16) {
+        // partial accumulators: issuer p holds matrix p % NM
+        uint32_t pv[P][16];
+#pragma unroll
+        for (int q = 0; q < P; ++q) tmem_ld16(lane_base + uint32_t((buf * P + q) * BN + cb), pv[q]);
+        tmem_ld_wait();
+        float gsum[16], usum[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          gsum[i] = 0.f;
+          usum[i] = 0.f;
+#pragma unroll
+          for (int q = 0; q < P; ++q) {
+            if (q % NM == 0)
+              gsum[i] += __uint_as_float(pv[q][i]);
+            else
+              usum[i] += __uint_as_float(pv[q][i]);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int col = cb + i;
+          if (col >= rows) break;
+          const int64_t r = int64_t(off) + chunk * BN + col;
+          const float xs = a.act_scale ? a.act_scale[r] : a.act_scale_const;
+          if constexpr (DUAL) {
+            float gg = gsum[i] * xs * wmul_a;
+            float uu = usum[i] * xs * wmul_b;
+            if (a.round_gu & 1) {
+              gg = bf16_round(gg);
+              uu = bf16_round(uu);
+            }
+            float h = tc_act(gg, uu, a.act, a.limit);
+            if (a.round_gu & 2) h = bf16_round(h);
+            a.h_out[(int64_t(rt) * a.h_rows_cap + r) * kStagePitch + rloc] = __float2half_rn(h * a.h_scale);
+          } else {
+            const int d = rt * kTmM + rloc;
+            if (d < a.out_rows) {
+              float v = gsum[i] * xs * wmul_a;
+              if (a.round_o) v = bf16_round(v);
+              const int64_t orow = a.o_row_map ? int64_t(a.o_row_map[r]) : r;
+              a.o_out[orow * a.ldo + d] = v;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == C::kMma0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <bool DUAL, int BN, int CW, int P>
+int launch_tm(const TmArgs& a, const void* staged, int64_t rows_cap, cudaStream_t stream) {
+  using C = TmCfg<DUAL, BN, CW, P>;
+  CUtensorMap map;
+  if (int rc = make_stage_map(&map, staged, rows_cap, a.kc_count, kTmBoxRows)) return rc;
+  const size_t smem = 1024 + size_t(C::kStages) * C::kStageBytes + 8 * (2 * C::kStages + 2 * C::kABufs + 5) + 16 +
+                      size_t(a.n_experts + 1) * 4;
+  auto kern = expert_tm_kernel<DUAL, BN, CW, P>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return check_launch("expert_tm smem attribute");
+  kern<<<num_sms(), C::kThreads, smem, stream>>>(a, map);
+  return check_launch("expert_tm");
+}
+
+constexpr int kTmBN = 32;
+constexpr int kTmCW = 8;
+constexpr int kTmP = 4;
+
+}  // namespace
+
+int expert_tm_gate_up(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int dim, const int32_t* offsets,
+                      int n_experts, const void* w1, const void* w3, int inter, int act, float limit, int round_gu,
+                      void* h_staged, float h_scale, int64_t n_rows, void* stream) {
+  TmArgs a{};
+  a.wa = static_cast<const uint8_t*>(w1);
+  a.wb = static_cast<const uint8_t*>(w3);
+  a.act_scale = x_row_scale;
+  a.act_scale_const = 1.f;
+  a.offsets = offsets;
+  a.n_rows = n_rows;
+  a.n_experts = n_experts;
+  a.out_rows = inter;
+  a.rt_count = int(ceil_div(inter, kTmM));
+  a.kc_count = int(ceil_div(dim, kChunkK));
+  a.act = act;
+  a.limit = limit;
+  a.round_gu = round_gu;
+  a.h_scale = h_scale;
+  a.h_out = static_cast<__half*>(h_staged);
+  a.h_rows_cap = rows_cap;
+  return launch_tm<true, kTmBN, kTmCW, kTmP>(a, x_staged, rows_cap, as_stream(stream));
+}
+
+int expert_tm_down(const void* h_staged, float h_scale, int64_t rows_cap, int inter, const int32_t* offsets,
+                   int n_experts, const void* w2, int dim, int round_o, float* o_rows, int ldo,
+                   const int32_t* o_row_map, int64_t n_rows, void* stream) {
+  TmArgs a{};
+  a.wa = static_cast<const uint8_t*>(w2);
+  a.wb = nullptr;
+  a.act_scale = nullptr;
+  a.act_scale_const = 1.f / h_scale;
+  a.offsets = offsets;
+  a.n_rows = n_rows;
+  a.n_experts = n_experts;
+  a.out_rows = dim;
+  a.rt_count = int(ceil_div(dim, kTmM));
+  a.kc_count = int(ceil_div(inter, kChunkK));
+  a.o_out = o_rows;
+  a.o_row_map = o_row_map;
+  a.ldo = ldo;
+  a.round_o = round_o;
+  return launch_tm<false, kTmBN, kTmCW, kTmP>(a, h_staged, rows_cap, as_stream(stream));
+}
+
+}  // namespace dsm

@@ -7,20 +7,23 @@
 //   header   float[E] per-expert multiplier (F16: power-of-two prescale; FP4: per-tensor
 //            scale; others 1), padded to a multiple of 256 bytes
 //   tiles    for e, for row tile rt (128 rows), for K chunk kc (128 columns):
-//              codes  [slab][m16 tile 0..7][lane 0..31][16 bytes]  -- one ld.shared.v4 per
-//                     lane per m16 tile per slab, already in mma.m16n8k16 A-fragment order
+//              codes  format dependent, below
 //              meta   per-tile scales (format dependent)
 //
+// F16, FP8, AFF8, AFF4 codes: [slab][m16 tile 0..7][lane 0..31][16 bytes] -- one
+// ld.shared.v4 per lane per m16 tile per slab, already in mma.m16n8k16 A-fragment order.
 // Lane (g = lane/4, q = lane%4) of m16 tile m holds rows r0 = 16m+g and r1 = r0+8; its
 // 16 bytes are [row r0 part][row r1 part] where the part covers K columns
 //   F16      (slab = 16 K): 4q .. 4q+3        (4 f16)
 //   FP8/AFF8 (slab = 32 K): 8q .. 8q+7        (8 bytes)
-//   FP4      (slab = 64 K): 16q .. 16q+15     (8 bytes, element 2j low nibble of byte j)
 //   AFF4     (slab = 64 K): 16q .. 16q+15     (8 bytes, nibble order k0,k2,k4,k6,k1,k3,k5,k7
 //                                              per 8 columns, for the magic-number unpack)
-// The expert kernel multiplies these against activations loaded with the same K subset per
+// The decode kernel multiplies these against activations loaded with the same K subset per
 // lane, which is a consistent permutation of K inside each MMA and leaves the dot product
 // unchanged.
+// FP4 codes: [32-K chunk c 0..3][row 0..127][16 bytes], byte j of a chunk = K 32c+2j (low
+// nibble) and 32c+2j+1 (high nibble): one converter thread per row reads a whole scale
+// group with one ld.shared.v4, and a warp reads 512 contiguous bytes.
 //
 // dsm_affine_quantize restates MLX's affine quantize (called by MoE.quantize,
 // dspark_mlx/model/moe.py:124-130): per group, an fp32 scale/bias with the edge of larger
@@ -90,7 +93,22 @@ __global__ void __launch_bounds__(256) pack_tiles_kernel(PackArgs a) {
   const int64_t R = a.rows, K = a.cols;
   float up = 1.f;
   if (a.wfmt == DSM_WFMT_F16) up = ldexpf(1.f, prescale_exp(a.header[e]));
-  for (int c = threadIdx.x; c < n_chunks; c += blockDim.x) {
+  if (a.wfmt == DSM_WFMT_FP4_G32) {  // row-sliced: [chunk][row][16 bytes]
+    const uint8_t* src = static_cast<const uint8_t*>(a.codes);
+    const int64_t kbytes = K / 2;
+    for (int c = threadIdx.x; c < n_chunks; c += blockDim.x) {
+      const int cc = c >> 7, rr = c & 127;
+      const int64_t r = int64_t(rt) * kTileRows + rr;
+      const int64_t kb0 = (int64_t(kc) * kChunkK + 32 * cc) / 2;
+      uint8_t out[16];
+      for (int j = 0; j < 16; ++j)
+        out[j] = (r < R && kb0 + j < kbytes) ? src[(int64_t(e) * R + r) * kbytes + kb0 + j] : uint8_t(0);
+      uint4 v;
+      memcpy(&v, out, 16);
+      *reinterpret_cast<uint4*>(dst + 16 * c) = v;
+    }
+  }
+  for (int c = threadIdx.x; c < n_chunks && a.wfmt != DSM_WFMT_FP4_G32; c += blockDim.x) {
     const int lane = c & 31, m = (c >> 5) & 7, slab = c >> 8;
     const int g = lane >> 2, q = lane & 3;
     const int64_t kb = int64_t(kc) * kChunkK + int64_t(slab) * slab_k;
@@ -118,13 +136,6 @@ __global__ void __launch_bounds__(256) pack_tiles_kernel(PackArgs a) {
         for (int j = 0; j < 8; ++j) {
           const int64_t k = kb + 8 * q + j;
           o[j] = (row_ok && k < K) ? src[(int64_t(e) * R + r) * K + k] : uint8_t(0);
-        }
-      } else if (a.wfmt == DSM_WFMT_FP4_G32) {
-        const uint8_t* src = static_cast<const uint8_t*>(a.codes);
-        const int64_t kbytes = K / 2;
-        for (int j = 0; j < 8; ++j) {
-          const int64_t kbyte = (kb + 16 * q) / 2 + j;
-          o[j] = (row_ok && kbyte < kbytes) ? src[(int64_t(e) * R + r) * kbytes + kbyte] : uint8_t(0);
         }
       } else {  // AFFINE4: source byte j = q(2j) | q(2j+1) << 4
         const uint8_t* src = static_cast<const uint8_t*>(a.codes);

@@ -179,6 +179,8 @@ FORMAT_CASES = [
     dict(base="fp8_decode", dim=384, inter=200, experts=12, topk=3, n_tokens=9),  # ragged (padding) shapes
     dict(base="fp4_decode", dim=512, inter=256, experts=16, topk=4, n_tokens=40),
     dict(base="fp4_decode", dim=512, inter=256, experts=8, topk=2, n_tokens=200),  # > 8 rows per expert
+    # skewed, many rows per expert: units of up to 64 rows running 1..8 n8 tiles
+    dict(base="fp4_decode", dim=512, inter=384, experts=16, topk=4, n_tokens=700),
     dict(base="fp8_decode", dim=512, inter=256, experts=16, topk=6, n_tokens=300, wfmt="bf16"),
 ]
 
@@ -198,8 +200,8 @@ def test_moe_forward_formats(case):
     assert max_rel_err(y, ref_y) < MOE_TOL, max_rel_err(y, ref_y)
 
 
-@pytest.mark.parametrize("bits", [8, 4])
-def test_affine_quantize_matches_oracle_and_forward(bits):
+@pytest.mark.parametrize("bits,n_tokens", [(8, 20), (4, 20), (8, 400), (4, 400)])
+def test_affine_quantize_matches_oracle_and_forward(bits, n_tokens):
     g = torch.Generator().manual_seed(21)
     w = (torch.randn(8, 256, 512, generator=g) * 0.05).to(torch.bfloat16)
     codes, s, b = affine_quantize(w.to(DEV), group_size=64, bits=bits)
@@ -208,7 +210,8 @@ def test_affine_quantize_matches_oracle_and_forward(bits):
     assert torch.equal(s.cpu().view(torch.int16), rs.view(torch.int16))
     assert torch.equal(b.cpu().view(torch.int16), rb.view(torch.int16))
     # quantised MoE vs the oracle's gather_qmm path
-    wl = small_workload("fp8_decode", dim=512, inter=256, experts=8, topk=2, n_tokens=20, wfmt="bf16", seed=4)
+    wl = small_workload("fp8_decode", dim=512, inter=256, experts=8, topk=2, n_tokens=n_tokens, wfmt="bf16", seed=4,
+                        zipf_alpha=1.2 if n_tokens > 100 else None)
     t = W.make_moe_tensors(wl, device="cpu")
     moe = W.build_moe(wl, t, DEV)
     moe.quantize(bits=bits, group_size=64)
