@@ -117,8 +117,7 @@ __global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(sbase + S * C::kStageBytes);
   uint64_t* empty = full + S;
   uint64_t* afull = empty + S;
-  uint64_t* aempty = afull + NA;
-  uint64_t* tfull = aempty + NA;
+  uint64_t* tfull = afull + NA;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -130,12 +129,10 @@ __global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], CW + P);  // converters done reading the codes + MMAs done reading B
+      // converters done reading the codes + MMAs done reading B and the stage's A buffer
+      mbar_init(&empty[s], CW + P);
     }
-    for (int b = 0; b < NA; ++b) {
-      mbar_init(&afull[b], CW);
-      mbar_init(&aempty[b], P);
-    }
+    for (int b = 0; b < NA; ++b) mbar_init(&afull[b], CW);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], P);
       mbar_init(&tempty[b], kTmEpiWarps);
@@ -222,9 +219,20 @@ __global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
     const int m = p % NM, kk0 = p / NM;
     if (lane == 0) {
       int s = 0, ab = 0;
-      uint32_t ph = 0, aph = 0;
+      uint32_t aph = 0;
       bool ok = true;
       int j = 0;
+      // descriptors and TMEM addresses, precomputed: one add per MMA in the loop
+      const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sbase));
+      constexpr int kSteps = 8 / C::kKkStride;  // k16 steps per stage of this issuer
+      uint64_t boff[kSteps];
+      uint32_t aoff[kSteps];
+#pragma unroll
+      for (int i = 0; i < kSteps; ++i) {
+        const int kk = kk0 + i * C::kKkStride;
+        boff[i] = uint64_t(((kk >> 2) * C::kBHalf + (kk & 3) * 32) >> 4);
+        aoff[i] = uint32_t(C::kDCols + m * 64 + kk * 8);
+      }
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++j) {
         const int e = tm_find(pre, E, u);
         const int cnt = tm_count(a, e);
@@ -239,27 +247,23 @@ __global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
           break;
         }
         tc_fence_after();
+        const uint32_t d = tmem + uint32_t((buf * P + p) * BN);
         for (int kc = 0; kc < kcs; ++kc) {
-          if (*abort_flag || !mbar_wait(&afull[ab], aph) || !mbar_wait(&full[s], ph)) {
+          // the converters arrive on afull only after they saw the stage's copies land
+          // (full[s]), so acquiring afull also orders the activation rows read below
+          if (*abort_flag || !mbar_wait(&afull[ab], aph)) {
             *abort_flag = 1;
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t st = smem_u32(sbase + s * C::kStageBytes);
-          const uint32_t dcol = uint32_t((buf * P + p) * BN);
+          const uint64_t bst = bdesc0 + uint64_t((s * C::kStageBytes) >> 4);
+          const uint32_t ast = tmem + uint32_t(ab * NM * 64);
 #pragma unroll
-          for (int kk = kk0; kk < 8; kk += C::kKkStride) {
-            const uint64_t bdesc = umma_desc_sw128(st + (kk >> 2) * C::kBHalf) + uint64_t((kk & 3) * 2);
-            const uint32_t acol = uint32_t(C::kDCols + (ab * NM + m) * 64 + kk * 8);
-            umma_f16_tmem_a(tmem + dcol, tmem + acol, bdesc, idesc, (kc > 0 || kk > kk0) ? 1u : 0u);
-          }
-          umma_commit(&empty[s]);   // activation rows read
-          umma_commit(&aempty[ab]);  // A buffer read
-          if (++s == S) {
-            s = 0;
-            ph ^= 1u;
-          }
+          for (int i = 0; i < kSteps; ++i)
+            umma_f16_tmem_a(d, ast + aoff[i], bst + boff[i], idesc, (kc > 0 || i > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);  // activation rows and the A buffer read
+          if (++s == S) s = 0;
           if (++ab == NA) {
             ab = 0;
             aph ^= 1u;
@@ -277,15 +281,29 @@ __global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
     const int part = (warp - kTmConv0) >> 2;     // K range of the stage: chunks part*kChunks ..
     const int row = 32 * sp + lane;              // weight row = TMEM lane
     const uint32_t lane_base = tmem + (uint32_t(32 * sp) << 16);
-    int s = 0, ab = 0;
-    uint32_t ph = 0, aph = 0;
+    // A buffer ab of stage g is free once the MMAs of stage g - NA completed: the empty
+    // barrier of that stage's slot (ws) in the phase of its lap (wph). That barrier cannot
+    // run a phase ahead: its next phase needs these converters' arrivals for a later stage.
+    int s = 0, ab = 0, g = 0, ws = 0;
+    uint32_t ph = 0, wph = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-      for (int kc = 0; kc < kcs; ++kc) {
-        if (*abort_flag || !mbar_wait(&full[s], ph) || !mbar_wait(&aempty[ab], aph ^ 1u)) {
+      for (int kc = 0; kc < kcs; ++kc, ++g) {
+        if (*abort_flag || !mbar_wait(&full[s], ph)) {
           *abort_flag = 1;
           ok = false;
           break;
+        }
+        if (g >= NA) {
+          if (*abort_flag || !mbar_wait(&empty[ws], wph)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          if (++ws == S) {
+            ws = 0;
+            wph ^= 1u;
+          }
         }
         tc_fence_after();
         const uint32_t st = smem_u32(sbase + s * C::kStageBytes) + C::kOffRaw;
@@ -326,10 +344,7 @@ __global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
           s = 0;
           ph ^= 1u;
         }
-        if (++ab == NA) {
-          ab = 0;
-          aph ^= 1u;
-        }
+        if (++ab == NA) ab = 0;
       }
     }
   } else if (warp < kTmEpiWarps) {
@@ -417,7 +432,7 @@ int launch_tm(const TmArgs& a, const void* staged, int64_t rows_cap, cudaStream_
   using C = TmCfg<DUAL, BN, CW, P>;
   CUtensorMap map;
   if (int rc = make_stage_map(&map, staged, rows_cap, a.kc_count, kTmBoxRows)) return rc;
-  const size_t smem = 1024 + size_t(C::kStages) * C::kStageBytes + 8 * (2 * C::kStages + 2 * C::kABufs + 5) + 16 +
+  const size_t smem = 1024 + size_t(C::kStages) * C::kStageBytes + 8 * (2 * C::kStages + C::kABufs + 5) + 16 +
                       size_t(a.n_experts + 1) * 4;
   auto kern = expert_tm_kernel<DUAL, BN, CW, P>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
