@@ -396,7 +396,7 @@ def run_gpu(args):
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp8 e4m3 weights x bf16 activations (f16 MMA, fp32 accumulate)",
+            "vs_baseline": None, "dtype": DTYPE_DESC.get(wl.wfmt, wl.wfmt),
             "data": "synthetic",
             "config": {"workload": wl.name, "tokens_per_step_per_gpu": N, "batch": wl.batch, "draft_block": wl.block,
                        "dim": dim, "n_experts": wl.args["n_routed_experts"], "topk": wl.args["n_activated_experts"],
@@ -422,6 +422,15 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+# arithmetic of the routed expert products per weight format
+DTYPE_DESC = {
+    "fp8": "fp8 e4m3 weights x bf16 activations (f16 MMA, fp32 accumulate)",
+    "fp4": "fp4 e2m1 weights (e4m3 group scales) x bf16 activations (f16 tcgen05 MMA, fp32 accumulate)",
+    "bf16": "bf16 weights x bf16 activations (f16 MMA, fp32 accumulate)",
+    "affine8": "8-bit affine weights x bf16 activations (f16 MMA, fp32 accumulate)",
+}
+
+
 def roofline_entry(ws, k_ms, k_bytes, k_touched, k_flops, k_tc, achieved, step_bytes, ms, hbm_peak, tc_peak,
                    peak_kind, traffic, wfmt="fp8"):
     """The roofline figure of the dominant kernel (or, for expert parallelism, of the step)."""
@@ -437,7 +446,9 @@ def roofline_entry(ws, k_ms, k_bytes, k_touched, k_flops, k_tc, achieved, step_b
                 "achieved": tflops, "peak": tc_peak, "unit": "TFLOP/s", "frac": tflops / tc_peak,
                 "peak_kind": peak_kind + " (dense bf16/f16 burst)", "algorithmic_flops_per_launch": k_flops,
                 "launch_ms": k_ms, "hbm_gbs": achieved, "traffic": None}
-    return {"bound": "hbm", "kernel": f"expert_kernel<{wfmt}, gate_up>", "achieved": achieved, "peak": hbm_peak,
+    kernel = ("expert_tm_kernel<gate_up> (e2m1 dequantised into TMEM, tcgen05 kind::f16)" if wfmt == "fp4"
+              else f"expert_kernel<{wfmt}, gate_up> (weight streaming, mma.sync)")
+    return {"bound": "hbm", "kernel": kernel, "achieved": achieved, "peak": hbm_peak,
             "unit": "GB/s", "frac": achieved / hbm_peak, "peak_kind": peak_kind,
             "frac_of_8tbs": achieved / SPEC_HBM_GBS, "algorithmic_bytes_per_launch": k_bytes, "launch_ms": k_ms,
             "touched_experts": k_touched, "traffic": traffic,
@@ -502,6 +513,209 @@ def time_gate_up(moe, x, ids, args, L, dev):
     return k_ms, w13 + act, touched, flops, tc
 
 
+QWEN3_METRIC = "Qwen3 draft-layer MLP tokens/s (8-bit affine, L2 flushed per step); HBM GB/s"
+QWEN3_KERNELS_PER_STEP = 3  # staging, gate/up, down
+
+
+def _qwen3_cpu_weights(mlp):
+    """The oracle's view of the projections, dequantised to fp32 once (the timed CPU leg then
+    measures the three matmuls and the elementwise ops, as the reference does after load)."""
+    import oracle
+
+    out = []
+    for p in (mlp.gate_proj, mlp.up_proj, mlp.down_proj):
+        if p.quant is None:
+            w = p.weight.detach().cpu().float()
+        else:
+            bits, gs = p.quant
+            w = oracle.OracleWeights("affine", p.q.cpu().unsqueeze(0), scales=p.scales.cpu().unsqueeze(0),
+                                     biases=p.biases.cpu().unsqueeze(0), group_size=gs, bits=bits).matrix(0)
+        out.append(oracle.OracleWeights("dense", w.unsqueeze(0).contiguous()))
+    return out
+
+
+def _qwen3_cpu_timed(x, weights, sample, budget_s, max_calls=1000):
+    import torch
+
+    import oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    xs = x[:sample].cpu()
+    oracle.qwen3_mlp(xs, *weights)
+    n, t0 = 0, time.perf_counter()
+    while n < max_calls and time.perf_counter() - t0 < budget_s:
+        oracle.qwen3_mlp(xs, *weights)
+        n += 1
+    el = time.perf_counter() - t0
+    return sample * n / el, n, el
+
+
+def run_qwen3(args):
+    """One step = one Qwen3 MLP call (hidden 2560, inter 9728, 8-bit affine g64) on 16 x 7
+    draft tokens. The quantised weights (79 MB) fit in L2, so L2 is flushed (a 256 MB write)
+    before every timed call, outside the CUDA-event bracket of that call."""
+    import ctypes
+
+    import torch
+
+    from dsm import _lib, workloads as W
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    wl = W.WORKLOADS[args.workload]
+    t = W.make_qwen3_tensors(wl, device=dev)
+    mlp = W.build_qwen3_mlp(wl, t, dev)
+    N, h, inter = wl.n_tokens, wl.args["hidden_size"], wl.args["intermediate_size"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4321 + rank)
+    xs = [t["x"]] + [torch.randn(N, h, generator=gen, device=dev).to(torch.bfloat16) for _ in range(3)]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        mlp(xs[i % 4])
+    torch.cuda.synchronize()
+
+    def timed(fn):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for i in range(args.steps):
+            flush.zero_()
+            evs[i][0].record(stream)
+            fn(i)
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs) / args.steps
+
+    _barrier(ws)
+    with ClockSampler(local) as clk:
+        ms = timed(lambda i: mlp(xs[i % 4]))
+    ms = _max_over_ranks(ms, ws, dev)
+    pg, pu, pd = mlp.gate_proj.packed(), mlp.up_proj.packed(), mlp.down_proj.packed()
+    weight_bytes = pg.nbytes + pu.nbytes + pd.nbytes
+    step_bytes = weight_bytes + 2 * N * h * 2
+    hbm_peak, _, peak_kind = _peaks()
+
+    # dominant kernel: the fused gate/up product, timed alone after the same flush
+    roofline = None
+    if not args.no_kernel_timing and ws == 1:
+        L = _lib.lib()
+        cap = L.dsm_stage_rows_cap(N)
+        xsb = torch.empty(L.dsm_stage_bytes(cap, h), dtype=torch.uint8, device=dev)
+        xsc = torch.empty(cap, dtype=torch.float32, device=dev)
+        hsb = torch.empty(L.dsm_stage_bytes(cap, inter), dtype=torch.uint8, device=dev)
+        sp = stream.cuda_stream
+        _lib.check(L.dsm_stage_rows(xs[0].data_ptr(), _lib.DT_BF16, N, h, None, N, 1, xsb.data_ptr(), cap,
+                                    xsc.data_ptr(), sp))
+
+        def gate_up(_i):
+            _lib.check(L.dsm_expert_gate_up(xsb.data_ptr(), xsc.data_ptr(), cap, h, None, 1, pg.wfmt, pg.group_size,
+                                            pg.packed.data_ptr(), pu.packed.data_ptr(), inter,
+                                            _lib.ACT_SILU_MUL_BF16, 0.0, 3, hsb.data_ptr(), 1.0 / 256, N, sp))
+
+        k_ms = timed(gate_up)
+        k_bytes = pg.nbytes + pu.nbytes + N * h * 2 + N * inter * 2
+        achieved = k_bytes / (k_ms * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "expert_kernel<affine8, gate_up> (weight streaming, mma.sync)",
+                    "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                    "peak_kind": peak_kind, "frac_of_8tbs": achieved / SPEC_HBM_GBS,
+                    "algorithmic_bytes_per_launch": k_bytes, "launch_ms": k_ms, "traffic": None}
+
+    e2e_ms = None
+    if not args.no_e2e:
+        xh = [x.cpu().pin_memory() for x in xs]
+        yh = torch.empty(N, h, dtype=torch.bfloat16).pin_memory()
+        for i in range(3):
+            yh.copy_(mlp(xh[i % 4].to(dev, non_blocking=True)), non_blocking=True)
+        torch.cuda.synchronize()
+
+        def e2e(i):
+            yh.copy_(mlp(xh[i % 4].to(dev, non_blocking=True)), non_blocking=True)
+
+        e2e_ms = _max_over_ranks(timed(e2e), ws, dev)
+
+    if rank == 0:
+        cpu = None
+        if ws == 1 and not args.no_cpu_baseline:
+            v, n, el = _qwen3_cpu_timed(t["x"], _qwen3_cpu_weights(mlp), min(8, N), args.cpu_seconds)
+            cpu = {"value": v, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+                   "sample": f"{min(8, N)} of the {N} tokens, {n} calls in {el:.1f} s; weights dequantised to "
+                             f"fp32 before timing; CPU restatement of Qwen3MLP.__call__ in PyTorch"}
+        line = {
+            "metric": QWEN3_METRIC, "value": ws * N / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": DTYPE_DESC["affine8"], "data": "synthetic",
+            "config": {"workload": wl.name, "tokens_per_step_per_gpu": N, "batch": wl.batch, "draft_block": wl.block,
+                       "hidden": h, "inter": inter, "weights": "affine8 g64 (bf16 scale, bias)",
+                       "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                       "l2": "flushed before every timed call (256 MB write outside the timed bracket)"},
+            "hbm_gbs_step": step_bytes / (ms * 1e-3) / 1e9,
+            "hbm_frac_of_8tbs_step": step_bytes / (ms * 1e-3) / 1e9 / SPEC_HBM_GBS,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": None if e2e_ms is None else {
+                "value": ws * N / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": N * h * 2,
+                "d2h_bytes_per_step": N * h * 2, "ms_per_step": e2e_ms},
+            "gpu_launches": QWEN3_KERNELS_PER_STEP * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line))
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def run_reference_qwen3(args):
+    ws, rank, _ = _dist()
+    if rank != 0:
+        return
+    import torch
+
+    from dsm import workloads as W
+
+    wl = W.WORKLOADS[args.workload]
+    t = W.make_qwen3_tensors(wl, device="cpu")
+    import oracle
+
+    ws_cpu = []
+    for n in ("gate_proj", "up_proj", "down_proj"):
+        q, sc, b = oracle.affine_quantize(t[n], 64, 8)
+        w = oracle.OracleWeights("affine", q.unsqueeze(0), scales=sc.unsqueeze(0), biases=b.unsqueeze(0),
+                                 group_size=64, bits=8).matrix(0)
+        ws_cpu.append(oracle.OracleWeights("dense", w.unsqueeze(0).contiguous()))
+    torch.set_num_threads(os.cpu_count() or 1)
+    sample = min(8, wl.n_tokens)
+    xs = t["x"][:sample]
+    vals = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        oracle.qwen3_mlp(xs, *ws_cpu)
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            vals.append(sample / dt)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": QWEN3_METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wl.n_tokens / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (bf16 in/out)",
+        "data": "synthetic",
+        "config": {"workload": wl.name, "tokens_per_step": wl.n_tokens, "hidden": wl.args["hidden_size"],
+                   "inter": wl.args["intermediate_size"], "weights": "affine8 g64"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+                         "sample": f"one call per step on {sample} of the {wl.n_tokens} tokens, weights dequantised "
+                                   f"to fp32 before timing; CPU restatement of Qwen3MLP.__call__ in PyTorch (mlx is "
+                                   f"not installable here)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -517,10 +731,11 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    qwen3 = args.workload.startswith("qwen3")
     if args.impl == "reference":
-        run_reference(args)
+        (run_reference_qwen3 if qwen3 else run_reference)(args)
     else:
-        run_gpu(args)
+        (run_qwen3 if qwen3 else run_gpu)(args)
 
 
 if __name__ == "__main__":

@@ -12,8 +12,9 @@ No dataset is involved: every tensor is drawn from a seeded ``torch.Generator``.
 * ``fp4_decode``   as fp8_decode with e2m1 codes (uniform over the 16 codes), e4m3 group-32
                    scales 2^U(-3, 3) and an fp32 per-expert scale 2^U(-9, -7); 448 tokens
                    (64 x 7); Zipf(1.1) routing skew.
-* ``qwen3_mlp_q8`` dense SwiGLU hidden 2560 / inter 9728, MLX affine 8-bit group 64,
-                   x [112, 2560] (16 x 7), no clamp.
+* ``qwen3_mlp_q8`` the Qwen3-4B-shaped dense draft layer's MLP: hidden 2560, inter 9728,
+                   bf16 weights N(0, 0.02) quantised to MLX affine 8-bit group 64 (bf16
+                   scale and bias), x bf16 N(0, 1) [112, 2560] (16 sequences x 7), no clamp.
 * ``prefill_fp8``  16384 tokens, 256 experts, top-8, fp8 experts, Zipf(1.2) skew.
 
 Zipf skew: expert ``e`` with popularity rank ``r_e`` (a seeded permutation) gets a selection
@@ -219,3 +220,29 @@ def expert_tensors(wl: Workload, experts, seed: Optional[int] = None) -> Dict[st
                 parts.setdefault(k, []).append(v)
         del one
     return {k: torch.cat(v, 0) for k, v in parts.items()}
+
+
+def make_qwen3_tensors(wl: Workload, device="cpu", seed: Optional[int] = None,
+                       n_tokens: Optional[int] = None) -> Dict[str, torch.Tensor]:
+    """x and the three bf16 projection weights of the Qwen3 MLP workload (before quantisation)."""
+    h, i = wl.args["hidden_size"], wl.args["intermediate_size"]
+    gen = torch.Generator(device=device)
+    gen.manual_seed(wl.seed if seed is None else seed)
+    out: Dict[str, torch.Tensor] = {"args": dict(wl.args)}
+    out["x"] = _randn((n_tokens or wl.n_tokens, h), gen, device, dtype=torch.bfloat16)
+    out["gate_proj"] = _randn((i, h), gen, device, std=0.02, dtype=torch.bfloat16)
+    out["up_proj"] = _randn((i, h), gen, device, std=0.02, dtype=torch.bfloat16)
+    out["down_proj"] = _randn((h, i), gen, device, std=0.02, dtype=torch.bfloat16)
+    return out
+
+
+def build_qwen3_mlp(wl: Workload, t: Dict[str, torch.Tensor], device="cuda", bits: int = 8, group_size: int = 64):
+    """A :class:`dsm.qwen3.Qwen3MLP` holding ``t``'s weights, quantised as ``quantize_drafter`` does."""
+    from .qwen3 import Qwen3MLP
+
+    mlp = Qwen3MLP(t["args"])
+    for n in ("gate_proj", "up_proj", "down_proj"):
+        getattr(mlp, n).weight = torch.nn.Parameter(t[n].to(device), requires_grad=False)
+    if wl.wfmt == "affine8":
+        mlp.quantize(bits=bits, group_size=group_size)
+    return mlp
