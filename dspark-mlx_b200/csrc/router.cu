@@ -34,9 +34,18 @@ __device__ __forceinline__ void dmma(double (&d)[2], double a, double b) {
                : "d"(a), "d"(b));
 }
 
-int router_k_slice(int64_t n_tokens, int dim) {
-  // decode-sized batches split K so the grid covers the GPU; large batches keep K whole
-  return n_tokens <= 256 ? 256 : int(ceil_div(dim, kPKS) * kPKS);
+// K slice of one partial-logit CTA. Decode-sized batches use 256. Larger batches split K
+// until the grid reaches ~2 CTAs per SM of a B200 (a fixed target, so the workspace query
+// and the launch agree on every device), with slices of at least 256; from ~2 000 tokens K
+// stays whole. The fp64 partials are summed in a fixed order: the logits do not depend on
+// the split beyond fp64 rounding.
+int router_k_slice(int64_t n_tokens, int dim, int n_experts) {
+  if (n_tokens <= 256) return 256;
+  constexpr int64_t kTargetCtas = 2 * 148;
+  const int64_t tiles = ceil_div(int64_t(n_experts), int64_t(kPE)) * ceil_div(n_tokens, int64_t(kPT));
+  int64_t slices = std::max<int64_t>(1, ceil_div(kTargetCtas, tiles));
+  slices = std::min<int64_t>(slices, std::max<int64_t>(1, dim / 256));
+  return int(ceil_div(ceil_div(int64_t(dim), slices), int64_t(kPKS)) * kPKS);
 }
 
 template <typename XT>
@@ -262,7 +271,7 @@ __global__ void __launch_bounds__(128) gate_topk_kernel(const float* __restrict_
 
 extern "C" size_t dsm_router_workspace_bytes(int64_t n_tokens, int dim, int n_experts) {
   if (n_tokens <= 0 || dim <= 0 || n_experts <= 0) return 256;
-  const int64_t slices = dsm::ceil_div(dim, dsm::router_k_slice(n_tokens, dim));
+  const int64_t slices = dsm::ceil_div(dim, dsm::router_k_slice(n_tokens, dim, n_experts));
   const size_t cells = size_t(n_tokens) * size_t(n_experts);
   return cells * (size_t(slices) * sizeof(double) + sizeof(float));
 }
@@ -290,7 +299,7 @@ extern "C" int dsm_router(const void* x, int x_dtype, int64_t n_tokens, int dim,
   }
   if (n_tokens == 0) return DSM_OK;
   cudaStream_t s = as_stream(stream);
-  const int k_slice = router_k_slice(n_tokens, dim);
+  const int k_slice = router_k_slice(n_tokens, dim, n_experts);
   const int n_slices = int(ceil_div(dim, k_slice));
   double* part = static_cast<double*>(workspace);
   float* logits = reinterpret_cast<float*>(part + int64_t(n_slices) * n_tokens * n_experts);
