@@ -35,13 +35,16 @@ int expert_tc_gate_up(int wfmt, const void* x_staged, const float* x_row_scale, 
 int expert_tc_down(int wfmt, const void* h_staged, float h_scale, int64_t rows_cap, int inter, const int32_t* offsets,
                    int n_experts, const void* w2, int dim, int round_o, float* o_rows, int ldo,
                    const int32_t* o_row_map, int64_t n_rows, void* stream);
-// fp4 experts at every token count (expert_tm.cu): weights dequantised into tensor memory
-int expert_tm_gate_up(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int dim, const int32_t* offsets,
-                      int n_experts, const void* w1, const void* w3, int inter, int act, float limit, int round_gu,
-                      void* h_staged, float h_scale, int64_t n_rows, void* stream);
-int expert_tm_down(const void* h_staged, float h_scale, int64_t rows_cap, int inter, const int32_t* offsets,
-                   int n_experts, const void* w2, int dim, int round_o, float* o_rows, int ldo,
-                   const int32_t* o_row_map, int64_t n_rows, void* stream);
+// fp4 and affine experts at every token count (expert_tm.cu): weights dequantised into
+// tensor memory
+bool tm_supports(int wfmt);
+int expert_tm_gate_up(int wfmt, int group_size, const void* x_staged, const float* x_row_scale, int64_t rows_cap,
+                      int dim, const int32_t* offsets, int n_experts, const void* w1, const void* w3, int inter,
+                      int act, float limit, int round_gu, void* h_staged, float h_scale, int64_t n_rows,
+                      void* stream);
+int expert_tm_down(int wfmt, int group_size, const void* h_staged, float h_scale, int64_t rows_cap, int inter,
+                   const int32_t* offsets, int n_experts, const void* w2, int dim, int round_o, float* o_rows,
+                   int ldo, const int32_t* o_row_map, int64_t n_rows, void* stream);
 // 0 = choose by rows per expert, 1 = always the decode kernel, 2 = tcgen05 where supported
 int expert_regime();
 
@@ -206,6 +209,16 @@ __device__ __forceinline__ void u4x8_to_f16_plus1024(uint32_t w, uint32_t (&o)[4
   o[1] = ((w >> 4) & 0x000F000Fu) | 0x64006400u;
   o[2] = ((w >> 8) & 0x000F000Fu) | 0x64006400u;
   o[3] = ((w >> 12) & 0x000F000Fu) | 0x64006400u;
+}
+__device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hfma2_bits(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
 __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
   uint32_t d;

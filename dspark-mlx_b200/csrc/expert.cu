@@ -7,18 +7,17 @@
 //
 // Per CTA: one producer warp issues, per pipeline stage (K chunk of 128), one bulk copy of
 // the packed weight tile (two for the fused gate/up pair) and one of the BN staged
-// activation rows into a ring of shared-memory stages (mbarrier complete_tx); four
-// consumer warps each own 32 weight rows, load their A fragments with one ld.shared.v4 per
+// activation rows into a ring of shared-memory stages (mbarrier complete_tx); eight
+// consumer warps each own 16 weight rows, load their A fragments with one ld.shared.v4 per
 // m16 tile (the packer stored them in fragment order), dequantise in registers (hardware
-// e4m3 -> f16 conversions, magic-number uint8/uint4 -> f16), and run
-// mma.sync m16n8k16 f16 x f16 -> fp32 against the activations. Weight streams are read
-// with an L2 evict-first policy, activations with evict-last.
+// e4m3 -> f16 conversion; f16 codes as they are), and run mma.sync m16n8k16 f16 x f16 ->
+// fp32 against the activations. Weight streams are read with an L2 evict-first policy,
+// activations with evict-last.
 //
-// Scales: fp8 128x128 block scales and affine group scale/bias are applied to fp32
-// partial sums at group boundaries (the affine bias term uses the activation group sums,
-// obtained with an all-ones MMA); the per-expert multiplier from the packed header (f16
-// prescale) and the activation row scale are applied in the epilogue. fp4 experts are
-// multiplied by the tensor-memory kernel (expert_tm.cu) at every token count.
+// Scales: the fp8 128x128 block scale is applied to each stage's fp32 partial sums; the
+// per-expert multiplier from the packed header (f16 prescale) and the activation row scale
+// are applied in the epilogue. fp4 and MLX affine experts are multiplied by the
+// tensor-memory kernel (expert_tm.cu) at every token count.
 //
 // Epilogue of the gate/up kernel: g, u -> (optional bf16 rounding, as bf16 / affine
 // weights give bf16 products in the reference) -> activation -> bf16 rounding (the
@@ -104,9 +103,9 @@ template <int FMT, bool DUAL, int NT>
 __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a, int n_stages) {
   constexpr int BN = 8 * NT;
   constexpr int NM = DUAL ? 2 : 1;
+  static_assert(FMT == DSM_WFMT_F16 || FMT == DSM_WFMT_FP8_B128, "f16 and fp8 tiles only");
   constexpr bool kBlockScaled = FMT == DSM_WFMT_FP8_B128;
-  constexpr bool kAffine = FMT == DSM_WFMT_AFFINE8 || FMT == DSM_WFMT_AFFINE4;
-  constexpr bool kTmp = kBlockScaled || kAffine;
+  constexpr bool kTmp = kBlockScaled;
   extern __shared__ __align__(1024) uint8_t smem[];
 
   const int tile_b = tile_bytes(FMT, a.group_size);
@@ -200,8 +199,6 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
   const int g = lane >> 2, q = lane & 3;
   int s = 0;
   uint32_t ph = 0;
-  const uint32_t ones = 0x3C003C00u;  // f16x2 (1, 1)
-  const uint32_t ones_a[4] = {ones, ones, ones, ones};
   for (int u = blockIdx.x; u < total; u += gridDim.x) {
     const int e = find_expert(pre, E, u);
     const int off = group_first(a, e);
@@ -212,7 +209,6 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
 
     float acc[NM][kMt][NT][4];
     float tmp[kTmp ? NM : 1][kMt][NT][4];
-    float xsum[kAffine ? NT : 1][4];
 #pragma unroll
     for (int m = 0; m < NM; ++m)
 #pragma unroll
@@ -224,10 +220,6 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
             acc[m][i][j][c] = 0.f;
             if (kTmp) tmp[m < (kTmp ? NM : 1) ? m : 0][i][j][c] = 0.f;
           }
-#pragma unroll
-    for (int j = 0; j < (kAffine ? NT : 1); ++j)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) xsum[j][c] = 0.f;
 
     bool ok = true;
     for (int kc = 0; kc < a.kc_count; ++kc) {
@@ -262,8 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
               for (int i = 0; i < kMt; ++i) mma_f16(acc[m][i][j], A[m][i], xb.x, xb.y);
           }
         }
-      } else if constexpr (FMT == DSM_WFMT_FP8_B128 || FMT == DSM_WFMT_AFFINE8) {
-        const int slabs_per_group = kAffine ? a.group_size / 32 : 4;
+      } else {  // FP8_B128: 128x128 block scale applied to the stage's fp32 partials
 #pragma unroll
         for (int sl = 0; sl < 4; ++sl) {
           uint32_t A[NM][kMt][2][4];  // [matrix][m16 tile][mma 0/1][regs]
@@ -272,17 +263,10 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
 #pragma unroll
             for (int i = 0; i < kMt; ++i) {
               const uint4 v = lds128(st + m * tile_b + ((sl * 8 + kMt * warp + i) * 32 + lane) * 16);
-              if constexpr (FMT == DSM_WFMT_FP8_B128) {
-                e4m3x4_to_f16(v.x, A[m][i][0][0], A[m][i][0][2]);
-                e4m3x4_to_f16(v.y, A[m][i][1][0], A[m][i][1][2]);
-                e4m3x4_to_f16(v.z, A[m][i][0][1], A[m][i][0][3]);
-                e4m3x4_to_f16(v.w, A[m][i][1][1], A[m][i][1][3]);
-              } else {
-                u8x4_to_f16_plus1024(v.x, A[m][i][0][0], A[m][i][0][2]);
-                u8x4_to_f16_plus1024(v.y, A[m][i][1][0], A[m][i][1][2]);
-                u8x4_to_f16_plus1024(v.z, A[m][i][0][1], A[m][i][0][3]);
-                u8x4_to_f16_plus1024(v.w, A[m][i][1][1], A[m][i][1][3]);
-              }
+              e4m3x4_to_f16(v.x, A[m][i][0][0], A[m][i][0][2]);
+              e4m3x4_to_f16(v.y, A[m][i][1][0], A[m][i][1][2]);
+              e4m3x4_to_f16(v.z, A[m][i][0][1], A[m][i][0][3]);
+              e4m3x4_to_f16(v.w, A[m][i][1][1], A[m][i][1][3]);
             }
 #pragma unroll
           for (int j = 0; j < NT; ++j) {
@@ -294,40 +278,6 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
                 mma_f16(tmp[m][i][j], A[m][i][0], xb.x, xb.y);
                 mma_f16(tmp[m][i][j], A[m][i][1], xb.z, xb.w);
               }
-            if constexpr (kAffine) {
-              mma_f16(xsum[j < (kAffine ? NT : 1) ? j : 0], ones_a, xb.x, xb.y);
-              mma_f16(xsum[j < (kAffine ? NT : 1) ? j : 0], ones_a, xb.z, xb.w);
-            }
-          }
-          if constexpr (kAffine) {
-            if ((sl + 1) % slabs_per_group == 0) {
-              const int grp = (sl + 1) / slabs_per_group - 1;
-              const int gpt = kChunkK / a.group_size;
-#pragma unroll
-              for (int m = 0; m < NM; ++m)
-#pragma unroll
-                for (int i = 0; i < kMt; ++i) {
-                  const int r0 = 16 * (kMt * warp + i) + g;
-                  const uint32_t sb0 = lds32(st + m * tile_b + tile_code_bytes(FMT) + (r0 * gpt + grp) * 4);
-                  const uint32_t sb1 = lds32(st + m * tile_b + tile_code_bytes(FMT) + ((r0 + 8) * gpt + grp) * 4);
-                  const float s0 = __uint_as_float(sb0 << 16), b0 = __uint_as_float(sb0 & 0xFFFF0000u);
-                  const float s1 = __uint_as_float(sb1 << 16), b1 = __uint_as_float(sb1 & 0xFFFF0000u);
-                  const float c0 = fmaf(-1024.f, s0, b0), c1 = fmaf(-1024.f, s1, b1);
-#pragma unroll
-                  for (int j = 0; j < NT; ++j) {
-                    acc[m][i][j][0] += s0 * tmp[m][i][j][0] + c0 * xsum[j][0];
-                    acc[m][i][j][1] += s0 * tmp[m][i][j][1] + c0 * xsum[j][1];
-                    acc[m][i][j][2] += s1 * tmp[m][i][j][2] + c1 * xsum[j][2];
-                    acc[m][i][j][3] += s1 * tmp[m][i][j][3] + c1 * xsum[j][3];
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) tmp[m][i][j][c] = 0.f;
-                  }
-                }
-#pragma unroll
-              for (int j = 0; j < NT; ++j)
-#pragma unroll
-                for (int c = 0; c < 4; ++c) xsum[j][c] = 0.f;
-            }
           }
         }
         if constexpr (kBlockScaled) {
@@ -343,82 +293,6 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
                   acc[m][i][j][c] = fmaf(sc, tmp[m][i][j][c], acc[m][i][j][c]);
                   tmp[m][i][j][c] = 0.f;
                 }
-          }
-        }
-      } else {  // AFFINE4 (slab = 64 K); fp4 experts run in expert_tm.cu
-        const int slabs_per_group = a.group_size / 64;
-#pragma unroll
-        for (int sl = 0; sl < 2; ++sl) {
-          uint32_t A[NM][kMt][4][4];  // [matrix][m16][mma t][regs]
-#pragma unroll
-          for (int m = 0; m < NM; ++m)
-#pragma unroll
-            for (int i = 0; i < kMt; ++i) {
-              const uint4 v = lds128(st + m * tile_b + ((sl * 8 + kMt * warp + i) * 32 + lane) * 16);
-              uint32_t c0[4], c1[4], c2[4], c3[4];
-              u4x8_to_f16_plus1024(v.x, c0);
-              u4x8_to_f16_plus1024(v.y, c1);
-              u4x8_to_f16_plus1024(v.z, c2);
-              u4x8_to_f16_plus1024(v.w, c3);
-              // mma t covers K 4t..4t+3 of this lane's 16: regs (k 4t,4t+1) and (k 4t+2,4t+3)
-              A[m][i][0][0] = c0[0]; A[m][i][0][1] = c2[0]; A[m][i][0][2] = c0[1]; A[m][i][0][3] = c2[1];
-              A[m][i][1][0] = c0[2]; A[m][i][1][1] = c2[2]; A[m][i][1][2] = c0[3]; A[m][i][1][3] = c2[3];
-              A[m][i][2][0] = c1[0]; A[m][i][2][1] = c3[0]; A[m][i][2][2] = c1[1]; A[m][i][2][3] = c3[1];
-              A[m][i][3][0] = c1[2]; A[m][i][3][1] = c3[2]; A[m][i][3][2] = c1[3]; A[m][i][3][3] = c3[3];
-            }
-#pragma unroll
-          for (int j = 0; j < NT; ++j) {
-            const int n = j * 8 + g;
-            const uint32_t base = sx + n * (kStagePitch * 2) + sl * 128 + q * 32;
-            const uint32_t odd = uint32_t(n & 1) * 16u;  // odd rows load their halves swapped
-            const uint4 p0 = lds128(base + odd);
-            const uint4 p1 = lds128(base + (16u - odd));
-            const uint4 lo = (n & 1) ? p1 : p0;
-            const uint4 hi = (n & 1) ? p0 : p1;
-            const uint32_t xr[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-#pragma unroll
-              for (int m = 0; m < NM; ++m)
-#pragma unroll
-                for (int i = 0; i < kMt; ++i) {
-                  if constexpr (kAffine)
-                    mma_f16(tmp[m][i][j], A[m][i][t], xr[2 * t], xr[2 * t + 1]);
-                  else
-                    mma_f16(acc[m][i][j], A[m][i][t], xr[2 * t], xr[2 * t + 1]);
-                }
-              if constexpr (kAffine) mma_f16(xsum[j < (kAffine ? NT : 1) ? j : 0], ones_a, xr[2 * t], xr[2 * t + 1]);
-            }
-          }
-          if constexpr (kAffine) {
-            if ((sl + 1) % slabs_per_group == 0) {
-              const int grp = (sl + 1) / slabs_per_group - 1;
-              const int gpt = kChunkK / a.group_size;
-#pragma unroll
-              for (int m = 0; m < NM; ++m)
-#pragma unroll
-                for (int i = 0; i < kMt; ++i) {
-                  const int r0 = 16 * (kMt * warp + i) + g;
-                  const uint32_t sb0 = lds32(st + m * tile_b + tile_code_bytes(FMT) + (r0 * gpt + grp) * 4);
-                  const uint32_t sb1 = lds32(st + m * tile_b + tile_code_bytes(FMT) + ((r0 + 8) * gpt + grp) * 4);
-                  const float s0 = __uint_as_float(sb0 << 16), b0 = __uint_as_float(sb0 & 0xFFFF0000u);
-                  const float s1 = __uint_as_float(sb1 << 16), b1 = __uint_as_float(sb1 & 0xFFFF0000u);
-                  const float c0 = fmaf(-1024.f, s0, b0), c1 = fmaf(-1024.f, s1, b1);
-#pragma unroll
-                  for (int j = 0; j < NT; ++j) {
-                    acc[m][i][j][0] += s0 * tmp[m][i][j][0] + c0 * xsum[j][0];
-                    acc[m][i][j][1] += s0 * tmp[m][i][j][1] + c0 * xsum[j][1];
-                    acc[m][i][j][2] += s1 * tmp[m][i][j][2] + c1 * xsum[j][2];
-                    acc[m][i][j][3] += s1 * tmp[m][i][j][3] + c1 * xsum[j][3];
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) tmp[m][i][j][c] = 0.f;
-                  }
-                }
-#pragma unroll
-              for (int j = 0; j < NT; ++j)
-#pragma unroll
-                for (int c = 0; c < 4; ++c) xsum[j][c] = 0.f;
-            }
           }
         }
       }
@@ -492,8 +366,6 @@ int dispatch(int wfmt, int nt, const ExpertArgs& a, cudaStream_t s) {
   switch (wfmt) {
     case DSM_WFMT_F16: { DSM_NT_CASES(DSM_WFMT_F16) }
     case DSM_WFMT_FP8_B128: { DSM_NT_CASES(DSM_WFMT_FP8_B128) }
-    case DSM_WFMT_AFFINE8: { DSM_NT_CASES(DSM_WFMT_AFFINE8) }
-    case DSM_WFMT_AFFINE4: { DSM_NT_CASES(DSM_WFMT_AFFINE4) }
     default: return fail(DSM_ERR_INVALID_ARGUMENT, "expert kernel: unknown weight format");
   }
 #undef DSM_NT_CASES
@@ -574,9 +446,9 @@ extern "C" int dsm_expert_gate_up(const void* x_staged, const float* x_row_scale
   a.h_scale = h_scale;
   a.h_out = static_cast<__half*>(h_staged);
   a.h_rows_cap = rows_cap;
-  if (wfmt == DSM_WFMT_FP4_G32)
-    return expert_tm_gate_up(x_staged, x_row_scale, rows_cap, dim, offsets, n_experts, w1_packed, w3_packed, inter, act,
-                             swiglu_limit, round_gu, h_staged, h_scale, n_rows, stream);
+  if (tm_supports(wfmt))
+    return expert_tm_gate_up(wfmt, group_size, x_staged, x_row_scale, rows_cap, dim, offsets, n_experts, w1_packed,
+                             w3_packed, inter, act, swiglu_limit, round_gu, h_staged, h_scale, n_rows, stream);
   if (use_tc(wfmt, n_rows, n_experts))
     return expert_tc_gate_up(wfmt, x_staged, x_row_scale, rows_cap, dim, offsets, n_experts, w1_packed, w3_packed, inter,
                              act, swiglu_limit, round_gu, h_staged, h_scale, n_rows, stream);
@@ -612,9 +484,9 @@ extern "C" int dsm_expert_down(const void* h_staged, float h_scale, int64_t rows
   a.o_row_map = o_row_map;
   a.ldo = ldo;
   a.round_o = round_o;
-  if (wfmt == DSM_WFMT_FP4_G32)
-    return expert_tm_down(h_staged, h_scale, rows_cap, inter, offsets, n_experts, w2_packed, dim, round_o, o_rows, ldo,
-                          o_row_map, n_rows, stream);
+  if (tm_supports(wfmt))
+    return expert_tm_down(wfmt, group_size, h_staged, h_scale, rows_cap, inter, offsets, n_experts, w2_packed, dim,
+                          round_o, o_rows, ldo, o_row_map, n_rows, stream);
   if (use_tc(wfmt, n_rows, n_experts))
     return expert_tc_down(wfmt, h_staged, h_scale, rows_cap, inter, offsets, n_experts, w2_packed, dim, round_o, o_rows, ldo,
                           o_row_map, n_rows, stream);

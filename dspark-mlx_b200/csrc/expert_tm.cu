@@ -1,7 +1,9 @@
 // Grouped expert products for fp4 experts (e2m1 codes, e4m3 scale per 32 K, fp32 per-expert
-// tensor scale; dspark_mlx/loading.py:110-114 dequantisation, applied inside the products of
-// dspark_mlx/model/moe.py:132-149) at every token count: the weights are dequantised in
-// registers straight into tensor memory and multiplied there by tcgen05.
+// tensor scale; dspark_mlx/loading.py:110-114 dequantisation) and MLX affine 8/4-bit experts
+// (MoE.quantize, dspark_mlx/model/moe.py:124-130, and the Qwen3 MLP's QuantizedLinears),
+// applied inside the products of dspark_mlx/model/moe.py:132-149, at every token count: the
+// weights are dequantised in registers straight into tensor memory and multiplied there by
+// tcgen05.
 //
 // Work unit = (expert e, 128 weight rows, up to BN of the expert's staged rows). Persistent
 // CTAs (one per SM), warp-specialised:
@@ -12,9 +14,15 @@
 //               (codes + group scales) and TMA loads of the unit's activation rows (16-row
 //               boxes of 64 f16, 128-byte swizzle) into a ring of shared-memory stages;
 //   warps 8-15  converters: each thread owns one weight row (its TMEM lane) and a K range of
-//               the stage: ld.shared.v4 of 32 codes, hardware e2m1 -> f16 conversion, one f16
-//               multiply by the group scale (exact: at most 6 significant bits), tcgen05.st
-//               into the A buffer;
+//               the stage, read with ld.shared.v4 (16 bytes per chunk), converted and
+//               written into the A buffer with tcgen05.st:
+//                 fp4    hardware e2m1 -> f16 conversion, one f16 multiply by the group
+//                        scale (exact: at most 6 significant bits);
+//                 affine magic-number uint8 / uint4 -> f16, then one f16 fma with the
+//                        group's scale and bias, both pre-multiplied at pack time by the
+//                        expert's power-of-two prescale (max |w| -> [2^14, 2^15)); the
+//                        epilogue undoes the prescale. One f16 rounding of each weight,
+//                        2^-11 relative, where MLX dequantises in fp32;
 //   warps 16..  P MMA issuers (one thread each): tcgen05.mma kind::f16, M = 128, N = the
 //               unit's rows rounded up to 16, A read from TMEM, B (activations) from shared
 //               memory. One thread issues at most one such MMA every ~46 cycles whatever N
@@ -25,10 +33,11 @@
 // The activations are read by the tensor core from shared memory, so no register traffic or
 // legacy MMA pipe is spent on them; the ALU work per weight byte is the conversion alone.
 //
-// Packed fp4 tile (128 rows x 128 K, written by dsm_pack_weights): codes [32-K chunk c][row]
-// [16 bytes], byte j of a chunk holding K 32c+2j (low nibble) and 32c+2j+1 (high nibble),
-// then the e4m3 group scales [row][chunk]. A warp's ld.shared.v4 of one chunk covers 32
-// consecutive rows: 512 contiguous bytes, no bank conflicts.
+// Packed tiles (128 rows x 128 K, written by dsm_pack_weights): codes [16-byte chunk][row]
+// [16 bytes] (fp4 and 4-bit affine: 32 K per chunk; 8-bit affine: 16 K), then the scales:
+// fp4 e4m3 [row][32-K group]; affine f16 (scale, bias) pairs [row][group]. A warp's
+// ld.shared.v4 of one chunk covers 32 consecutive rows: 512 contiguous bytes, no bank
+// conflicts.
 #include <algorithm>
 
 #include "tcgen05.cuh"
@@ -43,28 +52,40 @@ constexpr int kTmEpiWarps = 4;    // warps 0-3
 constexpr int kTmProducer = 4;
 constexpr int kTmConv0 = 8;       // first converter warp (a multiple of 4: warp % 4 = TMEM sub-partition)
 constexpr int kTmBoxRows = 16;
-constexpr int kFp4CodeBytes = 8192;
-constexpr int kFp4TileBytes = 8192 + 512;
 
-template <bool DUAL, int BN, int CW, int P>
+template <int FMT, bool DUAL, int BN, int CW, int P>
 struct TmCfg {
+  static constexpr bool kAffine = FMT != DSM_WFMT_FP4_G32;
+  static constexpr bool kB8 = FMT == DSM_WFMT_AFFINE8;
+  static constexpr int kCodeBytes = kB8 ? 16384 : 8192;
+  static constexpr int kChunkK = kB8 ? 16 : 32;         // K per 16-byte chunk
+  static constexpr int kRowChunks = 128 / kChunkK;      // chunks per row of a tile
   static constexpr int NM = DUAL ? 2 : 1;
+  // 128-K chunks per stage: two for the single-matrix (down) product, whose tiles carry half
+  // the bytes of a gate/up pair, so the per-stage barrier, copy and commit costs are spread
+  // over the same bytes; the gate/up pair keeps one (its A buffer is already 128 columns)
+  static constexpr int KS = DUAL ? 1 : 2;
   static constexpr int kMma0 = kTmConv0 + CW;  // first MMA issuer warp
   static constexpr int kThreads = 32 * (kMma0 + P);
   static constexpr int kKkStride = P / NM;     // issuer p: matrix p % NM, k16 steps p / NM + j * kKkStride
-  static constexpr int kBHalf = BN * 128;  // one 64-K half of the activation rows
-  static constexpr int kOffRaw = 2 * kBHalf;
-  static constexpr int kStageBytes = (kOffRaw + NM * kFp4TileBytes + 1023) / 1024 * 1024;
-  static constexpr int kStages = std::min(8, (200 * 1024) / kStageBytes);
+  static constexpr int kBHalf = BN * 128;    // one 64-K half of the activation rows
+  static constexpr int kOffRaw = 2 * KS * kBHalf;
   static constexpr int kDCols = 2 * P * BN;  // two buffers of P partial accumulators
-  static constexpr int kACols = NM * 64;      // one A buffer: 128 K of f16 per matrix
+  static constexpr int kACols = NM * KS * 64;  // one A buffer: KS x 128 K of f16 per matrix
+  static constexpr int kSteps = 8 * KS / kKkStride;  // k16 steps of one issuer per full stage
   static constexpr int kABufs = std::min(4, (512 - kDCols) / kACols);
-  static constexpr int kParts = CW / 4;           // converter warps per TMEM sub-partition
-  static constexpr int kChunks = 4 / kParts;      // 32-K chunks per converter thread per matrix
+  static constexpr int kParts = CW / 4;            // converter warps per TMEM sub-partition
+  static constexpr int kChunks = kRowChunks / kParts;  // chunks per converter thread per matrix
+  static constexpr int kCols = kChunks * kChunkK / 2;  // TMEM columns per converter thread per matrix
   static_assert(CW == 8 || CW == 16, "converter warps");
   static_assert(P % NM == 0 && 8 % (P / NM) == 0, "issuers split the k16 steps evenly");
   static_assert(kABufs >= 2, "TMEM budget");
+  static_assert(kCols == 16 || kCols == 32, "converter store width");
 };
+
+// shared-memory stage: [activation rows: KS chunks x 2 x 64-K halves][packed tile x KS x NM],
+// 1024-aligned
+inline int tm_stage_bytes(int off_raw, int tiles, int tile_b) { return (off_raw + tiles * tile_b + 1023) / 1024 * 1024; }
 
 struct TmArgs {
   const uint8_t* wa;
@@ -77,6 +98,9 @@ struct TmArgs {
   int out_rows;
   int rt_count;
   int kc_count;
+  int group_size;  // affine
+  int tile_b;      // packed tile bytes
+  int stage_b;     // shared-memory stage bytes
   int act;
   float limit;
   int round_gu;
@@ -105,16 +129,18 @@ __device__ __forceinline__ int tm_find(const int* pre, int n, int u) {
   return lo;
 }
 
-template <bool DUAL, int BN, int CW, int P>
-__global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
-    expert_tm_kernel(const TmArgs a, const __grid_constant__ CUtensorMap xmap) {
-  using C = TmCfg<DUAL, BN, CW, P>;
-  constexpr int NM = C::NM, S = C::kStages, NA = C::kABufs;
+template <int FMT, bool DUAL, int BN, int CW, int P>
+__global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
+    expert_tm_kernel(const TmArgs a, const __grid_constant__ CUtensorMap xmap, int n_stages) {
+  using C = TmCfg<FMT, DUAL, BN, CW, P>;
+  constexpr int NM = C::NM, NA = C::kABufs;
+  const int S = n_stages;
+  const int stage_b = a.stage_b, tile_b = a.tile_b;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw0 = smem_u32(smem_raw);
   const uint32_t base = (raw0 + 1023u) & ~1023u;
   uint8_t* sbase = smem_raw + (base - raw0);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sbase + S * C::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sbase + S * stage_b);
   uint64_t* empty = full + S;
   uint64_t* afull = empty + S;
   uint64_t* tfull = afull + NA;
@@ -187,23 +213,25 @@ __global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
         const int row0 = tm_first(a, e) + chunk * BN;
         const int nbox = (min(BN, cnt - chunk * BN) + kTmBoxRows - 1) / kTmBoxRows;
         const int64_t tile0 = (int64_t(e) * a.rt_count + rt) * kcs;
-        const uint32_t tx = uint32_t(NM * kFp4TileBytes + 2 * nbox * kTmBoxRows * 128);
-        for (int kc = 0; kc < kcs; ++kc) {
+        const uint32_t tx1 = uint32_t(NM * tile_b + 2 * nbox * kTmBoxRows * 128);  // per chunk
+        for (int kc = 0; kc < kcs; kc += C::KS) {
+          const int nk = min(C::KS, kcs - kc);
           if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u)) {
             *abort_flag = 1;
             ok = false;
             break;
           }
-          uint8_t* st = sbase + s * C::kStageBytes;
-          mbar_arrive_expect_tx(&full[s], tx);
-          bulk_g2s(st + C::kOffRaw, tiles_a + (tile0 + kc) * kFp4TileBytes, kFp4TileBytes, &full[s], pol_w);
-          if (DUAL)
-            bulk_g2s(st + C::kOffRaw + kFp4TileBytes, tiles_b + (tile0 + kc) * kFp4TileBytes, kFp4TileBytes,
-                     &full[s], pol_w);
-          for (int h = 0; h < 2; ++h)
-            for (int b = 0; b < nbox; ++b)
-              tma_load_3d(smem_u32(st + h * C::kBHalf + b * kTmBoxRows * 128), &xmap, h * 64, row0 + b * kTmBoxRows,
-                          kc, &full[s]);
+          uint8_t* st = sbase + s * stage_b;
+          mbar_arrive_expect_tx(&full[s], uint32_t(nk) * tx1);
+          for (int j = 0; j < nk; ++j) {
+            uint8_t* raw = st + C::kOffRaw + j * NM * tile_b;
+            bulk_g2s(raw, tiles_a + (tile0 + kc + j) * tile_b, uint32_t(tile_b), &full[s], pol_w);
+            if (DUAL) bulk_g2s(raw + tile_b, tiles_b + (tile0 + kc + j) * tile_b, uint32_t(tile_b), &full[s], pol_w);
+            for (int h = 0; h < 2; ++h)
+              for (int b = 0; b < nbox; ++b)
+                tma_load_3d(smem_u32(st + (2 * j + h) * C::kBHalf + b * kTmBoxRows * 128), &xmap, h * 64,
+                            row0 + b * kTmBoxRows, kc + j, &full[s]);
+          }
           if (++s == S) {
             s = 0;
             ph ^= 1u;
@@ -224,14 +252,14 @@ __global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
       int j = 0;
       // descriptors and TMEM addresses, precomputed: one add per MMA in the loop
       const uint64_t bdesc0 = umma_desc_sw128(smem_u32(sbase));
-      constexpr int kSteps = 8 / C::kKkStride;  // k16 steps per stage of this issuer
+      constexpr int kSteps = C::kSteps;
       uint64_t boff[kSteps];
       uint32_t aoff[kSteps];
 #pragma unroll
       for (int i = 0; i < kSteps; ++i) {
-        const int kk = kk0 + i * C::kKkStride;
+        const int kk = kk0 + i * C::kKkStride;  // k16 step of the stage: chunk kk / 8, half (kk % 8) / 4
         boff[i] = uint64_t(((kk >> 2) * C::kBHalf + (kk & 3) * 32) >> 4);
-        aoff[i] = uint32_t(C::kDCols + m * 64 + kk * 8);
+        aoff[i] = uint32_t(C::kDCols + m * 64 * C::KS + kk * 8);
       }
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++j) {
         const int e = tm_find(pre, E, u);
@@ -248,7 +276,8 @@ __global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem + uint32_t((buf * P + p) * BN);
-        for (int kc = 0; kc < kcs; ++kc) {
+        for (int kc = 0; kc < kcs; kc += C::KS) {
+          const int nkk = 8 * min(C::KS, kcs - kc);  // k16 steps in this stage
           // the converters arrive on afull only after they saw the stage's copies land
           // (full[s]), so acquiring afull also orders the activation rows read below
           if (*abort_flag || !mbar_wait(&afull[ab], aph)) {
@@ -257,11 +286,13 @@ __global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t bst = bdesc0 + uint64_t((s * C::kStageBytes) >> 4);
-          const uint32_t ast = tmem + uint32_t(ab * NM * 64);
+          const uint64_t bst = bdesc0 + uint64_t((s * stage_b) >> 4);
+          const uint32_t ast = tmem + uint32_t(ab * C::kACols);
 #pragma unroll
-          for (int i = 0; i < kSteps; ++i)
+          for (int i = 0; i < kSteps; ++i) {
+            if (kk0 + i * C::kKkStride >= nkk) break;
             umma_f16_tmem_a(d, ast + aoff[i], bst + boff[i], idesc, (kc > 0 || i > 0) ? 1u : 0u);
+          }
           umma_commit(&empty[s]);  // activation rows and the A buffer read
           if (++s == S) s = 0;
           if (++ab == NA) {
@@ -288,7 +319,8 @@ __global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
     uint32_t ph = 0, wph = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-      for (int kc = 0; kc < kcs; ++kc, ++g) {
+      for (int kc = 0; kc < kcs; kc += C::KS, ++g) {
+        const int nk = min(C::KS, kcs - kc);
         if (*abort_flag || !mbar_wait(&full[s], ph)) {
           *abort_flag = 1;
           ok = false;
@@ -306,29 +338,59 @@ __global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
           }
         }
         tc_fence_after();
-        const uint32_t st = smem_u32(sbase + s * C::kStageBytes) + C::kOffRaw;
+        const uint32_t st = smem_u32(sbase + s * stage_b) + C::kOffRaw;
 #pragma unroll
-        for (int m = 0; m < NM; ++m) {
-          const uint32_t raw = st + m * kFp4TileBytes;
-          const uint32_t sw = lds32(raw + kFp4CodeBytes + row * 4);  // e4m3 scales of the 4 chunks
-          uint32_t out[16 * C::kChunks];
+        for (int jm = 0; jm < C::KS * NM; ++jm) {
+          const int j = jm / NM, m = jm % NM;  // chunk of the stage, matrix
+          if (j >= nk) break;
+          const uint32_t raw = st + jm * tile_b;
+          const uint32_t meta = raw + C::kCodeBytes;
+          uint32_t out[C::kCols];
+          if constexpr (!C::kAffine) {
+            const uint32_t sw = lds32(meta + row * 4);  // e4m3 scales of the row's 4 groups
 #pragma unroll
-          for (int c = 0; c < C::kChunks; ++c) {
-            const int cc = part * C::kChunks + c;
-            const uint4 v = lds128(raw + (cc * kTmM + row) * 16);
-            const uint32_t sf = e4m3_to_f16_bits((sw >> (8 * cc)) & 0xFFu);
-            const uint32_t s2 = sf | (sf << 16);
-            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+            for (int c = 0; c < C::kChunks; ++c) {
+              const int cc = part * C::kChunks + c;
+              const uint4 v = lds128(raw + (cc * kTmM + row) * 16);
+              const uint32_t sf = e4m3_to_f16_bits((sw >> (8 * cc)) & 0xFFu);
+              const uint32_t s2 = sf | (sf << 16);
+              const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int wi = 0; wi < 4; ++wi) {
-              uint32_t o[4];
-              e2m1x8_to_f16(w4[wi], o);
+              for (int wi = 0; wi < 4; ++wi) {
+                uint32_t o[4];
+                e2m1x8_to_f16(w4[wi], o);
 #pragma unroll
-              for (int t = 0; t < 4; ++t) out[16 * c + 4 * wi + t] = hmul2_bits(o[t], s2);
+                for (int t = 0; t < 4; ++t) out[16 * c + 4 * wi + t] = hmul2_bits(o[t], s2);
+              }
+            }
+          } else {
+            const uint32_t magic = 0x64006400u;  // f16x2 (1024, 1024)
+            const int gpt = kChunkK / a.group_size;  // groups per tile row
+#pragma unroll
+            for (int c = 0; c < C::kChunks; ++c) {
+              const int cc = part * C::kChunks + c;
+              const uint32_t sb = lds32(meta + (row * gpt + (cc * C::kChunkK) / a.group_size) * 4);
+              const uint32_t s2 = __byte_perm(sb, 0, 0x1010), b2 = __byte_perm(sb, 0, 0x3232);
+              const uint4 v = lds128(raw + (cc * kTmM + row) * 16);
+              const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int wi = 0; wi < 4; ++wi) {
+                if constexpr (C::kB8) {  // bytes j, j+1 are one K pair
+                  uint32_t lo, hi;
+                  u8x4_to_f16_plus1024(w4[wi], lo, hi);
+                  out[8 * c + 2 * wi] = hfma2_bits(hsub2_bits(lo, magic), s2, b2);
+                  out[8 * c + 2 * wi + 1] = hfma2_bits(hsub2_bits(hi, magic), s2, b2);
+                } else {  // nibbles i, i+4 are one K pair
+                  uint32_t o[4];
+                  u4x8_to_f16_plus1024(w4[wi], o);
+#pragma unroll
+                  for (int t = 0; t < 4; ++t) out[16 * c + 4 * wi + t] = hfma2_bits(hsub2_bits(o[t], magic), s2, b2);
+                }
+              }
             }
           }
-          const uint32_t col = uint32_t(C::kDCols + (ab * NM + m) * 64 + part * 16 * C::kChunks);
-          if constexpr (C::kChunks == 2)
+          const uint32_t col = uint32_t(C::kDCols + ab * C::kACols + (m * C::KS + j) * 64 + part * C::kCols);
+          if constexpr (C::kCols == 32)
             tmem_st32(lane_base + col, out);
           else
             tmem_st16(lane_base + col, out);
@@ -427,29 +489,60 @@ __global__ void __launch_bounds__(TmCfg<DUAL, BN, CW, P>::kThreads, 1)
   }
 }
 
-template <bool DUAL, int BN, int CW, int P>
-int launch_tm(const TmArgs& a, const void* staged, int64_t rows_cap, cudaStream_t stream) {
-  using C = TmCfg<DUAL, BN, CW, P>;
+template <int FMT, bool DUAL, int BN, int CW, int P>
+int launch_tm(TmArgs a, const void* staged, int64_t rows_cap, cudaStream_t stream) {
+  using C = TmCfg<FMT, DUAL, BN, CW, P>;
   CUtensorMap map;
   if (int rc = make_stage_map(&map, staged, rows_cap, a.kc_count, kTmBoxRows)) return rc;
-  const size_t smem = 1024 + size_t(C::kStages) * C::kStageBytes + 8 * (2 * C::kStages + C::kABufs + 5) + 16 +
+  a.tile_b = tile_bytes(FMT, a.group_size);
+  a.stage_b = tm_stage_bytes(C::kOffRaw, C::NM * C::KS, a.tile_b);
+  const int n_stages = std::min(8, (200 * 1024) / a.stage_b);
+  if (n_stages < 2) return fail(DSM_ERR_UNSUPPORTED, "expert_tm: tile too large for the shared-memory ring");
+  const size_t smem = 1024 + size_t(n_stages) * a.stage_b + 8 * (2 * n_stages + C::kABufs + 5) + 16 +
                       size_t(a.n_experts + 1) * 4;
-  auto kern = expert_tm_kernel<DUAL, BN, CW, P>;
+  auto kern = expert_tm_kernel<FMT, DUAL, BN, CW, P>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return check_launch("expert_tm smem attribute");
-  kern<<<num_sms(), C::kThreads, smem, stream>>>(a, map);
+  kern<<<num_sms(), C::kThreads, smem, stream>>>(a, map, n_stages);
   return check_launch("expert_tm");
 }
 
-constexpr int kTmBN = 32;
 constexpr int kTmCW = 8;
-constexpr int kTmP = 4;
+
+// Unit width: decode draft blocks put a few rows on each expert (units of up to 32 rows,
+// four MMA issuers splitting each stage's k16 steps); from an average of 32 rows per busy
+// expert (a dense layer run as one expert, prefill) units of up to 64 rows with two
+// issuers convert each weight tile half as often -- as long as they still give every SM a
+// unit (a product with few row tiles keeps the narrower units). Both keep two accumulator
+// buffers of P x BN = 128 TMEM columns.
+template <int FMT, bool DUAL>
+int launch_width(const TmArgs& a, const void* staged, int64_t rows_cap, cudaStream_t s) {
+  const int64_t busy = std::max<int64_t>(1, std::min<int64_t>(a.n_rows, a.n_experts));
+  const int64_t units64 = int64_t(a.rt_count) * (busy + a.n_rows / 64);  // estimate
+  if (a.n_rows > 32 * busy && units64 >= num_sms()) return launch_tm<FMT, DUAL, 64, kTmCW, 2>(a, staged, rows_cap, s);
+  return launch_tm<FMT, DUAL, 32, kTmCW, 4>(a, staged, rows_cap, s);
+}
+
+template <bool DUAL>
+int dispatch_tm(int wfmt, const TmArgs& a, const void* staged, int64_t rows_cap, cudaStream_t s) {
+  switch (wfmt) {
+    case DSM_WFMT_FP4_G32: return launch_width<DSM_WFMT_FP4_G32, DUAL>(a, staged, rows_cap, s);
+    case DSM_WFMT_AFFINE8: return launch_width<DSM_WFMT_AFFINE8, DUAL>(a, staged, rows_cap, s);
+    case DSM_WFMT_AFFINE4: return launch_width<DSM_WFMT_AFFINE4, DUAL>(a, staged, rows_cap, s);
+    default: return fail(DSM_ERR_INVALID_ARGUMENT, "expert_tm: format not handled by the tensor-memory kernel");
+  }
+}
 
 }  // namespace
 
-int expert_tm_gate_up(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int dim, const int32_t* offsets,
-                      int n_experts, const void* w1, const void* w3, int inter, int act, float limit, int round_gu,
-                      void* h_staged, float h_scale, int64_t n_rows, void* stream) {
+bool tm_supports(int wfmt) {
+  return wfmt == DSM_WFMT_FP4_G32 || wfmt == DSM_WFMT_AFFINE8 || wfmt == DSM_WFMT_AFFINE4;
+}
+
+int expert_tm_gate_up(int wfmt, int group_size, const void* x_staged, const float* x_row_scale, int64_t rows_cap,
+                      int dim, const int32_t* offsets, int n_experts, const void* w1, const void* w3, int inter,
+                      int act, float limit, int round_gu, void* h_staged, float h_scale, int64_t n_rows,
+                      void* stream) {
   TmArgs a{};
   a.wa = static_cast<const uint8_t*>(w1);
   a.wb = static_cast<const uint8_t*>(w3);
@@ -467,12 +560,13 @@ int expert_tm_gate_up(const void* x_staged, const float* x_row_scale, int64_t ro
   a.h_scale = h_scale;
   a.h_out = static_cast<__half*>(h_staged);
   a.h_rows_cap = rows_cap;
-  return launch_tm<true, kTmBN, kTmCW, kTmP>(a, x_staged, rows_cap, as_stream(stream));
+  a.group_size = group_size > 0 ? group_size : 64;
+  return dispatch_tm<true>(wfmt, a, x_staged, rows_cap, as_stream(stream));
 }
 
-int expert_tm_down(const void* h_staged, float h_scale, int64_t rows_cap, int inter, const int32_t* offsets,
-                   int n_experts, const void* w2, int dim, int round_o, float* o_rows, int ldo,
-                   const int32_t* o_row_map, int64_t n_rows, void* stream) {
+int expert_tm_down(int wfmt, int group_size, const void* h_staged, float h_scale, int64_t rows_cap, int inter,
+                   const int32_t* offsets, int n_experts, const void* w2, int dim, int round_o, float* o_rows,
+                   int ldo, const int32_t* o_row_map, int64_t n_rows, void* stream) {
   TmArgs a{};
   a.wa = static_cast<const uint8_t*>(w2);
   a.wb = nullptr;
@@ -488,7 +582,8 @@ int expert_tm_down(const void* h_staged, float h_scale, int64_t rows_cap, int in
   a.o_row_map = o_row_map;
   a.ldo = ldo;
   a.round_o = round_o;
-  return launch_tm<false, kTmBN, kTmCW, kTmP>(a, h_staged, rows_cap, as_stream(stream));
+  a.group_size = group_size > 0 ? group_size : 64;
+  return dispatch_tm<false>(wfmt, a, h_staged, rows_cap, as_stream(stream));
 }
 
 }  // namespace dsm

@@ -4,26 +4,30 @@
 // nn.Linear convention, dspark_mlx/loading.py:88-100 / model/moe.py:118-120) into the tile
 // stream the expert kernels read with one bulk copy per pipeline stage:
 //
-//   header   float[E] per-expert multiplier (F16: power-of-two prescale; FP4: per-tensor
-//            scale; others 1), padded to a multiple of 256 bytes
+//   header   float[E] per-expert multiplier (F16 and affine: the inverse of a power-of-two
+//            prescale; FP4: per-tensor scale; FP8: 1), padded to a multiple of 256 bytes
 //   tiles    for e, for row tile rt (128 rows), for K chunk kc (128 columns):
 //              codes  format dependent, below
 //              meta   per-tile scales (format dependent)
 //
-// F16, FP8, AFF8, AFF4 codes: [slab][m16 tile 0..7][lane 0..31][16 bytes] -- one
-// ld.shared.v4 per lane per m16 tile per slab, already in mma.m16n8k16 A-fragment order.
-// Lane (g = lane/4, q = lane%4) of m16 tile m holds rows r0 = 16m+g and r1 = r0+8; its
-// 16 bytes are [row r0 part][row r1 part] where the part covers K columns
-//   F16      (slab = 16 K): 4q .. 4q+3        (4 f16)
-//   FP8/AFF8 (slab = 32 K): 8q .. 8q+7        (8 bytes)
-//   AFF4     (slab = 64 K): 16q .. 16q+15     (8 bytes, nibble order k0,k2,k4,k6,k1,k3,k5,k7
-//                                              per 8 columns, for the magic-number unpack)
-// The decode kernel multiplies these against activations loaded with the same K subset per
-// lane, which is a consistent permutation of K inside each MMA and leaves the dot product
+// F16, FP8 codes (the weight-streaming kernel): [slab][m16 tile 0..7][lane 0..31][16 bytes]
+// -- one ld.shared.v4 per lane per m16 tile per slab, already in mma.m16n8k16 A-fragment
+// order. Lane (g = lane/4, q = lane%4) of m16 tile m holds rows r0 = 16m+g and r1 = r0+8;
+// its 16 bytes are [row r0 part][row r1 part] where the part covers K columns
+//   F16 (slab = 16 K): 4q .. 4q+3 (4 f16);  FP8 (slab = 32 K): 8q .. 8q+7 (8 bytes).
+// The kernel multiplies these against activations loaded with the same K subset per lane,
+// which is a consistent permutation of K inside each MMA and leaves the dot product
 // unchanged.
-// FP4 codes: [32-K chunk c 0..3][row 0..127][16 bytes], byte j of a chunk = K 32c+2j (low
-// nibble) and 32c+2j+1 (high nibble): one converter thread per row reads a whole scale
-// group with one ld.shared.v4, and a warp reads 512 contiguous bytes.
+// FP4, AFF8, AFF4 codes (the tensor-memory kernel): row-sliced, [16-byte chunk c][row
+// 0..127][16 bytes], so that one converter thread per row reads a chunk with one
+// ld.shared.v4 and a warp reads 512 contiguous bytes:
+//   FP4  chunk = 32 K: byte j = K 32c+2j (low nibble), 32c+2j+1 (high nibble)
+//   AFF8 chunk = 16 K: byte j = K 16c+j
+//   AFF4 chunk = 32 K: word w holds K 32c+8w .. +7 in nibble order k0,k2,k4,k6,k1,k3,k5,k7
+//        (nibble i and i+4 of a word are one K pair, for the magic-number unpack)
+// Affine meta: per row and group, the f16 pair (scale, bias) times the expert's prescale
+// 2^p (max |w| * 2^p in [2^14, 2^15); the header holds 2^-p), so a converter forms
+// w * 2^p = q * scale' + bias' with one f16 fma.
 //
 // dsm_affine_quantize restates MLX's affine quantize (called by MoE.quantize,
 // dspark_mlx/model/moe.py:124-130): per group, an fp32 scale/bias with the edge of larger
@@ -57,6 +61,22 @@ __global__ void expert_amax_kernel(const T* __restrict__ w, int64_t per_expert, 
   if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<int*>(amax + e), __float_as_int(m));
 }
 
+// max |w| over an expert's affine groups: |w| <= max(|bias|, |bias + qmax * scale|)
+__global__ void affine_amax_kernel(const __nv_bfloat16* __restrict__ scales, const __nv_bfloat16* __restrict__ biases,
+                                   int64_t groups_per_expert, float qmax, float* __restrict__ amax) {
+  const int e = blockIdx.y;
+  float m = 0.f;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < groups_per_expert;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t j = int64_t(e) * groups_per_expert + i;
+    const float s = __bfloat162float(scales[j]), b = __bfloat162float(biases[j]);
+    m = fmaxf(m, fmaxf(fabsf(b), fabsf(fmaf(qmax, s, b))));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<int*>(amax + e), __float_as_int(m));
+}
+
 __device__ __forceinline__ int prescale_exp(float amax) {
   if (!(amax > 0.f) || !isfinite(amax)) return 0;
   int ex;
@@ -65,7 +85,7 @@ __device__ __forceinline__ int prescale_exp(float amax) {
   return s < -100 ? -100 : (s > 100 ? 100 : s);
 }
 
-__global__ void finalize_f16_header_kernel(float* header, int n_experts) {
+__global__ void finalize_prescale_header_kernel(float* header, int n_experts) {
   const int e = blockIdx.x * blockDim.x + threadIdx.x;
   if (e < n_experts) header[e] = ldexpf(1.f, -prescale_exp(header[e]));
 }
@@ -88,11 +108,12 @@ __global__ void __launch_bounds__(256) pack_tiles_kernel(PackArgs a) {
   const int e = int(tile / (int64_t(a.kc_count) * a.rt_count));
   const int code_bytes = tile_code_bytes(a.wfmt);
   uint8_t* dst = a.tiles + tile * int64_t(tile_bytes(a.wfmt, a.group_size));
-  const int slab_k = a.wfmt == DSM_WFMT_F16 ? 16 : (a.wfmt == DSM_WFMT_FP8_B128 || a.wfmt == DSM_WFMT_AFFINE8) ? 32 : 64;
+  const int slab_k = a.wfmt == DSM_WFMT_F16 ? 16 : 32;  // F16 / FP8 (fragment order)
   const int n_chunks = code_bytes / 16;
   const int64_t R = a.rows, K = a.cols;
   float up = 1.f;
-  if (a.wfmt == DSM_WFMT_F16) up = ldexpf(1.f, prescale_exp(a.header[e]));
+  const bool affine = a.wfmt == DSM_WFMT_AFFINE8 || a.wfmt == DSM_WFMT_AFFINE4;
+  if (a.wfmt == DSM_WFMT_F16 || affine) up = ldexpf(1.f, prescale_exp(a.header[e]));
   if (a.wfmt == DSM_WFMT_FP4_G32) {  // row-sliced: [chunk][row][16 bytes]
     const uint8_t* src = static_cast<const uint8_t*>(a.codes);
     const int64_t kbytes = K / 2;
@@ -108,7 +129,41 @@ __global__ void __launch_bounds__(256) pack_tiles_kernel(PackArgs a) {
       *reinterpret_cast<uint4*>(dst + 16 * c) = v;
     }
   }
-  for (int c = threadIdx.x; c < n_chunks && a.wfmt != DSM_WFMT_FP4_G32; c += blockDim.x) {
+  if (affine) {  // row-sliced, 8-bit: 16 K per chunk; 4-bit: 32 K per chunk
+    const uint8_t* src = static_cast<const uint8_t*>(a.codes);
+    const bool b8 = a.wfmt == DSM_WFMT_AFFINE8;
+    const int64_t kbytes = b8 ? K : K / 2;
+    for (int c = threadIdx.x; c < n_chunks; c += blockDim.x) {
+      const int cc = c >> 7, rr = c & 127;
+      const int64_t r = int64_t(rt) * kTileRows + rr;
+      const int64_t k0 = int64_t(kc) * kChunkK + (b8 ? 16 : 32) * cc;
+      uint8_t out[16];
+      if (b8) {
+        for (int j = 0; j < 16; ++j)
+          out[j] = (r < R && k0 + j < K) ? src[(int64_t(e) * R + r) * kbytes + k0 + j] : uint8_t(0);
+      } else {
+        for (int w = 0; w < 4; ++w) {
+          uint8_t nib[8];
+          for (int i = 0; i < 8; ++i) {
+            const int64_t k = k0 + 8 * w + i;
+            uint8_t v = 0;
+            if (r < R && k < K) {
+              const uint8_t b = src[(int64_t(e) * R + r) * kbytes + k / 2];
+              v = (k & 1) ? (b >> 4) : (b & 0xF);
+            }
+            nib[i] = v;
+          }
+          const uint8_t order[8] = {nib[0], nib[2], nib[4], nib[6], nib[1], nib[3], nib[5], nib[7]};
+          for (int j = 0; j < 4; ++j) out[4 * w + j] = uint8_t(order[2 * j] | (order[2 * j + 1] << 4));
+        }
+      }
+      uint4 v;
+      memcpy(&v, out, 16);
+      *reinterpret_cast<uint4*>(dst + 16 * c) = v;
+    }
+  }
+  for (int c = threadIdx.x; c < n_chunks && (a.wfmt == DSM_WFMT_F16 || a.wfmt == DSM_WFMT_FP8_B128);
+       c += blockDim.x) {
     const int lane = c & 31, m = (c >> 5) & 7, slab = c >> 8;
     const int g = lane >> 2, q = lane & 3;
     const int64_t kb = int64_t(kc) * kChunkK + int64_t(slab) * slab_k;
@@ -131,30 +186,11 @@ __global__ void __launch_bounds__(256) pack_tiles_kernel(PackArgs a) {
           o[2 * j] = uint8_t(bits & 0xFF);
           o[2 * j + 1] = uint8_t(bits >> 8);
         }
-      } else if (a.wfmt == DSM_WFMT_FP8_B128 || a.wfmt == DSM_WFMT_AFFINE8) {
+      } else {  // FP8
         const uint8_t* src = static_cast<const uint8_t*>(a.codes);
         for (int j = 0; j < 8; ++j) {
           const int64_t k = kb + 8 * q + j;
           o[j] = (row_ok && k < K) ? src[(int64_t(e) * R + r) * K + k] : uint8_t(0);
-        }
-      } else {  // AFFINE4: source byte j = q(2j) | q(2j+1) << 4
-        const uint8_t* src = static_cast<const uint8_t*>(a.codes);
-        const int64_t kbytes = K / 2;
-        uint8_t nib[16];
-        for (int j = 0; j < 16; ++j) {
-          const int64_t k = kb + 16 * q + j;
-          uint8_t v = 0;
-          if (row_ok && k < K) {
-            const uint8_t b = src[(int64_t(e) * R + r) * kbytes + k / 2];
-            v = (k & 1) ? (b >> 4) : (b & 0xF);
-          }
-          nib[j] = v;
-        }
-        // per 8 columns: nibbles [k0,k2,k4,k6,k1,k3,k5,k7] (nibble 0 = low nibble of byte 0)
-        for (int w = 0; w < 2; ++w) {
-          const uint8_t* n8 = nib + 8 * w;
-          const uint8_t order[8] = {n8[0], n8[2], n8[4], n8[6], n8[1], n8[3], n8[5], n8[7]};
-          for (int j = 0; j < 4; ++j) o[4 * w + j] = uint8_t(order[2 * j] | (order[2 * j + 1] << 4));
         }
       }
     }
@@ -182,19 +218,21 @@ __global__ void __launch_bounds__(256) pack_tiles_kernel(PackArgs a) {
       const int64_t grp = int64_t(kc) * 4 + gg;
       meta[i] = (r < R && grp < groups) ? gs[(int64_t(e) * R + r) * groups + grp] : uint8_t(0);
     }
-  } else if (a.wfmt == DSM_WFMT_AFFINE8 || a.wfmt == DSM_WFMT_AFFINE4) {
+  } else if (affine) {
     const int gpt = kChunkK / a.group_size;  // groups per tile row
     const int64_t groups = K / a.group_size;
-    const uint16_t* sc = static_cast<const uint16_t*>(a.scales);
-    const uint16_t* bi = static_cast<const uint16_t*>(a.biases);
-    uint16_t* m16 = reinterpret_cast<uint16_t*>(meta);
+    const __nv_bfloat16* sc = static_cast<const __nv_bfloat16*>(a.scales);
+    const __nv_bfloat16* bi = static_cast<const __nv_bfloat16*>(a.biases);
+    __half* m16 = reinterpret_cast<__half*>(meta);
     for (int i = threadIdx.x; i < kTileRows * gpt; i += blockDim.x) {
       const int rr = i / gpt, gg = i % gpt;
       const int64_t r = int64_t(rt) * kTileRows + rr;
       const int64_t grp = int64_t(kc) * gpt + gg;
       const bool ok = r < R && grp < groups;
-      m16[2 * i] = ok ? sc[(int64_t(e) * R + r) * groups + grp] : uint16_t(0);
-      m16[2 * i + 1] = ok ? bi[(int64_t(e) * R + r) * groups + grp] : uint16_t(0);
+      const int64_t j = (int64_t(e) * R + r) * groups + grp;
+      // bf16 times a power of two: exact in f16 within its normal range
+      m16[2 * i] = __float2half_rn(ok ? __bfloat162float(sc[j]) * up : 0.f);
+      m16[2 * i + 1] = __float2half_rn(ok ? __bfloat162float(bi[j]) * up : 0.f);
     }
   }
 }
@@ -286,6 +324,14 @@ extern "C" int dsm_pack_weights(int wfmt, int n_experts, int rows, int cols, int
     else
       expert_amax_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(codes), per_expert, header);
     if (int rc = check_launch("expert_amax")) return rc;
+  } else if (wfmt == DSM_WFMT_AFFINE8 || wfmt == DSM_WFMT_AFFINE4) {
+    if (cudaMemsetAsync(header, 0, sizeof(float) * n_experts, s) != cudaSuccess) return check_launch("memset");
+    const int64_t gpe = int64_t(rows) * (cols / group_size);
+    dim3 grid(unsigned(std::min<int64_t>(ceil_div(gpe, 256), 1024)), unsigned(n_experts));
+    affine_amax_kernel<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(scales),
+                                           static_cast<const __nv_bfloat16*>(biases), gpe,
+                                           wfmt == DSM_WFMT_AFFINE8 ? 255.f : 15.f, header);
+    if (int rc = check_launch("affine_amax")) return rc;
   } else if (wfmt == DSM_WFMT_FP4_G32) {
     if (cudaMemcpyAsync(header, tensor_scale, sizeof(float) * n_experts, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
       return check_launch("copy tensor scale");
@@ -310,9 +356,9 @@ extern "C" int dsm_pack_weights(int wfmt, int n_experts, int rows, int cols, int
   const int64_t tiles = int64_t(n_experts) * a.rt_count * a.kc_count;
   pack_tiles_kernel<<<unsigned(tiles), 256, 0, s>>>(a);
   if (int rc = check_launch("pack_tiles")) return rc;
-  if (wfmt == DSM_WFMT_F16) {
-    finalize_f16_header_kernel<<<unsigned(ceil_div(n_experts, 256)), 256, 0, s>>>(header, n_experts);
-    return check_launch("finalize_f16_header");
+  if (wfmt == DSM_WFMT_F16 || wfmt == DSM_WFMT_AFFINE8 || wfmt == DSM_WFMT_AFFINE4) {
+    finalize_prescale_header_kernel<<<unsigned(ceil_div(n_experts, 256)), 256, 0, s>>>(header, n_experts);
+    return check_launch("finalize_header");
   }
   return DSM_OK;
 }

@@ -200,12 +200,13 @@ def test_moe_forward_formats(case):
     assert max_rel_err(y, ref_y) < MOE_TOL, max_rel_err(y, ref_y)
 
 
-@pytest.mark.parametrize("bits,n_tokens", [(8, 20), (4, 20), (8, 400), (4, 400)])
-def test_affine_quantize_matches_oracle_and_forward(bits, n_tokens):
+@pytest.mark.parametrize("bits,n_tokens,gs", [(8, 20, 64), (4, 20, 64), (8, 400, 64), (4, 400, 64), (8, 20, 32),
+                                              (8, 40, 128), (4, 40, 128)])
+def test_affine_quantize_matches_oracle_and_forward(bits, n_tokens, gs):
     g = torch.Generator().manual_seed(21)
     w = (torch.randn(8, 256, 512, generator=g) * 0.05).to(torch.bfloat16)
-    codes, s, b = affine_quantize(w.to(DEV), group_size=64, bits=bits)
-    rc, rs, rb = oracle.affine_quantize(w, 64, bits)
+    codes, s, b = affine_quantize(w.to(DEV), group_size=gs, bits=bits)
+    rc, rs, rb = oracle.affine_quantize(w, gs, bits)
     assert torch.equal(codes.cpu(), rc)
     assert torch.equal(s.cpu().view(torch.int16), rs.view(torch.int16))
     assert torch.equal(b.cpu().view(torch.int16), rb.view(torch.int16))
@@ -214,11 +215,11 @@ def test_affine_quantize_matches_oracle_and_forward(bits, n_tokens):
                         zipf_alpha=1.2 if n_tokens > 100 else None)
     t = W.make_moe_tensors(wl, device="cpu")
     moe = W.build_moe(wl, t, DEV)
-    moe.quantize(bits=bits, group_size=64)
-    assert moe.quant == (bits, 64) and "w1" not in moe._buffers and "w1_q" in moe._buffers
+    moe.quantize(bits=bits, group_size=gs)
+    assert moe.quant == (bits, gs) and "w1" not in moe._buffers and "w1_q" in moe._buffers
     y = moe(t["x"].to(DEV))
     qs = {n: oracle.OracleWeights("affine", getattr(moe, f"{n}_q").cpu(), scales=getattr(moe, f"{n}_scales").cpu(),
-                                  biases=getattr(moe, f"{n}_biases").cpu(), group_size=64, bits=bits)
+                                  biases=getattr(moe, f"{n}_biases").cpu(), group_size=gs, bits=bits)
           for n in ("w1", "w3", "w2")}
     a = t["args"]
     ref = oracle.moe_forward(t["x"], None, gate_weight=t["gate_weight"], topk=2, score_func=a["score_func"],
