@@ -23,6 +23,13 @@ int check_launch(const char* what) {
   return DSM_OK;
 }
 
+thread_local int t_grid_ctas = 0;
+
+int persistent_ctas() { return t_grid_ctas > 0 ? t_grid_ctas : num_sms(); }
+
+GridLimit::GridLimit(int ctas) : prev_(t_grid_ctas) { t_grid_ctas = ctas; }
+GridLimit::~GridLimit() { t_grid_ctas = prev_; }
+
 int num_sms() {
   static int cached[64] = {0};
   int dev = 0;

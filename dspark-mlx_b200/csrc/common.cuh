@@ -26,6 +26,18 @@ int check_launch(const char* what);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 int num_sms();
+// CTAs of a persistent expert kernel launched by this thread: every SM, unless a GridLimit
+// in scope narrows it (two such kernels then share the GPU on disjoint SMs)
+int persistent_ctas();
+struct GridLimit {
+  explicit GridLimit(int ctas);
+  ~GridLimit();
+  GridLimit(const GridLimit&) = delete;
+  GridLimit& operator=(const GridLimit&) = delete;
+
+ private:
+  int prev_;
+};
 
 // tcgen05 grouped products at large token counts (expert_tc.cu): fp8 block-scaled and f16
 bool tc_supports(int wfmt);

@@ -353,7 +353,7 @@ int launch_expert(const ExpertArgs& a, cudaStream_t stream) {
   auto kern = expert_kernel<FMT, DUAL, NT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return check_launch("expert kernel smem attribute");
-  kern<<<num_sms(), kThreads, smem, stream>>>(a, n_stages);
+  kern<<<persistent_ctas(), kThreads, smem, stream>>>(a, n_stages);
   return check_launch("expert kernel");
 }
 
@@ -375,14 +375,16 @@ int dispatch(int wfmt, int nt, const ExpertArgs& a, cudaStream_t s) {
 // on most experts, so one n8 tile keeps the tensor-core work per weight byte minimal. A
 // wider tile re-reads each weight tile less often, but only while the grid stays full:
 // with few busy experts (the shared expert is one group holding every token) narrower
-// tiles give more work units, and the re-reads of a tile are served from L2.
+// tiles give more work units, and the re-reads of a tile are served from L2. The grid is
+// this launch's persistent grid: a slice of the SMs when the shared expert runs beside the
+// routed products, where wider tiles (fewer re-reads per SM) win.
 int pick_nt(int64_t n_rows, int n_experts, int rt_count) {
   const int64_t busy = std::max<int64_t>(1, std::min<int64_t>(n_rows, n_experts));
   const double avg = double(n_rows) / double(busy);
   int nt = avg <= 8.0 ? 1 : (avg <= 16.0 ? 2 : 4);
   while (nt > 1) {
     const int64_t units = busy * int64_t(std::ceil(avg / (8.0 * nt))) * rt_count;
-    if (units >= 2 * int64_t(num_sms())) break;
+    if (units >= 2 * int64_t(persistent_ctas())) break;
     nt >>= 1;
   }
   return nt;

@@ -418,7 +418,7 @@ int launch_tc(const TcArgs& a, const void* staged, int64_t rows_cap, cudaStream_
   auto kern = expert_tc_kernel<FMT, DUAL>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return check_launch("expert_tc smem attribute");
-  kern<<<num_sms(), kTcThreads, smem, stream>>>(a, map);
+  kern<<<persistent_ctas(), kTcThreads, smem, stream>>>(a, map);
   return check_launch("expert_tc");
 }
 

@@ -503,7 +503,7 @@ int launch_tm(TmArgs a, const void* staged, int64_t rows_cap, cudaStream_t strea
   auto kern = expert_tm_kernel<FMT, DUAL, BN, CW, P>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return check_launch("expert_tm smem attribute");
-  kern<<<num_sms(), C::kThreads, smem, stream>>>(a, map, n_stages);
+  kern<<<persistent_ctas(), C::kThreads, smem, stream>>>(a, map, n_stages);
   return check_launch("expert_tm");
 }
 

@@ -2,6 +2,13 @@
 // router -> permutation -> staged activations -> fused gate/up + activation -> down ->
 // (shared expert: same kernels, one group holding every token) -> weighted combine.
 // All scratch comes from the caller's workspace, carved up below.
+//
+// The shared expert runs next to the routed products: its kernels go to a side stream
+// (forked from the caller's stream after staging, joined before the combine) on a small
+// slice of the SMs, and the routed kernels' persistent grids leave that slice free. The
+// routed products are HBM-bound and keep their bandwidth on the remaining SMs, while the
+// shared expert (one dense matrix, few rows) is bound by latency rather than bandwidth and
+// would otherwise add its whole duration to the step.
 #include "common.cuh"
 
 namespace dsm {
@@ -16,6 +23,31 @@ struct Carve {
     return p;
   }
 };
+
+// Per thread and device: the side stream and fork/join events, created on first use and
+// kept for the life of the thread (the library allocates no device memory for them).
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  bool ready = false;
+};
+
+SideStream* side_stream() {
+  thread_local SideStream per_device[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  SideStream& ss = per_device[dev];
+  if (!ss.ready) {
+    if (cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+    if (cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming) != cudaSuccess)
+      return nullptr;
+    ss.ready = true;
+  }
+  return &ss;
+}
+
+constexpr int kSharedCtas = 16;  // SMs given to the shared expert while the routed products run
 
 float h_scale_for(int act, float limit) {
   // |h| <= limit^2 under the clamp; keep f16 headroom otherwise
@@ -110,20 +142,39 @@ extern "C" int dsm_moe_forward(const dsm_moe_desc* d, const void* x, int x_dtype
                        L.cap_s, L.xscale_s, stream);
   if (rc) return rc;
   const float hs = h_scale_for(d->act, d->swiglu_limit);
-  rc = dsm_expert_gate_up(L.xs_r, L.xscale_r, L.cap_r, d->dim, L.offsets, d->n_experts, d->wfmt, d->group_size, d->w1,
-                          d->w3, d->inter, d->act, d->swiglu_limit, d->round_gu, L.hs_r, hs, P, stream);
-  if (rc) return rc;
-  rc = dsm_expert_down(L.hs_r, hs, L.cap_r, d->inter, L.offsets, d->n_experts, d->wfmt, d->group_size, d->w2, d->dim,
-                       d->round_o, L.o_r, d->dim, nullptr, P, stream);
-  if (rc) return rc;
-  if (d->s1) {
-    rc = dsm_expert_gate_up(L.xs_s, L.xscale_s, L.cap_s, d->dim, nullptr, 1, d->shared_wfmt, d->shared_group_size,
-                            d->s1, d->s3, d->shared_inter, d->act, d->swiglu_limit, d->shared_round_gu, L.hs_s, hs, N,
-                            stream);
-    if (rc) return rc;
-    rc = dsm_expert_down(L.hs_s, hs, L.cap_s, d->shared_inter, nullptr, 1, d->shared_wfmt, d->shared_group_size, d->s2,
-                         d->dim, d->shared_round_o, L.o_s, d->dim, nullptr, N, stream);
-    if (rc) return rc;
+  auto routed = [&]() -> int {
+    int r = dsm_expert_gate_up(L.xs_r, L.xscale_r, L.cap_r, d->dim, L.offsets, d->n_experts, d->wfmt, d->group_size,
+                               d->w1, d->w3, d->inter, d->act, d->swiglu_limit, d->round_gu, L.hs_r, hs, P, stream);
+    if (r) return r;
+    return dsm_expert_down(L.hs_r, hs, L.cap_r, d->inter, L.offsets, d->n_experts, d->wfmt, d->group_size, d->w2,
+                           d->dim, d->round_o, L.o_r, d->dim, nullptr, P, stream);
+  };
+  auto shared = [&](void* st) -> int {
+    int r = dsm_expert_gate_up(L.xs_s, L.xscale_s, L.cap_s, d->dim, nullptr, 1, d->shared_wfmt, d->shared_group_size,
+                               d->s1, d->s3, d->shared_inter, d->act, d->swiglu_limit, d->shared_round_gu, L.hs_s,
+                               hs, N, st);
+    if (r) return r;
+    return dsm_expert_down(L.hs_s, hs, L.cap_s, d->shared_inter, nullptr, 1, d->shared_wfmt, d->shared_group_size,
+                           d->s2, d->dim, d->shared_round_o, L.o_s, d->dim, nullptr, N, st);
+  };
+  SideStream* side = d->s1 && num_sms() >= 4 * kSharedCtas ? side_stream() : nullptr;
+  if (side) {
+    cudaStream_t main = as_stream(stream);
+    if (cudaEventRecord(side->fork, main) != cudaSuccess || cudaStreamWaitEvent(side->s, side->fork, 0) != cudaSuccess)
+      return check_launch("dsm_moe_forward: fork");
+    {
+      GridLimit g(kSharedCtas);
+      if ((rc = shared(side->s))) return rc;
+    }
+    if (cudaEventRecord(side->join, side->s) != cudaSuccess) return check_launch("dsm_moe_forward: join record");
+    {
+      GridLimit g(num_sms() - kSharedCtas);
+      if ((rc = routed())) return rc;
+    }
+    if (cudaStreamWaitEvent(main, side->join, 0) != cudaSuccess) return check_launch("dsm_moe_forward: join");
+  } else {
+    if ((rc = routed())) return rc;
+    if (d->s1 && (rc = shared(stream))) return rc;
   }
   const int y_dtype = x_dtype;
   return dsm_combine(L.o_r, L.inv, L.weights, N, d->topk, d->dim, L.o_s, y, y_dtype, stream);
