@@ -70,8 +70,11 @@ struct TmCfg {
   static constexpr int kKkStride = P / NM;     // issuer p: matrix p % NM, k16 steps p / NM + j * kKkStride
   static constexpr int kBHalf = BN * 128;    // one 64-K half of the activation rows
   static constexpr int kOffRaw = 2 * KS * kBHalf;
-  static constexpr int kDCols = 2 * P * BN;  // two buffers of P partial accumulators
   static constexpr int kACols = NM * KS * 64;  // one A buffer: KS x 128 K of f16 per matrix
+  // accumulator buffers of P partials each: two (an epilogue overlaps the next unit's MMAs)
+  // when they fit beside two A buffers in the 512 TMEM columns, else one
+  static constexpr int DB = (2 * P * BN + 2 * kACols <= 512) ? 2 : 1;
+  static constexpr int kDCols = DB * P * BN;
   static constexpr int kSteps = 8 * KS / kKkStride;  // k16 steps of one issuer per full stage
   static constexpr int kABufs = std::min(4, (512 - kDCols) / kACols);
   static constexpr int kParts = CW / 4;            // converter warps per TMEM sub-partition
@@ -268,8 +271,8 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
         const int chunk = (u - pre[e]) % nch;
         const int n_mma = (min(BN, cnt - chunk * BN) + 15) / 16 * 16;
         const uint32_t idesc = umma_idesc_f16(kTmM, n_mma);
-        const int buf = j & 1;
-        if (*abort_flag || !mbar_wait(&tempty[buf], ((j >> 1) & 1) ^ 1u)) {
+        const int buf = j % C::DB;
+        if (*abort_flag || !mbar_wait(&tempty[buf], ((j / C::DB) & 1) ^ 1u)) {
           *abort_flag = 1;
           ok = false;
           break;
@@ -422,8 +425,8 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
       const int local = u - pre[e];
       const int rt = local / nch, chunk = local % nch;
       const int rows = min(BN, cnt - chunk * BN);
-      const int buf = j & 1;
-      if (*abort_flag || !mbar_wait(&tfull[buf], (j >> 1) & 1)) {
+      const int buf = j % C::DB;
+      if (*abort_flag || !mbar_wait(&tfull[buf], (j / C::DB) & 1)) {
         *abort_flag = 1;
         break;
       }
@@ -431,22 +434,21 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
       const float wmul_a = reinterpret_cast<const float*>(a.wa)[e];
       const float wmul_b = DUAL ? reinterpret_cast<const float*>(a.wb)[e] : 1.f;
       for (int cb = 0; cb < rows; cb += 16) {
-        // partial accumulators: issuer p holds matrix p % NM
-        uint32_t pv[P][16];
-#pragma unroll
-        for (int q = 0; q < P; ++q) tmem_ld16(lane_base + uint32_t((buf * P + q) * BN + cb), pv[q]);
-        tmem_ld_wait();
+        // partial accumulators, added in issuer order: issuer q holds matrix q % NM
         float gsum[16], usum[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          gsum[i] = 0.f;
-          usum[i] = 0.f;
+        for (int i = 0; i < 16; ++i) gsum[i] = usum[i] = 0.f;
 #pragma unroll
-          for (int q = 0; q < P; ++q) {
+        for (int q = 0; q < P; ++q) {
+          uint32_t pv[16];
+          tmem_ld16(lane_base + uint32_t((buf * P + q) * BN + cb), pv);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
             if (q % NM == 0)
-              gsum[i] += __uint_as_float(pv[q][i]);
+              gsum[i] += __uint_as_float(pv[i]);
             else
-              usum[i] += __uint_as_float(pv[q][i]);
+              usum[i] += __uint_as_float(pv[i]);
           }
         }
 #pragma unroll

@@ -8,7 +8,9 @@
 // slice of the SMs, and the routed kernels' persistent grids leave that slice free. The
 // routed products are HBM-bound and keep their bandwidth on the remaining SMs, while the
 // shared expert (one dense matrix, few rows) is bound by latency rather than bandwidth and
-// would otherwise add its whole duration to the step.
+// would otherwise add its whole duration to the step. Only decode-sized calls overlap: with
+// thousands of tokens both products are compute-bound, and splitting the SMs between them
+// gains nothing.
 #include "common.cuh"
 
 namespace dsm {
@@ -47,7 +49,8 @@ SideStream* side_stream() {
   return &ss;
 }
 
-constexpr int kSharedCtas = 16;  // SMs given to the shared expert while the routed products run
+constexpr int kSharedCtas = 16;        // SMs given to the shared expert while the routed products run
+constexpr int64_t kOverlapTokens = 2048;  // largest call that overlaps the shared expert
 
 float h_scale_for(int act, float limit) {
   // |h| <= limit^2 under the clamp; keep f16 headroom otherwise
@@ -157,7 +160,7 @@ extern "C" int dsm_moe_forward(const dsm_moe_desc* d, const void* x, int x_dtype
     return dsm_expert_down(L.hs_s, hs, L.cap_s, d->shared_inter, nullptr, 1, d->shared_wfmt, d->shared_group_size,
                            d->s2, d->dim, d->shared_round_o, L.o_s, d->dim, nullptr, N, st);
   };
-  SideStream* side = d->s1 && num_sms() >= 4 * kSharedCtas ? side_stream() : nullptr;
+  SideStream* side = d->s1 && N <= kOverlapTokens && num_sms() >= 4 * kSharedCtas ? side_stream() : nullptr;
   if (side) {
     cudaStream_t main = as_stream(stream);
     if (cudaEventRecord(side->fork, main) != cudaSuccess || cudaStreamWaitEvent(side->s, side->fork, 0) != cudaSuccess)
