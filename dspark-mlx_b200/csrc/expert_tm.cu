@@ -28,8 +28,8 @@
 //               memory. One thread issues at most one such MMA every ~46 cycles whatever N
 //               is, so the 8 x (gate, up) MMAs of a stage are split over P threads, each
 //               accumulating its share of the k16 steps of one matrix into its own partial
-//               D in TMEM (two buffers, so an epilogue overlaps the next unit); the epilogue
-//               adds the partials.
+//               D in TMEM (two buffers where TMEM allows, so an epilogue overlaps the next
+//               unit); the epilogue adds the partials.
 // The activations are read by the tensor core from shared memory, so no register traffic or
 // legacy MMA pipe is spent on them; the ALU work per weight byte is the conversion alone.
 //
@@ -517,11 +517,22 @@ constexpr int kTmCW = 8;
 // issuers convert each weight tile half as often -- as long as they still give every SM a
 // unit (a product with few row tiles keeps the narrower units). Both keep two accumulator
 // buffers of P x BN = 128 TMEM columns.
+// A dense layer's gate/up pair run as one expert (rows of 100+ tokens) takes units of up to
+// 128 rows when they fit in one wave: each SM then converts its weight tiles once, and the
+// single accumulator buffer this width leaves room for costs nothing with one unit per SM.
+// (The down product keeps narrower units: its two-chunk stages of 128 rows would leave two
+// stages in flight, and it has few row tiles to spread.)
 template <int FMT, bool DUAL>
 int launch_width(const TmArgs& a, const void* staged, int64_t rows_cap, cudaStream_t s) {
   const int64_t busy = std::max<int64_t>(1, std::min<int64_t>(a.n_rows, a.n_experts));
-  const int64_t units64 = int64_t(a.rt_count) * (busy + a.n_rows / 64);  // estimate
-  if (a.n_rows > 32 * busy && units64 >= num_sms()) return launch_tm<FMT, DUAL, 64, kTmCW, 2>(a, staged, rows_cap, s);
+  const int64_t units64 = int64_t(a.rt_count) * (busy + a.n_rows / 64);  // estimates
+  const int64_t units128 = int64_t(a.rt_count) * (busy + a.n_rows / 128);
+  if constexpr (DUAL) {
+    if (a.n_rows > 96 * busy && units128 <= persistent_ctas())
+      return launch_tm<FMT, DUAL, 128, kTmCW, 2>(a, staged, rows_cap, s);
+  }
+  if (a.n_rows > 32 * busy && units64 >= persistent_ctas())
+    return launch_tm<FMT, DUAL, 64, kTmCW, 2>(a, staged, rows_cap, s);
   return launch_tm<FMT, DUAL, 32, kTmCW, 4>(a, staged, rows_cap, s);
 }
 

@@ -179,8 +179,10 @@ FORMAT_CASES = [
     dict(base="fp8_decode", dim=384, inter=200, experts=12, topk=3, n_tokens=9),  # ragged (padding) shapes
     dict(base="fp4_decode", dim=512, inter=256, experts=16, topk=4, n_tokens=40),
     dict(base="fp4_decode", dim=512, inter=256, experts=8, topk=2, n_tokens=200),  # > 8 rows per expert
-    # skewed, many rows per expert: units of up to 64 rows running 1..8 n8 tiles
+    # many rows per expert on the tensor-memory kernel: units of up to 128 rows (3 row tiles)
+    # and of up to 64 rows (16 row tiles: 128-row units would exceed one wave)
     dict(base="fp4_decode", dim=512, inter=384, experts=16, topk=4, n_tokens=700),
+    dict(base="fp4_decode", dim=512, inter=2048, experts=16, topk=4, n_tokens=700),
     dict(base="fp8_decode", dim=512, inter=256, experts=16, topk=6, n_tokens=300, wfmt="bf16"),
 ]
 
