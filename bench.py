@@ -427,7 +427,7 @@ DTYPE_DESC = {
     "fp8": "fp8 e4m3 weights x bf16 activations (f16 MMA, fp32 accumulate)",
     "fp4": "fp4 e2m1 weights (e4m3 group scales) x bf16 activations (f16 tcgen05 MMA, fp32 accumulate)",
     "bf16": "bf16 weights x bf16 activations (f16 MMA, fp32 accumulate)",
-    "affine8": "8-bit affine weights x bf16 activations (f16 MMA, fp32 accumulate)",
+    "affine8": "8-bit affine weights x bf16 activations (f16 tcgen05 MMA, fp32 accumulate)",
 }
 
 
@@ -621,7 +621,7 @@ def run_qwen3(args):
         k_ms = timed(gate_up)
         k_bytes = pg.nbytes + pu.nbytes + N * h * 2 + N * inter * 2
         achieved = k_bytes / (k_ms * 1e-3) / 1e9
-        roofline = {"bound": "hbm", "kernel": "expert_kernel<affine8, gate_up> (weight streaming, mma.sync)",
+        roofline = {"bound": "hbm", "kernel": "expert_tm_kernel<affine8, gate_up> (dequantised into TMEM, tcgen05 kind::f16)",
                     "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                     "peak_kind": peak_kind, "frac_of_8tbs": achieved / SPEC_HBM_GBS,
                     "algorithmic_bytes_per_launch": k_bytes, "launch_ms": k_ms, "traffic": None}
