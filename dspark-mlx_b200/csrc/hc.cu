@@ -1,0 +1,264 @@
+// The MoE's neighbours in the DSpark draft block (dspark_mlx/model/block.py:83-86): the
+// hyper-connection reduction before the FFN and its RMSNorm, and the re-expansion after it.
+//
+//   dsm_hc_pre_norm  hc_pre (dspark_mlx/model/hyper.py:24-42, with kernels.hc_split_sinkhorn,
+//                    kernels.py:60-85) followed by ffn_norm (RMSNorm, model/norm_rope.py:22-39):
+//                    x [n, hc, d] -> the MoE input [n, d], plus post [n, hc], comb [n, hc, hc]
+//   dsm_hc_post      hc_post (hyper.py:45-51): out[c] = post[c] * h + sum_a comb[a, c] * res[a]
+//
+// Everything is fp32 inside, cast to the activation dtype where the reference casts. One
+// CTA per token for the pre-norm: a single pass over the token's hc*d values accumulates the
+// sum of squares and the (2 + hc) * hc mix projections (the projection matrix stays in L2
+// across tokens), a block reduction, the Sinkhorn split on one thread, then the pre-weighted
+// sum of the copies (rounded to the activation dtype, kept in shared memory) and its RMS.
+#include "common.cuh"
+
+namespace dsm {
+namespace {
+
+constexpr int kHcThreads = 256;
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+__device__ __forceinline__ float sigmoid_f(float v) { return 1.f / (1.f + expf(-v)); }
+
+// block-wide sum of NV values per thread (in place: every thread gets the totals)
+template <int NV>
+__device__ __forceinline__ void block_sum(float (&v)[NV], float* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < NV; ++i)
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v[i] += __shfl_xor_sync(0xffffffffu, v[i], o);
+  __syncthreads();
+  if (lane == 0)
+#pragma unroll
+    for (int i = 0; i < NV; ++i) red[warp * NV + i] = v[i];
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    float s = 0.f;
+    for (int w = 0; w < kHcThreads / 32; ++w) s += red[w * NV + i];
+    v[i] = s;
+  }
+}
+
+template <typename T, int HC>
+__global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(const T* __restrict__ x, int dim,
+                                                                   const float* __restrict__ fn,
+                                                                   const float* __restrict__ scale,
+                                                                   const float* __restrict__ base, int iters,
+                                                                   float norm_eps, float hc_eps,
+                                                                   const float* __restrict__ weight, T* __restrict__ xn,
+                                                                   float* __restrict__ post_out,
+                                                                   float* __restrict__ comb_out) {
+  constexpr int MIX = (2 + HC) * HC;
+  extern __shared__ float ysm[];  // dim floats: the reduced row, rounded to T
+  __shared__ float red[(kHcThreads / 32) * (MIX + 1)];
+  __shared__ float pre_s[HC];
+  const int64_t t = blockIdx.x;
+  const int hcd = HC * dim;
+  const T* xt = x + t * hcd;
+
+  // pass 1: sum of squares and the mix projections of the flattened copies
+  float acc[MIX + 1];
+#pragma unroll
+  for (int i = 0; i <= MIX; ++i) acc[i] = 0.f;
+  for (int k = threadIdx.x; k < hcd; k += kHcThreads) {
+    const float v = to_f(xt[k]);
+    acc[MIX] = fmaf(v, v, acc[MIX]);
+#pragma unroll
+    for (int j = 0; j < MIX; ++j) acc[j] = fmaf(v, fn[int64_t(j) * hcd + k], acc[j]);
+  }
+  block_sum(acc, red);
+
+  if (threadIdx.x == 0) {  // hc_split_sinkhorn on the token's mixes
+    const float inv_rms = rsqrtf(acc[MIX] / float(hcd) + norm_eps);
+    float m[MIX];
+#pragma unroll
+    for (int j = 0; j < MIX; ++j) m[j] = acc[j] * inv_rms;
+#pragma unroll
+    for (int c = 0; c < HC; ++c) {
+      pre_s[c] = sigmoid_f(m[c] * scale[0] + base[c]) + hc_eps;
+      post_out[t * HC + c] = 2.f * sigmoid_f(m[HC + c] * scale[1] + base[HC + c]);
+    }
+    float cb[HC][HC];
+#pragma unroll
+    for (int a = 0; a < HC; ++a) {  // row softmax
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < HC; ++c) {
+        cb[a][c] = m[2 * HC + a * HC + c] * scale[2] + base[2 * HC + a * HC + c];
+        mx = fmaxf(mx, cb[a][c]);
+      }
+      float s = 0.f;
+#pragma unroll
+      for (int c = 0; c < HC; ++c) {
+        cb[a][c] = expf(cb[a][c] - mx);
+        s += cb[a][c];
+      }
+#pragma unroll
+      for (int c = 0; c < HC; ++c) cb[a][c] = cb[a][c] / s + hc_eps;
+    }
+    auto col_norm = [&]() {
+#pragma unroll
+      for (int c = 0; c < HC; ++c) {
+        float s = 0.f;
+#pragma unroll
+        for (int a = 0; a < HC; ++a) s += cb[a][c];
+        s += hc_eps;
+#pragma unroll
+        for (int a = 0; a < HC; ++a) cb[a][c] /= s;
+      }
+    };
+    col_norm();
+    for (int it = 1; it < iters; ++it) {
+#pragma unroll
+      for (int a = 0; a < HC; ++a) {  // row normalisation
+        float s = 0.f;
+#pragma unroll
+        for (int c = 0; c < HC; ++c) s += cb[a][c];
+        s += hc_eps;
+#pragma unroll
+        for (int c = 0; c < HC; ++c) cb[a][c] /= s;
+      }
+      col_norm();
+    }
+#pragma unroll
+    for (int a = 0; a < HC; ++a)
+#pragma unroll
+      for (int c = 0; c < HC; ++c) comb_out[(t * HC + a) * HC + c] = cb[a][c];
+  }
+  __syncthreads();
+
+  // pass 2: y = sum_c pre[c] * x[c] (cast to T), then RMSNorm(y) * weight (cast to T)
+  float sq[1] = {0.f};
+  for (int j = threadIdx.x; j < dim; j += kHcThreads) {
+    float y = 0.f;
+#pragma unroll
+    for (int c = 0; c < HC; ++c) y = __fadd_rn(y, __fmul_rn(pre_s[c], to_f(xt[c * dim + j])));  // products, then sum
+    const float yq = to_f(from_f<T>(y));
+    ysm[j] = yq;
+    sq[0] = fmaf(yq, yq, sq[0]);
+  }
+  block_sum(sq, red);
+  const float r = rsqrtf(sq[0] / float(dim) + norm_eps);
+  T* out = xn + t * dim;
+  for (int j = threadIdx.x; j < dim; j += kHcThreads) {
+    const float v = ysm[j] * r;
+    out[j] = from_f<T>(weight ? weight[j] * v : v);
+  }
+}
+
+template <typename T, int HC>
+__global__ void __launch_bounds__(kHcThreads) hc_post_kernel(const T* __restrict__ h, const T* __restrict__ res,
+                                                               int dim, const float* __restrict__ post,
+                                                               const float* __restrict__ comb, T* __restrict__ out) {
+  const int64_t t = blockIdx.y;
+  const int j = blockIdx.x * kHcThreads + threadIdx.x;
+  if (j >= dim) return;
+  float p[HC], cm[HC][HC], r[HC];
+#pragma unroll
+  for (int c = 0; c < HC; ++c) p[c] = post[t * HC + c];
+#pragma unroll
+  for (int a = 0; a < HC; ++a) {
+    r[a] = to_f(res[(t * HC + a) * dim + j]);
+#pragma unroll
+    for (int c = 0; c < HC; ++c) cm[a][c] = comb[(t * HC + a) * HC + c];
+  }
+  const float hv = to_f(h[t * dim + j]);
+#pragma unroll
+  for (int c = 0; c < HC; ++c) {
+    float s = 0.f;
+#pragma unroll
+    for (int a = 0; a < HC; ++a) s = __fadd_rn(s, __fmul_rn(cm[a][c], r[a]));
+    out[(t * HC + c) * dim + j] = from_f<T>(__fadd_rn(__fmul_rn(p[c], hv), s));
+  }
+}
+
+template <typename T>
+int launch_pre(const void* x, int64_t n, int hc, int dim, const float* fn, const float* scale, const float* base,
+               int iters, float norm_eps, float hc_eps, const float* weight, void* xn, float* post, float* comb,
+               cudaStream_t s) {
+  const size_t smem = size_t(dim) * sizeof(float);
+  const T* xp = static_cast<const T*>(x);
+  T* xo = static_cast<T*>(xn);
+#define DSM_HC_PRE(H)                                                                                         \
+  {                                                                                                           \
+    auto k = hc_pre_norm_kernel<T, H>;                                                                        \
+    if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != \
+                                cudaSuccess)                                                                  \
+      return check_launch("hc_pre_norm smem attribute");                                                      \
+    k<<<unsigned(n), kHcThreads, smem, s>>>(xp, dim, fn, scale, base, iters, norm_eps, hc_eps, weight, xo,    \
+                                            post, comb);                                                      \
+    return check_launch("hc_pre_norm");                                                                       \
+  }
+  switch (hc) {
+    case 1: DSM_HC_PRE(1)
+    case 2: DSM_HC_PRE(2)
+    case 4: DSM_HC_PRE(4)
+    default: return fail(DSM_ERR_UNSUPPORTED, "dsm_hc_pre_norm: hc_mult must be 1, 2 or 4");
+  }
+#undef DSM_HC_PRE
+}
+
+template <typename T>
+int launch_post(const void* h, const void* res, int64_t n, int hc, int dim, const float* post, const float* comb,
+                void* out, cudaStream_t s) {
+  const dim3 grid(unsigned(ceil_div(dim, kHcThreads)), unsigned(n));
+  const T* hp = static_cast<const T*>(h);
+  const T* rp = static_cast<const T*>(res);
+  T* op = static_cast<T*>(out);
+  switch (hc) {
+    case 1: hc_post_kernel<T, 1><<<grid, kHcThreads, 0, s>>>(hp, rp, dim, post, comb, op); break;
+    case 2: hc_post_kernel<T, 2><<<grid, kHcThreads, 0, s>>>(hp, rp, dim, post, comb, op); break;
+    case 4: hc_post_kernel<T, 4><<<grid, kHcThreads, 0, s>>>(hp, rp, dim, post, comb, op); break;
+    default: return fail(DSM_ERR_UNSUPPORTED, "dsm_hc_post: hc_mult must be 1, 2 or 4");
+  }
+  return check_launch("hc_post");
+}
+
+}  // namespace
+}  // namespace dsm
+
+extern "C" int dsm_hc_pre_norm(const void* x, int x_dtype, int64_t n_tokens, int hc_mult, int dim, const float* hc_fn,
+                               const float* hc_scale, const float* hc_base, int sinkhorn_iters, float norm_eps,
+                               float hc_eps, const float* norm_weight, void* x_norm_out, float* post_out,
+                               float* comb_out, void* stream) {
+  using namespace dsm;
+  DSM_REQUIRE(n_tokens >= 0 && dim > 0 && hc_mult > 0 && sinkhorn_iters >= 1, "dsm_hc_pre_norm: bad shape");
+  DSM_REQUIRE(dim <= 48 * 1024, "dsm_hc_pre_norm: dim too large for the shared-memory row");
+  DSM_REQUIRE(x_dtype == DSM_DT_F32 || x_dtype == DSM_DT_BF16, "dsm_hc_pre_norm: x must be F32 or BF16");
+  if (n_tokens == 0) return DSM_OK;
+  DSM_REQUIRE(x && hc_fn && hc_scale && hc_base && x_norm_out && post_out && comb_out, "dsm_hc_pre_norm: NULL pointer");
+  cudaStream_t s = as_stream(stream);
+  if (x_dtype == DSM_DT_BF16)
+    return launch_pre<__nv_bfloat16>(x, n_tokens, hc_mult, dim, hc_fn, hc_scale, hc_base, sinkhorn_iters, norm_eps,
+                                     hc_eps, norm_weight, x_norm_out, post_out, comb_out, s);
+  return launch_pre<float>(x, n_tokens, hc_mult, dim, hc_fn, hc_scale, hc_base, sinkhorn_iters, norm_eps, hc_eps,
+                           norm_weight, x_norm_out, post_out, comb_out, s);
+}
+
+extern "C" int dsm_hc_post(const void* h, const void* residual, int dtype, int64_t n_tokens, int hc_mult, int dim,
+                           const float* post, const float* comb, void* out, void* stream) {
+  using namespace dsm;
+  DSM_REQUIRE(n_tokens >= 0 && dim > 0 && hc_mult > 0, "dsm_hc_post: bad shape");
+  DSM_REQUIRE(dtype == DSM_DT_F32 || dtype == DSM_DT_BF16, "dsm_hc_post: dtype must be F32 or BF16");
+  if (n_tokens == 0) return DSM_OK;
+  DSM_REQUIRE(h && residual && post && comb && out, "dsm_hc_post: NULL pointer");
+  cudaStream_t s = as_stream(stream);
+  if (dtype == DSM_DT_BF16)
+    return launch_post<__nv_bfloat16>(h, residual, n_tokens, hc_mult, dim, post, comb, out, s);
+  return launch_post<float>(h, residual, n_tokens, hc_mult, dim, post, comb, out, s);
+}

@@ -30,7 +30,7 @@ EXPORTED = (
     "dsm_stage_rows_cap", "dsm_stage_rows", "dsm_packed_bytes", "dsm_pack_weights",
     "dsm_affine_quantize", "dsm_expert_gate_up", "dsm_expert_down", "dsm_combine",
     "dsm_moe_workspace_bytes", "dsm_moe_forward", "dsm_gather_rows", "dsm_segment_ids",
-    "dsm_set_expert_regime",
+    "dsm_set_expert_regime", "dsm_hc_pre_norm", "dsm_hc_post",
 )
 
 
@@ -85,6 +85,8 @@ def _declare(lib):
         "dsm_segment_ids": (I, [V, I, I, V, I64, V]),
         "dsm_set_expert_regime": (I, [I]),
         "dsm_combine": (I, [V, V, V, I64, I, I, V, V, I, V]),
+        "dsm_hc_pre_norm": (I, [V, I, I64, I, I, V, V, V, I, F, F, V, V, V, V, V]),
+        "dsm_hc_post": (I, [V, V, I, I64, I, I, V, V, V, V]),
         "dsm_moe_workspace_bytes": (S, [POINTER(MoEDesc)]),
         "dsm_moe_forward": (I, [POINTER(MoEDesc), V, I, V, I, I64, V, V, V, V, S, V]),
     }

@@ -26,6 +26,9 @@
  *   dsm_moe_forward     MoE.__call__                          model/moe.py:151-161
  *   dsm_affine_quantize mx.quantize in MoE.quantize           model/moe.py:124-130
  *   dsm_pack_weights    stacked [E,out,in] expert weights      loading.py:88-100 (+103-114)
+ *   dsm_hc_pre_norm     hc_pre + ffn_norm before the MoE       model/hyper.py:24-42, kernels.py:60-85,
+ *                       (DSparkBlock.__call__, block.py:84-85) model/norm_rope.py:22-39
+ *   dsm_hc_post         hc_post after the MoE (block.py:86)    model/hyper.py:45-51
  *   dsm_gather_rows, dsm_segment_ids: expert-parallel plumbing; the reference runs on one
  *                       device (tests/reference_model.py:55-56 forces world_size 1) and has
  *                       no counterpart.
@@ -196,6 +199,22 @@ int dsm_segment_ids(const int32_t* counts, int n_segments, int e_local, int32_t*
 int dsm_combine(const float* o_sorted, const int32_t* inv, const float* route_weights,
                 int64_t n_tokens, int topk, int dim, const float* shared_rows, void* y,
                 int y_dtype, void* stream);
+
+/* ---- the MoE's neighbours in the draft block (DSparkBlock.__call__, block.py:83-86) ----
+ * x [n_tokens, hc_mult, dim] (F32 or BF16; the hyper-connection copies of each token).
+ * dsm_hc_pre_norm writes the MoE input x_norm [n_tokens, dim] (x's dtype) =
+ * RMSNorm(sum_c pre[c] * x[c]) * norm_weight (norm_weight may be NULL: no scale), and the
+ * mixing weights post [n_tokens, hc_mult], comb [n_tokens, hc_mult, hc_mult] (fp32) that
+ * dsm_hc_post uses to re-expand the MoE output h [n_tokens, dim] against the residual x:
+ * out[t, c] = post[t, c] * h[t] + sum_a comb[t, a, c] * x[t, a]. hc_fn is
+ * [(2 + hc_mult) * hc_mult, hc_mult * dim] fp32, hc_scale [3], hc_base [(2 + hc_mult) * hc_mult].
+ * hc_mult must be 1, 2 or 4. */
+int dsm_hc_pre_norm(const void* x, int x_dtype, int64_t n_tokens, int hc_mult, int dim,
+                    const float* hc_fn, const float* hc_scale, const float* hc_base,
+                    int sinkhorn_iters, float norm_eps, float hc_eps, const float* norm_weight,
+                    void* x_norm_out, float* post_out, float* comb_out, void* stream);
+int dsm_hc_post(const void* h, const void* residual, int dtype, int64_t n_tokens, int hc_mult,
+                int dim, const float* post, const float* comb, void* out, void* stream);
 
 /* ---- whole MoE.__call__ -----------------------------------------------------------------*/
 typedef struct dsm_moe_desc {
