@@ -172,8 +172,8 @@ class ExpertParallelMoE(nn.Module):
             self._host[E:].copy_(recv_counts, non_blocking=True)
         rgu, ro = self.local.routed_round_flags(x2.dtype)
         if x2.dtype == torch.bfloat16:
-            sgu = int(self.shared_experts.w1.weight.dtype == torch.bfloat16) | 2
-            so = int(self.shared_experts.w2.weight.dtype == torch.bfloat16)
+            sgu = int(self.shared_experts.weight_dtype("w1") == torch.bfloat16) | 2
+            so = int(self.shared_experts.weight_dtype("w2") == torch.bfloat16)
         else:
             sgu, so = 0, 0
         hsc = 1.0 if 0 < self.swiglu_limit and self.swiglu_limit ** 2 < 30000 else 1.0 / 256

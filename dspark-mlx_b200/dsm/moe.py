@@ -90,12 +90,24 @@ class Gate(nn.Module):
 
 
 class _Linear(nn.Module):
-    """Bias-free linear weight holder (``nn.Linear`` layout ``[out, in]``)."""
+    """Bias-free linear weight holder (``nn.Linear`` layout ``[out, in]``). A ``meta`` weight
+    marks a matrix the owning :class:`Expert` holds packed; it stays a placeholder through
+    ``.to()`` / ``.cuda()``."""
 
     def __init__(self, in_dim: int, out_dim: int):
         super().__init__()
         self.weight = nn.Parameter(torch.empty(out_dim, in_dim, dtype=torch.float32), requires_grad=False)
         nn.init.uniform_(self.weight, -in_dim ** -0.5, in_dim ** -0.5)
+
+    def _apply(self, fn, recurse=True):
+        w = self._parameters.get("weight")
+        if w is None or not w.is_meta:
+            return super()._apply(fn, recurse)
+        self._parameters["weight"] = None
+        try:
+            return super()._apply(fn, recurse)
+        finally:
+            self._parameters["weight"] = w
 
 
 class Expert(nn.Module):
@@ -109,11 +121,45 @@ class Expert(nn.Module):
         self.swiglu_limit = swiglu_limit
         self._cache = None
 
+    @property
+    def format(self) -> str:
+        """``"fp8"`` after :meth:`load_fp8` (the weights are then placeholders), else ``"dense"``."""
+        return "fp8" if self.w1.weight.is_meta else "dense"
+
+    def weight_dtype(self, name: str) -> torch.dtype:
+        """The dtype the reference computes this matrix in: its loader dequantises an fp8
+        checkpoint matrix to fp32 (``dspark_mlx/loading.py:103-107``)."""
+        return torch.float32 if self.format == "fp8" else getattr(self, name).weight.dtype
+
+    def load_fp8(self, **mats) -> None:
+        """Hold the shared expert as e4m3 codes + fp32 128x128 block scales, the checkpoint's
+        format for projection weights. Keywords ``w1``, ``w3``, ``w2``: ``(codes
+        uint8|float8_e4m3fn [out, in], scales fp32 [ceil(out/128), ceil(in/128)])``."""
+        for n in ("w1", "w3", "w2"):
+            codes, scales = mats[n]
+            lin = getattr(self, n)
+            shape = tuple(lin.weight.shape)
+            if tuple(codes.shape) != shape:
+                raise ValueError(f"shared expert {n}: codes must be {shape}, got {tuple(codes.shape)}")
+            lin.weight = nn.Parameter(torch.empty(shape, dtype=torch.float32, device="meta"), requires_grad=False)
+            self.register_buffer(f"{n}_codes", codes.view(torch.uint8) if codes.dtype != torch.uint8 else codes)
+            self.register_buffer(f"{n}_scale", scales.to(torch.float32))
+        self._cache = None
+
     def packed(self) -> Tuple[PackedMatrix, PackedMatrix, PackedMatrix]:
-        srcs = (self.w1.weight, self.w3.weight, self.w2.weight)
+        names = ("w1", "w3", "w2")
+        if self.format == "fp8":
+            srcs = tuple(getattr(self, f"{n}_{s}") for n in names for s in ("codes", "scale"))
+        else:
+            srcs = tuple(getattr(self, n).weight for n in names)
         key = tuple((t.data_ptr(), t._version, t.dtype, t.device) for t in srcs)
         if self._cache is None or self._cache[0] != key:
-            self._cache = (key, tuple(pack("dense", data=t.detach(), device=t.device) for t in srcs))
+            if self.format == "fp8":
+                mats = tuple(pack("fp8", data=srcs[2 * i], scales=srcs[2 * i + 1], device=srcs[2 * i].device)
+                             for i in range(3))
+            else:
+                mats = tuple(pack("dense", data=t.detach(), device=t.device) for t in srcs)
+            self._cache = (key, mats)
         return self._cache[1]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -134,15 +180,15 @@ class Expert(nn.Module):
         check(L.dsm_stage_rows(ptr(x2), dtype_code(x2.dtype), n, p1.cols, None, n, 1, ptr(xs), cap, ptr(xscale), s),
               "dsm_stage_rows")
         bf16x = x2.dtype == torch.bfloat16
-        rgu = int(bf16x and self.w1.weight.dtype == torch.bfloat16) | (2 if bf16x else 0)
-        rgo = int(bf16x and self.w2.weight.dtype == torch.bfloat16)
+        rgu = int(bf16x and self.weight_dtype("w1") == torch.bfloat16) | (2 if bf16x else 0)
+        rgo = int(bf16x and self.weight_dtype("w2") == torch.bfloat16)
         hsc = 1.0 if 0 < self.swiglu_limit and self.swiglu_limit ** 2 < 30000 else 1.0 / 256
         check(L.dsm_expert_gate_up(ptr(xs), ptr(xscale), cap, p1.cols, ptr(offsets), 1, p1.wfmt, p1.group_size,
                                    ptr(p1.packed), ptr(p3.packed), p1.rows, _lib.ACT_SWIGLU_CLAMP,
                                    float(self.swiglu_limit), rgu, ptr(hs), hsc, n, s), "dsm_expert_gate_up")
         check(L.dsm_expert_down(ptr(hs), hsc, cap, p2.cols, ptr(offsets), 1, p2.wfmt, p2.group_size, ptr(p2.packed),
                                 p2.rows, rgo, ptr(o), p2.rows, None, n, s), "dsm_expert_down")
-        out_dt = torch.promote_types(dt, self.w2.weight.dtype)
+        out_dt = torch.promote_types(dt, self.weight_dtype("w2"))
         return o.to(out_dt).reshape(*shape[:-1], p2.rows)
 
 
@@ -284,8 +330,8 @@ class MoE(nn.Module):
         bf16x = x_dtype == torch.bfloat16
         rgu, ro = self.routed_round_flags(x_dtype)
         sh = self.shared_experts
-        s_gu = bf16x and sh.w1.weight.dtype == torch.bfloat16
-        s_o = bf16x and sh.w2.weight.dtype == torch.bfloat16
+        s_gu = bf16x and sh.weight_dtype("w1") == torch.bfloat16
+        s_o = bf16x and sh.weight_dtype("w2") == torch.bfloat16
         hbit = 2 if bf16x else 0
         return rgu, ro, int(s_gu) | hbit, int(s_o)
 

@@ -43,7 +43,7 @@ class PackedMatrix:
 
 
 def _dev_u8(t: torch.Tensor, device) -> torch.Tensor:
-    if t.dtype in (torch.float8_e4m3fn,):
+    if t.dtype != torch.uint8 and t.element_size() == 1:  # e4m3 / e8m0 / packed e2m1 / int8 bytes
         t = t.view(torch.uint8)
     return t.to(device=device).contiguous()
 

@@ -32,6 +32,7 @@ __all__ = [
     "e4m3_decode",
     "e2m1_decode",
     "e4m3_encode",
+    "e8m0_decode",
     "dequant_fp8_blockwise",
     "dequant_fp4_groupwise",
     "fp8_weight_dequant",
@@ -64,6 +65,15 @@ def e2m1_decode(codes) -> torch.Tensor:
     normal = (1.0 + man / 2.0) * torch.pow(2.0, (exp - 1).to(torch.float64))
     sub = man * 0.5
     return (torch.where(exp == 0, sub, normal) * sign).to(torch.float32)
+
+
+def e8m0_decode(codes) -> torch.Tensor:
+    """e8m0 scale bytes -> fp32 ``2^(code - 127)`` (the checkpoint's block scales,
+    ``dspark_mlx/loading.py:7-18``; 255 is NaN). Computed in float64, where every such power
+    of two is exact, then rounded to fp32, where it is exact too (``2^-127`` as a subnormal)."""
+    c = torch.as_tensor(np.asarray(codes, dtype=np.uint8)).to(torch.float64)
+    val = torch.pow(torch.tensor(2.0, dtype=torch.float64), c - 127.0)
+    return torch.where(c == 255, torch.tensor(float("nan"), dtype=torch.float64), val).to(torch.float32)
 
 
 def e4m3_encode(values: torch.Tensor) -> torch.Tensor:
