@@ -249,6 +249,32 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], u
 
 __device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
+// Sigmoid of the expert activations: the hardware exp2 and reciprocal approximations (a few
+// fp32 ulps, far below the bf16 rounding that follows in most paths). The correctly rounded
+// reciprocal (or an IEEE 1/x) is a long instruction sequence and made the SwiGLU epilogues
+// latency-bound. Routing scores and the hyper-connection mixes keep expf and IEEE division.
+__device__ __forceinline__ float act_sigmoid(float v) { return __fdividef(1.f, 1.f + __expf(-v)); }
+
+// SwiGLU of the expert products (dspark_mlx/model/moe.py:37-44): silu(g) * u, with g clamped
+// above and u on both sides at `limit` when limit > 0. DSM_ACT_SILU_MUL_BF16 is nn.silu(g) * u
+// on bf16 arrays, where every elementwise op rounds to bf16. The kind is a compile-time
+// parameter and the clamp a select, so a loop over columns has no branch.
+template <bool kSiluBf16>
+__device__ __forceinline__ float swiglu(float g, float u, float limit) {
+  if constexpr (kSiluBf16) {
+    const float sig = bf16_round(act_sigmoid(g));
+    return bf16_round(g * sig) * u;
+  } else {
+    const bool clamp = limit > 0.f;
+    u = clamp ? fminf(fmaxf(u, -limit), limit) : u;
+    g = clamp ? fminf(g, limit) : g;
+    return g * act_sigmoid(g) * u;
+  }
+}
+__device__ __forceinline__ float swiglu(float g, float u, int act, float limit) {
+  return act == DSM_ACT_SILU_MUL_BF16 ? swiglu<true>(g, u, limit) : swiglu<false>(g, u, limit);
+}
+
 template <typename T>
 __device__ __forceinline__ float load_as_float(const T* p, int64_t i);
 template <>

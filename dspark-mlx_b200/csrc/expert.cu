@@ -70,22 +70,6 @@ __device__ __forceinline__ int group_count(const ExpertArgs& a, int e) {
   return a.offsets ? a.offsets[e + 1] - a.offsets[e] : int(a.n_rows);
 }
 
-__device__ __forceinline__ float sigmoidf_(float v) { return 1.f / (1.f + expf(-v)); }
-
-__device__ __forceinline__ float apply_act(float g, float u, int act, float limit) {
-  if (act == DSM_ACT_SILU_MUL_BF16) {
-    // nn.silu(g) * u with bf16 arrays: every elementwise op rounds to bf16
-    const float sig = bf16_round(sigmoidf_(g));
-    const float s = bf16_round(g * sig);
-    return s * u;
-  }
-  if (limit > 0.f) {
-    u = fminf(fmaxf(u, -limit), limit);
-    g = fminf(g, limit);
-  }
-  return g * sigmoidf_(g) * u;
-}
-
 // expert e owning unit u: the largest e with pre[e] <= u (pre[0] = 0, pre[E] = total)
 __device__ __forceinline__ int find_expert(const int* pre, int n_experts, int u) {
   int lo = 0, hi = n_experts - 1;
@@ -326,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
               gv = bf16_round(gv);
               uv = bf16_round(uv);
             }
-            float h = apply_act(gv, uv, a.act, a.limit);
+            float h = swiglu(gv, uv, a.act, a.limit);
             if (a.round_gu & 2) h = bf16_round(h);
             a.h_out[(int64_t(rt) * a.h_rows_cap + r) * kStagePitch + rloc] = __float2half_rn(h * a.h_scale);
           } else {

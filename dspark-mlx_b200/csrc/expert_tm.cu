@@ -39,6 +39,7 @@
 // ld.shared.v4 of one chunk covers 32 consecutive rows: 512 contiguous bytes, no bank
 // conflicts.
 #include <algorithm>
+#include <type_traits>
 
 #include "tcgen05.cuh"
 
@@ -451,30 +452,71 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
               usum[i] += __uint_as_float(pv[i]);
           }
         }
+        if constexpr (DUAL && P >= 4) {
+          // decode widths: the epilogue overlaps the next unit's main loop (two accumulator
+          // buffers), and the branch-free form below would not fit the register budget of
+          // this thread count
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int col = cb + i;
-          if (col >= rows) break;
-          const int64_t r = int64_t(off) + chunk * BN + col;
-          const float xs = a.act_scale ? a.act_scale[r] : a.act_scale_const;
-          if constexpr (DUAL) {
+          for (int i = 0; i < 16; ++i) {
+            const int col = cb + i;
+            if (col >= rows) break;
+            const int64_t r = int64_t(off) + chunk * BN + col;
+            const float xs = a.act_scale ? a.act_scale[r] : a.act_scale_const;
             float gg = gsum[i] * xs * wmul_a;
             float uu = usum[i] * xs * wmul_b;
             if (a.round_gu & 1) {
               gg = bf16_round(gg);
               uu = bf16_round(uu);
             }
-            float h = tc_act(gg, uu, a.act, a.limit);
+            float h = swiglu(gg, uu, a.act, a.limit);
             if (a.round_gu & 2) h = bf16_round(h);
             a.h_out[(int64_t(rt) * a.h_rows_cap + r) * kStagePitch + rloc] = __float2half_rn(h * a.h_scale);
-          } else {
-            const int d = rt * kTmM + rloc;
-            if (d < a.out_rows) {
-              float v = gsum[i] * xs * wmul_a;
-              if (a.round_o) v = bf16_round(v);
-              const int64_t orow = a.o_row_map ? int64_t(a.o_row_map[r]) : r;
-              a.o_out[orow * a.ldo + d] = v;
+          }
+          continue;
+        }
+        // the block's 16 row scales (and output rows): one guarded load per lane, broadcast
+        // with a constant source lane per column
+        const int cl = cb + (lane & 15);
+        const int rl = off + chunk * BN + cl;
+        const float xs_b = (cl < rows && a.act_scale) ? a.act_scale[rl] : a.act_scale_const;
+        if constexpr (DUAL) {
+          // all 16 columns are computed without a branch (columns past `rows` hold unused
+          // accumulators), so their activation chains interleave; only the stores are guarded
+          const bool rg = a.round_gu & 1, rh = a.round_gu & 2;
+          __half* hp = a.h_out + (int64_t(rt) * a.h_rows_cap + off + chunk * BN + cb) * kStagePitch + rloc;
+          auto block = [&](auto silu_tag) {
+#pragma unroll
+            for (int i0 = 0; i0 < 16; i0 += 8) {  // 8 chains at a time: ILP within the register budget
+              float hv[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float xs = __shfl_sync(0xffffffffu, xs_b, i0 + i);
+                float gg = gsum[i0 + i] * xs * wmul_a;
+                float uu = usum[i0 + i] * xs * wmul_b;
+                gg = rg ? bf16_round(gg) : gg;
+                uu = rg ? bf16_round(uu) : uu;
+                const float h = swiglu<decltype(silu_tag)::value>(gg, uu, a.limit);
+                hv[i] = (rh ? bf16_round(h) : h) * a.h_scale;
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                if (cb + i0 + i < rows) hp[int64_t(i0 + i) * kStagePitch] = __float2half_rn(hv[i]);
             }
+          };
+          if (a.act == DSM_ACT_SILU_MUL_BF16)
+            block(std::true_type{});
+          else
+            block(std::false_type{});
+        } else {
+          const int or_b = (cl < rows && a.o_row_map) ? a.o_row_map[rl] : rl;
+          const int d = rt * kTmM + rloc;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float xs = __shfl_sync(0xffffffffu, xs_b, i);
+            const int orow = __shfl_sync(0xffffffffu, or_b, i);
+            float v = gsum[i] * xs * wmul_a;
+            v = a.round_o ? bf16_round(v) : v;
+            if (cb + i < rows && d < a.out_rows) a.o_out[int64_t(orow) * a.ldo + d] = v;
           }
         }
       }

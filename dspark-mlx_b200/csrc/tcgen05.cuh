@@ -14,20 +14,6 @@ int make_stage_map(CUtensorMap* map, const void* staged, int64_t rows_cap, int k
 
 namespace tc {
 
-__device__ __forceinline__ float tc_sigmoid(float v) { return 1.f / (1.f + expf(-v)); }
-
-__device__ __forceinline__ float tc_act(float g, float u, int act, float limit) {
-  if (act == DSM_ACT_SILU_MUL_BF16) {
-    const float sig = bf16_round(tc_sigmoid(g));
-    return bf16_round(g * sig) * u;
-  }
-  if (limit > 0.f) {
-    u = fminf(fmaxf(u, -limit), limit);
-    g = fminf(g, limit);
-  }
-  return g * tc_sigmoid(g) * u;
-}
-
 // ---- tcgen05 / TMA wrappers -----------------------------------------------------------
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
                                             uint64_t* bar) {
