@@ -514,7 +514,7 @@ def time_gate_up(moe, x, ids, args, L, dev):
 
 
 QWEN3_METRIC = "Qwen3 draft-layer MLP tokens/s (8-bit affine, L2 flushed per step); HBM GB/s"
-QWEN3_KERNELS_PER_STEP = 3  # staging, gate/up, down
+QWEN3_KERNELS_PER_STEP = 4  # staging, gate/up, down (K-split), split sum + cast
 
 
 def _qwen3_cpu_weights(mlp):

@@ -57,6 +57,15 @@ int expert_tm_gate_up(int wfmt, int group_size, const void* x_staged, const floa
 int expert_tm_down(int wfmt, int group_size, const void* h_staged, float h_scale, int64_t rows_cap, int inter,
                    const int32_t* offsets, int n_experts, const void* w2, int dim, int round_o, float* o_rows,
                    int ldo, const int32_t* o_row_map, int64_t n_rows, void* stream);
+// Dense (one-expert) down product split along K into k_splits fp32 partial slabs
+// partials[s][n_rows][dim] (tm formats only; units of up to 128 rows); tm_down_splits picks
+// the split count that fills the GPU without an empty split
+int tm_down_splits(int inter, int dim, int64_t n_rows, int max_splits);
+int expert_tm_down_split(int wfmt, int group_size, const void* h_staged, float h_scale, int64_t rows_cap,
+                         int inter, const void* w2, int dim, int k_splits, float* partials, int64_t n_rows,
+                         void* stream);
+// h staging scale of the SwiGLU output: 1 when the clamp bounds |h| by limit^2, else 2^-8
+float h_scale_for(int act, float limit);
 // 0 = choose by rows per expert, 1 = always the decode kernel, 2 = tcgen05 where supported
 int expert_regime();
 

@@ -1,0 +1,135 @@
+// A dense SwiGLU MLP as one call: the Qwen3 draft layer's MLP (dspark_mlx/arch/qwen3.py:146-154,
+// down(silu(gate(x)) * up(x))) and, in general, one expert applied to every row
+// (dspark_mlx/model/moe.py:82-97). Stage x, gate/up with the activation fused, down, cast.
+//
+// A dense layer with few tokens has few weight row tiles for its down product (hidden / 128
+// of them), each with a long K (inter). Run whole, they leave most SMs idle. For the
+// tensor-memory formats the down product is split along K: every (row tile, K range) unit
+// converts its weight tiles once, for up to 128 token rows, and writes an fp32 partial slab.
+// reduce_splits_kernel then adds the slabs in split order, which is fixed, so the result
+// does not depend on scheduling. It applies the bf16 rounding of the reference's products
+// and casts to the output dtype.
+#include <algorithm>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace dsm {
+
+float h_scale_for(int act, float limit) {
+  // |h| <= limit^2 under the clamp; keep f16 headroom otherwise
+  if (act == DSM_ACT_SWIGLU_CLAMP && limit > 0.f && limit * limit < 30000.f) return 1.f;
+  return 1.f / 256.f;
+}
+
+namespace {
+
+constexpr int kMaxSplits = 8;
+constexpr int64_t kSplitCtaBound = 160;  // at least the SM count of the part: sizes the workspace
+
+template <typename YT>
+__global__ void __launch_bounds__(256) reduce_splits_kernel(const float* __restrict__ parts, int n_splits,
+                                                            int64_t stride, int64_t count, int round,
+                                                            YT* __restrict__ y) {
+  // four consecutive elements per thread; count and stride are multiples of 4 (dim % 4 == 0)
+  for (int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < count;
+       i += int64_t(gridDim.x) * blockDim.x * 4) {
+    float4 acc = *reinterpret_cast<const float4*>(parts + i);
+    for (int s = 1; s < n_splits; ++s) {
+      const float4 v = *reinterpret_cast<const float4*>(parts + s * stride + i);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    const float r[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float v = round ? bf16_round(r[c]) : r[c];
+      if constexpr (std::is_same<YT, __nv_bfloat16>::value)
+        y[i + c] = __float2bfloat16_rn(v);
+      else
+        y[i + c] = v;
+    }
+  }
+}
+
+struct DenseLayout {
+  void *xs, *hs;
+  float *xscale, *parts;
+  int64_t cap;
+  int max_splits;
+  size_t bytes;
+};
+
+int64_t split_bound(int64_t n_tokens, int dim) {
+  const int64_t units = ceil_div(dim, 128) * ceil_div(n_tokens, 128);
+  return std::max<int64_t>(1, std::min<int64_t>(kMaxSplits, kSplitCtaBound / units));
+}
+
+DenseLayout dense_layout(int64_t n_tokens, int dim, int inter, void* base) {
+  DenseLayout L{};
+  L.cap = dsm_stage_rows_cap(n_tokens);
+  L.max_splits = int(split_bound(n_tokens, dim));
+  char* p = static_cast<char*>(base);
+  size_t off = 0;
+  auto take = [&](size_t b) {
+    void* q = p ? p + off : nullptr;
+    off += (b + 255) / 256 * 256;
+    return q;
+  };
+  L.xs = take(dsm_stage_bytes(L.cap, dim));
+  L.xscale = static_cast<float*>(take(size_t(L.cap) * 4));
+  L.hs = take(dsm_stage_bytes(L.cap, inter));
+  L.parts = static_cast<float*>(take(size_t(L.max_splits) * size_t(n_tokens) * dim * 4));
+  L.bytes = off;
+  return L;
+}
+
+}  // namespace
+}  // namespace dsm
+
+using namespace dsm;
+
+extern "C" size_t dsm_dense_mlp_workspace_bytes(int64_t n_tokens, int dim, int inter) {
+  if (n_tokens <= 0 || dim <= 0 || inter <= 0) return 0;
+  return dense_layout(n_tokens, dim, inter, nullptr).bytes;
+}
+
+extern "C" int dsm_dense_mlp(const void* x, int x_dtype, int64_t n_tokens, int dim, int inter, int wfmt,
+                             int group_size, const void* w1, const void* w3, const void* w2, int act,
+                             float swiglu_limit, int round_gu, int round_o, void* y, int y_dtype, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  DSM_REQUIRE(n_tokens >= 0 && dim > 0 && inter > 0, "dsm_dense_mlp: bad shape");
+  DSM_REQUIRE(dim % 4 == 0, "dsm_dense_mlp: dim must be a multiple of 4");
+  DSM_REQUIRE(x && w1 && w3 && w2 && y, "dsm_dense_mlp: null pointer");
+  DSM_REQUIRE(y_dtype == DSM_DT_F32 || y_dtype == DSM_DT_BF16, "dsm_dense_mlp: y must be F32 or BF16");
+  if (n_tokens == 0) return DSM_OK;
+  const DenseLayout L = dense_layout(n_tokens, dim, inter, workspace);
+  if (!workspace || workspace_bytes < L.bytes) return fail(DSM_ERR_WORKSPACE, "dsm_dense_mlp: workspace too small");
+  cudaStream_t st = as_stream(stream);
+  int rc = dsm_stage_rows(x, x_dtype, n_tokens, dim, nullptr, n_tokens, 1, L.xs, L.cap, L.xscale, stream);
+  if (rc) return rc;
+  const float hs = h_scale_for(act, swiglu_limit);
+  rc = dsm_expert_gate_up(L.xs, L.xscale, L.cap, dim, nullptr, 1, wfmt, group_size, w1, w3, inter, act,
+                          swiglu_limit, round_gu, L.hs, hs, n_tokens, stream);
+  if (rc) return rc;
+  int splits = 1;
+  if (tm_supports(wfmt) && expert_regime() != 1)
+    splits = tm_down_splits(inter, dim, n_tokens, L.max_splits);
+  if (splits > 1) {
+    rc = expert_tm_down_split(wfmt, group_size, L.hs, hs, L.cap, inter, w2, dim, splits, L.parts, n_tokens, stream);
+  } else {
+    rc = dsm_expert_down(L.hs, hs, L.cap, inter, nullptr, 1, wfmt, group_size, w2, dim, 0, L.parts, dim, nullptr,
+                         n_tokens, stream);
+  }
+  if (rc) return rc;
+  const int64_t count = n_tokens * dim;
+  const int grid = int(std::min<int64_t>(ceil_div(count, 4 * 256), 4 * num_sms()));
+  if (y_dtype == DSM_DT_BF16)
+    reduce_splits_kernel<<<grid, 256, 0, st>>>(L.parts, splits, count, count, round_o,
+                                               static_cast<__nv_bfloat16*>(y));
+  else
+    reduce_splits_kernel<<<grid, 256, 0, st>>>(L.parts, splits, count, count, round_o, static_cast<float*>(y));
+  return check_launch("reduce_splits");
+}

@@ -64,8 +64,9 @@ struct TmCfg {
   static constexpr int NM = DUAL ? 2 : 1;
   // 128-K chunks per stage: two for the single-matrix (down) product, whose tiles carry half
   // the bytes of a gate/up pair, so the per-stage barrier, copy and commit costs are spread
-  // over the same bytes; the gate/up pair keeps one (its A buffer is already 128 columns)
-  static constexpr int KS = DUAL ? 1 : 2;
+  // over the same bytes; the gate/up pair keeps one (its A buffer is already 128 columns),
+  // and so do 128-row units, whose activation rows alone fill 32 KB per chunk
+  static constexpr int KS = (DUAL || BN >= 128) ? 1 : 2;
   static constexpr int kMma0 = kTmConv0 + CW;  // first MMA issuer warp
   static constexpr int kThreads = 32 * (kMma0 + P);
   static constexpr int kKkStride = P / NM;     // issuer p: matrix p % NM, k16 steps p / NM + j * kKkStride
@@ -105,6 +106,10 @@ struct TmArgs {
   int group_size;  // affine
   int tile_b;      // packed tile bytes
   int stage_b;     // shared-memory stage bytes
+  int k_splits;    // single-matrix product only: K ranges per row tile, each writing its own
+                   // fp32 partial slab (o_out + split * o_split_stride); 1 = no split
+  int k_per;       // 128-K chunks per split, a multiple of KS
+  int64_t o_split_stride;
   int act;
   float limit;
   int round_gu;
@@ -121,6 +126,31 @@ __device__ __forceinline__ int tm_first(const TmArgs& a, int e) { return a.offse
 __device__ __forceinline__ int tm_count(const TmArgs& a, int e) {
   return a.offsets ? a.offsets[e + 1] - a.offsets[e] : int(a.n_rows);
 }
+__device__ __forceinline__ int tm_find(const int* pre, int n, int u);
+
+// Work unit u: expert e, weight row tile rt, block `chunk` of the expert's rows, K split ks
+// covering 128-K chunks [kc0, kc1). Units of one row tile are adjacent, token blocks
+// innermost, so the CTAs re-reading a weight tile for other token blocks run together.
+struct TmUnit {
+  int e, rt, chunk, ks, kc0, kc1, cnt;
+};
+template <int BN>
+__device__ __forceinline__ TmUnit tm_unit(const TmArgs& a, const int* pre, int E, int u, int kcs) {
+  TmUnit w;
+  w.e = tm_find(pre, E, u);
+  w.cnt = tm_count(a, w.e);
+  const int nch = (w.cnt + BN - 1) / BN;
+  const int per_rt = nch * a.k_splits;
+  const int local = u - pre[w.e];
+  w.rt = local / per_rt;
+  const int r2 = local % per_rt;
+  w.ks = r2 / nch;
+  w.chunk = r2 % nch;
+  w.kc0 = w.ks * a.k_per;
+  w.kc1 = min(kcs, w.kc0 + a.k_per);
+  return w;
+}
+
 __device__ __forceinline__ int tm_find(const int* pre, int n, int u) {
   int lo = 0, hi = n - 1;
   while (lo < hi) {
@@ -180,7 +210,7 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
       int v = 0;
       if (e < E) {
         const int cnt = tm_count(a, e);
-        v = cnt > 0 ? a.rt_count * ((cnt + BN - 1) / BN) : 0;
+        v = cnt > 0 ? a.rt_count * ((cnt + BN - 1) / BN) * a.k_splits : 0;
       }
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -209,17 +239,13 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
       uint32_t ph = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-        const int e = tm_find(pre, E, u);
-        const int cnt = tm_count(a, e);
-        const int nch = (cnt + BN - 1) / BN;
-        const int local = u - pre[e];
-        const int rt = local / nch, chunk = local % nch;
-        const int row0 = tm_first(a, e) + chunk * BN;
-        const int nbox = (min(BN, cnt - chunk * BN) + kTmBoxRows - 1) / kTmBoxRows;
-        const int64_t tile0 = (int64_t(e) * a.rt_count + rt) * kcs;
+        const TmUnit w = tm_unit<BN>(a, pre, E, u, kcs);
+        const int row0 = tm_first(a, w.e) + w.chunk * BN;
+        const int nbox = (min(BN, w.cnt - w.chunk * BN) + kTmBoxRows - 1) / kTmBoxRows;
+        const int64_t tile0 = (int64_t(w.e) * a.rt_count + w.rt) * kcs;
         const uint32_t tx1 = uint32_t(NM * tile_b + 2 * nbox * kTmBoxRows * 128);  // per chunk
-        for (int kc = 0; kc < kcs; kc += C::KS) {
-          const int nk = min(C::KS, kcs - kc);
+        for (int kc = w.kc0; kc < w.kc1; kc += C::KS) {
+          const int nk = min(C::KS, w.kc1 - kc);
           if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u)) {
             *abort_flag = 1;
             ok = false;
@@ -266,11 +292,8 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
         aoff[i] = uint32_t(C::kDCols + m * 64 * C::KS + kk * 8);
       }
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++j) {
-        const int e = tm_find(pre, E, u);
-        const int cnt = tm_count(a, e);
-        const int nch = (cnt + BN - 1) / BN;
-        const int chunk = (u - pre[e]) % nch;
-        const int n_mma = (min(BN, cnt - chunk * BN) + 15) / 16 * 16;
+        const TmUnit w = tm_unit<BN>(a, pre, E, u, kcs);
+        const int n_mma = (min(BN, w.cnt - w.chunk * BN) + 15) / 16 * 16;
         const uint32_t idesc = umma_idesc_f16(kTmM, n_mma);
         const int buf = j % C::DB;
         if (*abort_flag || !mbar_wait(&tempty[buf], ((j / C::DB) & 1) ^ 1u)) {
@@ -280,8 +303,8 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem + uint32_t((buf * P + p) * BN);
-        for (int kc = 0; kc < kcs; kc += C::KS) {
-          const int nkk = 8 * min(C::KS, kcs - kc);  // k16 steps in this stage
+        for (int kc = w.kc0; kc < w.kc1; kc += C::KS) {
+          const int nkk = 8 * min(C::KS, w.kc1 - kc);  // k16 steps in this stage
           // the converters arrive on afull only after they saw the stage's copies land
           // (full[s]), so acquiring afull also orders the activation rows read below
           if (*abort_flag || !mbar_wait(&afull[ab], aph)) {
@@ -295,7 +318,7 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
 #pragma unroll
           for (int i = 0; i < kSteps; ++i) {
             if (kk0 + i * C::kKkStride >= nkk) break;
-            umma_f16_tmem_a(d, ast + aoff[i], bst + boff[i], idesc, (kc > 0 || i > 0) ? 1u : 0u);
+            umma_f16_tmem_a(d, ast + aoff[i], bst + boff[i], idesc, (kc > w.kc0 || i > 0) ? 1u : 0u);
           }
           umma_commit(&empty[s]);  // activation rows and the A buffer read
           if (++s == S) s = 0;
@@ -323,8 +346,9 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
     uint32_t ph = 0, wph = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-      for (int kc = 0; kc < kcs; kc += C::KS, ++g) {
-        const int nk = min(C::KS, kcs - kc);
+      const TmUnit w = tm_unit<BN>(a, pre, E, u, kcs);
+      for (int kc = w.kc0; kc < w.kc1; kc += C::KS, ++g) {
+        const int nk = min(C::KS, w.kc1 - kc);
         if (*abort_flag || !mbar_wait(&full[s], ph)) {
           *abort_flag = 1;
           ok = false;
@@ -419,13 +443,11 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
     const uint32_t lane_base = tmem + (uint32_t(32 * warp) << 16);
     int j = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++j) {
-      const int e = tm_find(pre, E, u);
+      const TmUnit w = tm_unit<BN>(a, pre, E, u, kcs);
+      const int e = w.e, rt = w.rt, chunk = w.chunk;
       const int off = tm_first(a, e);
-      const int cnt = tm_count(a, e);
-      const int nch = (cnt + BN - 1) / BN;
-      const int local = u - pre[e];
-      const int rt = local / nch, chunk = local % nch;
-      const int rows = min(BN, cnt - chunk * BN);
+      const int rows = min(BN, w.cnt - chunk * BN);
+      float* const o_out = a.o_out + w.ks * a.o_split_stride;
       const int buf = j % C::DB;
       if (*abort_flag || !mbar_wait(&tfull[buf], (j / C::DB) & 1)) {
         *abort_flag = 1;
@@ -516,7 +538,7 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
             const int orow = __shfl_sync(0xffffffffu, or_b, i);
             float v = gsum[i] * xs * wmul_a;
             v = a.round_o ? bf16_round(v) : v;
-            if (cb + i < rows && d < a.out_rows) a.o_out[int64_t(orow) * a.ldo + d] = v;
+            if (cb + i < rows && d < a.out_rows) o_out[int64_t(orow) * a.ldo + d] = v;
           }
         }
       }
@@ -566,6 +588,10 @@ constexpr int kTmCW = 8;
 // stages in flight, and it has few row tiles to spread.)
 template <int FMT, bool DUAL>
 int launch_width(const TmArgs& a, const void* staged, int64_t rows_cap, cudaStream_t s) {
+  if constexpr (!DUAL) {
+    // K-split dense products: every weight tile converted once, for up to 128 rows at a time
+    if (a.k_splits > 1) return launch_tm<FMT, DUAL, 128, kTmCW, 2>(a, staged, rows_cap, s);
+  }
   const int64_t busy = std::max<int64_t>(1, std::min<int64_t>(a.n_rows, a.n_experts));
   const int64_t units64 = int64_t(a.rt_count) * (busy + a.n_rows / 64);  // estimates
   const int64_t units128 = int64_t(a.rt_count) * (busy + a.n_rows / 128);
@@ -616,6 +642,8 @@ int expert_tm_gate_up(int wfmt, int group_size, const void* x_staged, const floa
   a.h_out = static_cast<__half*>(h_staged);
   a.h_rows_cap = rows_cap;
   a.group_size = group_size > 0 ? group_size : 64;
+  a.k_splits = 1;
+  a.k_per = a.kc_count;
   return dispatch_tm<true>(wfmt, a, x_staged, rows_cap, as_stream(stream));
 }
 
@@ -638,6 +666,43 @@ int expert_tm_down(int wfmt, int group_size, const void* h_staged, float h_scale
   a.ldo = ldo;
   a.round_o = round_o;
   a.group_size = group_size > 0 ? group_size : 64;
+  a.k_splits = 1;
+  a.k_per = a.kc_count;
+  return dispatch_tm<false>(wfmt, a, h_staged, rows_cap, as_stream(stream));
+}
+
+int tm_down_splits(int inter, int dim, int64_t n_rows, int max_splits) {
+  const int kcs = int(ceil_div(inter, kChunkK));
+  const int64_t units = ceil_div(dim, kTmM) * ceil_div(n_rows, 128);
+  int sp = int(std::min<int64_t>(std::min(max_splits, kcs), std::max<int64_t>(1, persistent_ctas() / units)));
+  if (sp <= 1) return 1;
+  const int per = (kcs + sp - 1) / sp;
+  return (kcs + per - 1) / per;  // no empty split
+}
+
+int expert_tm_down_split(int wfmt, int group_size, const void* h_staged, float h_scale, int64_t rows_cap,
+                         int inter, const void* w2, int dim, int k_splits, float* partials, int64_t n_rows,
+                         void* stream) {
+  TmArgs a{};
+  a.wa = static_cast<const uint8_t*>(w2);
+  a.wb = nullptr;
+  a.act_scale = nullptr;
+  a.act_scale_const = 1.f / h_scale;
+  a.offsets = nullptr;
+  a.n_rows = n_rows;
+  a.n_experts = 1;
+  a.out_rows = dim;
+  a.rt_count = int(ceil_div(dim, kTmM));
+  a.kc_count = int(ceil_div(inter, kChunkK));
+  a.o_out = partials;
+  a.o_row_map = nullptr;
+  a.ldo = dim;
+  a.round_o = 0;  // rounding belongs to the sum of the partials
+  a.group_size = group_size > 0 ? group_size : 64;
+  a.k_splits = std::max(1, k_splits);
+  a.k_per = (a.kc_count + a.k_splits - 1) / a.k_splits;  // 128-row units take one chunk per stage
+  if ((a.k_splits - 1) * a.k_per >= a.kc_count) return fail(DSM_ERR_INVALID_ARGUMENT, "expert_tm: empty K split");
+  a.o_split_stride = n_rows * dim;
   return dispatch_tm<false>(wfmt, a, h_staged, rows_cap, as_stream(stream));
 }
 

@@ -52,12 +52,6 @@ SideStream* side_stream() {
 constexpr int kSharedCtas = 16;        // SMs given to the shared expert while the routed products run
 constexpr int64_t kOverlapTokens = 2048;  // largest call that overlaps the shared expert
 
-float h_scale_for(int act, float limit) {
-  // |h| <= limit^2 under the clamp; keep f16 headroom otherwise
-  if (act == DSM_ACT_SWIGLU_CLAMP && limit > 0.f && limit * limit < 30000.f) return 1.f;
-  return 1.f / 256.f;
-}
-
 struct Layout {
   void* scores;
   float* weights;

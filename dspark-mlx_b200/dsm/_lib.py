@@ -30,7 +30,8 @@ EXPORTED = (
     "dsm_stage_rows_cap", "dsm_stage_rows", "dsm_packed_bytes", "dsm_pack_weights",
     "dsm_affine_quantize", "dsm_expert_gate_up", "dsm_expert_down", "dsm_combine",
     "dsm_moe_workspace_bytes", "dsm_moe_forward", "dsm_gather_rows", "dsm_segment_ids",
-    "dsm_set_expert_regime", "dsm_hc_pre_norm", "dsm_hc_post",
+    "dsm_set_expert_regime", "dsm_hc_pre_norm", "dsm_hc_post", "dsm_dense_mlp_workspace_bytes",
+    "dsm_dense_mlp",
 )
 
 
@@ -87,6 +88,8 @@ def _declare(lib):
         "dsm_combine": (I, [V, V, V, I64, I, I, V, V, I, V]),
         "dsm_hc_pre_norm": (I, [V, I, I64, I, I, V, V, V, I, F, F, V, V, V, V, V]),
         "dsm_hc_post": (I, [V, V, I, I64, I, I, V, V, V, V]),
+        "dsm_dense_mlp_workspace_bytes": (S, [I64, I, I]),
+        "dsm_dense_mlp": (I, [V, I, I64, I, I, I, I, V, V, V, I, F, I, I, V, I, V, S, V]),
         "dsm_moe_workspace_bytes": (S, [POINTER(MoEDesc)]),
         "dsm_moe_forward": (I, [POINTER(MoEDesc), V, I, V, I, I64, V, V, V, V, S, V]),
     }

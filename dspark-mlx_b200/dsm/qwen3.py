@@ -79,6 +79,7 @@ class Qwen3MLP(nn.Module):
         self.gate_proj = Projection(h, i)
         self.up_proj = Projection(h, i)
         self.down_proj = Projection(i, h)
+        self._ws: Optional[torch.Tensor] = None
 
     def quantize(self, bits: int = 8, group_size: int = 64) -> "Qwen3MLP":
         """``nn.quantize`` of the three projections with ``quantize_drafter``'s predicate."""
@@ -97,16 +98,6 @@ class Qwen3MLP(nn.Module):
         if pg.wfmt != pu.wfmt or pg.group_size != pu.group_size:
             raise ValueError("gate_proj and up_proj must share a weight format")
         n = x2.shape[0]
-        L = lib()
-        cap = L.dsm_stage_rows_cap(n)
-        dev = x.device
-        xs = torch.empty(L.dsm_stage_bytes(cap, pg.cols), dtype=torch.uint8, device=dev)
-        xscale = torch.empty(cap, dtype=torch.float32, device=dev)
-        hs = torch.empty(L.dsm_stage_bytes(cap, pg.rows), dtype=torch.uint8, device=dev)
-        o = torch.empty(n, pd.rows, dtype=torch.float32, device=dev)
-        s = stream_ptr()
-        check(L.dsm_stage_rows(ptr(x2), dtype_code(dt), n, pg.cols, None, n, 1, ptr(xs), cap, ptr(xscale), s),
-              "dsm_stage_rows")
         g_dt = self.gate_proj.product_dtype(dt)
         u_dt = self.up_proj.product_dtype(dt)
         h_dt = torch.promote_types(g_dt, u_dt)
@@ -114,10 +105,14 @@ class Qwen3MLP(nn.Module):
         # bit 0: g and u rounded to bf16; bit 1: h rounded to bf16 (the elementwise ops' dtype)
         rgu = int(g_dt == torch.bfloat16 and u_dt == torch.bfloat16) | (2 if h_dt == torch.bfloat16 else 0)
         act = _lib.ACT_SILU_MUL_BF16 if g_dt == torch.bfloat16 else _lib.ACT_SWIGLU_CLAMP
-        h_scale = 1.0 / 256  # no clamp: h is unbounded, stage it scaled down into f16 range
-        check(L.dsm_expert_gate_up(ptr(xs), ptr(xscale), cap, pg.cols, None, 1, pg.wfmt, pg.group_size,
-                                   ptr(pg.packed), ptr(pu.packed), pg.rows, act, 0.0, rgu, ptr(hs), h_scale, n, s),
-              "dsm_expert_gate_up")
-        check(L.dsm_expert_down(ptr(hs), h_scale, cap, pd.cols, None, 1, pd.wfmt, pd.group_size, ptr(pd.packed),
-                                pd.rows, int(o_dt == torch.bfloat16), ptr(o), pd.rows, None, n, s), "dsm_expert_down")
-        return o.to(o_dt).reshape(*shape[:-1], pd.rows)
+        y = torch.empty(n, pd.rows, dtype=o_dt, device=x.device)
+        if n == 0:
+            return y.reshape(*shape[:-1], pd.rows)
+        L = lib()
+        need = L.dsm_dense_mlp_workspace_bytes(n, pg.cols, pg.rows)
+        if self._ws is None or self._ws.numel() < need or self._ws.device != x.device:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+        check(L.dsm_dense_mlp(ptr(x2), dtype_code(dt), n, pg.cols, pg.rows, pg.wfmt, pg.group_size, ptr(pg.packed),
+                              ptr(pu.packed), ptr(pd.packed), act, 0.0, rgu, int(o_dt == torch.bfloat16), ptr(y),
+                              dtype_code(o_dt), ptr(self._ws), self._ws.numel(), stream_ptr()), "dsm_dense_mlp")
+        return y.reshape(*shape[:-1], pd.rows)

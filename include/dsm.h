@@ -29,6 +29,7 @@
  *   dsm_hc_pre_norm     hc_pre + ffn_norm before the MoE       model/hyper.py:24-42, kernels.py:60-85,
  *                       (DSparkBlock.__call__, block.py:84-85) model/norm_rope.py:22-39
  *   dsm_hc_post         hc_post after the MoE (block.py:86)    model/hyper.py:45-51
+ *   dsm_dense_mlp       Qwen3MLP.__call__ / Expert.__call__    arch/qwen3.py:146-154, model/moe.py:82-97
  *   dsm_gather_rows, dsm_segment_ids: expert-parallel plumbing; the reference runs on one
  *                       device (tests/reference_model.py:55-56 forces world_size 1) and has
  *                       no counterpart.
@@ -177,6 +178,20 @@ int dsm_expert_down(const void* h_staged, float h_scale, int64_t rows_cap, int i
                     const int32_t* offsets, int n_experts, int wfmt, int group_size,
                     const void* w2_packed, int dim, int round_o, float* o_rows, int ldo,
                     const int32_t* o_row_map, int64_t n_rows, void* stream);
+
+/* ---- dense SwiGLU MLP: y = down(act(gate(x), up(x))) for every token ---------------------
+ * One expert over all rows (arch/qwen3.py:146-154, model/moe.py:82-97): staging, gate/up with
+ * the activation, down, and the cast to y_dtype (F32 or BF16) in one call. w1/w3/w2 packed
+ * by dsm_pack_weights with n_experts = 1 (w1, w3 [inter, dim], w2 [dim, inter]); act,
+ * swiglu_limit and round_gu as for dsm_expert_gate_up; round_o rounds y to bf16 values
+ * first. dim % 4 == 0. The fp4 and affine down product is split along K into partial sums
+ * added in a fixed order when the row tiles alone would leave SMs idle. Workspace from
+ * dsm_dense_mlp_workspace_bytes. */
+size_t dsm_dense_mlp_workspace_bytes(int64_t n_tokens, int dim, int inter);
+int dsm_dense_mlp(const void* x, int x_dtype, int64_t n_tokens, int dim, int inter, int wfmt, int group_size,
+                  const void* w1_packed, const void* w3_packed, const void* w2_packed, int act, float swiglu_limit,
+                  int round_gu, int round_o, void* y, int y_dtype, void* workspace, size_t workspace_bytes,
+                  void* stream);
 
 /* Kernel regime of the grouped expert products: 0 (default) picks by rows per busy
  * expert -- the mma.sync weight-streaming kernel at decode sizes, the tcgen05/TMEM kernel

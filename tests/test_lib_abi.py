@@ -52,12 +52,15 @@ def test_size_queries():
     assert cap >= 336 + 32 and cap % 8 == 0
     assert L.dsm_stage_bytes(cap, 4096) == 32 * cap * 160 * 2
     assert L.dsm_permute_workspace_bytes(131072, 256) == 128 * 256 * 4
+    # dense MLP: staged x and h plus up to 8 fp32 partial slabs of the down product
+    assert L.dsm_dense_mlp_workspace_bytes(112, 2560, 9728) >= 8 * 112 * 2560 * 4
+    assert L.dsm_dense_mlp_workspace_bytes(0, 2560, 9728) == 0
     d = _lib.MoEDesc(n_tokens=56, dim=4096, inter=2048, n_experts=256, topk=6)
     d.s1 = 1
     assert L.dsm_moe_workspace_bytes(ctypes.byref(d)) > 56 * 6 * 4096 * 4
 
 
-@pytest.mark.parametrize("call", ["router", "permute", "combine", "quantize"])
+@pytest.mark.parametrize("call", ["router", "permute", "combine", "quantize", "dense_mlp"])
 def test_bad_arguments_are_rejected_on_the_host(call):
     L = _lib.lib()
     if call == "router":
@@ -67,8 +70,11 @@ def test_bad_arguments_are_rejected_on_the_host(call):
         rc = L.dsm_permute(None, 10, 0, None, None, None, None, None, 0, None)
     elif call == "combine":
         rc = L.dsm_combine(None, None, None, 4, 0, 16, None, None, _lib.DT_BF16, None)
-    else:
+    elif call == "quantize":
         rc = L.dsm_affine_quantize(None, _lib.DT_BF16, 4, 100, 64, 8, None, None, None, None)
+    else:  # dim not a multiple of 4
+        rc = L.dsm_dense_mlp(None, _lib.DT_BF16, 4, 6, 128, _lib.WFMT_AFFINE8, 64, None, None, None, 1, 0.0, 3, 1,
+                             None, _lib.DT_BF16, None, 0, None)
     assert rc == 1
     assert L.dsm_last_error_message().decode()
 

@@ -6,7 +6,7 @@ from __future__ import annotations
 import pytest
 import torch
 
-from dsm import workloads as W
+from dsm import _lib, workloads as W
 from dsm.qwen3 import Qwen3MLP
 from helpers import MOE_TOL, max_rel_err
 import oracle
@@ -94,3 +94,15 @@ def test_full_size_q8_mlp_matches_oracle():
     # leading dims are kept: [16, 7, 2560] in, [16, 7, 2560] out
     y3 = mlp(x.reshape(16, 7, -1))
     assert y3.shape == (16, 7, 2560) and torch.equal(y3.reshape(112, -1), y)
+    # the K-split down product (fp32 partial slabs added in a fixed order) against the whole-K
+    # product the streaming regime keeps: the same sums in another order, so at most a
+    # last-bit flip of the bf16 output here and there
+    L = _lib.lib()
+    try:
+        L.dsm_set_expert_regime(1)
+        y_whole = mlp(x)
+        torch.cuda.synchronize()
+    finally:
+        L.dsm_set_expert_regime(0)
+    assert max_rel_err(y_whole, y) < 1e-2
+    assert (y_whole == y).float().mean() > 0.95
