@@ -8,3 +8,4 @@ the product package (``dsm``) never does and has no CPU fallback.
 from .moe_oracle import *  # noqa: F401,F403
 from .formats import *  # noqa: F401,F403
 from .block_oracle import *  # noqa: F401,F403
+from .head_oracle import *  # noqa: F401,F403

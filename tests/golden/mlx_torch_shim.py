@@ -483,6 +483,32 @@ def silu(x):
     return x * sigmoid(x)
 
 
+class Embedding(Module):
+    def __init__(self, num_embeddings: int, dims: int):
+        super().__init__()
+        self.weight = array(torch.randn(num_embeddings, dims) * (1.0 / np.sqrt(dims)))
+
+    def __call__(self, x):
+        return array(self.weight.t[_t(x).to(torch.int64)])
+
+
+# mlx.core.random.uniform served from a seeded torch generator; every draw is recorded so a
+# golden case can store the uniforms the reference's sampler consumed
+_random_gen = torch.Generator().manual_seed(0)
+random_draws: list = []
+
+
+def _uniform(low=0.0, high=1.0, shape=(), dtype=float32, key=None):
+    u = torch.rand(tuple(shape), generator=_random_gen) * (high - low) + low
+    random_draws.append(u.clone())
+    return array(u.to(dtype))
+
+
+def random_seed(seed: int) -> None:
+    _random_gen.manual_seed(seed)
+    random_draws.clear()
+
+
 def _tree_unflatten(items):
     out = {}
     for path, v in items:
@@ -512,6 +538,11 @@ def install() -> None:
     nn.Module = Module
     nn.Linear = Linear
     nn.silu = silu
+    nn.Embedding = Embedding
+    rnd = types.ModuleType("mlx.core.random")
+    rnd.uniform = _uniform
+    rnd.seed = random_seed
+    core.random = rnd
     utils = types.ModuleType("mlx.utils")
     utils.tree_unflatten = _tree_unflatten
     utils.tree_flatten = _tree_flatten
