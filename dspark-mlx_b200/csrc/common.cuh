@@ -44,9 +44,11 @@ bool tc_supports(int wfmt);
 int expert_tc_gate_up(int wfmt, const void* x_staged, const float* x_row_scale, int64_t rows_cap, int dim,
                       const int32_t* offsets, int n_experts, const void* w1, const void* w3, int inter, int act,
                       float limit, int round_gu, void* h_staged, float h_scale, int64_t n_rows, void* stream);
+// x_row_scale (optional): per-row activation scales instead of the constant 1 / h_scale
+// (a plain linear layer over rows staged by dsm_stage_rows)
 int expert_tc_down(int wfmt, const void* h_staged, float h_scale, int64_t rows_cap, int inter, const int32_t* offsets,
                    int n_experts, const void* w2, int dim, int round_o, float* o_rows, int ldo,
-                   const int32_t* o_row_map, int64_t n_rows, void* stream);
+                   const int32_t* o_row_map, int64_t n_rows, void* stream, const float* x_row_scale = nullptr);
 // fp4 and affine experts at every token count (expert_tm.cu): weights dequantised into
 // tensor memory
 bool tm_supports(int wfmt);
@@ -56,7 +58,8 @@ int expert_tm_gate_up(int wfmt, int group_size, const void* x_staged, const floa
                       void* stream);
 int expert_tm_down(int wfmt, int group_size, const void* h_staged, float h_scale, int64_t rows_cap, int inter,
                    const int32_t* offsets, int n_experts, const void* w2, int dim, int round_o, float* o_rows,
-                   int ldo, const int32_t* o_row_map, int64_t n_rows, void* stream);
+                   int ldo, const int32_t* o_row_map, int64_t n_rows, void* stream,
+                   const float* x_row_scale = nullptr);
 // Dense (one-expert) down product split along K into k_splits fp32 partial slabs
 // partials[s][n_rows][dim] (tm formats only; units of up to 128 rows); tm_down_splits picks
 // the split count that fills the GPU without an empty split
@@ -74,6 +77,12 @@ int expert_regime();
 int stage_rows_pair(const void* x, int x_dtype, int64_t n_tokens, int dim, const int32_t* perm, int64_t n_rows,
                     int topk, void* staged, int64_t rows_cap, float* row_scale, int64_t n_rows_b, void* staged_b,
                     int64_t rows_cap_b, float* row_scale_b, void* stream);
+
+// Stage fp32 rows as two f16 rows each: row r the row itself (as dsm_stage_rows does), row
+// n_rows + r the residual x - hi, with its own power-of-two scale, so that a product over both
+// rows adds up to the fp32 row's product within ~2^-22. rows_cap >= dsm_stage_rows_cap(2 n_rows).
+int stage_rows_hilo(const float* x, int64_t n_rows, int dim, void* staged, int64_t rows_cap, float* row_scale,
+                    void* stream);
 
 // ------------------------------------------------------------------------------------------
 // geometry shared by staging, packing and the expert kernels

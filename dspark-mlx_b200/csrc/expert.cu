@@ -479,6 +479,42 @@ extern "C" int dsm_expert_down(const void* h_staged, float h_scale, int64_t rows
   return dispatch<false>(wfmt, pick_nt(n_rows, n_experts, a.rt_count), a, as_stream(stream));
 }
 
+extern "C" int dsm_linear(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int k_dim, int wfmt,
+                          int group_size, const void* w_packed, int out_dim, float* o_rows, int ldo, int64_t n_rows,
+                          void* stream) {
+  using namespace dsm;
+  if (int rc = check_common(wfmt, group_size, nullptr, 1)) return rc;
+  DSM_REQUIRE(out_dim > 0 && k_dim > 0 && n_rows >= 0 && ldo >= out_dim, "dsm_linear: bad shape");
+  DSM_REQUIRE(rows_cap >= dsm_stage_rows_cap(n_rows), "dsm_linear: rows_cap too small");
+  DSM_REQUIRE(x_staged && x_row_scale && w_packed && o_rows, "dsm_linear: NULL pointer");
+  if (n_rows == 0) return DSM_OK;
+  if (tm_supports(wfmt))
+    return expert_tm_down(wfmt, group_size, x_staged, 1.f, rows_cap, k_dim, nullptr, 1, w_packed, out_dim, 0, o_rows,
+                          ldo, nullptr, n_rows, stream, x_row_scale);
+  if (use_tc(wfmt, n_rows, 1))
+    return expert_tc_down(wfmt, x_staged, 1.f, rows_cap, k_dim, nullptr, 1, w_packed, out_dim, 0, o_rows, ldo, nullptr,
+                          n_rows, stream, x_row_scale);
+  ExpertArgs a{};
+  a.wa = static_cast<const uint8_t*>(w_packed);
+  a.wb = nullptr;
+  a.xin = static_cast<const __half*>(x_staged);
+  a.act_scale = x_row_scale;
+  a.act_scale_const = 1.f;
+  a.rows_cap = rows_cap;
+  a.offsets = nullptr;
+  a.n_rows = n_rows;
+  a.n_experts = 1;
+  a.out_rows = out_dim;
+  a.rt_count = int(ceil_div(out_dim, kTileRows));
+  a.kc_count = int(ceil_div(k_dim, kChunkK));
+  a.group_size = group_size > 0 ? group_size : 64;
+  a.o_out = o_rows;
+  a.o_row_map = nullptr;
+  a.ldo = ldo;
+  a.round_o = 0;
+  return dispatch<false>(wfmt, pick_nt(n_rows, 1, a.rt_count), a, as_stream(stream));
+}
+
 namespace dsm {
 int expert_regime() { return g_regime.load(); }
 }  // namespace dsm

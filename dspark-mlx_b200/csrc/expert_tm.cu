@@ -649,12 +649,12 @@ int expert_tm_gate_up(int wfmt, int group_size, const void* x_staged, const floa
 
 int expert_tm_down(int wfmt, int group_size, const void* h_staged, float h_scale, int64_t rows_cap, int inter,
                    const int32_t* offsets, int n_experts, const void* w2, int dim, int round_o, float* o_rows,
-                   int ldo, const int32_t* o_row_map, int64_t n_rows, void* stream) {
+                   int ldo, const int32_t* o_row_map, int64_t n_rows, void* stream, const float* x_row_scale) {
   TmArgs a{};
   a.wa = static_cast<const uint8_t*>(w2);
   a.wb = nullptr;
-  a.act_scale = nullptr;
-  a.act_scale_const = 1.f / h_scale;
+  a.act_scale = x_row_scale;
+  a.act_scale_const = x_row_scale ? 1.f : 1.f / h_scale;
   a.offsets = offsets;
   a.n_rows = n_rows;
   a.n_experts = n_experts;

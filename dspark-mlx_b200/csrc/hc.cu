@@ -5,6 +5,9 @@
 //                    kernels.py:60-85) followed by ffn_norm (RMSNorm, model/norm_rope.py:22-39):
 //                    x [n, hc, d] -> the MoE input [n, d], plus post [n, hc], comb [n, hc, hc]
 //   dsm_hc_post      hc_post (hyper.py:45-51): out[c] = post[c] * h + sum_a comb[a, c] * res[a]
+//   dsm_hc_head_norm hc_head (hyper.py:52-67) and the draft head's final RMSNorm
+//                    (block.py:111-112): x [n, hc, d] -> y [n, d], RMSNorm(y) [n, d] and the
+//                    hidden half of the confidence projection (heads.py:46-48)
 //
 // Everything is fp32 inside, cast to the activation dtype where the reference casts. One
 // CTA per token for the pre-norm: a single pass over the token's hc*d values accumulates the
@@ -187,6 +190,90 @@ __global__ void __launch_bounds__(kHcThreads) hc_post_kernel(const T* __restrict
   }
 }
 
+// hc_head (hyper.py:52-67) then the final RMSNorm: y = sum_c pre[c] x[c] with
+// pre = sigmoid(mixes * scale + base) + hc_eps, mixes = (x . fn) * rsqrt(mean(x^2) + eps); y
+// is rounded to T and written out; xn = RMSNorm(y) * weight, rounded to T; and
+// conf[t] = sum_j y[j] * conf_w[j] (the hidden half of the confidence projection).
+template <typename T, int HC>
+__global__ void __launch_bounds__(kHcThreads) hc_head_norm_kernel(const T* __restrict__ x, int dim,
+                                                                    const float* __restrict__ fn,
+                                                                    const float* __restrict__ scale,
+                                                                    const float* __restrict__ base, float norm_eps,
+                                                                    float hc_eps, const float* __restrict__ weight,
+                                                                    const float* __restrict__ conf_w,
+                                                                    T* __restrict__ y_out, T* __restrict__ xn,
+                                                                    float* __restrict__ conf_out) {
+  extern __shared__ float ysm[];  // dim floats: the reduced row, rounded to T
+  __shared__ float red[(kHcThreads / 32) * (HC + 2)];
+  __shared__ float pre_s[HC];
+  const int64_t t = blockIdx.x;
+  const int hcd = HC * dim;
+  const T* xt = x + t * hcd;
+  float acc[HC + 1];
+#pragma unroll
+  for (int i = 0; i <= HC; ++i) acc[i] = 0.f;
+  for (int k = threadIdx.x; k < hcd; k += kHcThreads) {
+    const float v = to_f(xt[k]);
+    acc[HC] = fmaf(v, v, acc[HC]);
+#pragma unroll
+    for (int j = 0; j < HC; ++j) acc[j] = fmaf(v, fn[int64_t(j) * hcd + k], acc[j]);
+  }
+  block_sum(acc, red);
+  if (threadIdx.x == 0) {
+    const float inv_rms = rsqrtf(acc[HC] / float(hcd) + norm_eps);
+#pragma unroll
+    for (int c = 0; c < HC; ++c)  // (mixes * rsqrt) * scale + base, each rounded as the reference's ops are
+      pre_s[c] = sigmoid_f(__fadd_rn(__fmul_rn(__fmul_rn(acc[c], inv_rms), scale[0]), base[c])) + hc_eps;
+  }
+  __syncthreads();
+  float sq[2] = {0.f, 0.f};
+  T* yt = y_out + t * dim;
+  for (int j = threadIdx.x; j < dim; j += kHcThreads) {
+    float y = 0.f;
+#pragma unroll
+    for (int c = 0; c < HC; ++c) y = __fadd_rn(y, __fmul_rn(pre_s[c], to_f(xt[c * dim + j])));  // products, then sum
+    const T yt_v = from_f<T>(y);
+    const float yq = to_f(yt_v);
+    yt[j] = yt_v;
+    ysm[j] = yq;
+    sq[0] = fmaf(yq, yq, sq[0]);
+    if (conf_w) sq[1] = fmaf(yq, conf_w[j], sq[1]);
+  }
+  block_sum(sq, red);
+  if (threadIdx.x == 0 && conf_out) conf_out[t] = sq[1];
+  const float r = rsqrtf(sq[0] / float(dim) + norm_eps);
+  T* out = xn + t * dim;
+  for (int j = threadIdx.x; j < dim; j += kHcThreads) {
+    const float v = ysm[j] * r;
+    out[j] = from_f<T>(weight ? weight[j] * v : v);
+  }
+}
+
+template <typename T>
+int launch_head(const void* x, int64_t n, int hc, int dim, const float* fn, const float* scale, const float* base,
+                float norm_eps, float hc_eps, const float* weight, const float* conf_w, void* y, void* xn,
+                float* conf, cudaStream_t s) {
+  const size_t smem = size_t(dim) * sizeof(float);
+  const T* xp = static_cast<const T*>(x);
+#define DSM_HC_HEAD(H)                                                                                        \
+  {                                                                                                           \
+    auto k = hc_head_norm_kernel<T, H>;                                                                       \
+    if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != \
+                                cudaSuccess)                                                                  \
+      return check_launch("hc_head_norm smem attribute");                                                     \
+    k<<<unsigned(n), kHcThreads, smem, s>>>(xp, dim, fn, scale, base, norm_eps, hc_eps, weight, conf_w,       \
+                                            static_cast<T*>(y), static_cast<T*>(xn), conf);                   \
+    return check_launch("hc_head_norm");                                                                      \
+  }
+  switch (hc) {
+    case 1: DSM_HC_HEAD(1)
+    case 2: DSM_HC_HEAD(2)
+    case 4: DSM_HC_HEAD(4)
+    default: return fail(DSM_ERR_UNSUPPORTED, "dsm_hc_head_norm: hc_mult must be 1, 2 or 4");
+  }
+#undef DSM_HC_HEAD
+}
+
 template <typename T>
 int launch_pre(const void* x, int64_t n, int hc, int dim, const float* fn, const float* scale, const float* base,
                int iters, float norm_eps, float hc_eps, const float* weight, void* xn, float* post, float* comb,
@@ -261,4 +348,23 @@ extern "C" int dsm_hc_post(const void* h, const void* residual, int dtype, int64
   if (dtype == DSM_DT_BF16)
     return launch_post<__nv_bfloat16>(h, residual, n_tokens, hc_mult, dim, post, comb, out, s);
   return launch_post<float>(h, residual, n_tokens, hc_mult, dim, post, comb, out, s);
+}
+
+extern "C" int dsm_hc_head_norm(const void* x, int x_dtype, int64_t n_tokens, int hc_mult, int dim, const float* hc_fn,
+                                const float* hc_scale, const float* hc_base, float norm_eps, float hc_eps,
+                                const float* norm_weight, const float* conf_w, void* y_out, void* x_norm_out,
+                                float* conf_out, void* stream) {
+  using namespace dsm;
+  DSM_REQUIRE(n_tokens >= 0 && dim > 0 && hc_mult > 0, "dsm_hc_head_norm: bad shape");
+  DSM_REQUIRE(dim <= 48 * 1024, "dsm_hc_head_norm: dim too large for the shared-memory row");
+  DSM_REQUIRE(x_dtype == DSM_DT_F32 || x_dtype == DSM_DT_BF16, "dsm_hc_head_norm: x must be F32 or BF16");
+  if (n_tokens == 0) return DSM_OK;
+  DSM_REQUIRE(x && hc_fn && hc_scale && hc_base && y_out && x_norm_out, "dsm_hc_head_norm: NULL pointer");
+  DSM_REQUIRE(!conf_w || conf_out, "dsm_hc_head_norm: conf_w without conf_out");
+  cudaStream_t s = as_stream(stream);
+  if (x_dtype == DSM_DT_BF16)
+    return launch_head<__nv_bfloat16>(x, n_tokens, hc_mult, dim, hc_fn, hc_scale, hc_base, norm_eps, hc_eps,
+                                      norm_weight, conf_w, y_out, x_norm_out, conf_out, s);
+  return launch_head<float>(x, n_tokens, hc_mult, dim, hc_fn, hc_scale, hc_base, norm_eps, hc_eps, norm_weight, conf_w,
+                            y_out, x_norm_out, conf_out, s);
 }

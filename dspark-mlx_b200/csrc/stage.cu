@@ -109,6 +109,74 @@ __global__ void __launch_bounds__(kStageThreads) stage_rows_kernel(const XT* __r
   }
 }
 
+// One CTA per fp32 row: the row staged as stage_rows_kernel does (row r), then the residual
+// x - hi, kept in shared memory, staged with its own power-of-two scale (row n_rows + r).
+__global__ void __launch_bounds__(kStageThreads) stage_hilo_kernel(const float* __restrict__ x, int64_t n_rows, int dim,
+                                                                   __half* __restrict__ staged, int64_t rows_cap,
+                                                                   float* __restrict__ row_scale, int k_chunks) {
+  extern __shared__ float res[];  // kpad floats: the residual row
+  __shared__ float red[kStageThreads / 32];
+  const int64_t r = blockIdx.x;
+  const float* row = x + r * dim;
+  const int kpad = k_chunks * kChunkK;
+  auto row_exp = [&](float amax) {  // power-of-two scale putting amax in [2^14, 2^15)
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = red[0];
+#pragma unroll
+    for (int i = 1; i < kStageThreads / 32; ++i) amax = fmaxf(amax, red[i]);
+    int s = 0;
+    if (amax > 0.f && isfinite(amax)) {
+      int ex;
+      frexpf(amax, &ex);
+      s = 15 - ex;
+      s = s < -100 ? -100 : (s > 100 ? 100 : s);
+    }
+    return s;
+  };
+  auto store8 = [&](int64_t srow, int k, const float (&v)[8], float up) {
+    uint32_t h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 p = __floats2half2_rn(v[2 * i] * up, v[2 * i + 1] * up);
+      h[i] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+    const int c = k / kChunkK, col = k % kChunkK;
+    *reinterpret_cast<uint4*>(staged + (int64_t(c) * rows_cap + srow) * kStagePitch + col) = make_uint4(h[0], h[1], h[2], h[3]);
+  };
+  float amax = 0.f;
+  for (int k = threadIdx.x; k < dim; k += kStageThreads) amax = fmaxf(amax, fabsf(row[k]));
+  const int s1 = row_exp(amax);
+  const float up1 = ldexpf(1.f, s1), down1 = ldexpf(1.f, -s1);
+  if (threadIdx.x == 0) row_scale[r] = down1;
+  float ramax = 0.f;
+  for (int k = threadIdx.x * 8; k < kpad; k += kStageThreads * 8) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = (k + i < dim) ? row[k + i] : 0.f;
+    store8(r, k, v, up1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float lo = v[i] - __half2float(__float2half_rn(v[i] * up1)) * down1;  // exact difference
+      res[k + i] = lo;
+      ramax = fmaxf(ramax, fabsf(lo));
+    }
+  }
+  const int s2 = row_exp(ramax);
+  const float up2 = ldexpf(1.f, s2);
+  if (threadIdx.x == 0) row_scale[n_rows + r] = ldexpf(1.f, -s2);
+  __syncthreads();
+  for (int k = threadIdx.x * 8; k < kpad; k += kStageThreads * 8) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = res[k + i];
+    store8(n_rows + r, k, v, up2);
+  }
+}
+
 }  // namespace
 }  // namespace dsm
 
@@ -135,6 +203,21 @@ extern "C" int dsm_stage_rows(const void* x, int x_dtype, int64_t n_tokens, int 
 }
 
 namespace dsm {
+int stage_rows_hilo(const float* x, int64_t n_rows, int dim, void* staged, int64_t rows_cap, float* row_scale,
+                    void* stream) {
+  DSM_REQUIRE(dim > 0 && n_rows >= 0, "stage_rows_hilo: bad shape");
+  DSM_REQUIRE(rows_cap >= dsm_stage_rows_cap(2 * n_rows), "stage_rows_hilo: rows_cap too small");
+  if (n_rows == 0) return DSM_OK;
+  const int kc = int(ceil_div(dim, kChunkK));
+  const size_t smem = size_t(kc) * kChunkK * sizeof(float);
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(stage_hilo_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return check_launch("stage_hilo smem attribute");
+  stage_hilo_kernel<<<unsigned(n_rows), kStageThreads, smem, as_stream(stream)>>>(
+      x, n_rows, dim, static_cast<__half*>(staged), rows_cap, row_scale, kc);
+  return check_launch("stage_hilo");
+}
+
 int stage_rows_pair(const void* x, int x_dtype, int64_t n_tokens, int dim, const int32_t* perm, int64_t n_rows,
                     int topk, void* staged, int64_t rows_cap, float* row_scale, int64_t n_rows_b, void* staged_b,
                     int64_t rows_cap_b, float* row_scale_b, void* stream) {

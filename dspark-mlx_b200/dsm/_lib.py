@@ -31,7 +31,8 @@ EXPORTED = (
     "dsm_affine_quantize", "dsm_expert_gate_up", "dsm_expert_down", "dsm_combine",
     "dsm_moe_workspace_bytes", "dsm_moe_forward", "dsm_gather_rows", "dsm_segment_ids",
     "dsm_set_expert_regime", "dsm_hc_pre_norm", "dsm_hc_post", "dsm_dense_mlp_workspace_bytes",
-    "dsm_dense_mlp",
+    "dsm_dense_mlp", "dsm_linear", "dsm_hc_head_norm", "dsm_markov_head", "dsm_draft_head_workspace_bytes",
+    "dsm_draft_head",
 )
 
 
@@ -52,6 +53,23 @@ class MoEDesc(ctypes.Structure):
         ("s1", c_void_p), ("s3", c_void_p), ("s2", c_void_p),
         ("shared_inter", c_int), ("shared_round_gu", c_int), ("shared_round_o", c_int),
         ("act", c_int),
+    ]
+
+
+class HeadDesc(ctypes.Structure):
+    """``dsm_head_desc`` (field order and types follow the C struct)."""
+
+    _fields_ = [
+        ("batch", c_int64),
+        ("block", c_int), ("hc_mult", c_int), ("dim", c_int), ("vocab", c_int), ("rank", c_int),
+        ("norm_eps", c_float), ("hc_eps", c_float),
+        ("hc_fn", c_void_p), ("hc_scale", c_void_p), ("hc_base", c_void_p), ("norm_weight", c_void_p),
+        ("head_wfmt", c_int), ("head_group_size", c_int),
+        ("head_w", c_void_p),
+        ("markov_dtype", c_int),
+        ("markov_w1", c_void_p), ("markov_w2", c_void_p),
+        ("conf_w", c_void_p),
+        ("conf_bias", c_float),
     ]
 
 
@@ -90,6 +108,11 @@ def _declare(lib):
         "dsm_hc_post": (I, [V, V, I, I64, I, I, V, V, V, V]),
         "dsm_dense_mlp_workspace_bytes": (S, [I64, I, I]),
         "dsm_dense_mlp": (I, [V, I, I64, I, I, I, I, V, V, V, I, F, I, I, V, I, V, S, V]),
+        "dsm_linear": (I, [V, V, I64, I, I, I, V, I, V, I, I64, V]),
+        "dsm_hc_head_norm": (I, [V, I, I64, I, I, V, V, V, F, F, V, V, V, V, V, V]),
+        "dsm_markov_head": (I, [V, I, I64, I, I, V, V, I, V, V, V]),
+        "dsm_draft_head_workspace_bytes": (S, [POINTER(HeadDesc), I]),
+        "dsm_draft_head": (I, [POINTER(HeadDesc), V, I, V, I, F, V, V, V, V, V, V, S, V]),
         "dsm_moe_workspace_bytes": (S, [POINTER(MoEDesc)]),
         "dsm_moe_forward": (I, [POINTER(MoEDesc), V, I, V, I, I64, V, V, V, V, S, V]),
     }

@@ -30,6 +30,11 @@
  *                       (DSparkBlock.__call__, block.py:84-85) model/norm_rope.py:22-39
  *   dsm_hc_post         hc_post after the MoE (block.py:86)    model/hyper.py:45-51
  *   dsm_dense_mlp       Qwen3MLP.__call__ / Expert.__call__    arch/qwen3.py:146-154, model/moe.py:82-97
+ *   dsm_linear          nn.Linear over packed weights (the LM head, drafter.py:29, block.py:112)
+ *   dsm_hc_head_norm    hc_head + the head's RMSNorm            model/hyper.py:52-67, block.py:111-112
+ *   dsm_markov_head     DSparkMarkovHead.__call__              model/heads.py:26-30
+ *   dsm_draft_head      DSparkBlock.forward_head + LM head      model/block.py:103-116, recipe.py:21-63,
+ *                       (Markov walk, sampler, confidence)     model/heads.py:11-49
  *   dsm_gather_rows, dsm_segment_ids: expert-parallel plumbing; the reference runs on one
  *                       device (tests/reference_model.py:55-56 forces world_size 1) and has
  *                       no counterpart.
@@ -192,6 +197,54 @@ int dsm_dense_mlp(const void* x, int x_dtype, int64_t n_tokens, int dim, int int
                   const void* w1_packed, const void* w3_packed, const void* w2_packed, int act, float swiglu_limit,
                   int round_gu, int round_o, void* y, int y_dtype, void* workspace, size_t workspace_bytes,
                   void* stream);
+
+/* ---- plain linear layer over packed weights -------------------------------------------------
+ * o[r, :out_dim] = x[r] W^T (fp32 rows, row stride ldo) for rows staged by dsm_stage_rows
+ * (their row scales in x_row_scale); W [out_dim, k_dim] packed by dsm_pack_weights with
+ * n_experts = 1. */
+int dsm_linear(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int k_dim, int wfmt, int group_size,
+               const void* w_packed, int out_dim, float* o_rows, int ldo, int64_t n_rows, void* stream);
+
+/* ---- the draft head ---------------------------------------------------------------------------
+ * hc_head_norm: x [n, hc, dim] -> y [n, dim] = hc_head(x) (x dtype), x_norm [n, dim] =
+ *   RMSNorm(y) * norm_weight (x dtype), conf_out[t] = y[t] . conf_w[:dim] when conf_w is given.
+ * markov_head: logits [n, vocab] = w1[ids] . w2^T in fp32 and embed [n, rank] = w1[ids]
+ *   (w dtype; NULL to skip). rank % 8 == 0, w2 16-byte aligned.
+ * draft_head: for x [batch, block, hc, dim] and anchor [batch], the hc_head, the final
+ *   RMSNorm, the LM head in fp32, then the block walk: at position i the Markov bias of the
+ *   previous token is added to the base logits (written to biased_logits [batch, block,
+ *   vocab]) and the next token is taken by argmax (temperature 0, lowest index on ties) or by
+ *   Gumbel-max over softmax(logits / temperature) with uniforms [block, batch, vocab];
+ *   out_ids [batch, block + 1] starts with the anchor; confidence [batch, block] =
+ *   [y || w1[token]] . conf_w + conf_bias. An F32 x is staged as two f16 rows (hi + lo) for
+ *   the LM head. batch <= 32. The walk is one cooperative launch (one CTA per SM, grid
+ *   barriers bounded by ~2 s: a stalled wait sets the device error and ends the kernel). */
+typedef struct dsm_head_desc {
+  int64_t batch;
+  int block, hc_mult, dim, vocab, rank;
+  float norm_eps, hc_eps;
+  const float* hc_fn;       /* [hc, hc * dim] */
+  const float* hc_scale;    /* [1] */
+  const float* hc_base;     /* [hc] */
+  const float* norm_weight; /* [dim] or NULL */
+  int head_wfmt, head_group_size;
+  const void* head_w; /* packed LM head [vocab, dim] */
+  int markov_dtype;   /* DSM_DT_F32 or DSM_DT_BF16 */
+  const void* markov_w1; /* [vocab, rank] */
+  const void* markov_w2; /* [vocab, rank] */
+  const float* conf_w;   /* [dim + rank] or NULL (no confidence) */
+  float conf_bias;
+} dsm_head_desc;
+int dsm_hc_head_norm(const void* x, int x_dtype, int64_t n_tokens, int hc_mult, int dim, const float* hc_fn,
+                     const float* hc_scale, const float* hc_base, float norm_eps, float hc_eps,
+                     const float* norm_weight, const float* conf_w, void* y_out, void* x_norm_out, float* conf_out,
+                     void* stream);
+int dsm_markov_head(const void* ids, int ids_dtype, int64_t n, int vocab, int rank, const void* w1, const void* w2,
+                    int w_dtype, float* logits, void* embed, void* stream);
+size_t dsm_draft_head_workspace_bytes(const dsm_head_desc* d, int x_dtype);
+int dsm_draft_head(const dsm_head_desc* d, const void* x, int x_dtype, const void* anchor, int anchor_dtype,
+                   float temperature, const float* uniforms, int32_t* out_ids, float* biased_logits, float* confidence,
+                   void* y_out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Kernel regime of the grouped expert products: 0 (default) picks by rows per busy
  * expert -- the mma.sync weight-streaming kernel at decode sizes, the tcgen05/TMEM kernel

@@ -79,6 +79,19 @@ def test_bad_arguments_are_rejected_on_the_host(call):
     assert L.dsm_last_error_message().decode()
 
 
+def test_draft_head_host_checks():
+    L = _lib.lib()
+    d = _lib.HeadDesc(batch=8, block=7, hc_mult=4, dim=4096, vocab=129280, rank=256)
+    need = L.dsm_draft_head_workspace_bytes(ctypes.byref(d), _lib.DT_BF16)
+    assert need >= 56 * 129280 * 4  # the fp32 base logits
+    assert L.dsm_draft_head_workspace_bytes(ctypes.byref(d), _lib.DT_F32) >= 2 * 56 * 129280 * 4  # hi + lo rows
+    bad = _lib.HeadDesc(batch=8, block=7, hc_mult=4, dim=64, vocab=100, rank=12)  # rank not a multiple of 8
+    rc = L.dsm_draft_head(ctypes.byref(bad), 1, _lib.DT_BF16, 1, _lib.DT_I32, 0.0, None, 1, 1, None, None, 1, 1 << 30,
+                          None)
+    assert rc != 0 and L.dsm_last_error_message().decode()
+    assert ctypes.sizeof(_lib.HeadDesc) % 8 == 0 and _lib.HeadDesc.hc_fn.offset % 8 == 0
+
+
 def test_desc_struct_layout_matches_header():
     # field offsets of the ctypes mirror must follow the C struct (8-byte pointers, int64 first)
     assert _lib.MoEDesc.n_tokens.offset == 0
