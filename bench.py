@@ -716,6 +716,192 @@ def run_reference_qwen3(args):
     print(json.dumps(line))
 
 
+HEAD_METRIC = "Draft-head tokens/s (hc_head + norm + LM head over 129280 words + Markov walk, greedy); HBM GB/s"
+HEAD_KERNELS_PER_STEP = 4  # hc_head+norm, staging, LM head product, walk
+
+
+def _head_oracle_args(t, wl):
+    import torch
+
+    a = wl.args
+    return dict(head_w=t["head_w"].to(torch.float32), hc_fn=t["fn"], hc_scale=t["scale"], hc_base=t["base"],
+                norm_w=t["norm_w"], w1=t["w1"], w2=t["w2"], wc=t["wc"], norm_eps=1e-6, hc_eps=1e-6,
+                temperature=float(a["temperature"]))
+
+
+def _head_cpu_setup(t, wl):
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    kw = _head_oracle_args({k: (v.cpu() if hasattr(v, "cpu") else v) for k, v in t.items()}, wl)
+    return kw, t["x"][:1].cpu(), t["anchor"][:1].cpu()
+
+
+def _head_cpu_timed(t, wl, budget_s, max_calls=50, setup=None):
+    """The oracle's forward_head on one batch row (a block of tokens) per call, all host threads."""
+    import oracle
+
+    kw, x, anchor = setup or _head_cpu_setup(t, wl)
+    if setup is None:
+        oracle.forward_head(x, anchor, **kw)
+    n, t0 = 0, time.perf_counter()
+    while n < max_calls and (n == 0 or time.perf_counter() - t0 < budget_s):
+        oracle.forward_head(x, anchor, **kw)
+        n += 1
+    el = time.perf_counter() - t0
+    return n * wl.block / el, n, el
+
+
+def run_head(args):
+    """One step = one draft-head call (8 sequences x 7 draft positions, DeepSeek-V4 widths).
+    The LM head (1.06 GB of bf16 weights) exceeds L2, so every step streams it from HBM."""
+    import ctypes
+
+    import torch
+
+    from dsm import _lib, workloads as W
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    wl = W.WORKLOADS["draft_head"]
+    t = W.make_head_tensors(wl, device=dev, seed=rank)
+    head = W.build_head(wl, t, dev)
+    b, s = wl.batch, wl.block
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(777 + rank)
+    xs = [t["x"]] + [torch.randn(t["x"].shape, generator=gen, device=dev).to(torch.bfloat16) for _ in range(3)]
+    anchor = t["anchor"]
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        head(xs[i % 4], anchor)
+    torch.cuda.synchronize()
+
+    def timed(fn):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            fn(i)
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs) / args.steps
+
+    _barrier(ws)
+    with ClockSampler(local) as clk:
+        ms = timed(lambda i: head(xs[i % 4], anchor))
+    ms = _max_over_ranks(ms, ws, dev)
+    hp = head.packed_head()
+    vocab, dim, rk = wl.args["vocab_size"], wl.args["dim"], wl.args["dspark_markov_rank"]
+    step_bytes = hp.nbytes + 2 * vocab * rk * 2 + b * s * vocab * 4 * 2 + b * s * 4 * dim * 2
+    hbm_peak, _, peak_kind = _peaks()
+
+    roofline = None
+    if not args.no_kernel_timing and ws == 1:  # the LM head product alone, on the staged normalised rows
+        L = _lib.lib()
+        n = b * s
+        cap = L.dsm_stage_rows_cap(n)
+        xn = torch.randn(n, dim, device=dev).to(torch.bfloat16)
+        xsb = torch.empty(L.dsm_stage_bytes(cap, dim), dtype=torch.uint8, device=dev)
+        xsc = torch.empty(cap, dtype=torch.float32, device=dev)
+        out = torch.empty(n, vocab, dtype=torch.float32, device=dev)
+        sp = stream.cuda_stream
+        _lib.check(L.dsm_stage_rows(xn.data_ptr(), _lib.DT_BF16, n, dim, None, n, 1, xsb.data_ptr(), cap,
+                                    xsc.data_ptr(), sp))
+        k_ms = timed(lambda i: _lib.check(L.dsm_linear(xsb.data_ptr(), xsc.data_ptr(), cap, dim, hp.wfmt, hp.group_size,
+                                                       hp.packed.data_ptr(), vocab, out.data_ptr(), vocab, n, sp)))
+        k_bytes = hp.nbytes + n * dim * 2 + n * vocab * 4
+        achieved = k_bytes / (k_ms * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "expert_kernel<f16, down> (LM head, weight streaming)",
+                    "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                    "peak_kind": peak_kind, "frac_of_8tbs": achieved / SPEC_HBM_GBS,
+                    "algorithmic_bytes_per_launch": k_bytes, "launch_ms": k_ms, "traffic": None}
+
+    e2e_ms = None
+    if not args.no_e2e:
+        xh = [x.cpu().pin_memory() for x in xs]
+        ah = anchor.cpu().pin_memory()
+        ids_h = torch.empty(b, s + 1, dtype=torch.int32).pin_memory()
+        conf_h = torch.empty(b, s, dtype=torch.float32).pin_memory()
+
+        def e2e(i):
+            ids, _, conf = head(xh[i % 4].to(dev, non_blocking=True), ah.to(dev, non_blocking=True))
+            ids_h.copy_(ids, non_blocking=True)
+            conf_h.copy_(conf, non_blocking=True)
+
+        for i in range(3):
+            e2e(i)
+        torch.cuda.synchronize()
+        e2e_ms = _max_over_ranks(timed(e2e), ws, dev)
+
+    if rank == 0:
+        cpu = None
+        if ws == 1 and not args.no_cpu_baseline:
+            v, calls, el = _head_cpu_timed(t, wl, args.cpu_seconds)
+            cpu = {"value": v, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+                   "sample": f"1 of the {b} sequences ({s} draft tokens) per call, {calls} calls in {el:.1f} s; "
+                             f"CPU restatement of DSparkBlock.forward_head + the LM head in PyTorch"}
+        line = {
+            "metric": HEAD_METRIC, "value": ws * b * s / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 weights x bf16 activations (f16 MMA, fp32 accumulate)",
+            "data": "synthetic",
+            "config": {"workload": wl.name, "tokens_per_step_per_gpu": b * s, "batch": b, "draft_block": s,
+                       "dim": dim, "vocab": vocab, "markov_rank": rk, "hc_mult": wl.args["hc_mult"],
+                       "sampling": "greedy", "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                       "l2": "inputs larger than L2 (1.06 GB LM head streamed every step)"},
+            "hbm_gbs_step": step_bytes / (ms * 1e-3) / 1e9,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": None if e2e_ms is None else {
+                "value": ws * b * s / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": xs[0].numel() * 2 + b * 4, "d2h_bytes_per_step": b * (s + 1) * 4 + b * s * 4,
+                "ms_per_step": e2e_ms},
+            "gpu_launches": HEAD_KERNELS_PER_STEP * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line))
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def run_reference_head(args):
+    ws, rank, _ = _dist()
+    if rank != 0:
+        return
+    from dsm import workloads as W
+
+    wl = W.WORKLOADS["draft_head"]
+    t = W.make_head_tensors(wl, device="cpu")
+    setup = _head_cpu_setup(t, wl)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, _, _ = _head_cpu_timed(t, wl, 0.0, max_calls=1, setup=setup)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": HEAD_METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wl.n_tokens / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (bf16 weights)",
+        "data": "synthetic",
+        "config": {"workload": wl.name, "tokens_per_step": wl.n_tokens, "batch": wl.batch, "draft_block": wl.block,
+                   "vocab": wl.args["vocab_size"], "dim": wl.args["dim"]},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+                         "sample": f"one sequence ({wl.block} draft tokens) per step; CPU restatement of "
+                                   f"DSparkBlock.forward_head + the LM head in PyTorch (mlx is not installable here)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -732,7 +918,9 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     qwen3 = args.workload.startswith("qwen3")
-    if args.impl == "reference":
+    if args.workload == "draft_head":
+        (run_reference_head if args.impl == "reference" else run_head)(args)
+    elif args.impl == "reference":
         (run_reference_qwen3 if qwen3 else run_reference)(args)
     else:
         (run_qwen3 if qwen3 else run_gpu)(args)

@@ -77,6 +77,16 @@ __device__ __forceinline__ void wload8(const void* w, int bf16, int64_t i, float
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
 
+// D += A (16x16 bf16, row) * B (16x8 bf16, col), fp32 accumulate
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // Grid barrier over the cooperative launch. Generation g completes when g * gridDim.x
 // arrivals are counted. Thread 0 waits with a ~2 s budget and an abort flag that any CTA
 // can raise. Every thread gets the same verdict.
@@ -115,11 +125,10 @@ __device__ bool walk_sync(const WalkArgs& a, unsigned& gen) {
   return ok_s != 0;
 }
 
-// per-batch-row (value, index) maximum over the block: lane/warp shuffles, then warps via
-// shared memory; threads b < batch return row b's winner
+// per-batch-row (value, index) maximum over the warp into sv/si[warp][b]
 template <int MAXB>
-__device__ __forceinline__ void block_best(const float (&bv)[MAXB], const int (&bi)[MAXB], int batch,
-                                           float (*sv)[MAXB], int (*si)[MAXB], float& out_v, int& out_i) {
+__device__ __forceinline__ void warp_best(const float (&bv)[MAXB], const int (&bi)[MAXB], int batch,
+                                          float (*sv)[MAXB], int (*si)[MAXB]) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
   for (int b = 0; b < MAXB; ++b) {
@@ -140,6 +149,11 @@ __device__ __forceinline__ void block_best(const float (&bv)[MAXB], const int (&
       si[warp][b] = ix;
     }
   }
+}
+
+// the warps' candidates in sv/si combined: threads b < batch return row b's winner
+template <int MAXB>
+__device__ __forceinline__ void warps_best(int batch, float (*sv)[MAXB], int (*si)[MAXB], float& out_v, int& out_i) {
   __syncthreads();
   if (int(threadIdx.x) < batch) {
     const int b = threadIdx.x;
@@ -174,12 +188,19 @@ __device__ __forceinline__ void block_sum_b(const float (&s)[MAXB], int batch, f
   }
 }
 
+__host__ __device__ __forceinline__ int walk_e_floats(int batch, int rank, int maxb) {
+  const int f32 = batch * rank, bf = (maxb * (rank + 8) + 1) / 2;
+  return f32 > bf ? f32 : bf;
+}
+
 template <int MAXB>
 __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs a) {
   extern __shared__ float sm[];
   const int B = a.batch, R = a.rank, V = a.vocab, S = a.block;
-  float* e_sm = sm;           // [B][R] Markov embeddings of the previous tokens
-  float* li_sm = sm + B * R;  // [B][slice] biased logits of this slice (sampling only)
+  // Markov embeddings of the previous tokens: [B][R] fp32, or [MAXB][R + 8] bf16 (tensor-core
+  // path); then [B][slice] biased logits of this slice (sampling only)
+  float* e_sm = sm;
+  float* li_sm = sm + walk_e_floats(B, R, MAXB);
   __shared__ int prev_s[MAXB];
   __shared__ float stat_m[MAXB], stat_z[MAXB];
   __shared__ float sv[kWalkWarps][MAXB];
@@ -203,53 +224,155 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
   }
   __syncthreads();
 
+  // bf16 tables (rank a multiple of 32) take the tensor-core path: warp tiles of 16 vocabulary rows x 8 batch rows,
+  // mma.m16n8k16 over the rank. Each lane loads 16 contiguous bytes of its two rows per 32
+  // rank entries. The k order inside each 32-entry block is permuted identically in both
+  // operands so that these bytes are the A fragments (lane q holds entries 8q .. 8q+7);
+  // the sum over the rank is unchanged.
+  const bool use_mma = a.w_bf16 != 0 && R % 32 == 0;  // whole 32-entry blocks of the rank
+  constexpr int NT = MAXB / 8;
+  const int RP = R + 8;  // padded row of the bf16 embeddings: conflict-free fragment loads
+  __nv_bfloat16* eb = reinterpret_cast<__nv_bfloat16*>(e_sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
   for (int i = 0; i < S; ++i) {
-    for (int k = threadIdx.x; k < B * R; k += kWalkThreads) {
-      const int b = k / R;
-      e_sm[k] = wload(a.w1, a.w_bf16, int64_t(prev_s[b]) * R + (k - b * R));
+    if (use_mma) {
+      const __nv_bfloat16* w1b = static_cast<const __nv_bfloat16*>(a.w1);
+      for (int k = threadIdx.x; k < NT * 8 * RP; k += kWalkThreads) {
+        const int b = k / RP, r = k - b * RP;
+        eb[k] = (b < B && r < R) ? w1b[int64_t(prev_s[b]) * R + r] : __float2bfloat16_rn(0.f);
+      }
+    } else {
+      for (int k = threadIdx.x; k < B * R; k += kWalkThreads) {
+        const int b = k / R;
+        e_sm[k] = wload(a.w1, a.w_bf16, int64_t(prev_s[b]) * R + (k - b * R));
+      }
     }
     __syncthreads();
-    float best[MAXB];
-    int bidx[MAXB];
+    auto emit = [&](int b, int v, float bias, float& bv, int& bi) {  // biased logit of (b, v): store, keep the best
+      const int64_t t = int64_t(b) * S + i;
+      float l = a.logits[t * V + v];
+      if (a.lo_offset) l += a.logits[(a.lo_offset + t) * V + v];
+      const float li = l + bias;
+      a.biased[t * V + v] = li;
+      if (sampled) {
+        li_sm[b * a.slice + (v - v0)] = li;
+        bv = fmaxf(bv, li / tp);
+      } else if (li > bv) {
+        bv = li;
+        bi = v;
+      }
+    };
+    if (use_mma) {
+      const int g = lane >> 2, q = lane & 3;
+      const __nv_bfloat16* w2b = static_cast<const __nv_bfloat16*>(a.w2);
+      float bv2[NT][2];
+      int bi2[NT][2];
 #pragma unroll
-    for (int b = 0; b < MAXB; ++b) {
-      best[b] = -INFINITY;
-      bidx[b] = INT_MAX;
-    }
-    for (int v = v0 + threadIdx.x; v < v1; v += kWalkThreads) {
-      float acc[MAXB];
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int b = 0; b < MAXB; ++b) acc[b] = 0.f;
-      for (int r = 0; r < R; r += 8) {
-        float w[8];
-        wload8(a.w2, a.w_bf16, int64_t(v) * R + r, w);
+        for (int c = 0; c < 2; ++c) {
+          bv2[nt][c] = -INFINITY;
+          bi2[nt][c] = INT_MAX;
+        }
+      for (int tile = warp; v0 + tile * 16 < v1; tile += kWalkWarps) {
+        const int ra = v0 + tile * 16 + g, rb = ra + 8;
+        const bool oka = ra < v1, okb = rb < v1;
+        float d[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+        for (int k4 = 0; k4 < R; k4 += 128) {  // four 32-entry blocks: their 8 loads in flight together
+          const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+          uint4 A0[4], A1[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int k2 = k4 + 32 * u;
+            A0[u] = (oka && k2 < R) ? __ldg(reinterpret_cast<const uint4*>(w2b + int64_t(ra) * R + k2 + 8 * q)) : z;
+            A1[u] = (okb && k2 < R) ? __ldg(reinterpret_cast<const uint4*>(w2b + int64_t(rb) * R + k2 + 8 * q)) : z;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int k2 = k4 + 32 * u;
+            if (k2 >= R) break;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              if (nt * 8 >= B) break;
+              const uint4 Bv = *reinterpret_cast<const uint4*>(eb + (nt * 8 + g) * RP + k2 + 8 * q);
+              mma_bf16_16816(d[nt], A0[u].x, A1[u].x, A0[u].y, A1[u].y, Bv.x, Bv.y);
+              mma_bf16_16816(d[nt], A0[u].z, A1[u].z, A0[u].w, A1[u].w, Bv.z, Bv.w);
+            }
+          }
+        }
+        // D fragment: d0, d1 row ra; d2, d3 row rb; batch nt*8 + 2q + {0, 1}
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          if (nt * 8 >= B) break;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int b = nt * 8 + 2 * q + c;
+            if (b >= B) continue;
+            if (oka) emit(b, ra, d[nt][c], bv2[nt][c], bi2[nt][c]);
+            if (okb) emit(b, rb, d[nt][2 + c], bv2[nt][c], bi2[nt][c]);
+          }
+        }
+      }
+      // the warp's best per batch row: lanes of equal q hold the same batch columns
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        if (nt * 8 >= B) break;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float v = bv2[nt][c];
+          int ix = bi2[nt][c];
+#pragma unroll
+          for (int o = 4; o < 32; o <<= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
+            if (better(ov, oi, v, ix)) {
+              v = ov;
+              ix = oi;
+            }
+          }
+          const int b = nt * 8 + 2 * q + c;
+          if (g == 0 && b < B) {
+            sv[warp][b] = v;
+            si[warp][b] = ix;
+          }
+        }
+      }
+    } else {
+      float best[MAXB];
+      int bidx[MAXB];
+#pragma unroll
+      for (int b = 0; b < MAXB; ++b) {
+        best[b] = -INFINITY;
+        bidx[b] = INT_MAX;
+      }
+      for (int v = v0 + threadIdx.x; v < v1; v += kWalkThreads) {
+        float acc[MAXB];
+#pragma unroll
+        for (int b = 0; b < MAXB; ++b) acc[b] = 0.f;
+        for (int r = 0; r < R; r += 8) {
+          float w[8];
+          wload8(a.w2, a.w_bf16, int64_t(v) * R + r, w);
+#pragma unroll
+          for (int b = 0; b < MAXB; ++b) {
+            if (b >= B) break;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[b] = fmaf(w[j], e_sm[b * R + r + j], acc[b]);
+          }
+        }
 #pragma unroll
         for (int b = 0; b < MAXB; ++b) {
           if (b >= B) break;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[b] = fmaf(w[j], e_sm[b * R + r + j], acc[b]);
+          emit(b, v, acc[b], best[b], bidx[b]);
         }
       }
-#pragma unroll
-      for (int b = 0; b < MAXB; ++b) {
-        if (b >= B) break;
-        const int64_t t = int64_t(b) * S + i;
-        float l = a.logits[t * V + v];
-        if (a.lo_offset) l += a.logits[(a.lo_offset + t) * V + v];
-        const float li = l + acc[b];
-        a.biased[t * V + v] = li;
-        if (sampled) {
-          li_sm[b * a.slice + (v - v0)] = li;
-          best[b] = fmaxf(best[b], li / tp);
-        } else if (li > best[b]) {
-          best[b] = li;
-          bidx[b] = v;
-        }
-      }
+      warp_best<MAXB>(best, bidx, B, sv, si);
     }
     float cv = 0.f;
     int ci = 0;
-    block_best<MAXB>(best, bidx, B, sv, si, cv, ci);
+    warps_best<MAXB>(B, sv, si, cv, ci);
     if (int(threadIdx.x) < B) {
       a.cand_v[(int64_t(buf) * G + blockIdx.x) * B + threadIdx.x] = cv;
       a.cand_i[(int64_t(buf) * G + blockIdx.x) * B + threadIdx.x] = ci;
@@ -301,6 +424,8 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
       buf ^= 1;
       __syncthreads();
       // Gumbel-max: argmax of p / (-log(g + 1e-20)), p = exp(z - max) / sum
+      float best[MAXB];
+      int bidx[MAXB];
 #pragma unroll
       for (int b = 0; b < MAXB; ++b) {
         best[b] = -INFINITY;
@@ -318,7 +443,8 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
             bidx[b] = v;
           }
         }
-      block_best<MAXB>(best, bidx, B, sv, si, cv, ci);
+      warp_best<MAXB>(best, bidx, B, sv, si);
+      warps_best<MAXB>(B, sv, si, cv, ci);
       if (int(threadIdx.x) < B) {
         a.cand_v[(int64_t(buf) * G + blockIdx.x) * B + threadIdx.x] = cv;
         a.cand_i[(int64_t(buf) * G + blockIdx.x) * B + threadIdx.x] = ci;
@@ -350,7 +476,6 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
 
   // confidence (CTA 0): hidden half from hc_head_norm plus the Markov half, w1[tok] . wc_r
   if (blockIdx.x == 0 && a.confidence) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int p = warp; p < B * S; p += kWalkWarps) {
       const int b = p / S, i = p - b * S;
       const int tok = a.out_ids[int64_t(b) * (S + 1) + i];
@@ -452,7 +577,9 @@ int launch_walk(const WalkArgs& a0, void* walk_ws, cudaStream_t s) {
   a.cand_v = reinterpret_cast<float*>(w + kWalkHeader);
   a.cand_i = reinterpret_cast<int*>(w + kWalkHeader + 2 * size_t(kWalkCtaBound) * a.batch * 4);
   if (cudaMemsetAsync(w, 0, kWalkHeader, s) != cudaSuccess) return check_launch("draft head walk reset");
-  const size_t smem = (size_t(a.batch) * a.rank + (a.temperature > 0.f ? size_t(a.batch) * a.slice : 0)) * 4;
+  const int maxb = a.batch <= 8 ? 8 : 32;
+  const size_t smem =
+      (size_t(walk_e_floats(a.batch, a.rank, maxb)) + (a.temperature > 0.f ? size_t(a.batch) * a.slice : 0)) * 4;
   void* args[] = {&a};
   auto go = [&](auto kern) {
     if (smem > 48 * 1024 &&

@@ -77,6 +77,12 @@ WORKLOADS = {
         "prefill_fp8", _args(vocab_size=129280, dim=4096, moe_inter_dim=2048, n_routed_experts=256,
                              n_activated_experts=8, score_func="sigmoid", route_scale=2.5),
         n_tokens=16384, wfmt="fp8", zipf_alpha=1.2, batch=1, block=16384),
+    # the draft head of the last block: hc_head + norm, LM head over the DeepSeek-V4
+    # vocabulary, Markov-biased walk over a 7-token block for 8 sequences
+    "draft_head": Workload(
+        "draft_head", dict(vocab_size=129280, dim=4096, hc_mult=4, dspark_markov_rank=256, dspark_block_size=7,
+                           temperature=0.0),
+        n_tokens=56, wfmt="bf16", batch=8, block=7),
 }
 
 
@@ -246,3 +252,34 @@ def build_qwen3_mlp(wl: Workload, t: Dict[str, torch.Tensor], device="cuda", bit
     if wl.wfmt == "affine8":
         mlp.quantize(bits=bits, group_size=group_size)
     return mlp
+
+
+def make_head_tensors(wl: Workload, device="cpu", seed: Optional[int] = None) -> Dict[str, torch.Tensor]:
+    """Inputs and bf16 weights of the draft head workload (seeded normal values)."""
+    a = wl.args
+    g = torch.Generator(device=device)
+    g.manual_seed(wl.seed if seed is None else seed)
+    b, s, hc, dim, vocab, rank = wl.batch, wl.block, a["hc_mult"], a["dim"], a["vocab_size"], a["dspark_markov_rank"]
+    r = lambda *shape, std=1.0: torch.randn(shape, generator=g, device=device) * std  # noqa: E731
+    return {"args": a, "x": r(b, s, hc, dim).to(torch.bfloat16), "fn": r(hc, hc * dim, std=0.02), "scale": r(1),
+            "base": r(hc, std=0.5), "norm_w": 1 + r(dim, std=0.1), "head_w": r(vocab, dim, std=0.02).to(torch.bfloat16),
+            "w1": r(vocab, rank, std=0.2).to(torch.bfloat16), "w2": r(vocab, rank, std=0.2).to(torch.bfloat16),
+            "wc": r(1, dim + rank, std=0.02),
+            "anchor": torch.randint(0, vocab, (b,), generator=g, device=device, dtype=torch.int32)}
+
+
+def build_head(wl: Workload, t: Dict[str, torch.Tensor], device="cuda"):
+    """A :class:`dsm.head.DSparkHead` holding ``t``'s weights."""
+    from .head import DSparkHead
+
+    h = DSparkHead(wl.args).to(device)
+    with torch.no_grad():
+        h.hc_head_fn.copy_(t["fn"])
+        h.hc_head_scale.copy_(t["scale"])
+        h.hc_head_base.copy_(t["base"])
+        h.norm.weight.copy_(t["norm_w"])
+        h.confidence_head.proj.weight.copy_(t["wc"])
+    h.markov_head.markov_w1.weight = torch.nn.Parameter(t["w1"].to(device), requires_grad=False)
+    h.markov_head.markov_w2.weight = torch.nn.Parameter(t["w2"].to(device), requires_grad=False)
+    h.head.weight = torch.nn.Parameter(t["head_w"].to(device), requires_grad=False)
+    return h
