@@ -188,6 +188,43 @@ __device__ __forceinline__ void block_sum_b(const float (&s)[MAXB], int batch, f
   }
 }
 
+// The CTAs' candidates for batch row b (generation buffer buf) combined by one warp: each
+// lane reads every 32nd CTA (independent loads), then a shuffle reduction in value order,
+// ties to the lowest index. Every lane returns the winner.
+__device__ __forceinline__ void combine_best(const WalkArgs& a, int buf, int b, float& v, int& ix) {
+  const int G = gridDim.x, B = a.batch, lane = threadIdx.x & 31;
+  v = -INFINITY;
+  ix = INT_MAX;
+  for (int c = lane; c < G; c += 32) {
+    const float ov = __ldcg(&a.cand_v[(int64_t(buf) * G + c) * B + b]);
+    const int oi = __ldcg(&a.cand_i[(int64_t(buf) * G + c) * B + b]);
+    if (better(ov, oi, v, ix)) {
+      v = ov;
+      ix = oi;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
+    if (better(ov, oi, v, ix)) {
+      v = ov;
+      ix = oi;
+    }
+  }
+}
+
+// sum of the CTAs' partial sums for batch row b, in CTA order within each lane's share
+// and then a fixed shuffle tree: the same on every CTA and every run
+__device__ __forceinline__ float combine_sum(const WalkArgs& a, int buf, int b) {
+  const int G = gridDim.x, B = a.batch, lane = threadIdx.x & 31;
+  float z = 0.f;
+  for (int c = lane; c < G; c += 32) z += __ldcg(&a.cand_v[(int64_t(buf) * G + c) * B + b]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+  return z;
+}
+
 __host__ __device__ __forceinline__ int walk_e_floats(int batch, int rank, int maxb) {
   const int f32 = batch * rank, bf = (maxb * (rank + 8) + 1) / 2;
   return f32 > bf ? f32 : bf;
@@ -249,11 +286,8 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
       }
     }
     __syncthreads();
-    auto emit = [&](int b, int v, float bias, float& bv, int& bi) {  // biased logit of (b, v): store, keep the best
+    auto emit_l = [&](int b, int v, float li, float& bv, int& bi) {  // biased logit of (b, v): store, keep the best
       const int64_t t = int64_t(b) * S + i;
-      float l = a.logits[t * V + v];
-      if (a.lo_offset) l += a.logits[(a.lo_offset + t) * V + v];
-      const float li = l + bias;
       a.biased[t * V + v] = li;
       if (sampled) {
         li_sm[b * a.slice + (v - v0)] = li;
@@ -262,6 +296,12 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
         bv = li;
         bi = v;
       }
+    };
+    auto emit = [&](int b, int v, float bias, float& bv, int& bi) {  // base logit of (b, v) plus the bias
+      const int64_t t = int64_t(b) * S + i;
+      float l = a.logits[t * V + v];
+      if (a.lo_offset) l += a.logits[(a.lo_offset + t) * V + v];
+      emit_l(b, v, l + bias, bv, bi);
     };
     if (use_mma) {
       const int g = lane >> 2, q = lane & 3;
@@ -303,7 +343,22 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
             }
           }
         }
-        // D fragment: d0, d1 row ra; d2, d3 row rb; batch nt*8 + 2q + {0, 1}
+        // D fragment: d0, d1 row ra; d2, d3 row rb; batch nt*8 + 2q + {0, 1}. The tile's base
+        // logits are read first, so no load waits behind a store of a biased logit
+        float lg[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          if (nt * 8 >= B) break;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int b = nt * 8 + 2 * q + c;
+            const int64_t t = int64_t(b) * S + i;
+            lg[nt][c] = lg[nt][2 + c] = 0.f;
+            if (b >= B) continue;
+            if (oka) lg[nt][c] = __ldg(&a.logits[t * V + ra]) + (a.lo_offset ? __ldg(&a.logits[(a.lo_offset + t) * V + ra]) : 0.f);
+            if (okb) lg[nt][2 + c] = __ldg(&a.logits[t * V + rb]) + (a.lo_offset ? __ldg(&a.logits[(a.lo_offset + t) * V + rb]) : 0.f);
+          }
+        }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           if (nt * 8 >= B) break;
@@ -311,8 +366,8 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
           for (int c = 0; c < 2; ++c) {
             const int b = nt * 8 + 2 * q + c;
             if (b >= B) continue;
-            if (oka) emit(b, ra, d[nt][c], bv2[nt][c], bi2[nt][c]);
-            if (okb) emit(b, rb, d[nt][2 + c], bv2[nt][c], bi2[nt][c]);
+            if (oka) emit_l(b, ra, lg[nt][c] + d[nt][c], bv2[nt][c], bi2[nt][c]);
+            if (okb) emit_l(b, rb, lg[nt][2 + c] + d[nt][2 + c], bv2[nt][c], bi2[nt][c]);
           }
         }
       }
@@ -379,22 +434,16 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
       __threadfence();
     }
     if (!walk_sync(a, gen)) return;
-    if (int(threadIdx.x) < B) {  // every CTA takes the same winner
-      const int b = threadIdx.x;
-      float v = -INFINITY;
-      int ix = INT_MAX;
-      for (int c = 0; c < G; ++c) {
-        const float ov = __ldcg(&a.cand_v[(int64_t(buf) * G + c) * B + b]);
-        const int oi = __ldcg(&a.cand_i[(int64_t(buf) * G + c) * B + b]);
-        if (better(ov, oi, v, ix)) {
-          v = ov;
-          ix = oi;
-        }
+    for (int b = warp; b < B; b += kWalkWarps) {  // every CTA takes the same winner
+      float v;
+      int ix;
+      combine_best(a, buf, b, v, ix);
+      if (lane == 0) {
+        if (sampled)
+          stat_m[b] = v;  // max over the vocabulary of logits / temperature
+        else
+          prev_s[b] = ix;
       }
-      if (sampled)
-        stat_m[b] = v;  // max over the vocabulary of logits / temperature
-      else
-        prev_s[b] = ix;
     }
     buf ^= 1;
     if (sampled) {
@@ -416,10 +465,9 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
         __threadfence();
       }
       if (!walk_sync(a, gen)) return;
-      if (int(threadIdx.x) < B) {
-        float z = 0.f;
-        for (int c = 0; c < G; ++c) z += __ldcg(&a.cand_v[(int64_t(buf) * G + c) * B + threadIdx.x]);
-        stat_z[threadIdx.x] = z;
+      for (int b = warp; b < B; b += kWalkWarps) {
+        const float z = combine_sum(a, buf, b);
+        if (lane == 0) stat_z[b] = z;
       }
       buf ^= 1;
       __syncthreads();
@@ -451,22 +499,15 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
         __threadfence();
       }
       if (!walk_sync(a, gen)) return;
-      if (int(threadIdx.x) < B) {
-        const int b = threadIdx.x;
-        float v = -INFINITY;
-        int ix = INT_MAX;
-        for (int c = 0; c < G; ++c) {
-          const float ov = __ldcg(&a.cand_v[(int64_t(buf) * G + c) * B + b]);
-          const int oi = __ldcg(&a.cand_i[(int64_t(buf) * G + c) * B + b]);
-          if (better(ov, oi, v, ix)) {
-            v = ov;
-            ix = oi;
-          }
-        }
-        prev_s[b] = ix;
+      for (int b = warp; b < B; b += kWalkWarps) {
+        float v;
+        int ix;
+        combine_best(a, buf, b, v, ix);
+        if (lane == 0) prev_s[b] = ix;
       }
       buf ^= 1;
     }
+    __syncthreads();  // prev_s[b] was written by the warp that combined row b
     if (int(threadIdx.x) < B) {
       if (prev_s[threadIdx.x] < 0 || prev_s[threadIdx.x] >= V) prev_s[threadIdx.x] = 0;  // all-NaN row
       if (blockIdx.x == 0) a.out_ids[int64_t(threadIdx.x) * (S + 1) + i + 1] = prev_s[threadIdx.x];
