@@ -9,3 +9,4 @@ from .moe_oracle import *  # noqa: F401,F403
 from .formats import *  # noqa: F401,F403
 from .block_oracle import *  # noqa: F401,F403
 from .head_oracle import *  # noqa: F401,F403
+from .attention_oracle import *  # noqa: F401,F403

@@ -164,6 +164,12 @@ class array:
     def __rtruediv__(self, o):
         return self._bin(o, lambda a, b: b / a)
 
+    def __pow__(self, o):
+        return self._bin(o, torch.pow)
+
+    def __rpow__(self, o):
+        return array(torch.pow(torch.tensor(o, dtype=self.t.dtype), self.t))
+
     def __matmul__(self, o):
         return matmul(self, o)
 
@@ -337,6 +343,10 @@ def stack(xs, axis=0):
 
 def broadcast_to(x, shape):
     return array(_t(x).expand(*shape))
+
+
+def swapaxes(x, a, b):
+    return array(_t(x).transpose(a, b))
 
 
 def outer(a, b):
