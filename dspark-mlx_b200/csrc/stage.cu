@@ -202,6 +202,14 @@ extern "C" int dsm_stage_rows(const void* x, int x_dtype, int64_t n_tokens, int 
                          nullptr, stream);
 }
 
+extern "C" int dsm_stage_rows_hilo(const float* x, int64_t n_rows, int dim, void* staged, int64_t rows_cap,
+                                   float* row_scale, void* stream) {
+  using namespace dsm;
+  DSM_REQUIRE(!n_rows || (x && staged && row_scale), "dsm_stage_rows_hilo: NULL pointer");
+  DSM_REQUIRE((reinterpret_cast<uintptr_t>(staged) & 15) == 0, "dsm_stage_rows_hilo: staged must be 16-byte aligned");
+  return stage_rows_hilo(x, n_rows, dim, staged, rows_cap, row_scale, stream);
+}
+
 namespace dsm {
 int stage_rows_hilo(const float* x, int64_t n_rows, int dim, void* staged, int64_t rows_cap, float* row_scale,
                     void* stream) {

@@ -32,7 +32,8 @@ EXPORTED = (
     "dsm_moe_workspace_bytes", "dsm_moe_forward", "dsm_gather_rows", "dsm_segment_ids",
     "dsm_set_expert_regime", "dsm_hc_pre_norm", "dsm_hc_post", "dsm_dense_mlp_workspace_bytes",
     "dsm_dense_mlp", "dsm_linear", "dsm_hc_head_norm", "dsm_markov_head", "dsm_draft_head_workspace_bytes",
-    "dsm_draft_head",
+    "dsm_draft_head", "dsm_rows_norm_rope", "dsm_q_head_norm_rope", "dsm_kv_window_write",
+    "dsm_sparse_attn_scratch_bytes", "dsm_sparse_attn", "dsm_round_rows", "dsm_stage_rows_hilo",
 )
 
 
@@ -113,6 +114,13 @@ def _declare(lib):
         "dsm_markov_head": (I, [V, I, I64, I, I, V, V, I, V, V, V]),
         "dsm_draft_head_workspace_bytes": (S, [POINTER(HeadDesc), I]),
         "dsm_draft_head": (I, [POINTER(HeadDesc), V, I, V, I, F, V, V, V, V, V, V, S, V]),
+        "dsm_rows_norm_rope": (I, [V, V, I64, I, V, F, I, V, V, I, I, V, I, V]),
+        "dsm_q_head_norm_rope": (I, [V, V, I64, I, I, F, I, V, V, I, I, V, I, V]),
+        "dsm_kv_window_write": (I, [V, I, I, I, I, I, I, V, V]),
+        "dsm_sparse_attn_scratch_bytes": (S, [I, I, I, I]),
+        "dsm_sparse_attn": (I, [V, V, V, I, V, I, I, I, I, I, I, F, I, V, V, I, I, V, V, V]),
+        "dsm_round_rows": (I, [V, V, I64, V, I, V]),
+        "dsm_stage_rows_hilo": (I, [V, I64, I, V, I64, V, V]),
         "dsm_moe_workspace_bytes": (S, [POINTER(MoEDesc)]),
         "dsm_moe_forward": (I, [POINTER(MoEDesc), V, I, V, I, I64, V, V, V, V, S, V]),
     }

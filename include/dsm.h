@@ -35,6 +35,9 @@
  *   dsm_markov_head     DSparkMarkovHead.__call__              model/heads.py:26-30
  *   dsm_draft_head      DSparkBlock.forward_head + LM head      model/block.py:103-116, recipe.py:21-63,
  *                       (Markov walk, sampler, confidence)     model/heads.py:11-49
+ *   dsm_rows_norm_rope, dsm_q_head_norm_rope, dsm_kv_window_write, dsm_sparse_attn, dsm_round_rows:
+ *                       DSparkAttention.__call__ / advance_window around dsm_linear
+ *                       (model/attention.py:27-142, kernels.py:20-57, norm_rope.py:22-77)
  *   dsm_gather_rows, dsm_segment_ids: expert-parallel plumbing; the reference runs on one
  *                       device (tests/reference_model.py:55-56 forces world_size 1) and has
  *                       no counterpart.
@@ -142,6 +145,12 @@ int64_t dsm_stage_rows_cap(int64_t n_rows);
 int dsm_stage_rows(const void* x, int x_dtype, int64_t n_tokens, int dim, const int32_t* perm,
                    int64_t n_rows, int topk, void* staged, int64_t rows_cap, float* row_scale,
                    void* stream);
+/* fp32 rows x [n_rows, dim] staged as 2 * n_rows f16 rows: row r as dsm_stage_rows stages it
+ * (hi), row n_rows + r the residual x - hi with its own scale (lo); a product over all rows
+ * then adds up, hi + lo, to the fp32 row's product within ~2^-22 relative.
+ * rows_cap >= dsm_stage_rows_cap(2 * n_rows). */
+int dsm_stage_rows_hilo(const float* x, int64_t n_rows, int dim, void* staged, int64_t rows_cap, float* row_scale,
+                        void* stream);
 
 /* ---- expert weight packing (load time) ------------------------------------------------
  * Converts stacked expert weights [n_experts, rows, cols] (nn.Linear [out, in] layout)
@@ -245,6 +254,34 @@ size_t dsm_draft_head_workspace_bytes(const dsm_head_desc* d, int x_dtype);
 int dsm_draft_head(const dsm_head_desc* d, const void* x, int x_dtype, const void* anchor, int anchor_dtype,
                    float temperature, const float* uniforms, int32_t* out_ids, float* biased_logits, float* confidence,
                    void* y_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- the draft attention (compress_ratio == 0 MLA) --------------------------------------------
+ * The projections run on dsm_linear (fp32 rows; an F32 activation staged hi + lo gives a second
+ * block of rows, passed as *_lo). cos_t / sin_t are [positions, rope_dim / 2] fp32 tables.
+ * rows_norm_rope: out[r] = RoPE(T(RMSNorm(T(in[r] + in_lo[r])) * weight)), the RoPE on the last
+ *   rope_dim columns at position pos0 + r % period (rope_dim 0: none). cols <= 49152.
+ * q_head_norm_rope: each head of in [n_rows, n_heads * head_dim] scaled by rsqrt(mean(q^2) + eps)
+ *   with every elementwise op rounded to T, then RoPE as above.
+ * kv_window_write: window[b, (pos0 + j) % window] = rows[b, j] for j < n <= window.
+ * sparse_attn: for token (b, m) and head h, attention over the window's first n_win slots and the
+ *   block's rows [b, block] of the shared KV head, with a denominator sink exp(sink[h] - max),
+ *   then the inverse RoPE at position pos0 + m; out is group-major [n_groups][b * block]
+ *   [(n_heads / n_groups) * head_dim]. scratch: dsm_sparse_attn_scratch_bytes.
+ * round_rows: out = T(in + in_lo). */
+int dsm_rows_norm_rope(const float* in, const float* in_lo, int64_t n_rows, int cols, const float* weight, float eps,
+                       int rope_dim, const float* cos_t, const float* sin_t, int pos0, int period, void* out,
+                       int out_dtype, void* stream);
+int dsm_q_head_norm_rope(const float* in, const float* in_lo, int64_t n_rows, int n_heads, int head_dim, float eps,
+                         int rope_dim, const float* cos_t, const float* sin_t, int pos0, int period, void* out,
+                         int out_dtype, void* stream);
+int dsm_kv_window_write(const void* rows, int dtype, int batch, int n, int dim, int pos0, int window, void* win,
+                        void* stream);
+size_t dsm_sparse_attn_scratch_bytes(int batch, int block, int n_heads, int n_win);
+int dsm_sparse_attn(const void* q, const void* window_kv, const void* block_kv, int dtype, const float* sink, int batch,
+                    int block, int n_heads, int head_dim, int window, int n_win, float scale, int rope_dim,
+                    const float* cos_t, const float* sin_t, int pos0, int n_groups, void* out, float* scratch,
+                    void* stream);
+int dsm_round_rows(const float* in, const float* in_lo, int64_t n, void* out, int out_dtype, void* stream);
 
 /* Kernel regime of the grouped expert products: 0 (default) picks by rows per busy
  * expert -- the mma.sync weight-streaming kernel at decode sizes, the tcgen05/TMEM kernel
