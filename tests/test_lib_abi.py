@@ -79,6 +79,30 @@ def test_bad_arguments_are_rejected_on_the_host(call):
     assert L.dsm_last_error_message().decode()
 
 
+def test_attention_entry_points_reject_bad_arguments_on_the_host():
+    L = _lib.lib()
+    bf = _lib.DT_BF16
+    cases = [
+        # n_heads not a multiple of n_groups
+        lambda: L.dsm_sparse_attn(1, 1, 1, bf, 1, 2, 5, 6, 64, 8, 4, 0.1, 16, 1, 1, 0, 4, 1, 1, None),
+        # n_win beyond the window
+        lambda: L.dsm_sparse_attn(1, 1, 1, bf, 1, 2, 5, 8, 64, 8, 9, 0.1, 16, 1, 1, 0, 4, 1, 1, None),
+        # more rows than window slots in one write
+        lambda: L.dsm_kv_window_write(1, bf, 2, 9, 64, 0, 8, 1, None),
+        # odd rope width
+        lambda: L.dsm_rows_norm_rope(1, None, 4, 64, None, 1e-6, 15, 1, 1, 0, 4, 1, bf, None),
+        # odd head_dim
+        lambda: L.dsm_q_head_norm_rope(1, None, 4, 2, 63, 1e-6, 0, None, None, 0, 1, 1, bf, None),
+        # NULL staging buffers
+        lambda: L.dsm_stage_rows_hilo(None, 4, 64, None, 1 << 10, None, None),
+        lambda: L.dsm_round_rows(1, None, 8, 1, _lib.DT_I32, None),
+    ]
+    for i, call in enumerate(cases):
+        assert call() != 0, i
+        assert L.dsm_last_error_message().decode()
+    assert L.dsm_sparse_attn_scratch_bytes(8, 7, 64, 128) == 8 * 7 * 64 * 135 * 4
+
+
 def test_draft_head_host_checks():
     L = _lib.lib()
     d = _lib.HeadDesc(batch=8, block=7, hc_mult=4, dim=4096, vocab=129280, rank=256)

@@ -173,3 +173,4 @@ def test_shared_fp8_expert_survives_to():
     loading.load_moe(moe, t, "mtp.0.ffn")
     moe = moe.to(torch.device("cpu"))  # meta placeholders stay placeholders
     assert moe.shared_experts.format == "fp8" and moe.shared_experts.w1.weight.is_meta
+
