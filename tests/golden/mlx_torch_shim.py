@@ -514,6 +514,19 @@ def _uniform(low=0.0, high=1.0, shape=(), dtype=float32, key=None):
     return array(u.to(dtype))
 
 
+def _sdpa(q, k, v, scale, mask=None):
+    """``mx.fast.scaled_dot_product_attention``: softmax(q k^T * scale) v with fp32
+    accumulation and q's dtype out; grouped-query heads share their KV head."""
+    tq, tk, tv = _t(q), _t(k), _t(v)
+    rep = tq.shape[1] // tk.shape[1]
+    kf = tk.to(torch.float32).repeat_interleave(rep, dim=1)
+    vf = tv.to(torch.float32).repeat_interleave(rep, dim=1)
+    s = (tq.to(torch.float32) @ kf.transpose(-1, -2)) * scale
+    if mask is not None:
+        s = s + _t(mask).to(torch.float32)
+    return array((torch.softmax(s, dim=-1) @ vf).to(tq.dtype))
+
+
 def random_seed(seed: int) -> None:
     _random_gen.manual_seed(seed)
     random_draws.clear()
@@ -549,6 +562,9 @@ def install() -> None:
     nn.Linear = Linear
     nn.silu = silu
     nn.Embedding = Embedding
+    fast = types.ModuleType("mlx.core.fast")
+    fast.scaled_dot_product_attention = _sdpa
+    core.fast = fast
     rnd = types.ModuleType("mlx.core.random")
     rnd.uniform = _uniform
     rnd.seed = random_seed
