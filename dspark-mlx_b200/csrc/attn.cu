@@ -19,36 +19,12 @@
 //
 // Everything is fp32 inside; values are rounded to the activation dtype where the reference's
 // arrays carry it. One CTA per row (norms), per (token, head) warp (attention).
-#include <type_traits>
-
 #include "common.cuh"
 
 namespace dsm {
 namespace {
 
 constexpr int kAttnThreads = 256;
-
-template <typename T>
-__device__ __forceinline__ float ld_f(const T* p, int64_t i) {
-  if constexpr (std::is_same<T, float>::value)
-    return p[i];
-  else
-    return __bfloat162float(p[i]);
-}
-template <typename T>
-__device__ __forceinline__ T st_f(float v) {
-  if constexpr (std::is_same<T, float>::value)
-    return v;
-  else
-    return __float2bfloat16_rn(v);
-}
-template <typename T>
-__device__ __forceinline__ float rnd(float v) {  // v rounded to T
-  if constexpr (std::is_same<T, float>::value)
-    return v;
-  else
-    return __bfloat162float(__float2bfloat16_rn(v));
-}
 
 __device__ __forceinline__ float block_sum256(float v, float* red) {
 #pragma unroll

@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <type_traits>
 
 #include "dsm.h"
 
@@ -302,6 +303,30 @@ __device__ __forceinline__ float load_as_float<float>(const float* p, int64_t i)
 template <>
 __device__ __forceinline__ float load_as_float<__nv_bfloat16>(const __nv_bfloat16* p, int64_t i) {
   return __bfloat162float(p[i]);
+}
+
+// Activations of the attention paths are fp32 or bf16 (T): loads to fp32, stores from fp32,
+// and an fp32 value rounded to T as the reference's arrays of dtype T hold it.
+template <typename T>
+__device__ __forceinline__ float ld_f(const T* p, int64_t i) {
+  if constexpr (std::is_same<T, float>::value)
+    return p[i];
+  else
+    return __bfloat162float(p[i]);
+}
+template <typename T>
+__device__ __forceinline__ T st_f(float v) {
+  if constexpr (std::is_same<T, float>::value)
+    return v;
+  else
+    return __float2bfloat16_rn(v);
+}
+template <typename T>
+__device__ __forceinline__ float rnd(float v) {
+  if constexpr (std::is_same<T, float>::value)
+    return v;
+  else
+    return __bfloat162float(__float2bfloat16_rn(v));
 }
 
 }  // namespace dsm

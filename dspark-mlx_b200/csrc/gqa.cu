@@ -1,0 +1,420 @@
+// The Qwen3 DSpark draft attention (dspark_mlx/arch/qwen3.py:85-143): grouped-query attention
+// of the draft block over [context || block], around the packed-weight projections
+// (dsm_linear):
+//
+//   dsm_qkv_norm_rope  a fused projection's fp32 rows [n, (n_q + 2 n_kv) * head_dim] (plus the
+//                      lo rows of an fp32 input staged hi + lo): every head rounded to the
+//                      activation dtype; the q and k heads RMSNormed with their weights
+//                      (norm_rope.py:22-39) and rotated by NeoX half-split RoPE with the
+//                      tables cast to the activation dtype (qwen3.py:65-75); q heads written
+//                      [n, n_q, head_dim], k and v heads into [batch, n_kv, cap, head_dim]
+//                      caches at rows row0 + t (qwen3.py:96-108, 121-137).
+//   dsm_gqa_attn       softmax(q k^T * scale) v of every query head over its KV head's
+//                      context rows and then the block's own rows, with no mask
+//                      (mx.fast.scaled_dot_product_attention, qwen3.py:111-115, 138-143),
+//                      written [batch, block, n_heads * head_dim] for o_proj.
+//
+// The attention is split over keys. A CTA holds one KV head's query rows (the group's heads
+// x the block's tokens, up to 32) and one key range; it streams 64-key tiles of K and V
+// through shared memory with an online softmax and leaves fp32 partials (m, l, acc) per row
+// and range. A second kernel combines the ranges in order. Everything is fp32 inside; the
+// output is rounded once to the activation dtype.
+#include "common.cuh"
+
+namespace dsm {
+namespace {
+
+constexpr int kGqaThreads = 256;
+constexpr int kGqaWarps = kGqaThreads / 32;
+constexpr int kKeyTile = 64;    // keys per shared-memory tile
+constexpr int kRowBlock = 32;   // query rows per CTA
+constexpr int kMaxSplits = 64;  // key ranges per KV head
+constexpr int kMaxHeadDim = 256;
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// One warp per (row, head). Heads [0, n_q) are queries, [n_q, n_q + n_kv) keys, then values.
+// Row r belongs to sequence r / period at token t = r % period: RoPE table row tab0 + t,
+// cache row row0 + t.
+template <typename T>
+__global__ void __launch_bounds__(kGqaThreads) qkv_norm_rope_kernel(
+    const float* __restrict__ in, const float* __restrict__ in_lo, int64_t n_rows, int n_q, int n_kv, int head_dim,
+    const float* __restrict__ q_w, const float* __restrict__ k_w, float eps, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, int tab0, int period, T* __restrict__ q_out, T* __restrict__ k_out,
+    T* __restrict__ v_out, int kv_cap, int row0) {
+  __shared__ float buf[kGqaWarps][kMaxHeadDim];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int heads = n_q + 2 * n_kv;
+  const int64_t wid = int64_t(blockIdx.x) * kGqaWarps + warp;
+  if (wid >= n_rows * heads) return;  // whole warps leave; only warp-level syncs follow
+  const int64_t r = wid / heads;
+  const int hh = int(wid % heads);
+  const int64_t off = (r * heads + hh) * int64_t(head_dim);
+  float* x = buf[warp];
+  float sq = 0.f;
+  for (int d = lane; d < head_dim; d += 32) {
+    float v = in[off + d];
+    if (in_lo) v += in_lo[off + d];
+    v = rnd<T>(v);  // the projection's output dtype
+    x[d] = v;
+    sq = fmaf(v, v, sq);
+  }
+  const int t = int(r % period);
+  const int64_t b = r / period;
+  if (hh >= n_q + n_kv) {  // a value head: the projection as it is
+    const int g = hh - n_q - n_kv;
+    T* dst = v_out + ((b * n_kv + g) * kv_cap + row0 + t) * int64_t(head_dim);
+    for (int d = lane; d < head_dim; d += 32) dst[d] = st_f<T>(x[d]);
+    return;
+  }
+  const float rs = rsqrtf(warp_sum(sq) / float(head_dim) + eps);
+  const float* w = hh < n_q ? q_w : k_w;
+  for (int d = lane; d < head_dim; d += 32) x[d] = rnd<T>(__fmul_rn(w[d], __fmul_rn(x[d], rs)));
+  __syncwarp();
+  const int half = head_dim / 2;
+  const int64_t p = int64_t(tab0) + t;
+  T* dst = hh < n_q ? q_out + (r * n_q + hh) * int64_t(head_dim)
+                    : k_out + ((b * n_kv + (hh - n_q)) * kv_cap + row0 + t) * int64_t(head_dim);
+  for (int d = lane; d < head_dim; d += 32) {
+    // x * cos + rotate_half(x) * sin, each product and the sum rounded to T
+    const float c = rnd<T>(cos_t[p * head_dim + d]);
+    const float s = rnd<T>(sin_t[p * head_dim + d]);
+    const float rot = d < half ? -x[d + half] : x[d - half];
+    dst[d] = st_f<T>(__fadd_rn(rnd<T>(__fmul_rn(x[d], c)), rnd<T>(__fmul_rn(rot, s))));
+  }
+}
+
+// Grid (split, kv head, batch * row_blocks). Local row r is query row ri = row_block * 32 + r
+// of KV head g: head g * G + ri / block, token ri % block. Keys [split * chunk, +chunk) of
+// the n_ctx context rows followed by the block rows.
+template <typename T, int HD>
+__global__ void __launch_bounds__(kGqaThreads) gqa_attn_kernel(
+    const T* __restrict__ q, const T* __restrict__ ctx_k, const T* __restrict__ ctx_v, int64_t ctx_sb,
+    int64_t ctx_sh, int n_ctx, const T* __restrict__ blk_k, const T* __restrict__ blk_v, int block, int n_heads,
+    int n_kv, int row_blocks, int chunk, int n_splits, float scale, float* __restrict__ part,
+    float* __restrict__ ml) {
+  constexpr int KP = HD + 1;                           // padded K rows: conflict-free reads by key
+  constexpr int RS = kGqaThreads / kKeyTile;           // row stride of the score threads
+  constexpr int SR = kRowBlock / RS;                   // scores per thread per tile
+  constexpr int RPP = kGqaThreads / HD;                // row stride of the P.V threads
+  constexpr int NACC = kRowBlock / RPP;                // accumulators per thread
+  static_assert(HD >= 32 && HD <= kMaxHeadDim && kGqaThreads % HD == 0, "head_dim");
+  extern __shared__ float smem[];
+  float* Qs = smem;                          // [kRowBlock][HD]
+  float* Ks = Qs + kRowBlock * HD;           // [kKeyTile][KP]
+  float* Vs = Ks + kKeyTile * KP;            // [kKeyTile][HD]
+  float* P = Vs + kKeyTile * HD;             // [kRowBlock][kKeyTile]
+  float* m_run = P + kRowBlock * kKeyTile;   // [kRowBlock]
+  float* l_run = m_run + kRowBlock;          // [kRowBlock]
+  float* alpha = l_run + kRowBlock;          // [kRowBlock]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int split = blockIdx.x, g = blockIdx.y;
+  const int b = int(blockIdx.z) / row_blocks, r0 = (int(blockIdx.z) % row_blocks) * kRowBlock;
+  const int G = n_heads / n_kv;
+  const int nrows = min(kRowBlock, G * block - r0);
+  const int nk = n_ctx + block;
+  const int k0 = split * chunk, k1 = min(nk, k0 + chunk);
+
+  for (int i = tid; i < kRowBlock * HD; i += kGqaThreads) {
+    const int r = i / HD, d = i % HD;
+    float v = 0.f;
+    if (r < nrows) {
+      const int ri = r0 + r;
+      const int h = g * G + ri / block, t = ri % block;
+      v = ld_f(q, ((int64_t(b) * block + t) * n_heads + h) * HD + d);
+    }
+    Qs[i] = v;
+  }
+  for (int i = tid; i < kRowBlock * kKeyTile; i += kGqaThreads) P[i] = 0.f;
+  if (tid < kRowBlock) {
+    m_run[tid] = -INFINITY;
+    l_run[tid] = 0.f;
+    alpha[tid] = 0.f;
+  }
+  float acc[NACC];
+#pragma unroll
+  for (int i = 0; i < NACC; ++i) acc[i] = 0.f;
+  const int pd = tid % HD, prow = tid / HD;              // P.V: column pd of rows prow + i * RPP
+  const int sj = tid % kKeyTile, srow = tid / kKeyTile;  // scores: key sj of rows srow + i * RS
+  const int64_t ctx_base = int64_t(b) * ctx_sb + int64_t(g) * ctx_sh;
+  const int64_t blk_base = (int64_t(b) * n_kv + g) * block;
+
+  for (int kt0 = k0; kt0 < k1; kt0 += kKeyTile) {
+    const int kt = min(kKeyTile, k1 - kt0);
+    __syncthreads();  // the previous tile is consumed (and the initial fills are visible)
+    for (int i = tid; i < kKeyTile * HD; i += kGqaThreads) {
+      const int j = i / HD, d = i % HD;
+      float kv = 0.f, vv = 0.f;
+      if (j < kt) {
+        const int k = kt0 + j;
+        if (k < n_ctx) {
+          const int64_t o = ctx_base + int64_t(k) * HD + d;
+          kv = ld_f(ctx_k, o);
+          vv = ld_f(ctx_v, o);
+        } else {
+          const int64_t o = (blk_base + (k - n_ctx)) * HD + d;
+          kv = ld_f(blk_k, o);
+          vv = ld_f(blk_v, o);
+        }
+      }
+      Ks[j * KP + d] = kv;
+      Vs[j * HD + d] = vv;
+    }
+    __syncthreads();
+    {
+      float s[SR];
+#pragma unroll
+      for (int i = 0; i < SR; ++i) s[i] = 0.f;
+      const float* kr = Ks + sj * KP;
+      for (int d = 0; d < HD; ++d) {
+        const float kd = kr[d];
+#pragma unroll
+        for (int i = 0; i < SR; ++i) s[i] = fmaf(Qs[(srow + i * RS) * HD + d], kd, s[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < SR; ++i) P[(srow + i * RS) * kKeyTile + sj] = s[i] * scale;
+    }
+    __syncthreads();
+    for (int r = warp; r < nrows; r += kGqaWarps) {  // online softmax of row r over this tile
+      float* pr = P + r * kKeyTile;
+      float mt = -INFINITY;
+      for (int j = lane; j < kt; j += 32) mt = fmaxf(mt, pr[j]);
+      const float m_old = m_run[r];
+      const float m_new = fmaxf(m_old, warp_max(mt));
+      float ls = 0.f;
+      for (int j = lane; j < kKeyTile; j += 32) {
+        const float e = j < kt ? expf(pr[j] - m_new) : 0.f;
+        pr[j] = e;
+        ls += e;
+      }
+      ls = warp_sum(ls);
+      if (lane == 0) {
+        const float a = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
+        alpha[r] = a;
+        l_run[r] = l_run[r] * a + ls;
+        m_run[r] = m_new;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < NACC; ++i) acc[i] *= alpha[prow + i * RPP];
+    for (int j = 0; j < kt; ++j) {
+      const float v = Vs[j * HD + pd];
+#pragma unroll
+      for (int i = 0; i < NACC; ++i) acc[i] = fmaf(P[(prow + i * RPP) * kKeyTile + j], v, acc[i]);
+    }
+  }
+  // partials of query row (b, h, t): part[row][split][HD], ml[row][split][2]
+#pragma unroll
+  for (int i = 0; i < NACC; ++i) {
+    const int r = prow + i * RPP;
+    if (r < nrows) {
+      const int ri = r0 + r;
+      const int64_t row = (int64_t(b) * n_heads + g * G + ri / block) * block + ri % block;
+      part[(row * n_splits + split) * HD + pd] = acc[i];
+    }
+  }
+  if (tid < nrows) {
+    const int ri = r0 + tid;
+    const int64_t row = (int64_t(b) * n_heads + g * G + ri / block) * block + ri % block;
+    ml[(row * n_splits + split) * 2] = m_run[tid];
+    ml[(row * n_splits + split) * 2 + 1] = l_run[tid];
+  }
+}
+
+// One warp per query row (b, h, t): the key ranges' partials combined in range order,
+// divided by the total denominator, rounded to T into out[b, t, h, :].
+template <typename T>
+__global__ void __launch_bounds__(kGqaThreads) gqa_combine_kernel(const float* __restrict__ part,
+                                                                  const float* __restrict__ ml, int64_t n_rows,
+                                                                  int n_splits, int head_dim, int n_heads, int block,
+                                                                  T* __restrict__ out) {
+  __shared__ float wts[kGqaWarps][kMaxSplits];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = int64_t(blockIdx.x) * kGqaWarps + warp;
+  if (row >= n_rows) return;  // whole warps leave; only warp-level syncs follow
+  const float* mlr = ml + row * n_splits * 2;
+  float m = -INFINITY;
+  for (int s = lane; s < n_splits; s += 32) m = fmaxf(m, mlr[2 * s]);
+  m = warp_max(m);
+  float l = 0.f;
+  for (int s = lane; s < n_splits; s += 32) {
+    const float w = expf(mlr[2 * s] - m);
+    wts[warp][s] = w;
+    l = fmaf(w, mlr[2 * s + 1], l);
+  }
+  l = warp_sum(l);
+  __syncwarp();
+  const int t = int(row % block);
+  const int64_t bh = row / block;
+  const int h = int(bh % n_heads);
+  const int64_t b = bh / n_heads;
+  T* dst = out + ((b * block + t) * n_heads + h) * int64_t(head_dim);
+  const float* pr = part + row * n_splits * int64_t(head_dim);
+  for (int d = lane; d < head_dim; d += 32) {
+    float o = 0.f;
+    for (int s = 0; s < n_splits; ++s) o = fmaf(pr[int64_t(s) * head_dim + d], wts[warp][s], o);
+    dst[d] = st_f<T>(o / l);
+  }
+}
+
+struct GqaPlan {
+  int row_blocks, chunk, n_splits;
+};
+
+// Key ranges: enough CTAs for two per SM, whole tiles per range, no empty range.
+GqaPlan gqa_plan(int batch, int block, int n_heads, int n_kv, int n_ctx) {
+  GqaPlan p;
+  p.row_blocks = int(ceil_div(int64_t(n_heads / n_kv) * block, kRowBlock));
+  const int64_t nk = int64_t(n_ctx) + block;
+  const int64_t base = int64_t(batch) * n_kv * p.row_blocks;
+  const int64_t tiles = ceil_div(nk, kKeyTile);
+  int64_t want = ceil_div(2 * int64_t(num_sms()), base);
+  want = want < 1 ? 1 : (want > kMaxSplits ? kMaxSplits : want);
+  if (want > tiles) want = tiles;
+  const int64_t per = ceil_div(tiles, want);
+  p.chunk = int(per * kKeyTile);
+  p.n_splits = int(ceil_div(nk, p.chunk));
+  return p;
+}
+
+size_t gqa_smem_bytes(int hd) {
+  return size_t(kRowBlock * hd + kKeyTile * (hd + 1) + kKeyTile * hd + kRowBlock * kKeyTile + 3 * kRowBlock) * 4;
+}
+
+template <typename T, int HD>
+int launch_gqa(const void* q, const void* ctx_k, const void* ctx_v, int64_t sb, int64_t sh, int n_ctx,
+               const void* blk_k, const void* blk_v, int batch, int block, int n_heads, int n_kv, float scale,
+               const GqaPlan& p, float* part, float* ml, cudaStream_t s) {
+  auto k = gqa_attn_kernel<T, HD>;
+  const size_t smem = gqa_smem_bytes(HD);
+  if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return check_launch("gqa_attn smem attribute");
+  const dim3 grid(unsigned(p.n_splits), unsigned(n_kv), unsigned(batch * p.row_blocks));
+  k<<<grid, kGqaThreads, smem, s>>>(static_cast<const T*>(q), static_cast<const T*>(ctx_k),
+                                     static_cast<const T*>(ctx_v), sb, sh, n_ctx, static_cast<const T*>(blk_k),
+                                     static_cast<const T*>(blk_v), block, n_heads, n_kv, p.row_blocks, p.chunk,
+                                     p.n_splits, scale, part, ml);
+  return check_launch("gqa_attn");
+}
+
+template <typename T>
+int launch_gqa_hd(int hd, const void* q, const void* ctx_k, const void* ctx_v, int64_t sb, int64_t sh, int n_ctx,
+                  const void* blk_k, const void* blk_v, int batch, int block, int n_heads, int n_kv, float scale,
+                  const GqaPlan& p, float* part, float* ml, cudaStream_t s) {
+  switch (hd) {
+    case 32:
+      return launch_gqa<T, 32>(q, ctx_k, ctx_v, sb, sh, n_ctx, blk_k, blk_v, batch, block, n_heads, n_kv, scale, p,
+                               part, ml, s);
+    case 64:
+      return launch_gqa<T, 64>(q, ctx_k, ctx_v, sb, sh, n_ctx, blk_k, blk_v, batch, block, n_heads, n_kv, scale, p,
+                               part, ml, s);
+    case 128:
+      return launch_gqa<T, 128>(q, ctx_k, ctx_v, sb, sh, n_ctx, blk_k, blk_v, batch, block, n_heads, n_kv, scale, p,
+                                part, ml, s);
+    case 256:
+      return launch_gqa<T, 256>(q, ctx_k, ctx_v, sb, sh, n_ctx, blk_k, blk_v, batch, block, n_heads, n_kv, scale, p,
+                                part, ml, s);
+    default:
+      return fail(DSM_ERR_UNSUPPORTED, "dsm_gqa_attn: head_dim must be 32, 64, 128 or 256");
+  }
+}
+
+size_t gqa_ws_bytes(int batch, int block, int n_heads, int head_dim, const GqaPlan& p) {
+  const size_t rows = size_t(batch) * n_heads * block;
+  return rows * size_t(p.n_splits) * (size_t(head_dim) + 2) * 4;
+}
+
+}  // namespace
+}  // namespace dsm
+
+using namespace dsm;
+
+extern "C" int dsm_qkv_norm_rope(const float* in, const float* in_lo, int64_t n_rows, int n_q, int n_kv,
+                                 int head_dim, const float* q_norm_w, const float* k_norm_w, float eps,
+                                 const float* cos_t, const float* sin_t, int tab_rows, int tab0, int period,
+                                 void* q_out, void* k_out, void* v_out, int kv_cap, int row0, int dtype,
+                                 void* stream) {
+  DSM_REQUIRE(n_rows >= 0 && n_q >= 0 && n_kv > 0, "dsm_qkv_norm_rope: bad shape");
+  DSM_REQUIRE(head_dim >= 2 && head_dim % 2 == 0 && head_dim <= kMaxHeadDim,
+              "dsm_qkv_norm_rope: head_dim must be even and at most 256");
+  DSM_REQUIRE(period > 0 && n_rows % period == 0, "dsm_qkv_norm_rope: rows must be whole sequences of period rows");
+  DSM_REQUIRE(tab0 >= 0 && int64_t(tab0) + period <= tab_rows, "dsm_qkv_norm_rope: RoPE table rows out of range");
+  DSM_REQUIRE(row0 >= 0 && int64_t(row0) + period <= kv_cap, "dsm_qkv_norm_rope: cache rows out of range");
+  DSM_REQUIRE(dtype == DSM_DT_F32 || dtype == DSM_DT_BF16, "dsm_qkv_norm_rope: dtype must be F32 or BF16");
+  if (n_rows == 0) return DSM_OK;
+  DSM_REQUIRE(in && k_norm_w && cos_t && sin_t && k_out && v_out && (n_q == 0 || (q_out && q_norm_w)),
+              "dsm_qkv_norm_rope: NULL pointer");
+  const int64_t warps = n_rows * (n_q + 2 * int64_t(n_kv));
+  const int64_t grid = ceil_div(warps, kGqaWarps);
+  DSM_REQUIRE(grid <= 0x7fffffff, "dsm_qkv_norm_rope: too many rows");
+  cudaStream_t s = as_stream(stream);
+  if (dtype == DSM_DT_BF16)
+    qkv_norm_rope_kernel<__nv_bfloat16><<<unsigned(grid), kGqaThreads, 0, s>>>(
+        in, in_lo, n_rows, n_q, n_kv, head_dim, q_norm_w, k_norm_w, eps, cos_t, sin_t, tab0, period,
+        static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_out), static_cast<__nv_bfloat16*>(v_out),
+        kv_cap, row0);
+  else
+    qkv_norm_rope_kernel<float><<<unsigned(grid), kGqaThreads, 0, s>>>(
+        in, in_lo, n_rows, n_q, n_kv, head_dim, q_norm_w, k_norm_w, eps, cos_t, sin_t, tab0, period,
+        static_cast<float*>(q_out), static_cast<float*>(k_out), static_cast<float*>(v_out), kv_cap, row0);
+  return check_launch("qkv_norm_rope");
+}
+
+extern "C" size_t dsm_gqa_attn_workspace_bytes(int batch, int block, int n_heads, int n_kv, int head_dim,
+                                               int n_ctx) {
+  if (batch <= 0 || block <= 0 || n_kv <= 0 || n_heads <= 0 || n_heads % n_kv != 0 || n_ctx < 0 || head_dim <= 0)
+    return 0;
+  return gqa_ws_bytes(batch, block, n_heads, head_dim, gqa_plan(batch, block, n_heads, n_kv, n_ctx));
+}
+
+extern "C" int dsm_gqa_attn(const void* q, const void* ctx_k, const void* ctx_v, int64_t ctx_batch_stride,
+                            int64_t ctx_head_stride, int n_ctx, const void* blk_k, const void* blk_v, int dtype,
+                            int batch, int block, int n_heads, int n_kv, int head_dim, float scale, void* out,
+                            void* ws, size_t ws_bytes, void* stream) {
+  DSM_REQUIRE(batch >= 0 && block > 0 && n_kv > 0 && n_heads > 0 && n_heads % n_kv == 0,
+              "dsm_gqa_attn: bad shape (n_heads must be a multiple of n_kv)");
+  DSM_REQUIRE(n_ctx >= 0 && int64_t(n_ctx) + block <= 0x7fffffff, "dsm_gqa_attn: bad context length");
+  DSM_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128 || head_dim == 256,
+              "dsm_gqa_attn: head_dim must be 32, 64, 128 or 256");
+  DSM_REQUIRE(n_ctx == 0 || (ctx_batch_stride >= 0 && ctx_head_stride >= 0), "dsm_gqa_attn: bad context strides");
+  DSM_REQUIRE(dtype == DSM_DT_F32 || dtype == DSM_DT_BF16, "dsm_gqa_attn: dtype must be F32 or BF16");
+  if (batch == 0) return DSM_OK;
+  DSM_REQUIRE(q && blk_k && blk_v && out && ws && (n_ctx == 0 || (ctx_k && ctx_v)), "dsm_gqa_attn: NULL pointer");
+  const GqaPlan p = gqa_plan(batch, block, n_heads, n_kv, n_ctx);
+  DSM_REQUIRE(int64_t(batch) * p.row_blocks <= 65535 && n_kv <= 65535, "dsm_gqa_attn: batch or n_kv too large");
+  const size_t need = gqa_ws_bytes(batch, block, n_heads, head_dim, p);
+  if (ws_bytes < need) return fail(DSM_ERR_WORKSPACE, "dsm_gqa_attn: workspace too small");
+  const int64_t rows = int64_t(batch) * n_heads * block;
+  float* part = static_cast<float*>(ws);
+  float* ml = part + rows * p.n_splits * int64_t(head_dim);
+  cudaStream_t s = as_stream(stream);
+  const int64_t sb = n_ctx ? ctx_batch_stride : 0, sh = n_ctx ? ctx_head_stride : 0;
+  int st;
+  if (dtype == DSM_DT_BF16)
+    st = launch_gqa_hd<__nv_bfloat16>(head_dim, q, ctx_k, ctx_v, sb, sh, n_ctx, blk_k, blk_v, batch, block, n_heads,
+                                      n_kv, scale, p, part, ml, s);
+  else
+    st = launch_gqa_hd<float>(head_dim, q, ctx_k, ctx_v, sb, sh, n_ctx, blk_k, blk_v, batch, block, n_heads, n_kv,
+                              scale, p, part, ml, s);
+  if (st != DSM_OK) return st;
+  const int64_t grid = ceil_div(rows, kGqaWarps);
+  DSM_REQUIRE(grid <= 0x7fffffff, "dsm_gqa_attn: too many rows");
+  if (dtype == DSM_DT_BF16)
+    gqa_combine_kernel<__nv_bfloat16><<<unsigned(grid), kGqaThreads, 0, s>>>(
+        part, ml, rows, p.n_splits, head_dim, n_heads, block, static_cast<__nv_bfloat16*>(out));
+  else
+    gqa_combine_kernel<float><<<unsigned(grid), kGqaThreads, 0, s>>>(part, ml, rows, p.n_splits, head_dim, n_heads,
+                                                                     block, static_cast<float*>(out));
+  return check_launch("gqa_combine");
+}

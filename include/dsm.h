@@ -38,6 +38,8 @@
  *   dsm_rows_norm_rope, dsm_q_head_norm_rope, dsm_kv_window_write, dsm_sparse_attn, dsm_round_rows:
  *                       DSparkAttention.__call__ / advance_window around dsm_linear
  *                       (model/attention.py:27-142, kernels.py:20-57, norm_rope.py:22-77)
+ *   dsm_qkv_norm_rope, dsm_gqa_attn: Qwen3DSparkAttention.__call__ / context_kv /
+ *                       attend_cached around dsm_linear (arch/qwen3.py:65-143)
  *   dsm_gather_rows, dsm_segment_ids: expert-parallel plumbing; the reference runs on one
  *                       device (tests/reference_model.py:55-56 forces world_size 1) and has
  *                       no counterpart.
@@ -282,6 +284,31 @@ int dsm_sparse_attn(const void* q, const void* window_kv, const void* block_kv, 
                     const float* cos_t, const float* sin_t, int pos0, int n_groups, void* out, float* scratch,
                     void* stream);
 int dsm_round_rows(const float* in, const float* in_lo, int64_t n, void* out, int out_dtype, void* stream);
+
+/* ---- the Qwen3 draft attention (grouped-query) ------------------------------------------------
+ * Qwen3DSparkAttention (arch/qwen3.py:85-143) around dsm_linear. cos_t / sin_t are the
+ * caller's [tab_rows, head_dim] fp32 tables (rope_tables, qwen3.py:77-82).
+ * qkv_norm_rope: in [n_rows, (n_q + 2 n_kv) * head_dim] fp32 (+ in_lo) holds q, k, v heads in
+ *   that order. Row r is token t = r % period of sequence b = r / period. Every head is
+ *   rounded to T; q and k heads get RMSNorm with q_norm_w / k_norm_w (head_dim fp32) and NeoX
+ *   RoPE with table row tab0 + t (x * T(cos) + rotate_half(x) * T(sin), each op rounded to T).
+ *   q heads -> q_out [n_rows, n_q, head_dim] (n_q may be 0); k and v heads -> k_out / v_out
+ *   [n_rows / period, n_kv, kv_cap, head_dim] at row row0 + t. head_dim even, <= 256.
+ * gqa_attn: out [batch, block, n_heads, head_dim] (T) = softmax(q k^T * scale) v per head h
+ *   over KV head h / (n_heads / n_kv): the n_ctx context rows ctx_k / ctx_v (element offset
+ *   b * ctx_batch_stride + g * ctx_head_stride + row * head_dim) and then the block's rows
+ *   blk_k / blk_v [batch, n_kv, block, head_dim]; q is [batch, block, n_heads, head_dim].
+ *   head_dim 32, 64, 128 or 256. workspace: dsm_gqa_attn_workspace_bytes (fp32 partials of
+ *   the key ranges). */
+int dsm_qkv_norm_rope(const float* in, const float* in_lo, int64_t n_rows, int n_q, int n_kv, int head_dim,
+                      const float* q_norm_w, const float* k_norm_w, float eps, const float* cos_t, const float* sin_t,
+                      int tab_rows, int tab0, int period, void* q_out, void* k_out, void* v_out, int kv_cap, int row0,
+                      int dtype, void* stream);
+size_t dsm_gqa_attn_workspace_bytes(int batch, int block, int n_heads, int n_kv, int head_dim, int n_ctx);
+int dsm_gqa_attn(const void* q, const void* ctx_k, const void* ctx_v, int64_t ctx_batch_stride,
+                 int64_t ctx_head_stride, int n_ctx, const void* blk_k, const void* blk_v, int dtype, int batch,
+                 int block, int n_heads, int n_kv, int head_dim, float scale, void* out, void* workspace,
+                 size_t workspace_bytes, void* stream);
 
 /* Kernel regime of the grouped expert products: 0 (default) picks by rows per busy
  * expert -- the mma.sync weight-streaming kernel at decode sizes, the tcgen05/TMEM kernel

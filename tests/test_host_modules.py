@@ -29,3 +29,31 @@ def test_gpu_modules_reject_cpu_tensors():
         from dsm.config import DSparkArgs
 
         MoE(DSparkArgs.from_dict(ARGS), 0)(torch.zeros(2, 256))
+
+
+QWEN3_ARGS = dict(hidden_size=96, num_attention_heads=4, num_key_value_heads=2, head_dim=32, rms_norm_eps=1e-6)
+
+
+def test_qwen3_attention_rejects_cpu_tensors_and_bad_arguments():
+    from dsm.qwen3_attention import Qwen3DSparkAttention
+
+    a = Qwen3DSparkAttention(QWEN3_ARGS)
+    cos, sin = torch.zeros(9, 32), torch.zeros(9, 32)
+    with pytest.raises(ValueError, match="GPU"):
+        a(torch.zeros(1, 4, 96), torch.zeros(1, 5, 96), cos, sin)
+    with pytest.raises(ValueError, match="GPU"):
+        a.context_kv(torch.zeros(1, 5, 96), cos[:5], sin[:5])
+    with pytest.raises(ValueError, match="GPU"):
+        a.attend_cached(torch.zeros(1, 4, 96), None, None, cos[:4], sin[:4])
+    with pytest.raises(ValueError, match="multiple"):
+        Qwen3DSparkAttention(dict(QWEN3_ARGS, num_key_value_heads=3))
+
+
+def test_qwen3_rope_tables_match_the_oracle():
+    import oracle
+    from dsm.qwen3_attention import rope_tables
+
+    for pos in (torch.arange(13), torch.arange(2048, 2055)):
+        mine = rope_tables(pos, 128, 1000000.0)
+        ref = oracle.qwen3_rope_tables(pos, 128, 1000000.0)
+        assert torch.equal(mine[0], ref[0]) and torch.equal(mine[1], ref[1])

@@ -103,6 +103,39 @@ def test_attention_entry_points_reject_bad_arguments_on_the_host():
     assert L.dsm_sparse_attn_scratch_bytes(8, 7, 64, 128) == 8 * 7 * 64 * 135 * 4
 
 
+def test_gqa_attention_entry_points_reject_bad_arguments_on_the_host():
+    L = _lib.lib()
+    bf = _lib.DT_BF16
+    cases = [
+        # odd head_dim
+        lambda: L.dsm_qkv_norm_rope(1, None, 14, 4, 2, 63, 1, 1, 1e-6, 1, 1, 100, 0, 7, 1, 1, 1, 7, 0, bf, None),
+        # rows that are not whole sequences of period rows
+        lambda: L.dsm_qkv_norm_rope(1, None, 13, 4, 2, 64, 1, 1, 1e-6, 1, 1, 100, 0, 7, 1, 1, 1, 7, 0, bf, None),
+        # RoPE table rows out of range
+        lambda: L.dsm_qkv_norm_rope(1, None, 14, 4, 2, 64, 1, 1, 1e-6, 1, 1, 10, 5, 7, 1, 1, 1, 7, 0, bf, None),
+        # cache rows out of range
+        lambda: L.dsm_qkv_norm_rope(1, None, 14, 4, 2, 64, 1, 1, 1e-6, 1, 1, 100, 0, 7, 1, 1, 1, 7, 1, bf, None),
+        # query heads without a q output
+        lambda: L.dsm_qkv_norm_rope(1, None, 14, 4, 2, 64, 1, 1, 1e-6, 1, 1, 100, 0, 7, None, 1, 1, 7, 0, bf, None),
+        # n_heads not a multiple of n_kv
+        lambda: L.dsm_gqa_attn(1, 1, 1, 0, 0, 16, 1, 1, bf, 1, 7, 6, 4, 64, 0.1, 1, 1, 1 << 30, None),
+        # unsupported head_dim
+        lambda: L.dsm_gqa_attn(1, 1, 1, 0, 0, 16, 1, 1, bf, 1, 7, 8, 4, 96, 0.1, 1, 1, 1 << 30, None),
+        # context rows without context pointers
+        lambda: L.dsm_gqa_attn(1, None, None, 0, 0, 16, 1, 1, bf, 1, 7, 8, 4, 64, 0.1, 1, 1, 1 << 30, None),
+        # workspace too small
+        lambda: L.dsm_gqa_attn(1, 1, 1, 0, 0, 16, 1, 1, bf, 1, 7, 8, 4, 64, 0.1, 1, 1, 16, None),
+    ]
+    for i, call in enumerate(cases):
+        assert call() != 0, i
+        assert L.dsm_last_error_message().decode()
+    # 32 query heads over 8 KV heads, a block of 7 after 2048 context rows: 33 key ranges of
+    # one 64-key tile each (two CTAs per SM on 148 SMs), fp32 partials of 128 + 2 per row
+    assert L.dsm_gqa_attn_workspace_bytes(1, 7, 32, 8, 128, 2048) == 32 * 7 * 33 * 130 * 4
+    assert L.dsm_gqa_attn_workspace_bytes(1, 7, 32, 8, 128, 0) == 32 * 7 * 1 * 130 * 4
+    assert L.dsm_gqa_attn_workspace_bytes(1, 7, 6, 4, 128, 0) == 0
+
+
 def test_draft_head_host_checks():
     L = _lib.lib()
     d = _lib.HeadDesc(batch=8, block=7, hc_mult=4, dim=4096, vocab=129280, rank=256)
