@@ -902,6 +902,195 @@ def run_reference_head(args):
     print(json.dumps(line))
 
 
+GQA_METRIC = ("Qwen3 draft-layer attention tokens/s (attend_cached over 2048 cached context rows, 8-bit affine "
+              "projections); HBM GB/s")
+# staging, q/k/v products, head norms + RoPE, attention, range combine, staging, o_proj, cast
+GQA_KERNELS_PER_STEP = 10
+
+
+def _gqa_cpu_setup(t, wl):
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    from dsm.qwen3_attention import rope_tables
+
+    a, ctx, s = wl.args, wl.extra["ctx"], wl.block
+    w = {k: t[k].cpu() for k in ("q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm")}
+    cos, sin = rope_tables(torch.arange(ctx, ctx + s), a["head_dim"], a["rope_theta"])
+    return w, t["x"][:1].cpu(), t["ctx_k"][:1].cpu(), t["ctx_v"][:1].cpu(), cos, sin
+
+
+def _gqa_cpu_timed(wl, setup, budget_s, max_calls=50):
+    """The oracle's attend_cached on one sequence per call, all host threads."""
+    import oracle
+
+    a = wl.args
+    w, x, ck, cv, cos, sin = setup
+    call = lambda: oracle.qwen3_attend_cached(w, a["num_attention_heads"], a["num_key_value_heads"],  # noqa: E731
+                                              a["head_dim"], a["rms_norm_eps"], x, ck, cv, cos, sin)
+    n, t0 = 0, time.perf_counter()
+    while n < max_calls and (n == 0 or time.perf_counter() - t0 < budget_s):
+        call()
+        n += 1
+    el = time.perf_counter() - t0
+    return n * wl.block / el, n, el
+
+
+def run_gqa(args):
+    """One step = ``attend_cached`` of 16 sequences' 7-token blocks over 2048 cached context rows
+    each (Qwen3-4B widths). The cached K/V (134 MB) and the projections (~28 MB) exceed L2, so
+    every step streams them from HBM."""
+    import torch
+
+    from dsm import _lib, workloads as W
+    from dsm.qwen3_attention import rope_tables
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    wl = W.WORKLOADS["qwen3_attn_q8"]
+    a = wl.args
+    t = W.make_gqa_tensors(wl, device=dev, seed=rank)
+    attn = W.build_gqa(wl, t, dev)
+    b, s, ctx = wl.batch, wl.block, wl.extra["ctx"]
+    nh, nkv, hd, h = a["num_attention_heads"], a["num_key_value_heads"], a["head_dim"], a["hidden_size"]
+    cos, sin = rope_tables(torch.arange(ctx, ctx + s), hd, a["rope_theta"])
+    cos, sin = cos.to(dev), sin.to(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(555 + rank)
+    xs = [t["x"]] + [torch.randn(t["x"].shape, generator=gen, device=dev).to(torch.bfloat16) for _ in range(3)]
+    kc, vc = t["ctx_k"], t["ctx_v"]
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        attn.attend_cached(xs[i % 4], kc, vc, cos, sin)
+    torch.cuda.synchronize()
+
+    def timed(fn):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            fn(i)
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+        return sum(x.elapsed_time(y) for x, y in evs) / args.steps
+
+    _barrier(ws)
+    with ClockSampler(local) as clk:
+        ms = timed(lambda i: attn.attend_cached(xs[i % 4], kc, vc, cos, sin))
+    ms = _max_over_ranks(ms, ws, dev)
+    kv_bytes = 2 * b * nkv * ctx * hd * 2
+    w_bytes = sum(getattr(attn, n).packed().nbytes for n in ("q_proj", "k_proj", "v_proj", "o_proj"))
+    act_bytes = b * s * h * 2 * 2  # the block in, the output out
+    step_bytes = w_bytes + kv_bytes + act_bytes
+    hbm_peak, _, peak_kind = _peaks()
+
+    roofline = None
+    if not args.no_kernel_timing and ws == 1:  # dsm_gqa_attn alone (attention + range combine)
+        bk = torch.empty(b, nkv, s, hd, dtype=torch.bfloat16, device=dev)
+        bv = torch.empty_like(bk)
+        q = attn._heads(xs[0], torch.bfloat16, True, cos, sin, 0, bk, bv, s, 0)
+        L = _lib.lib()
+        wsb = L.dsm_gqa_attn_workspace_bytes(b, s, nh, nkv, hd, ctx)
+        wsbuf = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        out = torch.empty(b, s, nh * hd, dtype=torch.bfloat16, device=dev)
+        sp = stream.cuda_stream
+        k_ms = timed(lambda i: _lib.check(L.dsm_gqa_attn(
+            q.data_ptr(), kc.data_ptr(), vc.data_ptr(), kc.stride(0), kc.stride(1), ctx, bk.data_ptr(), bv.data_ptr(),
+            _lib.DT_BF16, b, s, nh, nkv, hd, float(attn.scale), out.data_ptr(), wsbuf.data_ptr(), wsb, sp),
+            "dsm_gqa_attn"))
+        k_bytes = kv_bytes + 2 * b * nkv * s * hd * 2 + 2 * b * s * nh * hd * 2
+        achieved = k_bytes / (k_ms * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "gqa_attn_kernel<bf16, 128> + gqa_combine_kernel",
+                    "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                    "peak_kind": peak_kind, "frac_of_8tbs": achieved / SPEC_HBM_GBS,
+                    "algorithmic_bytes_per_launch": k_bytes, "launch_ms": k_ms, "traffic": None}
+
+    e2e_ms = None
+    if not args.no_e2e:
+        xh = [x.cpu().pin_memory() for x in xs]
+        yh = torch.empty(b, s, h, dtype=torch.bfloat16).pin_memory()
+
+        def e2e(i):
+            y = attn.attend_cached(xh[i % 4].to(dev, non_blocking=True), kc, vc, cos, sin)
+            yh.copy_(y, non_blocking=True)
+
+        for i in range(3):
+            e2e(i)
+        torch.cuda.synchronize()
+        e2e_ms = _max_over_ranks(timed(e2e), ws, dev)
+
+    if rank == 0:
+        cpu = None
+        if ws == 1 and not args.no_cpu_baseline:
+            v, calls, el = _gqa_cpu_timed(wl, _gqa_cpu_setup(t, wl), args.cpu_seconds)
+            cpu = {"value": v, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+                   "sample": f"1 of the {b} sequences ({s} block tokens over {ctx} context rows) per call, {calls} "
+                             f"calls in {el:.1f} s; CPU restatement of Qwen3DSparkAttention.attend_cached in "
+                             f"PyTorch with the bf16 weights before quantisation"}
+        line = {
+            "metric": GQA_METRIC, "value": ws * b * s / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 affine weights x bf16 activations (f16 MMA, fp32 accumulate); fp32 attention",
+            "data": "synthetic",
+            "config": {"workload": wl.name, "tokens_per_step_per_gpu": b * s, "batch": b, "draft_block": s,
+                       "context_rows": ctx, "hidden": h, "heads": nh, "kv_heads": nkv, "head_dim": hd,
+                       "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                       "l2": "inputs larger than L2 (134 MB of cached K/V + 28 MB of weights streamed every step)"},
+            "hbm_gbs_step": step_bytes / (ms * 1e-3) / 1e9,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": None if e2e_ms is None else {
+                "value": ws * b * s / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": xs[0].numel() * 2, "d2h_bytes_per_step": b * s * h * 2,
+                "ms_per_step": e2e_ms},
+            "gpu_launches": GQA_KERNELS_PER_STEP * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line))
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def run_reference_gqa(args):
+    ws, rank, _ = _dist()
+    if rank != 0:
+        return
+    from dsm import workloads as W
+
+    wl = W.WORKLOADS["qwen3_attn_q8"]
+    t = W.make_gqa_tensors(wl, device="cpu")
+    setup = _gqa_cpu_setup(t, wl)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, _, _ = _gqa_cpu_timed(wl, setup, 0.0, max_calls=1)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": GQA_METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wl.n_tokens / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (bf16 weights)",
+        "data": "synthetic",
+        "config": {"workload": wl.name, "tokens_per_step": wl.n_tokens, "batch": wl.batch, "draft_block": wl.block,
+                   "context_rows": wl.extra["ctx"]},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+                         "sample": f"one sequence ({wl.block} block tokens over {wl.extra['ctx']} context rows) per "
+                                   f"step; CPU restatement of Qwen3DSparkAttention.attend_cached in PyTorch (mlx is "
+                                   f"not installable here)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -920,6 +1109,8 @@ def main():
     qwen3 = args.workload.startswith("qwen3")
     if args.workload == "draft_head":
         (run_reference_head if args.impl == "reference" else run_head)(args)
+    elif args.workload == "qwen3_attn_q8":
+        (run_reference_gqa if args.impl == "reference" else run_gqa)(args)
     elif args.impl == "reference":
         (run_reference_qwen3 if qwen3 else run_reference)(args)
     else:

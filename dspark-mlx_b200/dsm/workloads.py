@@ -83,6 +83,13 @@ WORKLOADS = {
         "draft_head", dict(vocab_size=129280, dim=4096, hc_mult=4, dspark_markov_rank=256, dspark_block_size=7,
                            temperature=0.0),
         n_tokens=56, wfmt="bf16", batch=8, block=7),
+    # the Qwen3-4B draft layer's attention (32 query / 8 KV heads of 128) on its cached path:
+    # 16 sequences x a 7-token block over 2048 cached context rows, 8-bit affine projections
+    # as quantize_drafter leaves them
+    "qwen3_attn_q8": Workload(
+        "qwen3_attn_q8", dict(hidden_size=2560, num_attention_heads=32, num_key_value_heads=8, head_dim=128,
+                              rms_norm_eps=1e-6, rope_theta=1000000.0),
+        n_tokens=112, wfmt="affine8", batch=16, block=7, extra={"ctx": 2048}),
 }
 
 
@@ -283,3 +290,36 @@ def build_head(wl: Workload, t: Dict[str, torch.Tensor], device="cuda"):
     h.markov_head.markov_w2.weight = torch.nn.Parameter(t["w2"].to(device), requires_grad=False)
     h.head.weight = torch.nn.Parameter(t["head_w"].to(device), requires_grad=False)
     return h
+
+
+def make_gqa_tensors(wl: Workload, device="cpu", seed: Optional[int] = None) -> Dict[str, torch.Tensor]:
+    """Inputs, cached context K/V (N(0, 1)) and bf16 weights of the Qwen3 attention workload."""
+    a = wl.args
+    g = torch.Generator(device=device)
+    g.manual_seed(wl.seed if seed is None else seed)
+    h, nh, nkv, hd = a["hidden_size"], a["num_attention_heads"], a["num_key_value_heads"], a["head_dim"]
+    b, s, ctx = wl.batch, wl.block, wl.extra["ctx"]
+    r = lambda *shape, std=1.0: torch.randn(shape, generator=g, device=device) * std  # noqa: E731
+    return {"q_proj": r(nh * hd, h, std=h ** -0.5).to(torch.bfloat16),
+            "k_proj": r(nkv * hd, h, std=h ** -0.5).to(torch.bfloat16),
+            "v_proj": r(nkv * hd, h, std=h ** -0.5).to(torch.bfloat16),
+            "o_proj": r(h, nh * hd, std=(nh * hd) ** -0.5).to(torch.bfloat16),
+            "q_norm": 1 + r(hd, std=0.1), "k_norm": 1 + r(hd, std=0.1),
+            "x": r(b, s, h).to(torch.bfloat16),
+            "ctx_k": r(b, nkv, ctx, hd).to(torch.bfloat16), "ctx_v": r(b, nkv, ctx, hd).to(torch.bfloat16)}
+
+
+def build_gqa(wl: Workload, t: Dict[str, torch.Tensor], device="cuda", bits: int = 8, group_size: int = 64):
+    """A :class:`dsm.qwen3_attention.Qwen3DSparkAttention` holding ``t``'s weights, quantised
+    like ``quantize_drafter`` when the workload is affine."""
+    from .qwen3_attention import Qwen3DSparkAttention
+
+    attn = Qwen3DSparkAttention(wl.args).to(device)
+    for n in ("q_proj", "k_proj", "v_proj", "o_proj"):
+        getattr(attn, n).weight = torch.nn.Parameter(t[n].to(device), requires_grad=False)
+        if wl.wfmt == "affine8":
+            getattr(attn, n).quantize(bits=bits, group_size=group_size)
+    with torch.no_grad():
+        attn.q_norm.weight.copy_(t["q_norm"])
+        attn.k_norm.weight.copy_(t["k_norm"])
+    return attn
