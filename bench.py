@@ -1091,6 +1091,200 @@ def run_reference_gqa(args):
     print(json.dumps(line))
 
 
+DSATTN_METRIC = ("DeepSeek-V4 draft attention tokens/s (MLA decode of 7-token blocks over a full 128-slot window, "
+                 "bf16); HBM GB/s")
+# staging + product per projection (wq_a, wkv x2, wq_b, 8 wo_a groups, wo_b), 4 norm/RoPE
+# kernels (main kv, q latents, q heads, block kv), window write, sparse attention, 2 casts
+DSATTN_KERNELS_PER_STEP = 2 * 13 + 4 + 1 + 1 + 2
+
+
+def _dsattn_cpu_setup(t, wl):
+    import torch
+
+    import oracle
+    from oracle.attention_oracle import AttnDims
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    a = wl.args
+    p = {k: t[k].cpu() for k in ("wq_a", "wq_b", "wkv", "wo_a", "wo_b", "q_norm", "kv_norm", "attn_sink")}
+    dims = AttnDims(n_heads=a["n_heads"], head_dim=a["head_dim"], rope_head_dim=a["rope_head_dim"],
+                    o_groups=a["o_groups"], o_lora_rank=a["o_lora_rank"], window_size=a["window_size"],
+                    eps=a["norm_eps"])
+    cos, sin = oracle.rope_tables(a["rope_head_dim"], wl.extra["max_seq_len"], a["rope_theta"])
+    cache = oracle.KVWindow(a["window_size"])
+    x, main = t["x"][:1].cpu(), t["main"][:1].cpu()
+    oracle.attention_forward(p, dims, x, 0, t["prefill_main"][:1].cpu(), cache, cos, sin)
+    return p, dims, x, main, cache, cos, sin
+
+
+def _dsattn_cpu_timed(wl, setup, budget_s, max_calls=50):
+    """The oracle's DSparkAttention decode step on one sequence per call, all host threads."""
+    import oracle
+
+    p, dims, x, main, cache, cos, sin = setup
+    pos = wl.extra["prefill"]
+    n, t0 = 0, time.perf_counter()
+    while n < max_calls and (n == 0 or time.perf_counter() - t0 < budget_s):
+        oracle.attention_forward(p, dims, x, pos, main, cache, cos, sin)
+        n += 1
+    el = time.perf_counter() - t0
+    return n * wl.block / el, n, el
+
+
+def run_dsattn(args):
+    """One step = one decode call of the DeepSeek draft attention: 8 sequences x 7-token
+    blocks, each over its full 128-slot KV window. The projections (214 MB of bf16 weights)
+    exceed L2, so every step streams them from HBM."""
+    import torch
+
+    from dsm import _lib, workloads as W
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    wl = W.WORKLOADS["draft_attn_dsv4"]
+    a = wl.args
+    t = W.make_dsattn_tensors(wl, device=dev, seed=rank)
+    attn = W.build_dsattn(wl, t, dev)
+    b, s, pos = wl.batch, wl.block, wl.extra["prefill"]
+    d, h, hd = a["dim"], a["n_heads"], a["head_dim"]
+    attn(t["x"], 0, t["prefill_main"])  # seeds the window with the last 128 prefill positions
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(333 + rank)
+    xs = [t["x"]] + [torch.randn(t["x"].shape, generator=gen, device=dev).to(torch.bfloat16) for _ in range(3)]
+    mains = [t["main"]] + [torch.randn(t["main"].shape, generator=gen, device=dev).to(torch.bfloat16)
+                           for _ in range(3)]
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        attn(xs[i % 4], pos, mains[i % 4])
+    torch.cuda.synchronize()
+
+    def timed(fn):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            fn(i)
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+        return sum(x.elapsed_time(y) for x, y in evs) / args.steps
+
+    _barrier(ws)
+    with ClockSampler(local) as clk:
+        ms = timed(lambda i: attn(xs[i % 4], pos, mains[i % 4]))
+    ms = _max_over_ranks(ms, ws, dev)
+    w_bytes = sum(pm.nbytes for _, pm in attn._packed.values())
+    win_bytes = b * a["window_size"] * hd * 2
+    step_bytes = w_bytes + win_bytes + b * (2 * s + 1) * d * 2
+    hbm_peak, _, peak_kind = _peaks()
+
+    roofline = None
+    if not args.no_kernel_timing and ws == 1:  # the largest projection alone: wq_b over the q latents
+        L = _lib.lib()
+        n = b * s
+        pm = attn._pm("wq_b", attn.wq_b.weight)
+        k = a["q_lora_rank"]
+        cap = L.dsm_stage_rows_cap(n)
+        xl = torch.randn(n, k, device=dev).to(torch.bfloat16)
+        xsb = torch.empty(L.dsm_stage_bytes(cap, k), dtype=torch.uint8, device=dev)
+        xsc = torch.empty(cap, dtype=torch.float32, device=dev)
+        out = torch.empty(n, pm.rows, dtype=torch.float32, device=dev)
+        sp = stream.cuda_stream
+        _lib.check(L.dsm_stage_rows(xl.data_ptr(), _lib.DT_BF16, n, k, None, n, 1, xsb.data_ptr(), cap,
+                                    xsc.data_ptr(), sp))
+        k_ms = timed(lambda i: _lib.check(L.dsm_linear(xsb.data_ptr(), xsc.data_ptr(), cap, k, pm.wfmt, pm.group_size,
+                                                       pm.packed.data_ptr(), pm.rows, out.data_ptr(), pm.rows, n, sp)))
+        k_bytes = pm.nbytes + n * k * 2 + n * pm.rows * 4
+        achieved = k_bytes / (k_ms * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "expert_kernel<f16, down> (wq_b, weight streaming)",
+                    "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                    "peak_kind": peak_kind, "frac_of_8tbs": achieved / SPEC_HBM_GBS,
+                    "algorithmic_bytes_per_launch": k_bytes, "launch_ms": k_ms, "traffic": None}
+
+    e2e_ms = None
+    if not args.no_e2e:
+        xh = [x.cpu().pin_memory() for x in xs]
+        mh = [m.cpu().pin_memory() for m in mains]
+        yh = torch.empty(b, s, d, dtype=torch.bfloat16).pin_memory()
+
+        def e2e(i):
+            y = attn(xh[i % 4].to(dev, non_blocking=True), pos, mh[i % 4].to(dev, non_blocking=True))
+            yh.copy_(y, non_blocking=True)
+
+        for i in range(3):
+            e2e(i)
+        torch.cuda.synchronize()
+        e2e_ms = _max_over_ranks(timed(e2e), ws, dev)
+
+    if rank == 0:
+        cpu = None
+        if ws == 1 and not args.no_cpu_baseline:
+            v, calls, el = _dsattn_cpu_timed(wl, _dsattn_cpu_setup(t, wl), args.cpu_seconds)
+            cpu = {"value": v, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+                   "sample": f"1 of the {b} sequences ({s} block tokens over a full window) per call, {calls} calls "
+                             f"in {el:.1f} s; CPU restatement of DSparkAttention.__call__ in PyTorch"}
+        line = {
+            "metric": DSATTN_METRIC, "value": ws * b * s / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 weights x bf16 activations (f16 MMA, fp32 accumulate); fp32 attention",
+            "data": "synthetic",
+            "config": {"workload": wl.name, "tokens_per_step_per_gpu": b * s, "batch": b, "draft_block": s,
+                       "dim": d, "heads": h, "head_dim": hd, "window": a["window_size"],
+                       "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                       "l2": "inputs larger than L2 (214 MB of projection weights streamed every step)"},
+            "hbm_gbs_step": step_bytes / (ms * 1e-3) / 1e9,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": None if e2e_ms is None else {
+                "value": ws * b * s / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": (xs[0].numel() + mains[0].numel()) * 2, "d2h_bytes_per_step": b * s * d * 2,
+                "ms_per_step": e2e_ms},
+            "gpu_launches": DSATTN_KERNELS_PER_STEP * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line))
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def run_reference_dsattn(args):
+    ws, rank, _ = _dist()
+    if rank != 0:
+        return
+    from dsm import workloads as W
+
+    wl = W.WORKLOADS["draft_attn_dsv4"]
+    t = W.make_dsattn_tensors(wl, device="cpu")
+    setup = _dsattn_cpu_setup(t, wl)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, _, _ = _dsattn_cpu_timed(wl, setup, 0.0, max_calls=1)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": DSATTN_METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wl.n_tokens / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (bf16 weights)",
+        "data": "synthetic",
+        "config": {"workload": wl.name, "tokens_per_step": wl.n_tokens, "batch": wl.batch, "draft_block": wl.block,
+                   "window": wl.args["window_size"]},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+                         "sample": f"one sequence ({wl.block} block tokens over a full window) per step; CPU "
+                                   f"restatement of DSparkAttention.__call__ in PyTorch (mlx is not installable here)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1111,6 +1305,8 @@ def main():
         (run_reference_head if args.impl == "reference" else run_head)(args)
     elif args.workload == "qwen3_attn_q8":
         (run_reference_gqa if args.impl == "reference" else run_gqa)(args)
+    elif args.workload == "draft_attn_dsv4":
+        (run_reference_dsattn if args.impl == "reference" else run_dsattn)(args)
     elif args.impl == "reference":
         (run_reference_qwen3 if qwen3 else run_reference)(args)
     else:

@@ -90,6 +90,13 @@ WORKLOADS = {
         "qwen3_attn_q8", dict(hidden_size=2560, num_attention_heads=32, num_key_value_heads=8, head_dim=128,
                               rms_norm_eps=1e-6, rope_theta=1000000.0),
         n_tokens=112, wfmt="affine8", batch=16, block=7, extra={"ctx": 2048}),
+    # the DeepSeek-V4 draft attention (compress_ratio 0 MLA: 64 heads of 512, q rank 1024,
+    # 8 output groups of rank 1024, a 128-slot window) decoding 7-token blocks for 8
+    # sequences after a 160-token prefill: the window is full
+    "draft_attn_dsv4": Workload(
+        "draft_attn_dsv4", dict(dim=4096, n_heads=64, head_dim=512, rope_head_dim=64, q_lora_rank=1024, o_groups=8,
+                                o_lora_rank=1024, window_size=128, norm_eps=1e-6, rope_theta=10000.0),
+        n_tokens=56, wfmt="bf16", batch=8, block=7, extra={"prefill": 160, "max_seq_len": 4096}),
 }
 
 
@@ -322,4 +329,34 @@ def build_gqa(wl: Workload, t: Dict[str, torch.Tensor], device="cuda", bits: int
     with torch.no_grad():
         attn.q_norm.weight.copy_(t["q_norm"])
         attn.k_norm.weight.copy_(t["k_norm"])
+    return attn
+
+
+def make_dsattn_tensors(wl: Workload, device="cpu", seed: Optional[int] = None) -> Dict[str, torch.Tensor]:
+    """Inputs and bf16 weights of the DeepSeek draft attention workload (seeded normal values)."""
+    a = wl.args
+    g = torch.Generator(device=device)
+    g.manual_seed(wl.seed if seed is None else seed)
+    d, h, hd, ql, og, orank = (a[k] for k in ("dim", "n_heads", "head_dim", "q_lora_rank", "o_groups", "o_lora_rank"))
+    b, s, pre = wl.batch, wl.block, wl.extra["prefill"]
+    r = lambda *shape, std=1.0: torch.randn(shape, generator=g, device=device) * std  # noqa: E731
+    bf = torch.bfloat16
+    return {"wq_a": r(ql, d, std=d ** -0.5).to(bf), "wq_b": r(h * hd, ql, std=ql ** -0.5).to(bf),
+            "wkv": r(hd, d, std=d ** -0.5).to(bf), "wo_a": r(og * orank, h * hd // og, std=(h * hd // og) ** -0.5).to(bf),
+            "wo_b": r(d, og * orank, std=(og * orank) ** -0.5).to(bf),
+            "q_norm": 1 + r(ql, std=0.1), "kv_norm": 1 + r(hd, std=0.1), "attn_sink": r(h),
+            "prefill_main": r(b, pre, d).to(bf), "x": r(b, s, d).to(bf), "main": r(b, 1, d).to(bf)}
+
+
+def build_dsattn(wl: Workload, t: Dict[str, torch.Tensor], device="cuda"):
+    """A :class:`dsm.attention.DSparkAttention` holding ``t``'s weights."""
+    from .attention import DSparkAttention
+
+    attn = DSparkAttention(wl.args, max_seq_len=wl.extra["max_seq_len"]).to(device)
+    for n in ("wq_a", "wq_b", "wkv", "wo_a", "wo_b"):
+        getattr(attn, n).weight = torch.nn.Parameter(t[n].to(device), requires_grad=False)
+    with torch.no_grad():
+        attn.q_norm.weight.copy_(t["q_norm"])
+        attn.kv_norm.weight.copy_(t["kv_norm"])
+        attn.attn_sink.copy_(t["attn_sink"])
     return attn
