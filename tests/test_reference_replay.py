@@ -47,3 +47,47 @@ def test_reference_dequant_unit_tests(reference):
     mod = _load_test_module(os.path.join(REF, "tests", "test_loading.py"))
     mod.test_dequant_fp8_blockwise()
     mod.test_dequant_fp4_groupwise()
+
+
+def test_qwen3_attention_oracle_matches_reference_torch_model(reference):
+    """The reference pins its Qwen3 backbone to a torch transcription of DeepSpec's model
+    (``tests/qwen3_ref.py``, ``tests/test_qwen3_arch.py:30-66``): the rope tables against a
+    numpy formula within 1e-5, the layer within 2e-3. The oracle's attention is held to the
+    same torch model's ``RefAttn`` in fp32, on the reference test's shapes and weight scale."""
+    import numpy as np
+    import torch
+
+    import oracle
+
+    import sys
+
+    # transformers probes for an installed mlx; the stand-in must not be visible to it
+    shim_mods = {k: sys.modules.pop(k) for k in list(sys.modules) if k == "mlx" or k.startswith("mlx.")}
+    try:
+        ref = _load_test_module(os.path.join(REF, "tests", "qwen3_ref.py"))
+    finally:
+        sys.modules.update(shim_mods)
+    h, nh, nkv, hd, eps, theta = 32, 4, 2, 16, 1e-6, 1_000_000.0
+    rng = np.random.default_rng(0)
+    attn = ref.RefAttn(h, nh, nkv, hd, eps)
+    weights = {k: torch.tensor((rng.standard_normal(tuple(v.shape)) * 0.05).astype(np.float32))
+               for k, v in attn.state_dict().items()}
+    weights["q_norm.weight"] = weights["q_norm.weight"] + 1
+    weights["k_norm.weight"] = weights["k_norm.weight"] + 1
+    attn.load_state_dict(weights)
+    b, ctx, block = 2, 5, 3
+    noise = torch.tensor((rng.standard_normal((b, block, h)) * 0.3).astype(np.float32))
+    target = torch.tensor((rng.standard_normal((b, ctx, h)) * 0.3).astype(np.float32))
+    positions = np.arange(ctx + block)
+    inv = 1.0 / (theta ** (np.arange(0, hd, 2) / hd))
+    emb = np.concatenate([positions[:, None] * inv[None, :]] * 2, axis=-1)
+    cos_np, sin_np = np.cos(emb).astype(np.float32), np.sin(emb).astype(np.float32)
+    cos, sin = oracle.qwen3_rope_tables(torch.from_numpy(positions), hd, theta)
+    assert np.max(np.abs(cos.numpy() - cos_np)) < 1e-5 and np.max(np.abs(sin.numpy() - sin_np)) < 1e-5
+    p = {"q_proj": weights["q_proj.weight"], "k_proj": weights["k_proj.weight"], "v_proj": weights["v_proj.weight"],
+         "o_proj": weights["o_proj.weight"], "q_norm": weights["q_norm.weight"], "k_norm": weights["k_norm.weight"]}
+    with torch.no_grad():
+        want = attn(noise, target, torch.from_numpy(cos_np), torch.from_numpy(sin_np))
+    got = oracle.qwen3_attention(p, nh, nkv, hd, eps, noise, target, torch.from_numpy(cos_np),
+                                 torch.from_numpy(sin_np))
+    assert float((got - want).abs().max()) <= 1e-5 * float(want.abs().max())
