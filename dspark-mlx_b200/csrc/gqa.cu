@@ -17,8 +17,16 @@
 // The attention is split over keys. A CTA holds one KV head's query rows (the group's heads
 // x the block's tokens, up to 32) and one key range; it streams 64-key tiles of K and V
 // through shared memory with an online softmax and leaves fp32 partials (m, l, acc) per row
-// and range. A second kernel combines the ranges in order. Everything is fp32 inside; the
-// output is rounded once to the activation dtype.
+// and range. A second kernel combines the ranges in order. The output is rounded once to the
+// activation dtype. Two CTA kernels:
+//   gqa_attn_kernel  fp32 CUDA-core products, any dtype and head_dim 32..256;
+//   gqa_mma_kernel   bf16 with head_dim 64 or 128: K/V tiles double-buffered by cp.async,
+//                    q.k and p.v on mma.m16n8k16 (bf16 in, fp32 accumulate; p rounded to
+//                    bf16 for the second product), each warp an online softmax over half of
+//                    every tile, so each key range leaves two partials.
+// dsm_set_gqa_kernel picks between them (process-wide).
+#include <atomic>
+
 #include "common.cuh"
 
 namespace dsm {
@@ -29,7 +37,13 @@ constexpr int kGqaWarps = kGqaThreads / 32;
 constexpr int kKeyTile = 64;    // keys per shared-memory tile
 constexpr int kRowBlock = 32;   // query rows per CTA
 constexpr int kMaxSplits = 64;  // key ranges per KV head
+constexpr int kMaxParts = 2 * kMaxSplits;  // partials per query row (two per range on the mma path)
 constexpr int kMaxHeadDim = 256;
+constexpr int kMmaThreads = 128;  // 4 warps: 2 row tiles of 16 x 2 key halves of 32
+constexpr int kMmaStages = 2;
+
+// 0: the mma kernel wherever it applies, 1: the CUDA-core kernel everywhere
+std::atomic<int> g_gqa_kernel{1};
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -232,23 +246,241 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_attn_kernel(
   }
 }
 
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+// 16 bytes global -> shared; a key past the range reads nothing and fills zeros
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::); }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// c += a (16 x 16, row-major) * b (16 x 8, column-major); bf16 in, fp32 accumulate
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Grid and rows as gqa_attn_kernel; bf16 only. Warp w takes row tile w & 1 (rows 16 (w & 1)
+// ..) and key half w >> 1 (keys 32 (w >> 1) .. of every 64-key tile), keeps its own running
+// max / denominator / output, and leaves partial 2 * split + (w >> 1). Fragment layouts are
+// those of mma.m16n8k16: thread (g, t) = (lane / 4, lane % 4) holds rows g and g + 8,
+// columns 2t and 2t + 1 of each 8-wide accumulator tile. Shared rows are padded by 8
+// elements so the ldmatrix row addresses of one 8x8 matrix fall in distinct banks.
+template <int HD>
+__global__ void __launch_bounds__(kMmaThreads) gqa_mma_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ ctx_k,
+    const __nv_bfloat16* __restrict__ ctx_v, int64_t ctx_sb, int64_t ctx_sh, int n_ctx,
+    const __nv_bfloat16* __restrict__ blk_k, const __nv_bfloat16* __restrict__ blk_v, int block, int n_heads,
+    int n_kv, int row_blocks, int chunk, int n_parts, float scale, float* __restrict__ part,
+    float* __restrict__ ml) {
+  constexpr int RS = HD + 8;   // shared row stride (elements)
+  constexpr int CPR = HD / 8;  // 16-byte chunks per row
+  constexpr int KS = HD / 16;  // k-steps of q.k
+  constexpr int NT = HD / 8;   // 8-wide output tiles
+  static_assert(HD == 64 || HD == 128, "head_dim");
+  extern __shared__ __align__(16) unsigned char gqa_smem[];
+  __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(gqa_smem);  // [32][RS]
+  __nv_bfloat16* Ks = Qs + kRowBlock * RS;                          // [stage][64][RS]
+  __nv_bfloat16* Vs = Ks + kMmaStages * kKeyTile * RS;              // [stage][64][RS]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const int mt = warp & 1, kh = warp >> 1;
+  const int split = blockIdx.x, g = blockIdx.y;
+  const int b = int(blockIdx.z) / row_blocks, r0 = (int(blockIdx.z) % row_blocks) * kRowBlock;
+  const int G = n_heads / n_kv;
+  const int nrows = min(kRowBlock, G * block - r0);
+  const int nk = n_ctx + block;
+  const int k0 = split * chunk, k1 = min(nk, k0 + chunk);
+  const int n_tiles = (k1 - k0 + kKeyTile - 1) / kKeyTile;
+  const int64_t ctx_base = int64_t(b) * ctx_sb + int64_t(g) * ctx_sh;
+  const int64_t blk_base = (int64_t(b) * n_kv + g) * block;
+
+  for (int i = tid; i < kRowBlock * CPR; i += kMmaThreads) {
+    const int r = i / CPR, c = i % CPR;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (r < nrows) {
+      const int ri = r0 + r;
+      const int h = g * G + ri / block, t = ri % block;
+      v = *reinterpret_cast<const uint4*>(q + ((int64_t(b) * block + t) * n_heads + h) * HD + c * 8);
+    }
+    *reinterpret_cast<uint4*>(Qs + r * RS + c * 8) = v;
+  }
+  auto load_tile = [&](int tile, int stage) {
+    const int kt0 = k0 + tile * kKeyTile;
+    __nv_bfloat16* ks = Ks + stage * kKeyTile * RS;
+    __nv_bfloat16* vs = Vs + stage * kKeyTile * RS;
+    for (int i = tid; i < kKeyTile * CPR; i += kMmaThreads) {
+      const int j = i / CPR, c = i % CPR;
+      const int k = kt0 + j;
+      const bool valid = k < k1;
+      const __nv_bfloat16* ksrc;
+      const __nv_bfloat16* vsrc;
+      if (valid && k < n_ctx) {
+        ksrc = ctx_k + ctx_base + int64_t(k) * HD + c * 8;
+        vsrc = ctx_v + ctx_base + int64_t(k) * HD + c * 8;
+      } else {
+        const int kb = valid ? k - n_ctx : 0;  // nothing is read past the range: any in-range row
+        ksrc = blk_k + (blk_base + kb) * HD + c * 8;
+        vsrc = blk_v + (blk_base + kb) * HD + c * 8;
+      }
+      cp_async16(smem_u32(ks + j * RS + c * 8), ksrc, valid);
+      cp_async16(smem_u32(vs + j * RS + c * 8), vsrc, valid);
+    }
+  };
+  load_tile(0, 0);  // every range holds at least one key
+  cp_async_commit();
+  __syncthreads();  // Qs
+  uint32_t qa[KS][4];
+#pragma unroll
+  for (int kk = 0; kk < KS; ++kk)
+    ldsm_x4(smem_u32(Qs + (16 * mt + (lane & 7) + 8 * ((lane >> 3) & 1)) * RS + 16 * kk + 8 * (lane >> 4)),
+            qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+
+  float o[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    if (tile + 1 < n_tiles) load_tile(tile + 1, (tile + 1) & 1);
+    cp_async_commit();
+    cp_async_wait1();  // this tile's group has landed
+    __syncthreads();
+    const int kt = min(kKeyTile, k1 - (k0 + tile * kKeyTile));
+    const __nv_bfloat16* ks = Ks + ((tile & 1) * kKeyTile + 32 * kh) * RS;
+    const __nv_bfloat16* vs = Vs + ((tile & 1) * kKeyTile + 32 * kh) * RS;
+    float s[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {  // keys 16p .. 16p + 15 of this warp's half: two 8-key tiles
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(smem_u32(ks + (16 * p + (lane & 7) + 8 * (lane >> 4)) * RS + 16 * kk + 8 * ((lane >> 3) & 1)), b0,
+                b1, b2, b3);
+        mma_16816(s[2 * p], qa[kk], b0, b1);
+        mma_16816(s[2 * p + 1], qa[kk], b2, b3);
+      }
+    }
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int key = 32 * kh + 8 * n + 2 * t4 + (c & 1);
+        const float v = key < kt ? s[n][c] * scale : -INFINITY;
+        s[n][c] = v;
+        mx[c >> 1] = fmaxf(mx[c >> 1], v);
+      }
+    float alpha[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+      const float m_new = fmaxf(m_run[i], mx[i]);
+      const float mref = m_new == -INFINITY ? 0.f : m_new;  // a row with no key yet stays empty
+      alpha[i] = expf(m_run[i] - mref);
+      m_run[i] = m_new;
+      mx[i] = mref;
+    }
+    float ls[2] = {0.f, 0.f};
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float pv = expf(s[n][c] - mx[c >> 1]);
+        s[n][c] = pv;
+        ls[c >> 1] += pv;
+      }
+    l_run[0] = l_run[0] * alpha[0] + ls[0];
+    l_run[1] = l_run[1] * alpha[1] + ls[1];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      o[n][0] *= alpha[0];
+      o[n][1] *= alpha[0];
+      o[n][2] *= alpha[1];
+      o[n][3] *= alpha[1];
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {  // keys 16j .. 16j + 15: the score tiles 2j, 2j + 1 as the A operand
+      uint32_t pa[4];
+      pa[0] = pack_bf16x2(s[2 * j][0], s[2 * j][1]);
+      pa[1] = pack_bf16x2(s[2 * j][2], s[2 * j][3]);
+      pa[2] = pack_bf16x2(s[2 * j + 1][0], s[2 * j + 1][1]);
+      pa[3] = pack_bf16x2(s[2 * j + 1][2], s[2 * j + 1][3]);
+#pragma unroll
+      for (int dp = 0; dp < HD / 16; ++dp) {  // output columns 16dp .. 16dp + 15
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(smem_u32(vs + (16 * j + (lane & 7) + 8 * ((lane >> 3) & 1)) * RS + 16 * dp + 8 * (lane >> 4)), b0,
+                  b1, b2, b3);
+        mma_16816(o[2 * dp], pa, b0, b1);
+        mma_16816(o[2 * dp + 1], pa, b2, b3);
+      }
+    }
+    __syncthreads();  // the next iteration refills this stage
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 1);
+    l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 2);
+  }
+  const int pi = 2 * split + kh;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int r = 16 * mt + g8 + 8 * i;
+    if (r < nrows) {
+      const int ri = r0 + r;
+      const int64_t row = (int64_t(b) * n_heads + g * G + ri / block) * block + ri % block;
+      float* dst = part + (row * n_parts + pi) * HD;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        dst[8 * n + 2 * t4] = o[n][2 * i];
+        dst[8 * n + 2 * t4 + 1] = o[n][2 * i + 1];
+      }
+      if (t4 == 0) {
+        ml[(row * n_parts + pi) * 2] = m_run[i];
+        ml[(row * n_parts + pi) * 2 + 1] = l_run[i];
+      }
+    }
+  }
+}
+
 // One warp per query row (b, h, t): the key ranges' partials combined in range order,
 // divided by the total denominator, rounded to T into out[b, t, h, :].
 template <typename T>
 __global__ void __launch_bounds__(kGqaThreads) gqa_combine_kernel(const float* __restrict__ part,
                                                                   const float* __restrict__ ml, int64_t n_rows,
-                                                                  int n_splits, int head_dim, int n_heads, int block,
+                                                                  int n_parts, int head_dim, int n_heads, int block,
                                                                   T* __restrict__ out) {
-  __shared__ float wts[kGqaWarps][kMaxSplits];
+  __shared__ float wts[kGqaWarps][kMaxParts];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * kGqaWarps + warp;
   if (row >= n_rows) return;  // whole warps leave; only warp-level syncs follow
-  const float* mlr = ml + row * n_splits * 2;
+  const float* mlr = ml + row * n_parts * 2;
   float m = -INFINITY;
-  for (int s = lane; s < n_splits; s += 32) m = fmaxf(m, mlr[2 * s]);
+  for (int s = lane; s < n_parts; s += 32) m = fmaxf(m, mlr[2 * s]);
   m = warp_max(m);
   float l = 0.f;
-  for (int s = lane; s < n_splits; s += 32) {
+  for (int s = lane; s < n_parts; s += 32) {
     const float w = expf(mlr[2 * s] - m);
     wts[warp][s] = w;
     l = fmaf(w, mlr[2 * s + 1], l);
@@ -260,10 +492,10 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_combine_kernel(const float* _
   const int h = int(bh % n_heads);
   const int64_t b = bh / n_heads;
   T* dst = out + ((b * block + t) * n_heads + h) * int64_t(head_dim);
-  const float* pr = part + row * n_splits * int64_t(head_dim);
+  const float* pr = part + row * n_parts * int64_t(head_dim);
   for (int d = lane; d < head_dim; d += 32) {
     float o = 0.f;
-    for (int s = 0; s < n_splits; ++s) o = fmaf(pr[int64_t(s) * head_dim + d], wts[warp][s], o);
+    for (int s = 0; s < n_parts; ++s) o = fmaf(pr[int64_t(s) * head_dim + d], wts[warp][s], o);
     dst[d] = st_f<T>(o / l);
   }
 }
@@ -330,10 +562,32 @@ int launch_gqa_hd(int hd, const void* q, const void* ctx_k, const void* ctx_v, i
   }
 }
 
+// room for two partials per range (the mma kernel's key halves), whichever kernel runs
 size_t gqa_ws_bytes(int batch, int block, int n_heads, int head_dim, const GqaPlan& p) {
   const size_t rows = size_t(batch) * n_heads * block;
-  return rows * size_t(p.n_splits) * (size_t(head_dim) + 2) * 4;
+  return rows * size_t(2 * p.n_splits) * (size_t(head_dim) + 2) * 4;
 }
+
+size_t gqa_mma_smem_bytes(int hd) { return size_t(kRowBlock + 2 * kMmaStages * kKeyTile) * (hd + 8) * 2; }
+
+template <int HD>
+int launch_gqa_mma(const void* q, const void* ctx_k, const void* ctx_v, int64_t sb, int64_t sh, int n_ctx,
+                   const void* blk_k, const void* blk_v, int batch, int block, int n_heads, int n_kv, float scale,
+                   const GqaPlan& p, float* part, float* ml, cudaStream_t s) {
+  auto k = gqa_mma_kernel<HD>;
+  const size_t smem = gqa_mma_smem_bytes(HD);
+  if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return check_launch("gqa_mma smem attribute");
+  const dim3 grid(unsigned(p.n_splits), unsigned(n_kv), unsigned(batch * p.row_blocks));
+  using B = __nv_bfloat16;
+  k<<<grid, kMmaThreads, smem, s>>>(static_cast<const B*>(q), static_cast<const B*>(ctx_k),
+                                     static_cast<const B*>(ctx_v), sb, sh, n_ctx, static_cast<const B*>(blk_k),
+                                     static_cast<const B*>(blk_v), block, n_heads, n_kv, p.row_blocks, p.chunk,
+                                     2 * p.n_splits, scale, part, ml);
+  return check_launch("gqa_mma");
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
 }  // namespace dsm
@@ -396,12 +650,22 @@ extern "C" int dsm_gqa_attn(const void* q, const void* ctx_k, const void* ctx_v,
   const size_t need = gqa_ws_bytes(batch, block, n_heads, head_dim, p);
   if (ws_bytes < need) return fail(DSM_ERR_WORKSPACE, "dsm_gqa_attn: workspace too small");
   const int64_t rows = int64_t(batch) * n_heads * block;
-  float* part = static_cast<float*>(ws);
-  float* ml = part + rows * p.n_splits * int64_t(head_dim);
-  cudaStream_t s = as_stream(stream);
   const int64_t sb = n_ctx ? ctx_batch_stride : 0, sh = n_ctx ? ctx_head_stride : 0;
+  // the mma kernel moves 16-byte chunks: every row and base it reads must sit on 16 bytes
+  const bool mma = g_gqa_kernel.load(std::memory_order_relaxed) == 0 && dtype == DSM_DT_BF16 &&
+                   (head_dim == 64 || head_dim == 128) && aligned16(q) && aligned16(blk_k) && aligned16(blk_v) &&
+                   (n_ctx == 0 || (aligned16(ctx_k) && aligned16(ctx_v) && sb % 8 == 0 && sh % 8 == 0));
+  const int n_parts = mma ? 2 * p.n_splits : p.n_splits;
+  float* part = static_cast<float*>(ws);
+  float* ml = part + rows * n_parts * int64_t(head_dim);
+  cudaStream_t s = as_stream(stream);
   int st;
-  if (dtype == DSM_DT_BF16)
+  if (mma)
+    st = head_dim == 64 ? launch_gqa_mma<64>(q, ctx_k, ctx_v, sb, sh, n_ctx, blk_k, blk_v, batch, block, n_heads,
+                                             n_kv, scale, p, part, ml, s)
+                        : launch_gqa_mma<128>(q, ctx_k, ctx_v, sb, sh, n_ctx, blk_k, blk_v, batch, block, n_heads,
+                                              n_kv, scale, p, part, ml, s);
+  else if (dtype == DSM_DT_BF16)
     st = launch_gqa_hd<__nv_bfloat16>(head_dim, q, ctx_k, ctx_v, sb, sh, n_ctx, blk_k, blk_v, batch, block, n_heads,
                                       n_kv, scale, p, part, ml, s);
   else
@@ -412,9 +676,15 @@ extern "C" int dsm_gqa_attn(const void* q, const void* ctx_k, const void* ctx_v,
   DSM_REQUIRE(grid <= 0x7fffffff, "dsm_gqa_attn: too many rows");
   if (dtype == DSM_DT_BF16)
     gqa_combine_kernel<__nv_bfloat16><<<unsigned(grid), kGqaThreads, 0, s>>>(
-        part, ml, rows, p.n_splits, head_dim, n_heads, block, static_cast<__nv_bfloat16*>(out));
+        part, ml, rows, n_parts, head_dim, n_heads, block, static_cast<__nv_bfloat16*>(out));
   else
-    gqa_combine_kernel<float><<<unsigned(grid), kGqaThreads, 0, s>>>(part, ml, rows, p.n_splits, head_dim, n_heads,
+    gqa_combine_kernel<float><<<unsigned(grid), kGqaThreads, 0, s>>>(part, ml, rows, n_parts, head_dim, n_heads,
                                                                      block, static_cast<float*>(out));
   return check_launch("gqa_combine");
+}
+
+extern "C" int dsm_set_gqa_kernel(int kernel) {
+  DSM_REQUIRE(kernel == 0 || kernel == 1, "dsm_set_gqa_kernel: kernel must be 0 or 1");
+  g_gqa_kernel.store(kernel);
+  return DSM_OK;
 }

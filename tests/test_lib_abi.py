@@ -130,9 +130,11 @@ def test_gqa_attention_entry_points_reject_bad_arguments_on_the_host():
         assert call() != 0, i
         assert L.dsm_last_error_message().decode()
     # 32 query heads over 8 KV heads, a block of 7 after 2048 context rows: 33 key ranges of
-    # one 64-key tile each (two CTAs per SM on 148 SMs), fp32 partials of 128 + 2 per row
-    assert L.dsm_gqa_attn_workspace_bytes(1, 7, 32, 8, 128, 2048) == 32 * 7 * 33 * 130 * 4
-    assert L.dsm_gqa_attn_workspace_bytes(1, 7, 32, 8, 128, 0) == 32 * 7 * 1 * 130 * 4
+    # one 64-key tile each (two CTAs per SM on 148 SMs), room for two fp32 partials of
+    # 128 + 2 per row and range
+    assert L.dsm_gqa_attn_workspace_bytes(1, 7, 32, 8, 128, 2048) == 32 * 7 * 66 * 130 * 4
+    assert L.dsm_gqa_attn_workspace_bytes(1, 7, 32, 8, 128, 0) == 32 * 7 * 2 * 130 * 4
+    assert L.dsm_set_gqa_kernel(2) != 0 and L.dsm_set_gqa_kernel(1) == 0
     assert L.dsm_gqa_attn_workspace_bytes(1, 7, 6, 4, 128, 0) == 0
 
 
