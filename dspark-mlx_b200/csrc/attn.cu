@@ -19,7 +19,13 @@
 //
 // Everything is fp32 inside; values are rounded to the activation dtype where the reference's
 // arrays carry it. One CTA per row (norms), per (token, head) warp (attention).
+//
+// sparse_attn_mma_kernel is the tensor-core form of dsm_sparse_attn for bf16 (opt-in through
+// dsm_set_attn_kernel): the 64 heads of a token share one KV row set, so a CTA takes 16
+// (token, head) rows of one sequence against all of its keys, streamed through shared memory
+// in 32-key chunks, with q.k and p.v on mma.m16n8k16.
 #include "common.cuh"
+#include "warp_mma.cuh"
 
 namespace dsm {
 namespace {
@@ -213,6 +219,232 @@ __global__ void __launch_bounds__(kAttnThreads) sparse_attn_kernel(
   }
 }
 
+constexpr int kSaThreads = 128;   // 4 warps
+constexpr int kSaChunk = 32;      // keys per shared-memory chunk
+constexpr int kSaMaxKeys = 256;   // window slots + block rows
+constexpr int kSaRows = 16;       // (token, head) rows per CTA
+
+// Grid (row tile, sequence). Row r of a sequence is (token r / n_heads, head r % n_heads), so
+// a tile is 16 consecutive rows of q. Keys: the window's first n_win slots, then the block's
+// rows (the same rows serve as values).
+// Phase 1: warp w scores keys 8w .. 8w + 7 of every chunk (q.k on mma, fp32).
+// Phase 2: the row max and the softmax denominator (plus exp(sink - max)) across the four
+//          warps through shared memory; p = exp(s - max) goes to shared memory as bf16.
+// Phase 3: warp w takes output columns [HD/4 w, HD/4 (w + 1)) of p.v over all chunks.
+// Epilogue: divide, round to bf16, inverse RoPE of the last rope_dim columns, group-major
+// store as sparse_attn_kernel.
+template <int HD>
+__global__ void __launch_bounds__(kSaThreads) sparse_attn_mma_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ win, const __nv_bfloat16* __restrict__ blk,
+    const float* __restrict__ sink, int batch, int block, int n_heads, int window, int n_win, float scale,
+    int rope_dim, const float* __restrict__ cos_t, const float* __restrict__ sin_t, int pos0, int n_groups,
+    __nv_bfloat16* __restrict__ out) {
+  using B = __nv_bfloat16;
+  constexpr int RS = HD + 8;               // shared row stride of q and key rows (elements)
+  constexpr int CPR = HD / 8;              // 16-byte chunks per row
+  constexpr int KS = HD / 16;              // k-steps of q.k
+  constexpr int NKP = kSaMaxKeys + 8;      // shared row stride of p
+  constexpr int WC = HD / 4;               // output columns per warp
+  constexpr int WNT = WC / 8;              // 8-wide output tiles per warp
+  constexpr int MAXC = kSaMaxKeys / kSaChunk;
+  static_assert(HD % 64 == 0 && HD <= 512, "head_dim");
+  extern __shared__ __align__(16) unsigned char sa_smem[];
+  B* Qs = reinterpret_cast<B*>(sa_smem);            // [16][RS]
+  B* Cs = Qs + kSaRows * RS;                        // [2][32][RS]
+  B* Ps = Cs + 2 * kSaChunk * RS;                   // [16][NKP]
+  float* red_max = reinterpret_cast<float*>(Ps + kSaRows * NKP);  // [4][16]
+  float* red_sum = red_max + 4 * kSaRows;                         // [4][16]
+  float* row_max = red_sum + 4 * kSaRows;                         // [16]
+  float* row_den = row_max + kSaRows;                             // [16]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, t4 = lane & 3;
+  const int b = blockIdx.y;
+  const int rows = block * n_heads;
+  const int r0 = blockIdx.x * kSaRows;
+  const int nk = n_win + block;
+  const int nchunks = (nk + kSaChunk - 1) / kSaChunk;
+  const int64_t qrow0 = int64_t(b) * rows + r0;
+
+  for (int i = tid; i < kSaRows * CPR; i += kSaThreads) {
+    const int r = i / CPR, c = i % CPR;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (r0 + r < rows) v = *reinterpret_cast<const uint4*>(q + (qrow0 + r) * HD + c * 8);
+    *reinterpret_cast<uint4*>(Qs + r * RS + c * 8) = v;
+  }
+  auto load_chunk = [&](int ch, int stage) {
+    B* cs = Cs + stage * kSaChunk * RS;
+    for (int i = tid; i < kSaChunk * CPR; i += kSaThreads) {
+      const int j = i / CPR, c = i % CPR;
+      const int k = ch * kSaChunk + j;
+      const bool valid = k < nk;
+      const B* src = (valid && k < n_win) ? win + (int64_t(b) * window + k) * HD + c * 8
+                                          : blk + (int64_t(b) * block + (valid ? k - n_win : 0)) * HD + c * 8;
+      cp_async16(smem_u32(cs + j * RS + c * 8), src, valid);
+    }
+  };
+
+  // phase 1: scores of this warp's keys
+  float s[MAXC][4];
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) s[c][0] = s[c][1] = s[c][2] = s[c][3] = 0.f;
+  load_chunk(0, 0);
+  cp_async_commit();
+  __syncthreads();  // Qs
+  const uint32_t qa_base = smem_u32(Qs + ((lane & 7) + 8 * ((lane >> 3) & 1)) * RS + 8 * (lane >> 4));
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    if (c < nchunks) {
+      if (c + 1 < nchunks) load_chunk(c + 1, (c + 1) & 1);
+      cp_async_commit();
+      cp_async_wait1();
+      __syncthreads();
+      const uint32_t kb = smem_u32(Cs + ((c & 1) * kSaChunk + 8 * warp + (lane & 7)) * RS + 8 * (lane >> 3));
+#pragma unroll 4
+      for (int kk = 0; kk < KS; kk += 2) {  // two k-steps: one x4 load of 8 keys x 32 dims
+        uint32_t a0[4], a1[4], b0, b1, b2, b3;
+        ldsm_x4(qa_base + 32 * kk, a0[0], a0[1], a0[2], a0[3]);
+        ldsm_x4(qa_base + 32 * (kk + 1), a1[0], a1[1], a1[2], a1[3]);
+        ldsm_x4(kb + 32 * kk, b0, b1, b2, b3);
+        mma_16816(s[c], a0, b0, b1);
+        mma_16816(s[c], a1, b2, b3);
+      }
+      __syncthreads();  // the next iteration refills this stage
+    }
+  }
+  // phase 2: softmax statistics across the warps, p to shared memory
+  float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    if (c < nchunks) {
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const int key = c * kSaChunk + 8 * warp + 2 * t4 + (cc & 1);
+        const float v = key < nk ? s[c][cc] * scale : -INFINITY;
+        s[c][cc] = v;
+        mx[cc >> 1] = fmaxf(mx[cc >> 1], v);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+    mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+  }
+  if (t4 == 0) {
+    red_max[warp * kSaRows + g8] = mx[0];
+    red_max[warp * kSaRows + g8 + 8] = mx[1];
+  }
+  __syncthreads();
+  if (tid < kSaRows)
+    row_max[tid] = fmaxf(fmaxf(red_max[tid], red_max[kSaRows + tid]),
+                         fmaxf(red_max[2 * kSaRows + tid], red_max[3 * kSaRows + tid]));
+  __syncthreads();
+  const float m_row[2] = {row_max[g8], row_max[g8 + 8]};  // finite: every row has a valid key
+  float ls[2] = {0.f, 0.f};
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    if (c < nchunks) {
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const float pv = expf(s[c][cc] - m_row[cc >> 1]);
+        s[c][cc] = pv;
+        ls[cc >> 1] += pv;
+      }
+      const int key = c * kSaChunk + 8 * warp + 2 * t4;
+      *reinterpret_cast<uint32_t*>(Ps + g8 * NKP + key) = pack_bf16x2(s[c][0], s[c][1]);
+      *reinterpret_cast<uint32_t*>(Ps + (g8 + 8) * NKP + key) = pack_bf16x2(s[c][2], s[c][3]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    ls[i] += __shfl_xor_sync(0xffffffffu, ls[i], 1);
+    ls[i] += __shfl_xor_sync(0xffffffffu, ls[i], 2);
+  }
+  if (t4 == 0) {
+    red_sum[warp * kSaRows + g8] = ls[0];
+    red_sum[warp * kSaRows + g8 + 8] = ls[1];
+  }
+  __syncthreads();
+  if (tid < kSaRows) {
+    const int r = r0 + tid;
+    const int h = r < rows ? r % n_heads : 0;
+    row_den[tid] = red_sum[tid] + red_sum[kSaRows + tid] + red_sum[2 * kSaRows + tid] + red_sum[3 * kSaRows + tid] +
+                   expf(sink[h] - row_max[tid]);
+  }
+  // phase 3: p.v for this warp's columns
+  float o[WNT][4];
+#pragma unroll
+  for (int n = 0; n < WNT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  load_chunk(0, 0);
+  cp_async_commit();
+  const uint32_t pa_base = smem_u32(Ps + ((lane & 7) + 8 * ((lane >> 3) & 1)) * NKP + 8 * (lane >> 4));
+  for (int c = 0; c < nchunks; ++c) {
+    if (c + 1 < nchunks) load_chunk(c + 1, (c + 1) & 1);
+    cp_async_commit();
+    cp_async_wait1();
+    __syncthreads();  // this chunk, and (first pass) p and the row statistics
+    const uint32_t vb =
+        smem_u32(Cs + ((c & 1) * kSaChunk + (lane & 7) + 8 * ((lane >> 3) & 1)) * RS + WC * warp + 8 * (lane >> 4));
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {  // keys 16j .. 16j + 15 of the chunk
+      uint32_t pa[4];
+      ldsm_x4(pa_base + 2 * (c * kSaChunk + 16 * j), pa[0], pa[1], pa[2], pa[3]);
+#pragma unroll
+      for (int dp = 0; dp < WNT / 2; ++dp) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vb + 2 * (16 * j * RS + 16 * dp), b0, b1, b2, b3);
+        mma_16816(o[2 * dp], pa, b0, b1);
+        mma_16816(o[2 * dp + 1], pa, b2, b3);
+      }
+    }
+    __syncthreads();  // the next iteration refills this stage
+  }
+  // epilogue
+  const int hpg = n_heads / n_groups;
+  const int64_t n_tok = int64_t(batch) * block;
+  const int half = rope_dim / 2, base = HD - rope_dim;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int lr = g8 + 8 * i;
+    const int r = r0 + lr;
+    if (r >= rows) continue;
+    const int m = r / n_heads, h = r % n_heads;
+    const float den = row_den[lr];
+    B* orow = out + (int64_t(h / hpg) * n_tok + int64_t(b) * block + m) * (int64_t(hpg) * HD) +
+              int64_t(h % hpg) * HD;
+#pragma unroll
+    for (int n = 0; n < WNT; ++n) {
+      const int col = WC * warp + 8 * n + 2 * t4;
+      float a = rnd<B>(o[n][2 * i] / den), c = rnd<B>(o[n][2 * i + 1] / den);
+      if (col >= base) rope_pair(a, c, cos_t, sin_t, pos0 + m, half, (col - base) >> 1, true);
+      *reinterpret_cast<__nv_bfloat162*>(orow + col) = __floats2bfloat162_rn(a, c);
+    }
+  }
+}
+
+size_t sparse_mma_smem_bytes(int hd) {
+  return size_t(kSaRows + 2 * kSaChunk) * (hd + 8) * 2 + size_t(kSaRows) * (kSaMaxKeys + 8) * 2 +
+         size_t(4 * kSaRows * 2 + 2 * kSaRows) * 4;
+}
+
+template <int HD>
+int launch_sparse_mma(const void* q, const void* win, const void* blk, const float* sink, int batch, int block,
+                      int n_heads, int window, int n_win, float scale, int rope_dim, const float* cos_t,
+                      const float* sin_t, int pos0, int n_groups, void* out, cudaStream_t s) {
+  auto k = sparse_attn_mma_kernel<HD>;
+  const size_t smem = sparse_mma_smem_bytes(HD);
+  if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return check_launch("sparse_attn_mma smem attribute");
+  const dim3 grid(unsigned(ceil_div(int64_t(block) * n_heads, kSaRows)), unsigned(batch));
+  using B = __nv_bfloat16;
+  k<<<grid, kSaThreads, smem, s>>>(static_cast<const B*>(q), static_cast<const B*>(win), static_cast<const B*>(blk),
+                                   sink, batch, block, n_heads, window, n_win, scale, rope_dim, cos_t, sin_t, pos0,
+                                   n_groups, static_cast<B*>(out));
+  return check_launch("sparse_attn_mma");
+}
+
+bool aligned_to(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
 }  // namespace
 }  // namespace dsm
 
@@ -305,9 +537,31 @@ extern "C" int dsm_sparse_attn(const void* q, const void* window_kv, const void*
   DSM_REQUIRE(dtype == DSM_DT_F32 || dtype == DSM_DT_BF16, "dsm_sparse_attn: dtype must be F32 or BF16");
   if (batch == 0) return DSM_OK;
   DSM_REQUIRE(q && block_kv && sink && out && scratch && (n_win == 0 || window_kv), "dsm_sparse_attn: NULL pointer");
+  cudaStream_t s = as_stream(stream);
+  // the tensor-core kernel moves 16-byte rows and stores bf16 pairs
+  const void* win_any = n_win ? window_kv : block_kv;  // never read when n_win == 0
+  if (attn_kernel() == 0 && dtype == DSM_DT_BF16 && head_dim % 64 == 0 && head_dim <= 512 &&
+      n_win + block <= kSaMaxKeys && batch <= 65535 && aligned_to(q, 16) && aligned_to(win_any, 16) &&
+      aligned_to(block_kv, 16) && aligned_to(out, 4)) {
+    switch (head_dim) {
+      case 64:
+        return launch_sparse_mma<64>(q, win_any, block_kv, sink, batch, block, n_heads, window, n_win, scale, rope_dim,
+                                     cos_t, sin_t, pos0, n_groups, out, s);
+      case 128:
+        return launch_sparse_mma<128>(q, win_any, block_kv, sink, batch, block, n_heads, window, n_win, scale,
+                                      rope_dim, cos_t, sin_t, pos0, n_groups, out, s);
+      case 256:
+        return launch_sparse_mma<256>(q, win_any, block_kv, sink, batch, block, n_heads, window, n_win, scale,
+                                      rope_dim, cos_t, sin_t, pos0, n_groups, out, s);
+      case 512:
+        return launch_sparse_mma<512>(q, win_any, block_kv, sink, batch, block, n_heads, window, n_win, scale,
+                                      rope_dim, cos_t, sin_t, pos0, n_groups, out, s);
+      default:
+        break;  // 192, 320, 384, 448: the CUDA-core kernel
+    }
+  }
   const int64_t warps = int64_t(batch) * block * n_heads;
   const unsigned grid = unsigned(ceil_div(warps * 32, kAttnThreads));
-  cudaStream_t s = as_stream(stream);
   if (dtype == DSM_DT_BF16)
     sparse_attn_kernel<__nv_bfloat16><<<grid, kAttnThreads, 0, s>>>(
         static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(window_kv),

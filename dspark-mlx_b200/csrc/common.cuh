@@ -72,6 +72,8 @@ int expert_tm_down_split(int wfmt, int group_size, const void* h_staged, float h
 float h_scale_for(int act, float limit);
 // 0 = choose by rows per expert, 1 = always the decode kernel, 2 = tcgen05 where supported
 int expert_regime();
+// attention kernels: 0 = tensor-core kernels where they apply, 1 = CUDA-core kernels
+int attn_kernel();
 
 // Stage two row sets of the same x in one launch: rows of x in perm order (job a) and, when
 // n_rows_b > 0, the first n_rows_b tokens in order (job b). Arguments as dsm_stage_rows.

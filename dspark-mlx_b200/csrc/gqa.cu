@@ -24,10 +24,11 @@
 //                    q.k and p.v on mma.m16n8k16 (bf16 in, fp32 accumulate; p rounded to
 //                    bf16 for the second product), each warp an online softmax over half of
 //                    every tile, so each key range leaves two partials.
-// dsm_set_gqa_kernel picks between them (process-wide).
+// dsm_set_attn_kernel picks between them (process-wide).
 #include <atomic>
 
 #include "common.cuh"
+#include "warp_mma.cuh"
 
 namespace dsm {
 namespace {
@@ -42,8 +43,7 @@ constexpr int kMaxHeadDim = 256;
 constexpr int kMmaThreads = 128;  // 4 warps: 2 row tiles of 16 x 2 key halves of 32
 constexpr int kMmaStages = 2;
 
-// 0: the mma kernel wherever it applies, 1: the CUDA-core kernel everywhere
-std::atomic<int> g_gqa_kernel{1};
+
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -244,38 +244,6 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_attn_kernel(
     ml[(row * n_splits + split) * 2] = m_run[tid];
     ml[(row * n_splits + split) * 2 + 1] = l_run[tid];
   }
-}
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-// 16 bytes global -> shared; a key past the range reads nothing and fills zeros
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::); }
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];\n"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];\n"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-// c += a (16 x 16, row-major) * b (16 x 8, column-major); bf16 in, fp32 accumulate
-__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&v);
 }
 
 // Grid and rows as gqa_attn_kernel; bf16 only. Warp w takes row tile w & 1 (rows 16 (w & 1)
@@ -652,7 +620,7 @@ extern "C" int dsm_gqa_attn(const void* q, const void* ctx_k, const void* ctx_v,
   const int64_t rows = int64_t(batch) * n_heads * block;
   const int64_t sb = n_ctx ? ctx_batch_stride : 0, sh = n_ctx ? ctx_head_stride : 0;
   // the mma kernel moves 16-byte chunks: every row and base it reads must sit on 16 bytes
-  const bool mma = g_gqa_kernel.load(std::memory_order_relaxed) == 0 && dtype == DSM_DT_BF16 &&
+  const bool mma = attn_kernel() == 0 && dtype == DSM_DT_BF16 &&
                    (head_dim == 64 || head_dim == 128) && aligned16(q) && aligned16(blk_k) && aligned16(blk_v) &&
                    (n_ctx == 0 || (aligned16(ctx_k) && aligned16(ctx_v) && sb % 8 == 0 && sh % 8 == 0));
   const int n_parts = mma ? 2 * p.n_splits : p.n_splits;
@@ -683,8 +651,16 @@ extern "C" int dsm_gqa_attn(const void* q, const void* ctx_k, const void* ctx_v,
   return check_launch("gqa_combine");
 }
 
-extern "C" int dsm_set_gqa_kernel(int kernel) {
-  DSM_REQUIRE(kernel == 0 || kernel == 1, "dsm_set_gqa_kernel: kernel must be 0 or 1");
-  g_gqa_kernel.store(kernel);
+namespace dsm {
+namespace {
+// 0: the tensor-core attention kernels wherever they apply, 1: the CUDA-core kernels
+std::atomic<int> g_attn_kernel{1};
+}  // namespace
+int attn_kernel() { return g_attn_kernel.load(std::memory_order_relaxed); }
+}  // namespace dsm
+
+extern "C" int dsm_set_attn_kernel(int kernel) {
+  DSM_REQUIRE(kernel == 0 || kernel == 1, "dsm_set_attn_kernel: kernel must be 0 or 1");
+  dsm::g_attn_kernel.store(kernel);
   return DSM_OK;
 }

@@ -34,7 +34,7 @@ EXPORTED = (
     "dsm_dense_mlp", "dsm_linear", "dsm_hc_head_norm", "dsm_markov_head", "dsm_draft_head_workspace_bytes",
     "dsm_draft_head", "dsm_rows_norm_rope", "dsm_q_head_norm_rope", "dsm_kv_window_write",
     "dsm_sparse_attn_scratch_bytes", "dsm_sparse_attn", "dsm_round_rows", "dsm_stage_rows_hilo",
-    "dsm_qkv_norm_rope", "dsm_gqa_attn_workspace_bytes", "dsm_gqa_attn", "dsm_set_gqa_kernel",
+    "dsm_qkv_norm_rope", "dsm_gqa_attn_workspace_bytes", "dsm_gqa_attn", "dsm_set_attn_kernel",
 )
 
 
@@ -124,7 +124,7 @@ def _declare(lib):
         "dsm_qkv_norm_rope": (I, [V, V, I64, I, I, I, V, V, F, V, V, I, I, I, V, V, V, I, I, I, V]),
         "dsm_gqa_attn_workspace_bytes": (S, [I, I, I, I, I, I]),
         "dsm_gqa_attn": (I, [V, V, V, I64, I64, I, V, V, I, I, I, I, I, I, F, V, V, S, V]),
-        "dsm_set_gqa_kernel": (I, [I]),
+        "dsm_set_attn_kernel": (I, [I]),
         "dsm_stage_rows_hilo": (I, [V, I64, I, V, I64, V, V]),
         "dsm_moe_workspace_bytes": (S, [POINTER(MoEDesc)]),
         "dsm_moe_forward": (I, [POINTER(MoEDesc), V, I, V, I, I64, V, V, V, V, S, V]),

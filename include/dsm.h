@@ -300,10 +300,11 @@ int dsm_round_rows(const float* in, const float* in_lo, int64_t n, void* out, in
  *   blk_k / blk_v [batch, n_kv, block, head_dim]; q is [batch, block, n_heads, head_dim].
  *   head_dim 32, 64, 128 or 256. workspace: dsm_gqa_attn_workspace_bytes (fp32 partials of
  *   the key ranges).
- * set_gqa_kernel: 0 runs bf16 attention with head_dim 64 / 128 on the tensor-core kernel
- *   (mma.m16n8k16; every pointer 16-byte aligned and the context strides multiples of 8,
- *   else the CUDA-core kernel runs); 1 (the default) runs the CUDA-core kernel everywhere.
- *   Process-wide. */
+ * set_attn_kernel: 0 runs bf16 attention on the tensor-core kernels (mma.m16n8k16) where
+ *   they apply: dsm_gqa_attn with head_dim 64 / 128, every pointer 16-byte aligned and the
+ *   context strides multiples of 8; dsm_sparse_attn with head_dim 64..512 (a multiple of 64),
+ *   at most 256 keys, q / window / block rows 16-byte aligned. Elsewhere the CUDA-core kernels
+ *   run. 1 (the default) runs the CUDA-core kernels everywhere. Process-wide. */
 int dsm_qkv_norm_rope(const float* in, const float* in_lo, int64_t n_rows, int n_q, int n_kv, int head_dim,
                       const float* q_norm_w, const float* k_norm_w, float eps, const float* cos_t, const float* sin_t,
                       int tab_rows, int tab0, int period, void* q_out, void* k_out, void* v_out, int kv_cap, int row0,
@@ -313,7 +314,7 @@ int dsm_gqa_attn(const void* q, const void* ctx_k, const void* ctx_v, int64_t ct
                  int64_t ctx_head_stride, int n_ctx, const void* blk_k, const void* blk_v, int dtype, int batch,
                  int block, int n_heads, int n_kv, int head_dim, float scale, void* out, void* workspace,
                  size_t workspace_bytes, void* stream);
-int dsm_set_gqa_kernel(int kernel);
+int dsm_set_attn_kernel(int kernel);
 
 /* Kernel regime of the grouped expert products: 0 (default) picks by rows per busy
  * expert -- the mma.sync weight-streaming kernel at decode sizes, the tcgen05/TMEM kernel

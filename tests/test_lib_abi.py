@@ -134,7 +134,7 @@ def test_gqa_attention_entry_points_reject_bad_arguments_on_the_host():
     # 128 + 2 per row and range
     assert L.dsm_gqa_attn_workspace_bytes(1, 7, 32, 8, 128, 2048) == 32 * 7 * 66 * 130 * 4
     assert L.dsm_gqa_attn_workspace_bytes(1, 7, 32, 8, 128, 0) == 32 * 7 * 2 * 130 * 4
-    assert L.dsm_set_gqa_kernel(2) != 0 and L.dsm_set_gqa_kernel(1) == 0
+    assert L.dsm_set_attn_kernel(2) != 0 and L.dsm_set_attn_kernel(1) == 0
     assert L.dsm_gqa_attn_workspace_bytes(1, 7, 6, 4, 128, 0) == 0
 
 
