@@ -904,8 +904,9 @@ def run_reference_head(args):
 
 GQA_METRIC = ("Qwen3 draft-layer attention tokens/s (attend_cached over 2048 cached context rows, 8-bit affine "
               "projections); HBM GB/s")
-# staging, q/k/v products, head norms + RoPE, attention, range combine, staging, o_proj, cast
-GQA_KERNELS_PER_STEP = 10
+# staging, q/k/v products (split K: product + sum each), head norms + RoPE, attention, range
+# combine, staging, o_proj (product + sum), cast
+GQA_KERNELS_PER_STEP = 1 + 3 * 2 + 1 + 1 + 1 + 1 + 2 + 1
 
 
 def _gqa_cpu_setup(t, wl):

@@ -67,7 +67,7 @@ int expert_tm_down(int wfmt, int group_size, const void* h_staged, float h_scale
 int tm_down_splits(int inter, int dim, int64_t n_rows, int max_splits);
 int expert_tm_down_split(int wfmt, int group_size, const void* h_staged, float h_scale, int64_t rows_cap,
                          int inter, const void* w2, int dim, int k_splits, float* partials, int64_t n_rows,
-                         void* stream);
+                         void* stream, const float* x_row_scale = nullptr);
 // h staging scale of the SwiGLU output: 1 when the clamp bounds |h| by limit^2, else 2^-8
 float h_scale_for(int act, float limit);
 // 0 = choose by rows per expert, 1 = always the decode kernel, 2 = tcgen05 where supported

@@ -86,6 +86,27 @@ DenseLayout dense_layout(int64_t n_tokens, int dim, int inter, void* base) {
   return L;
 }
 
+// o[r * ldo + c] = sum over s of parts[s][r][c], in split order: the split-K linear's fp32 rows
+__global__ void __launch_bounds__(256) sum_splits_rows_kernel(const float* __restrict__ parts, int n_splits,
+                                                              int64_t n_rows, int dim, int ldo, float* __restrict__ o) {
+  // four consecutive columns per thread: dim, ldo and the pointers are 16-byte multiples
+  const int64_t count = n_rows * dim;
+  for (int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < count;
+       i += int64_t(gridDim.x) * blockDim.x * 4) {
+    float4 acc = *reinterpret_cast<const float4*>(parts + i);
+    for (int s = 1; s < n_splits; ++s) {
+      const float4 v = *reinterpret_cast<const float4*>(parts + s * count + i);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    const int64_t r = i / dim;
+    const int c = int(i % dim);
+    *reinterpret_cast<float4*>(o + r * ldo + c) = acc;
+  }
+}
+
 }  // namespace
 }  // namespace dsm
 
@@ -132,4 +153,38 @@ extern "C" int dsm_dense_mlp(const void* x, int x_dtype, int64_t n_tokens, int d
   else
     reduce_splits_kernel<<<grid, 256, 0, st>>>(L.parts, splits, count, count, round_o, static_cast<float*>(y));
   return check_launch("reduce_splits");
+}
+
+extern "C" size_t dsm_linear_splitk_workspace_bytes(int64_t n_rows, int out_dim) {
+  if (n_rows <= 0 || out_dim <= 0) return 0;
+  return size_t(kMaxSplits) * size_t(n_rows) * size_t(out_dim) * 4;
+}
+
+extern "C" int dsm_linear_splitk(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int k_dim,
+                                 int wfmt, int group_size, const void* w_packed, int out_dim, float* o_rows, int ldo,
+                                 int64_t n_rows, void* ws, size_t ws_bytes, void* stream) {
+  DSM_REQUIRE(out_dim > 0 && k_dim > 0 && n_rows >= 0 && ldo >= out_dim, "dsm_linear_splitk: bad shape");
+  DSM_REQUIRE(wfmt >= DSM_WFMT_F16 && wfmt <= DSM_WFMT_AFFINE4, "dsm_linear_splitk: unknown weight format");
+  if (wfmt == DSM_WFMT_AFFINE8)
+    DSM_REQUIRE(group_size == 32 || group_size == 64 || group_size == 128, "dsm_linear_splitk: affine8 group_size");
+  if (wfmt == DSM_WFMT_AFFINE4)
+    DSM_REQUIRE(group_size == 64 || group_size == 128, "dsm_linear_splitk: affine4 group_size");
+  DSM_REQUIRE(x_staged && x_row_scale && w_packed && o_rows, "dsm_linear_splitk: NULL pointer");
+  if (n_rows == 0) return DSM_OK;
+  const bool aligned = (reinterpret_cast<uintptr_t>(o_rows) & 15) == 0 && (reinterpret_cast<uintptr_t>(ws) & 15) == 0;
+  const int splits = tm_supports(wfmt) ? tm_down_splits(k_dim, out_dim, n_rows, kMaxSplits) : 1;
+  if (splits <= 1 || !ws || !aligned || out_dim % 4 || ldo % 4)
+    return dsm_linear(x_staged, x_row_scale, rows_cap, k_dim, wfmt, group_size, w_packed, out_dim, o_rows, ldo,
+                      n_rows, stream);
+  DSM_REQUIRE(rows_cap >= dsm_stage_rows_cap(n_rows), "dsm_linear_splitk: rows_cap too small");
+  const size_t need = size_t(splits) * size_t(n_rows) * size_t(out_dim) * 4;
+  if (ws_bytes < need) return fail(DSM_ERR_WORKSPACE, "dsm_linear_splitk: workspace too small");
+  float* parts = static_cast<float*>(ws);
+  int rc = expert_tm_down_split(wfmt, group_size, x_staged, 1.f, rows_cap, k_dim, w_packed, out_dim, splits, parts,
+                                n_rows, stream, x_row_scale);
+  if (rc != DSM_OK) return rc;
+  const int64_t count = n_rows * out_dim;
+  const int grid = int(std::min<int64_t>(ceil_div(count, 4 * 256), 4 * num_sms()));
+  sum_splits_rows_kernel<<<grid, 256, 0, as_stream(stream)>>>(parts, splits, n_rows, out_dim, ldo, o_rows);
+  return check_launch("sum_splits_rows");
 }

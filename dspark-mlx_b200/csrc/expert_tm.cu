@@ -682,12 +682,12 @@ int tm_down_splits(int inter, int dim, int64_t n_rows, int max_splits) {
 
 int expert_tm_down_split(int wfmt, int group_size, const void* h_staged, float h_scale, int64_t rows_cap,
                          int inter, const void* w2, int dim, int k_splits, float* partials, int64_t n_rows,
-                         void* stream) {
+                         void* stream, const float* x_row_scale) {
   TmArgs a{};
   a.wa = static_cast<const uint8_t*>(w2);
   a.wb = nullptr;
-  a.act_scale = nullptr;
-  a.act_scale_const = 1.f / h_scale;
+  a.act_scale = x_row_scale;  // per-row scales are linear in K: each partial carries them
+  a.act_scale_const = x_row_scale ? 1.f : 1.f / h_scale;
   a.offsets = nullptr;
   a.n_rows = n_rows;
   a.n_experts = 1;

@@ -15,7 +15,8 @@ Same constructor (``Qwen3DSparkAttention(args)``), parameter names (``q_proj``, 
   rows (``qwen3.py:130-143``).
 
 The projections are ``Projection``s, dense or MLX affine after ``quantize`` as
-``quantize_drafter`` leaves them, on ``dsm_linear``. q, k and v share one staging of the
+``quantize_drafter`` leaves them, on ``dsm_linear`` (quantised ones on
+``dsm_linear_splitk``, which spreads K over the GPU). q, k and v share one staging of the
 input and one fp32 output slab. The head norms, NeoX RoPE and the cache layout are one
 ``dsm_qkv_norm_rope``; the attention is ``dsm_gqa_attn``; ``o_proj`` is one more
 ``dsm_linear``. The activation dtype is the projections' MLX product dtype (bf16 or fp32).
@@ -96,10 +97,19 @@ class Qwen3DSparkAttention(nn.Module):
 
     @staticmethod
     def _project(st, proj: Projection, out: torch.Tensor, ldo: int) -> None:
+        """out[:, :proj.out_dim] (row stride ldo) = the staged rows times the projection. Quantised
+        projections split K across the GPU (``dsm_linear_splitk``)."""
         staged, xscale, cap, rows, k = st
         pm = proj.packed()
-        check(lib().dsm_linear(ptr(staged), ptr(xscale), cap, k, pm.wfmt, pm.group_size, ptr(pm.packed), pm.rows,
+        L = lib()
+        if proj.quant is None:
+            check(L.dsm_linear(ptr(staged), ptr(xscale), cap, k, pm.wfmt, pm.group_size, ptr(pm.packed), pm.rows,
                                ptr(out), ldo, rows, stream_ptr()), "dsm_linear")
+            return
+        ws_bytes = L.dsm_linear_splitk_workspace_bytes(rows, pm.rows)
+        ws = torch.empty(max(1, ws_bytes), dtype=torch.uint8, device=out.device)
+        check(L.dsm_linear_splitk(ptr(staged), ptr(xscale), cap, k, pm.wfmt, pm.group_size, ptr(pm.packed), pm.rows,
+                                  ptr(out), ldo, rows, ptr(ws), ws_bytes, stream_ptr()), "dsm_linear_splitk")
 
     def _prep(self, x: torch.Tensor, name: str) -> Tuple[torch.Tensor, torch.dtype]:
         if not x.is_cuda:

@@ -215,6 +215,16 @@ int dsm_dense_mlp(const void* x, int x_dtype, int64_t n_tokens, int dim, int int
  * n_experts = 1. */
 int dsm_linear(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int k_dim, int wfmt, int group_size,
                const void* w_packed, int out_dim, float* o_rows, int ldo, int64_t n_rows, void* stream);
+/* dsm_linear with K split across the GPU for the tensor-memory formats (fp4, affine), whose
+ * units hold up to 128 rows each: a few row tiles of a decode-sized product would leave most
+ * SMs idle. fp32 partial slabs per K range go to the workspace
+ * (dsm_linear_splitk_workspace_bytes) and are summed in range order into o_rows. Other
+ * formats, one-range products, out_dim or ldo not a multiple of 4, or pointers off 16 bytes
+ * run dsm_linear. */
+size_t dsm_linear_splitk_workspace_bytes(int64_t n_rows, int out_dim);
+int dsm_linear_splitk(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int k_dim, int wfmt,
+                      int group_size, const void* w_packed, int out_dim, float* o_rows, int ldo, int64_t n_rows,
+                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- the draft head ---------------------------------------------------------------------------
  * hc_head_norm: x [n, hc, dim] -> y [n, dim] = hc_head(x) (x dtype), x_norm [n, dim] =

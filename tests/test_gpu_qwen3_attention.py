@@ -93,6 +93,31 @@ def _oracle_case(dtype, b, q, ctx, h, nh, nkv, hd, seed):
     return w, hidden, target
 
 
+def test_qwen3_attention_8bit_projections_match_oracle():
+    """Projections quantised as quantize_drafter leaves them (MLX affine, 8 bits, groups of 64)
+    run split along K (dsm_linear_splitk). The oracle multiplies by the dequantised weights in
+    fp32; the GPU's bf16 activations round after every product."""
+    from oracle.formats import affine_dequantize
+
+    dtype, b, q, ctx, h, nh, nkv, hd = torch.bfloat16, 2, 7, 300, 2560, 32, 8, 128
+    theta, eps = 1000000.0, 1e-6
+    w, hidden, target = _oracle_case(dtype, b, q, ctx, h, nh, nkv, hd, seed=11)
+    a = _module(dict(hidden_size=h, num_attention_heads=nh, num_key_value_heads=nkv, head_dim=hd, rms_norm_eps=eps),
+                w)
+    wd = dict(w)
+    for n in ("q_proj", "k_proj", "v_proj", "o_proj"):
+        proj = getattr(a, n)
+        assert proj.quantize(bits=8, group_size=64)
+        wd[n] = affine_dequantize(proj.q.cpu(), proj.scales.cpu(), proj.biases.cpu(), 64, 8)
+    cos, sin = rope_tables(torch.arange(ctx + q), hd, theta)
+    out = a(hidden.to(DEV), target.to(DEV), cos, sin)
+    torch.cuda.synchronize()
+    ref = oracle.qwen3_attention(wd, nh, nkv, hd, eps, hidden.float(), target.float(), cos, sin)
+    assert out.dtype == torch.bfloat16
+    assert max_rel_err(out, ref) < 2e-2, max_rel_err(out, ref)
+    assert _lib.device_error() == 0
+
+
 @pytest.mark.parametrize("dtype,b,q,ctx,h,nh,nkv,hd", [
     (torch.bfloat16, 2, 7, 2048, 2560, 32, 8, 128),   # the Qwen3-4B draft layer, 2048 context rows
     (torch.bfloat16, 3, 7, 333, 1024, 16, 2, 64),     # 8 heads per KV head: 56 query rows, two row blocks
