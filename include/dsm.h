@@ -40,6 +40,7 @@
  *                       (model/attention.py:27-142, kernels.py:20-57, norm_rope.py:22-77)
  *   dsm_qkv_norm_rope, dsm_gqa_attn: Qwen3DSparkAttention.__call__ / context_kv /
  *                       attend_cached around dsm_linear (arch/qwen3.py:65-143)
+ *   dsm_add_rms_norm    the residual adds and RMSNorms of Qwen3DSparkLayer (arch/qwen3.py:157-176)
  *   dsm_gather_rows, dsm_segment_ids: expert-parallel plumbing; the reference runs on one
  *                       device (tests/reference_model.py:55-56 forces world_size 1) and has
  *                       no counterpart.
@@ -325,6 +326,14 @@ int dsm_gqa_attn(const void* q, const void* ctx_k, const void* ctx_v, int64_t ct
                  int block, int n_heads, int n_kv, int head_dim, float scale, void* out, void* workspace,
                  size_t workspace_bytes, void* stream);
 int dsm_set_attn_kernel(int kernel);
+
+/* ---- the Qwen3 draft layer's glue --------------------------------------------------------------
+ * add_rms_norm (Qwen3DSparkLayer.__call__ / forward_cached, arch/qwen3.py:165-176): for each of
+ * n_rows rows of dim values, s = T(x + delta) (delta NULL: s = x) and y = T(RMSNorm(s) * weight)
+ * with the norm in fp32 (norm_rope.py:22-39). sum_out (s) and norm_out (y) are each optional,
+ * not both NULL. dim <= 49152. */
+int dsm_add_rms_norm(const void* x, const void* delta, int dtype, int64_t n_rows, int dim, const float* weight,
+                     float eps, void* sum_out, void* norm_out, void* stream);
 
 /* Kernel regime of the grouped expert products: 0 (default) picks by rows per busy
  * expert -- the mma.sync weight-streaming kernel at decode sizes, the tcgen05/TMEM kernel

@@ -12,6 +12,9 @@ CPU with MLX's dtype rules:
 
 The attention is softmax(q k^T * scale) v accumulated in fp32 with q's dtype out, as
 ``mx.fast.scaled_dot_product_attention`` documents.
+
+The whole draft layer (``Qwen3DSparkLayer``, ``qwen3.py:157-176``) adds the pre-attention and
+pre-MLP RMSNorms, the residual adds and the MLP (``qwen3.py:146-154``).
 """
 
 from __future__ import annotations
@@ -24,7 +27,7 @@ from .attention_oracle import linear
 from .block_oracle import rms_norm
 
 __all__ = ["qwen3_rope_tables", "qwen3_apply_rope", "qwen3_sdpa", "qwen3_attention", "qwen3_context_kv",
-           "qwen3_attend_cached"]
+           "qwen3_attend_cached", "qwen3_layer", "qwen3_layer_cached"]
 
 
 def qwen3_rope_tables(position_ids: torch.Tensor, head_dim: int, theta: float) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -101,3 +104,38 @@ def qwen3_attend_cached(p: Dict[str, torch.Tensor], nh: int, nkv: int, hd: int, 
     v = nv if ctx_v is None else torch.cat([ctx_v, nv], dim=2)
     out = qwen3_sdpa(qh, k, v, hd ** -0.5)
     return linear(out.transpose(1, 2).reshape(b, q, nh * hd), p["o_proj"])
+
+
+def _qwen3_mlp(p: Dict[str, torch.Tensor], x: torch.Tensor) -> torch.Tensor:
+    """``Qwen3MLP.__call__`` (``qwen3.py:153-154``) on dense weights: ``nn.silu`` is
+    ``x * sigmoid(x)``, each elementwise op rounded to the activation dtype."""
+    g = linear(x, p["gate_proj"])
+    u = linear(x, p["up_proj"])
+    sig = torch.sigmoid(g.to(torch.float32)).to(g.dtype)
+    s = (g.to(torch.float32) * sig.to(torch.float32)).to(g.dtype)
+    h = (s.to(torch.float32) * u.to(torch.float32)).to(torch.promote_types(g.dtype, u.dtype))
+    return linear(h, p["down_proj"])
+
+
+def _add(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """``a + b`` as MLX evaluates it: in the promoted dtype, one rounding."""
+    dt = torch.promote_types(a.dtype, b.dtype)
+    return (a.to(torch.float32) + b.to(torch.float32)).to(dt)
+
+
+def qwen3_layer(p: Dict[str, torch.Tensor], nh: int, nkv: int, hd: int, eps: float, hidden: torch.Tensor,
+                target_ctx: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """``Qwen3DSparkLayer.__call__`` (``qwen3.py:165-167``): ``p`` holds the attention's weights,
+    ``input_layernorm``, ``post_attention_layernorm``, ``gate_proj``, ``up_proj``, ``down_proj``."""
+    a = qwen3_attention(p, nh, nkv, hd, eps, rms_norm(hidden, p["input_layernorm"], eps), target_ctx, cos, sin)
+    hidden = _add(hidden, a)
+    return _add(hidden, _qwen3_mlp(p, rms_norm(hidden, p["post_attention_layernorm"], eps)))
+
+
+def qwen3_layer_cached(p: Dict[str, torch.Tensor], nh: int, nkv: int, hd: int, eps: float, hidden: torch.Tensor,
+                       ctx_k: Optional[torch.Tensor], ctx_v: Optional[torch.Tensor], cos: torch.Tensor,
+                       sin: torch.Tensor) -> torch.Tensor:
+    """``Qwen3DSparkLayer.forward_cached`` (``qwen3.py:174-176``)."""
+    a = qwen3_attend_cached(p, nh, nkv, hd, eps, rms_norm(hidden, p["input_layernorm"], eps), ctx_k, ctx_v, cos, sin)
+    hidden = _add(hidden, a)
+    return _add(hidden, _qwen3_mlp(p, rms_norm(hidden, p["post_attention_layernorm"], eps)))

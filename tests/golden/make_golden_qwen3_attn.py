@@ -7,7 +7,10 @@ by ``mlx_torch_shim``. Each case records
 * the cached path: ``context_kv`` of the committed context in two pieces (as
   ``extend_context`` appends them), then ``attend_cached`` of the block at its own absolute
   positions, and ``attend_cached`` with no context at all.
-Everything goes to ``qwen3_attn_*.npz`` next to this script; the tests read only the fixtures.
+Layer cases run the whole ``Qwen3DSparkLayer`` (``qwen3.py:157-176``: RMSNorms, residual adds,
+the attention and the MLP) on the full and the cached path. Everything goes to
+``qwen3_attn_*.npz`` / ``qwen3_layer_*.npz`` next to this script; the tests read only the
+fixtures.
 
     python tests/golden/make_golden_qwen3_attn.py [--reference PATH]
 """
@@ -95,6 +98,58 @@ def build_case(q3, spec: dict, rng) -> dict:
     return out
 
 
+LAYER_CASES = {
+    "qwen3_layer_bf16_b2_c9": dict(dtype=torch.bfloat16, b=2, block=7, ctx=9, inter=160),
+    "qwen3_layer_f32_b1_c4": dict(dtype=torch.float32, b=1, block=3, ctx=4, inter=64),
+}
+
+
+def build_layer_case(q3, spec: dict, rng) -> dict:
+    mx = shim
+    dt = spec["dtype"]
+    args = q3.Qwen3DSparkArgs.from_dict(dict(DIMS, intermediate_size=spec["inter"]))
+    layer = q3.Qwen3DSparkLayer(args)
+    h, nh, nkv, hd = (DIMS[k] for k in ("hidden_size", "num_attention_heads", "num_key_value_heads", "head_dim"))
+    inter = spec["inter"]
+
+    def w(*shape, std):
+        return torch.from_numpy((rng.standard_normal(shape) * std).astype(np.float32)).to(dt)
+
+    weights = {"q_proj": w(nh * hd, h, std=h ** -0.5), "k_proj": w(nkv * hd, h, std=h ** -0.5),
+               "v_proj": w(nkv * hd, h, std=h ** -0.5), "o_proj": w(h, nh * hd, std=(nh * hd) ** -0.5),
+               "gate_proj": w(inter, h, std=h ** -0.5), "up_proj": w(inter, h, std=h ** -0.5),
+               "down_proj": w(h, inter, std=inter ** -0.5)}
+    norms = {"q_norm": (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32),
+             "k_norm": (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32),
+             "input_layernorm": (1 + 0.1 * rng.standard_normal(h)).astype(np.float32),
+             "post_attention_layernorm": (1 + 0.1 * rng.standard_normal(h)).astype(np.float32)}
+    for k in ("q_proj", "k_proj", "v_proj", "o_proj"):
+        getattr(layer.self_attn, k).weight = mx.array(weights[k])
+    for k in ("gate_proj", "up_proj", "down_proj"):
+        getattr(layer.mlp, k).weight = mx.array(weights[k])
+    layer.self_attn.q_norm.weight = mx.array(norms["q_norm"])
+    layer.self_attn.k_norm.weight = mx.array(norms["k_norm"])
+    layer.input_layernorm.weight = mx.array(norms["input_layernorm"])
+    layer.post_attention_layernorm.weight = mx.array(norms["post_attention_layernorm"])
+
+    def raw(t):
+        tt = t.t if isinstance(t, shim.array) else t
+        return tt.view(torch.int16).numpy() if tt.dtype == torch.bfloat16 else tt.to(torch.float32).numpy()
+
+    b, block, ctx = spec["b"], spec["block"], spec["ctx"]
+    out = {"dtype_bf16": np.array(dt == torch.bfloat16), **{k: raw(v) for k, v in weights.items()}, **norms}
+    hidden = torch.from_numpy(rng.standard_normal((b, block, h)).astype(np.float32)).to(dt)
+    target = torch.from_numpy(rng.standard_normal((b, ctx, h)).astype(np.float32)).to(dt)
+    out["hidden"], out["target_ctx"] = raw(hidden), raw(target)
+    cos, sin = q3.rope_tables(mx.arange(ctx + block), hd, DIMS["rope_theta"])
+    out["full_out"] = raw(layer(mx.array(hidden), mx.array(target), cos, sin))
+    c, s = q3.rope_tables(mx.arange(ctx), hd, DIMS["rope_theta"])
+    ck, cv = layer.context_kv(mx.array(target), c, s)
+    c, s = q3.rope_tables(mx.arange(ctx, ctx + block), hd, DIMS["rope_theta"])
+    out["cached_out"] = raw(layer.forward_cached(mx.array(hidden), ck, cv, c, s))
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -103,6 +158,12 @@ def main() -> None:
     rng = np.random.default_rng(20263)
     for name, spec in CASES.items():
         case = build_case(q3, spec, rng)
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, **case)
+        print("wrote", path, sorted(k for k in case if k.endswith("_out")))
+    rng = np.random.default_rng(20264)
+    for name, spec in LAYER_CASES.items():
+        case = build_layer_case(q3, spec, rng)
         path = os.path.join(HERE, f"{name}.npz")
         np.savez_compressed(path, **case)
         print("wrote", path, sorted(k for k in case if k.endswith("_out")))

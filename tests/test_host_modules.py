@@ -57,3 +57,13 @@ def test_qwen3_rope_tables_match_the_oracle():
         mine = rope_tables(pos, 128, 1000000.0)
         ref = oracle.qwen3_rope_tables(pos, 128, 1000000.0)
         assert torch.equal(mine[0], ref[0]) and torch.equal(mine[1], ref[1])
+
+
+def test_qwen3_layer_rejects_cpu_tensors():
+    from dsm.qwen3_layer import Qwen3DSparkLayer
+
+    layer = Qwen3DSparkLayer(dict(QWEN3_ARGS, intermediate_size=128))
+    with pytest.raises(ValueError, match="GPU"):
+        layer(torch.zeros(1, 4, 96), torch.zeros(1, 5, 96), torch.zeros(9, 32), torch.zeros(9, 32))
+    with pytest.raises(ValueError, match="GPU"):
+        layer.forward_cached(torch.zeros(1, 4, 96), None, None, torch.zeros(4, 32), torch.zeros(4, 32))

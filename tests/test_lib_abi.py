@@ -142,6 +142,10 @@ def test_gqa_attention_entry_points_reject_bad_arguments_on_the_host():
                                None) != 0
     assert L.dsm_linear_splitk(1, 1, 1 << 10, 2560, _lib.WFMT_AFFINE8, 64, 1, 1024, 1, 512, 112, 1, 1 << 30,
                                None) != 0  # ldo < out_dim
+    # residual add + RMSNorm: nothing to write, a norm without weights, an unsupported dtype
+    assert L.dsm_add_rms_norm(1, 1, bf, 4, 64, None, 1e-6, None, None, None) != 0
+    assert L.dsm_add_rms_norm(1, 1, bf, 4, 64, None, 1e-6, None, 1, None) != 0
+    assert L.dsm_add_rms_norm(1, 1, _lib.DT_I32, 4, 64, 1, 1e-6, 1, 1, None) != 0
     assert L.dsm_gqa_attn_workspace_bytes(1, 7, 6, 4, 128, 0) == 0
 
 

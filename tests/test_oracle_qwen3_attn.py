@@ -1,7 +1,8 @@
 """The oracle's restatement of the Qwen3 DSpark draft attention against golden vectors from the
 reference's own ``Qwen3DSparkAttention`` (``dspark_mlx/arch/qwen3.py:85-143``): the full path
 over ``[context || block]``, the cached context K/V built in two appends, and the cached
-attention with and without a context (``tests/golden/make_golden_qwen3_attn.py``)."""
+attention with and without a context; and the whole draft layer (``Qwen3DSparkLayer``,
+``qwen3.py:157-176``) on both paths (``tests/golden/make_golden_qwen3_attn.py``)."""
 
 from __future__ import annotations
 
@@ -16,6 +17,9 @@ import oracle
 
 HERE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(HERE, "qwen3_attn_*.npz")))
+LAYER_CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(HERE, "qwen3_layer_*.npz")))
+LAYER_KEYS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "q_norm", "k_norm",
+              "input_layernorm", "post_attention_layernorm")
 DIMS = dict(nh=4, nkv=2, hd=32, eps=1e-6, theta=1000000.0)
 
 
@@ -30,7 +34,23 @@ def _weights(z):
 
 
 def test_golden_cases_exist():
-    assert len(CASES) == 2
+    assert len(CASES) == 2 and len(LAYER_CASES) == 2
+
+
+@pytest.mark.parametrize("name", LAYER_CASES)
+def test_layer_oracle_matches_reference_goldens(name):
+    z = dict(np.load(os.path.join(HERE, name + ".npz")))
+    p = {k: _t(z[k]) for k in LAYER_KEYS}
+    nh, nkv, hd, eps, theta = (DIMS[k] for k in ("nh", "nkv", "hd", "eps", "theta"))
+    hidden, target = _t(z["hidden"]), _t(z["target_ctx"])
+    q, ctx = hidden.shape[1], target.shape[1]
+    cos, sin = oracle.qwen3_rope_tables(torch.arange(ctx + q), hd, theta)
+    full = oracle.qwen3_layer(p, nh, nkv, hd, eps, hidden, target, cos, sin)
+    assert full.dtype == hidden.dtype and torch.equal(full, _t(z["full_out"]))
+    c, s = oracle.qwen3_rope_tables(torch.arange(ctx), hd, theta)
+    ck, cv = oracle.qwen3_context_kv(p, nkv, hd, eps, target, c, s)
+    c, s = oracle.qwen3_rope_tables(torch.arange(ctx, ctx + q), hd, theta)
+    assert torch.equal(oracle.qwen3_layer_cached(p, nh, nkv, hd, eps, hidden, ck, cv, c, s), _t(z["cached_out"]))
 
 
 @pytest.mark.parametrize("name", CASES)
