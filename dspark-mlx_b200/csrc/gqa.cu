@@ -1,4 +1,4 @@
-// The Qwen3 DSpark draft attention (dspark_mlx/arch/qwen3.py:85-143): grouped-query attention
+// The Qwen3 DSpark draft attention (dspark_mlx/arch/qwen3.py:84-143): grouped-query attention
 // of the draft block over [context || block], around the packed-weight projections
 // (dsm_linear):
 //
@@ -6,12 +6,12 @@
 //                      lo rows of an fp32 input staged hi + lo): every head rounded to the
 //                      activation dtype; the q and k heads RMSNormed with their weights
 //                      (norm_rope.py:22-39) and rotated by NeoX half-split RoPE with the
-//                      tables cast to the activation dtype (qwen3.py:65-75); q heads written
+//                      tables cast to the activation dtype (qwen3.py:64-73); q heads written
 //                      [n, n_q, head_dim], k and v heads into [batch, n_kv, cap, head_dim]
-//                      caches at rows row0 + t (qwen3.py:96-108, 121-137).
+//                      caches at rows row0 + t (qwen3.py:97-108, 122-137).
 //   dsm_gqa_attn       softmax(q k^T * scale) v of every query head over its KV head's
 //                      context rows and then the block's own rows, with no mask
-//                      (mx.fast.scaled_dot_product_attention, qwen3.py:111-115, 138-143),
+//                      (mx.fast.scaled_dot_product_attention, qwen3.py:114-116, 141-143),
 //                      written [batch, block, n_heads * head_dim] for o_proj.
 //
 // The attention is split over keys. A CTA holds one KV head's query rows (the group's heads

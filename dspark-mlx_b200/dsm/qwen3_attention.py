@@ -1,14 +1,14 @@
 """The Qwen3 DSpark draft attention on the GPU: ``Qwen3DSparkAttention``
-(``dspark_mlx/arch/qwen3.py:85-143``).
+(``dspark_mlx/arch/qwen3.py:84-143``).
 
 Same constructor (``Qwen3DSparkAttention(args)``), parameter names (``q_proj``, ``k_proj``,
 ``v_proj``, ``o_proj``, ``q_norm``, ``k_norm``) and calls as the reference:
 
 * ``attn(hidden [b, q, hidden], target_ctx [b, ctx, hidden], cos_full, sin_full)``: the block
   over ``[context || block]``; the tables have ``ctx + q`` rows and the block's queries take
-  the last ``q`` (``qwen3.py:96-116``);
+  the last ``q`` (``qwen3.py:97-116``);
 * ``context_kv(proj_ctx [b, n, hidden], cos, sin)`` -> RoPE'd ``(k, v)`` ``[b, n_kv, n,
-  head_dim]`` (``qwen3.py:121-128``); ``out=(k_cache, v_cache), row0=`` writes them into
+  head_dim]`` (``qwen3.py:122-128``); ``out=(k_cache, v_cache), row0=`` writes them into
   rows ``row0 ..`` of preallocated ``[b, n_kv, cap, head_dim]`` caches instead;
 * ``attend_cached(noise, ctx_k, ctx_v, cos, sin)``: the block over cached context K/V
   (``None`` for none; any view whose rows are ``head_dim`` contiguous values) and its own
@@ -36,7 +36,7 @@ from .qwen3 import Projection
 
 
 def rope_tables(position_ids, head_dim: int, theta: float) -> Tuple[torch.Tensor, torch.Tensor]:
-    """``rope_tables`` (``qwen3.py:77-82``): cos/sin ``[len(position_ids), head_dim]`` in fp32,
+    """``rope_tables`` (``qwen3.py:76-81``): cos/sin ``[len(position_ids), head_dim]`` in fp32,
     computed on the CPU as the reference computes them."""
     pos = torch.as_tensor(position_ids).cpu()
     inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2).to(torch.float32) / head_dim))

@@ -39,7 +39,7 @@
  *                       DSparkAttention.__call__ / advance_window around dsm_linear
  *                       (model/attention.py:27-142, kernels.py:20-57, norm_rope.py:22-77)
  *   dsm_qkv_norm_rope, dsm_gqa_attn: Qwen3DSparkAttention.__call__ / context_kv /
- *                       attend_cached around dsm_linear (arch/qwen3.py:65-143)
+ *                       attend_cached around dsm_linear (arch/qwen3.py:64-143)
  *   dsm_add_rms_norm    the residual adds and RMSNorms of Qwen3DSparkLayer (arch/qwen3.py:157-176)
  *   dsm_gather_rows, dsm_segment_ids: expert-parallel plumbing; the reference runs on one
  *                       device (tests/reference_model.py:55-56 forces world_size 1) and has
@@ -297,8 +297,8 @@ int dsm_sparse_attn(const void* q, const void* window_kv, const void* block_kv, 
 int dsm_round_rows(const float* in, const float* in_lo, int64_t n, void* out, int out_dtype, void* stream);
 
 /* ---- the Qwen3 draft attention (grouped-query) ------------------------------------------------
- * Qwen3DSparkAttention (arch/qwen3.py:85-143) around dsm_linear. cos_t / sin_t are the
- * caller's [tab_rows, head_dim] fp32 tables (rope_tables, qwen3.py:77-82).
+ * Qwen3DSparkAttention (arch/qwen3.py:84-143) around dsm_linear. cos_t / sin_t are the
+ * caller's [tab_rows, head_dim] fp32 tables (rope_tables, qwen3.py:76-81).
  * qkv_norm_rope: in [n_rows, (n_q + 2 n_kv) * head_dim] fp32 (+ in_lo) holds q, k, v heads in
  *   that order. Row r is token t = r % period of sequence b = r / period. Every head is
  *   rounded to T; q and k heads get RMSNorm with q_norm_w / k_norm_w (head_dim fp32) and NeoX

@@ -1,14 +1,14 @@
 """CPU oracle for the Qwen3 DSpark draft attention (test infrastructure only).
 
-Restates ``Qwen3DSparkAttention`` (``dspark_mlx/arch/qwen3.py:85-143``) in PyTorch on the
+Restates ``Qwen3DSparkAttention`` (``dspark_mlx/arch/qwen3.py:84-143``) in PyTorch on the
 CPU with MLX's dtype rules:
 * grouped-query attention, ``num_attention_heads`` query heads over ``num_key_value_heads``
   KV heads;
 * per-head RMSNorm on q and k;
-* NeoX half-split RoPE (``qwen3.py:65-82``), whose tables are cast to the activation dtype
+* NeoX half-split RoPE (``qwen3.py:64-81``), whose tables are cast to the activation dtype
   before the rotation;
 * unmasked scaled dot-product attention of the draft block over ``[context || block]``;
-* the cached form, whose context K/V are projected once and reused (``qwen3.py:121-143``).
+* the cached form, whose context K/V are projected once and reused (``qwen3.py:122-143``).
 
 The attention is softmax(q k^T * scale) v accumulated in fp32 with q's dtype out, as
 ``mx.fast.scaled_dot_product_attention`` documents.
@@ -31,7 +31,7 @@ __all__ = ["qwen3_rope_tables", "qwen3_apply_rope", "qwen3_sdpa", "qwen3_attenti
 
 
 def qwen3_rope_tables(position_ids: torch.Tensor, head_dim: int, theta: float) -> Tuple[torch.Tensor, torch.Tensor]:
-    """``rope_tables`` (``qwen3.py:77-82``): cos/sin ``[len(position_ids), head_dim]``."""
+    """``rope_tables`` (``qwen3.py:76-81``): cos/sin ``[len(position_ids), head_dim]``."""
     inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2).to(torch.float32) / head_dim))
     freqs = position_ids.to(torch.float32)[:, None] * inv_freq[None, :]
     emb = torch.cat([freqs, freqs], dim=-1)
@@ -44,7 +44,7 @@ def _rotate_half(x: torch.Tensor) -> torch.Tensor:
 
 
 def qwen3_apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """``_apply_rope`` (``qwen3.py:70-75``): x ``[b, seq, heads, hd]``, all in x's dtype."""
+    """``_apply_rope`` (``qwen3.py:69-73``): x ``[b, seq, heads, hd]``, all in x's dtype."""
     c = cos[None, :, None, :].to(x.dtype)
     s = sin[None, :, None, :].to(x.dtype)
     return x * c + _rotate_half(x) * s
@@ -66,7 +66,7 @@ def _heads_norm(x: torch.Tensor, heads: int, hd: int, w: torch.Tensor, eps: floa
 
 def qwen3_attention(p: Dict[str, torch.Tensor], nh: int, nkv: int, hd: int, eps: float, hidden: torch.Tensor,
                     target_ctx: torch.Tensor, cos_full: torch.Tensor, sin_full: torch.Tensor) -> torch.Tensor:
-    """``Qwen3DSparkAttention.__call__`` (``qwen3.py:96-116``)."""
+    """``Qwen3DSparkAttention.__call__`` (``qwen3.py:97-116``)."""
     b, q, _ = hidden.shape
     ctx = target_ctx.shape[1]
     qh = _heads_norm(linear(hidden, p["q_proj"]), nh, hd, p["q_norm"], eps)
@@ -81,7 +81,7 @@ def qwen3_attention(p: Dict[str, torch.Tensor], nh: int, nkv: int, hd: int, eps:
 
 def qwen3_context_kv(p: Dict[str, torch.Tensor], nkv: int, hd: int, eps: float, proj_ctx: torch.Tensor,
                      cos: torch.Tensor, sin: torch.Tensor):
-    """``context_kv`` (``qwen3.py:121-128``): RoPE'd context K, V ``[b, nkv, n, hd]``."""
+    """``context_kv`` (``qwen3.py:122-128``): RoPE'd context K, V ``[b, nkv, n, hd]``."""
     k = _heads_norm(linear(proj_ctx, p["k_proj"]), nkv, hd, p["k_norm"], eps)
     b, n, _ = proj_ctx.shape
     v = linear(proj_ctx, p["v_proj"]).reshape(b, n, nkv, hd)

@@ -1,5 +1,5 @@
 """The oracle's restatement of the Qwen3 DSpark draft attention against golden vectors from the
-reference's own ``Qwen3DSparkAttention`` (``dspark_mlx/arch/qwen3.py:85-143``): the full path
+reference's own ``Qwen3DSparkAttention`` (``dspark_mlx/arch/qwen3.py:84-143``): the full path
 over ``[context || block]``, the cached context K/V built in two appends, and the cached
 attention with and without a context; and the whole draft layer (``Qwen3DSparkLayer``,
 ``qwen3.py:157-176``) on both paths (``tests/golden/make_golden_qwen3_attn.py``)."""
