@@ -51,7 +51,7 @@ def test_reference_dequant_unit_tests(reference):
 
 def test_qwen3_attention_oracle_matches_reference_torch_model(reference):
     """The reference pins its Qwen3 backbone to a torch transcription of DeepSpec's model
-    (``tests/qwen3_ref.py``, ``tests/test_qwen3_arch.py:30-66``): the rope tables against a
+    (``tests/qwen3_ref.py``, ``tests/test_qwen3_arch.py:30-60``): the rope tables against a
     numpy formula within 1e-5, the layer within 2e-3. The oracle's attention is held to the
     same torch model's ``RefAttn`` in fp32, on the reference test's shapes and weight scale."""
     import numpy as np
