@@ -113,48 +113,59 @@ class DSparkHead(nn.Module):
         used above temperature 0; drawn here when not given."""
         if not x.is_cuda:
             raise ValueError("DSparkHead runs on the GPU only: x must be a CUDA tensor")
-        b, s, hc, dim = x.shape
-        if hc != self.hc_mult or dim != self.dim:
-            raise ValueError(f"x must be [b, s, {self.hc_mult}, {self.dim}], got {tuple(x.shape)}")
-        if x.dtype not in (torch.bfloat16, torch.float32):
-            x = x.to(torch.float32)
-        x = x.contiguous()
-        dev = x.device
-        temp = float(self.temperature if temperature is None else temperature)
-        ids = input_ids.reshape(-1).contiguous()
-        if ids.dtype not in (torch.int32, torch.int64):
-            ids = ids.to(torch.int32)
-        if ids.numel() != b:
-            raise ValueError("input_ids must hold one anchor token per batch row")
-        if temp > 0 and uniforms is None:
-            uniforms = torch.rand(s, b, self.vocab, device=dev)
-        if uniforms is not None:
-            uniforms = uniforms.to(device=dev, dtype=torch.float32).contiguous()
-            if tuple(uniforms.shape) != (s, b, self.vocab):
-                raise ValueError(f"uniforms must be [{s}, {b}, {self.vocab}], got {tuple(uniforms.shape)}")
-        f32 = lambda t: t.detach().to(device=dev, dtype=torch.float32).contiguous()  # noqa: E731
-        fn, sc, base, nw = f32(self.hc_head_fn), f32(self.hc_head_scale), f32(self.hc_head_base), f32(self.norm.weight)
-        proj = self.confidence_head.proj
-        cw = f32(proj.weight.reshape(-1))
-        w1, w2, wdt = _markov_tables(self.markov_head.markov_w1.weight.detach().to(dev),
-                                     self.markov_head.markov_w2.weight.detach().to(dev))
-        hp = self.packed_head()
-        d = HeadDesc()
-        d.batch, d.block, d.hc_mult, d.dim, d.vocab, d.rank = b, s, hc, dim, self.vocab, self.rank
-        d.norm_eps, d.hc_eps = float(self.norm_eps), float(self.hc_eps)
-        d.hc_fn, d.hc_scale, d.hc_base, d.norm_weight = ptr(fn), ptr(sc), ptr(base), ptr(nw)
-        d.head_wfmt, d.head_group_size, d.head_w = hp.wfmt, hp.group_size, ptr(hp.packed)
-        d.markov_dtype, d.markov_w1, d.markov_w2 = wdt, ptr(w1), ptr(w2)
-        d.conf_w = ptr(cw)
-        d.conf_bias = float(proj.bias.reshape(-1)[0]) if hasattr(proj, "bias") else 0.0
-        L = lib()
-        need = L.dsm_draft_head_workspace_bytes(ctypes.byref(d), dtype_code(x.dtype))
-        if self._ws is None or self._ws.numel() < need or self._ws.device != dev:
-            self._ws = torch.empty(need, dtype=torch.uint8, device=dev)
-        out_ids = torch.empty(b, s + 1, dtype=torch.int32, device=dev)
-        biased = torch.empty(b, s, self.vocab, dtype=torch.float32, device=dev)
-        conf = torch.empty(b, s, dtype=torch.float32, device=dev)
-        check(L.dsm_draft_head(ctypes.byref(d), ptr(x), dtype_code(x.dtype), ptr(ids), dtype_code(ids.dtype), temp,
-                               ptr(uniforms), ptr(out_ids), ptr(biased), ptr(conf), None, ptr(self._ws),
-                               self._ws.numel(), stream_ptr()), "dsm_draft_head")
-        return out_ids, biased, conf
+        return run_draft_head(self, self.packed_head(), x, input_ids, temperature=temperature, uniforms=uniforms)
+
+
+def run_draft_head(owner, hp: PackedMatrix, x: torch.Tensor, input_ids: torch.Tensor, *,
+                   temperature: Optional[float] = None, uniforms: Optional[torch.Tensor] = None):
+    """The draft head of ``owner`` (a module with the head's parameters under the reference's
+    names: ``hc_head_fn`` / ``hc_head_scale`` / ``hc_head_base``, ``norm``, ``markov_head``,
+    ``confidence_head``, and the settings ``hc_mult``, ``dim``, ``vocab``, ``rank``,
+    ``temperature``, ``norm_eps``, ``hc_eps``; ``_ws`` caches the workspace) over the packed
+    LM head ``hp``."""
+    if not x.is_cuda:
+        raise ValueError("DSparkHead runs on the GPU only: x must be a CUDA tensor")
+    b, s, hc, dim = x.shape
+    if hc != owner.hc_mult or dim != owner.dim:
+        raise ValueError(f"x must be [b, s, {owner.hc_mult}, {owner.dim}], got {tuple(x.shape)}")
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        x = x.to(torch.float32)
+    x = x.contiguous()
+    dev = x.device
+    temp = float(owner.temperature if temperature is None else temperature)
+    ids = input_ids.reshape(-1).contiguous()
+    if ids.dtype not in (torch.int32, torch.int64):
+        ids = ids.to(torch.int32)
+    if ids.numel() != b:
+        raise ValueError("input_ids must hold one anchor token per batch row")
+    if temp > 0 and uniforms is None:
+        uniforms = torch.rand(s, b, owner.vocab, device=dev)
+    if uniforms is not None:
+        uniforms = uniforms.to(device=dev, dtype=torch.float32).contiguous()
+        if tuple(uniforms.shape) != (s, b, owner.vocab):
+            raise ValueError(f"uniforms must be [{s}, {b}, {owner.vocab}], got {tuple(uniforms.shape)}")
+    f32 = lambda t: t.detach().to(device=dev, dtype=torch.float32).contiguous()  # noqa: E731
+    fn, sc, base, nw = f32(owner.hc_head_fn), f32(owner.hc_head_scale), f32(owner.hc_head_base), f32(owner.norm.weight)
+    proj = owner.confidence_head.proj
+    cw = f32(proj.weight.reshape(-1))
+    w1, w2, wdt = _markov_tables(owner.markov_head.markov_w1.weight.detach().to(dev),
+                                 owner.markov_head.markov_w2.weight.detach().to(dev))
+    d = HeadDesc()
+    d.batch, d.block, d.hc_mult, d.dim, d.vocab, d.rank = b, s, hc, dim, owner.vocab, owner.rank
+    d.norm_eps, d.hc_eps = float(owner.norm_eps), float(owner.hc_eps)
+    d.hc_fn, d.hc_scale, d.hc_base, d.norm_weight = ptr(fn), ptr(sc), ptr(base), ptr(nw)
+    d.head_wfmt, d.head_group_size, d.head_w = hp.wfmt, hp.group_size, ptr(hp.packed)
+    d.markov_dtype, d.markov_w1, d.markov_w2 = wdt, ptr(w1), ptr(w2)
+    d.conf_w = ptr(cw)
+    d.conf_bias = float(proj.bias.reshape(-1)[0]) if hasattr(proj, "bias") else 0.0
+    L = lib()
+    need = L.dsm_draft_head_workspace_bytes(ctypes.byref(d), dtype_code(x.dtype))
+    if owner._ws is None or owner._ws.numel() < need or owner._ws.device != dev:
+        owner._ws = torch.empty(need, dtype=torch.uint8, device=dev)
+    out_ids = torch.empty(b, s + 1, dtype=torch.int32, device=dev)
+    biased = torch.empty(b, s, owner.vocab, dtype=torch.float32, device=dev)
+    conf = torch.empty(b, s, dtype=torch.float32, device=dev)
+    check(L.dsm_draft_head(ctypes.byref(d), ptr(x), dtype_code(x.dtype), ptr(ids), dtype_code(ids.dtype), temp,
+                           ptr(uniforms), ptr(out_ids), ptr(biased), ptr(conf), None, ptr(owner._ws),
+                           owner._ws.numel(), stream_ptr()), "dsm_draft_head")
+    return out_ids, biased, conf

@@ -67,3 +67,20 @@ def test_qwen3_layer_rejects_cpu_tensors():
         layer(torch.zeros(1, 4, 96), torch.zeros(1, 5, 96), torch.zeros(9, 32), torch.zeros(9, 32))
     with pytest.raises(ValueError, match="GPU"):
         layer.forward_cached(torch.zeros(1, 4, 96), None, None, torch.zeros(4, 32), torch.zeros(4, 32))
+
+
+def test_draft_block_rejects_cpu_tensors_and_wrong_stages():
+    from dsm.draft_block import DSparkBlock
+    from test_oracle_draft_block import ARGS
+
+    blk = DSparkBlock(ARGS, 0, max_seq_len=16)
+    with pytest.raises(ValueError, match="GPU"):
+        blk(torch.zeros(1, 5, 4, 256), 3, torch.zeros(1, dtype=torch.int32), torch.zeros(1, 1, 256))
+    with pytest.raises(ValueError, match="GPU"):
+        blk.forward_embed(torch.zeros(1, 3, 768), torch.zeros(1, dtype=torch.int32), blk.main_proj)
+    later = DSparkBlock(dict(ARGS, n_mtp_layers=3), 1, max_seq_len=16)
+    assert not hasattr(later, "main_proj") and not hasattr(later, "markov_head")
+    with pytest.raises(ValueError, match="stage 0"):
+        later.forward_embed(torch.zeros(1, 3, 768), torch.zeros(1, dtype=torch.int32), None)
+    with pytest.raises(ValueError, match="last stage"):
+        later.forward_head(torch.zeros(1, 5, 4, 256), torch.zeros(1, dtype=torch.int32), None)
