@@ -116,12 +116,13 @@ def test_markov_head_matches_oracle(dtype):
     torch.testing.assert_close(logits.cpu(), rl, rtol=1e-5, atol=1e-5)
 
 
-@pytest.mark.parametrize("temperature", [0.0, 0.7])
-def test_draft_head_large_batch_and_vocab(temperature):
-    """DeepSeek-V4 widths (dim 4096, hc 4, rank 256) with a 32000-word vocabulary, 8 x 7
-    draft tokens, bf16 weights and activations, a confidence bias."""
-    g = torch.Generator().manual_seed(5)
-    b, s, hc, dim, vocab, rank = 8, 7, 4, 4096, 32000, 256
+@pytest.mark.parametrize("b,temperature", [(8, 0.0), (8, 0.7), (20, 0.0), (32, 0.7)])
+def test_draft_head_large_batch_and_vocab(b, temperature):
+    """DeepSeek-V4 widths (dim 4096, hc 4, rank 256) with a 32000-word vocabulary, b x 7 draft
+    tokens, bf16 weights and activations, a confidence bias. Batches above 8 run the walk's
+    32-row instance (four 8-row tensor-core tiles, the last ones partly padding)."""
+    g = torch.Generator().manual_seed(5 + b)
+    s, hc, dim, vocab, rank = 7, 4, 4096, 32000, 256
     c = {"x": torch.randn(b, s, hc, dim, generator=g).to(torch.bfloat16),
          "fn": torch.randn(hc, hc * dim, generator=g) * 0.02, "scale": torch.randn(1, generator=g),
          "base": torch.randn(hc, generator=g) * 0.5, "norm_w": 1 + 0.1 * torch.randn(dim, generator=g),
