@@ -27,7 +27,8 @@ from .attention_oracle import linear
 from .block_oracle import rms_norm
 
 __all__ = ["qwen3_rope_tables", "qwen3_apply_rope", "qwen3_sdpa", "qwen3_attention", "qwen3_context_kv",
-           "qwen3_attend_cached", "qwen3_layer", "qwen3_layer_cached"]
+           "qwen3_attend_cached", "qwen3_layer", "qwen3_layer_cached", "qwen3_layer_params", "qwen3_project_context",
+           "qwen3_backbone"]
 
 
 def qwen3_rope_tables(position_ids: torch.Tensor, head_dim: int, theta: float) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -139,3 +140,25 @@ def qwen3_layer_cached(p: Dict[str, torch.Tensor], nh: int, nkv: int, hd: int, e
     a = qwen3_attend_cached(p, nh, nkv, hd, eps, rms_norm(hidden, p["input_layernorm"], eps), ctx_k, ctx_v, cos, sin)
     hidden = _add(hidden, a)
     return _add(hidden, _qwen3_mlp(p, rms_norm(hidden, p["post_attention_layernorm"], eps)))
+
+
+def qwen3_layer_params(t: Dict[str, torch.Tensor], i: int) -> Dict[str, torch.Tensor]:
+    """Layer ``i``'s tensors under the short names the layer functions take, from the
+    backbone's reference names (``layers.{i}.self_attn.q_proj.weight`` -> ``q_proj`` ...)."""
+    pre = f"layers.{i}."
+    return {k[len(pre):].split(".")[-2]: v for k, v in t.items() if k.startswith(pre)}
+
+
+def qwen3_project_context(t: Dict[str, torch.Tensor], eps: float, target_hidden: torch.Tensor) -> torch.Tensor:
+    """``Qwen3Backbone.project_context`` (``qwen3.py:189-191``): ``hidden_norm(fc(target_hidden))``."""
+    return rms_norm(linear(target_hidden, t["fc.weight"]), t["hidden_norm.weight"], eps)
+
+
+def qwen3_backbone(t: Dict[str, torch.Tensor], n_layers: int, nh: int, nkv: int, hd: int, eps: float,
+                   noise_embed: torch.Tensor, target_ctx: torch.Tensor, cos: torch.Tensor,
+                   sin: torch.Tensor) -> torch.Tensor:
+    """``Qwen3Backbone.__call__`` (``qwen3.py:193-197``): the layers, then the final norm."""
+    h = noise_embed
+    for i in range(n_layers):
+        h = qwen3_layer(qwen3_layer_params(t, i), nh, nkv, hd, eps, h, target_ctx, cos, sin)
+    return rms_norm(h, t["norm.weight"], eps)

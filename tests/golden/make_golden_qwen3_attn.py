@@ -8,9 +8,10 @@ by ``mlx_torch_shim``. Each case records
   ``extend_context`` appends them), then ``attend_cached`` of the block at its own absolute
   positions, and ``attend_cached`` with no context at all.
 Layer cases run the whole ``Qwen3DSparkLayer`` (``qwen3.py:157-176``: RMSNorms, residual adds,
-the attention and the MLP) on the full and the cached path. Everything goes to
-``qwen3_attn_*.npz`` / ``qwen3_layer_*.npz`` next to this script; the tests read only the
-fixtures.
+the attention and the MLP) on the full and the cached path; backbone cases run
+``Qwen3Backbone`` (``qwen3.py:178-197``: the context projection, the layers, the final norm).
+Everything goes to ``qwen3_attn_*.npz`` / ``qwen3_layer_*.npz`` / ``qwen3_backbone_*.npz``
+next to this script; the tests read only the fixtures.
 
     python tests/golden/make_golden_qwen3_attn.py [--reference PATH]
 """
@@ -150,6 +151,63 @@ def build_layer_case(q3, spec: dict, rng) -> dict:
     return out
 
 
+BACKBONE_CASES = {
+    "qwen3_backbone_bf16_b2_c6": dict(dtype=torch.bfloat16, b=2, block=7, ctx=6, inter=160, layers=2, targets=3),
+}
+
+
+def build_backbone_case(q3, spec: dict, rng) -> dict:
+    """``Qwen3Backbone`` (``qwen3.py:178-197``): project_context, then the layers and the norm."""
+    mx = shim
+    dt = spec["dtype"]
+    args = q3.Qwen3DSparkArgs.from_dict(dict(DIMS, intermediate_size=spec["inter"], num_hidden_layers=spec["layers"],
+                                             target_layer_ids=list(range(spec["targets"]))))
+    bb = q3.Qwen3Backbone(args)
+    h, nh, nkv, hd = (DIMS[k] for k in ("hidden_size", "num_attention_heads", "num_key_value_heads", "head_dim"))
+    inter, fc_in = spec["inter"], h * spec["targets"]
+
+    def w(*shape, std):
+        return torch.from_numpy((rng.standard_normal(shape) * std).astype(np.float32)).to(dt)
+
+    def norm(n):
+        return (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+
+    def raw(t):
+        tt = t.t if isinstance(t, shim.array) else t
+        if isinstance(tt, np.ndarray):
+            return tt
+        return tt.view(torch.int16).numpy() if tt.dtype == torch.bfloat16 else tt.to(torch.float32).numpy()
+
+    out = {"dtype_bf16": np.array(dt == torch.bfloat16)}
+    t = {"fc.weight": w(h, fc_in, std=fc_in ** -0.5), "hidden_norm.weight": norm(h), "norm.weight": norm(h)}
+    for i in range(spec["layers"]):
+        p = f"layers.{i}."
+        t.update({p + "self_attn.q_proj.weight": w(nh * hd, h, std=h ** -0.5),
+                  p + "self_attn.k_proj.weight": w(nkv * hd, h, std=h ** -0.5),
+                  p + "self_attn.v_proj.weight": w(nkv * hd, h, std=h ** -0.5),
+                  p + "self_attn.o_proj.weight": w(h, nh * hd, std=(nh * hd) ** -0.5),
+                  p + "self_attn.q_norm.weight": norm(hd), p + "self_attn.k_norm.weight": norm(hd),
+                  p + "mlp.gate_proj.weight": w(inter, h, std=h ** -0.5), p + "mlp.up_proj.weight": w(inter, h, std=h ** -0.5),
+                  p + "mlp.down_proj.weight": w(h, inter, std=inter ** -0.5),
+                  p + "input_layernorm.weight": norm(h), p + "post_attention_layernorm.weight": norm(h)})
+    for name, v in t.items():
+        *path, leaf = name.split(".")
+        obj = bb
+        for part in path:
+            obj = obj[int(part)] if isinstance(obj, list) else getattr(obj, part)
+        setattr(obj, leaf, mx.array(v))
+    out.update({k: raw(v) for k, v in t.items()})
+    b, block, ctx = spec["b"], spec["block"], spec["ctx"]
+    target_hidden = w(b, ctx, fc_in, std=1.0)
+    noise = w(b, block, h, std=1.0)
+    out["target_hidden"], out["noise_embed"] = raw(target_hidden), raw(noise)
+    tctx = bb.project_context(mx.array(target_hidden))
+    out["target_ctx"] = raw(tctx)
+    cos, sin = q3.rope_tables(mx.arange(ctx + block), hd, DIMS["rope_theta"])
+    out["full_out"] = raw(bb(mx.array(noise), tctx, cos, sin))
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -164,6 +222,12 @@ def main() -> None:
     rng = np.random.default_rng(20264)
     for name, spec in LAYER_CASES.items():
         case = build_layer_case(q3, spec, rng)
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, **case)
+        print("wrote", path, sorted(k for k in case if k.endswith("_out")))
+    rng = np.random.default_rng(20266)
+    for name, spec in BACKBONE_CASES.items():
+        case = build_backbone_case(q3, spec, rng)
         path = os.path.join(HERE, f"{name}.npz")
         np.savez_compressed(path, **case)
         print("wrote", path, sorted(k for k in case if k.endswith("_out")))

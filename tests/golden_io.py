@@ -46,10 +46,10 @@ class GoldenCase:
 
 def names():
     """The MoE golden cases (the hyper-connection ``hc_*``, draft-head ``head_*`` and
-    draft-attention ``attn_*`` / ``qwen3_attn_*``, draft-layer ``qwen3_layer_*`` and draft-block
-    ``block_*`` fixtures have their own loaders)."""
+    draft-attention ``attn_*`` / ``qwen3_attn_*``, draft-layer ``qwen3_layer_*`` /
+    ``qwen3_backbone_*`` and draft-block ``block_*`` fixtures have their own loaders)."""
     return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))
-                  if not os.path.basename(p).startswith(("hc_", "head_", "attn_", "qwen3_attn_", "qwen3_layer_", "block_")))
+                  if not os.path.basename(p).startswith(("hc_", "head_", "attn_", "qwen3_attn_", "qwen3_layer_", "qwen3_backbone_", "block_")))
 
 
 def load(name: str) -> GoldenCase:

@@ -92,3 +92,41 @@ def test_qwen3_layer_matches_oracle_at_qwen3_4b_widths():
     ref = oracle.qwen3_layer_cached(w, nh, nkv, hd, 1e-6, hidden, rk, rv, cb, sb)
     assert max_rel_err(out, ref) < 2e-2, max_rel_err(out, ref)
     assert _lib.device_error() == 0
+
+
+BACKBONE_CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(HERE, "qwen3_backbone_*.npz")))
+
+
+@pytest.mark.parametrize("name", BACKBONE_CASES)
+def test_qwen3_backbone_matches_reference_goldens(name):
+    """``Qwen3Backbone``: the context projection, two layers and the final norm (bf16, 2e-2)."""
+    from dsm.qwen3_layer import Qwen3Backbone
+
+    z = dict(np.load(os.path.join(HERE, name + ".npz")))
+    t = {k: _t(v) for k, v in z.items() if k.endswith(".weight")}
+    n_layers = len({k.split(".")[1] for k in t if k.startswith("layers.")})
+    fc_in = t["fc.weight"].shape[1]
+    inter = t["layers.0.mlp.gate_proj.weight"].shape[0]
+    args = dict(hidden_size=96, num_attention_heads=DIMS["nh"], num_key_value_heads=DIMS["nkv"], head_dim=DIMS["hd"],
+                rms_norm_eps=DIMS["eps"], intermediate_size=inter, num_hidden_layers=n_layers,
+                target_layer_ids=list(range(fc_in // 96)))
+    bb = Qwen3Backbone(args).to(DEV)
+    for name_, v in t.items():
+        *path, leaf = name_.split(".")
+        obj = bb
+        for part in path:
+            obj = obj[int(part)] if part.isdigit() else getattr(obj, part)
+        if leaf == "weight" and isinstance(obj, torch.nn.Module) and v.dtype == torch.float32 and v.dim() == 1:
+            with torch.no_grad():
+                obj.weight.copy_(v)  # norm weights (fp32)
+        else:
+            setattr(obj, leaf, torch.nn.Parameter(v.to(DEV), requires_grad=False))
+    tctx = bb.project_context(_t(z["target_hidden"]).to(DEV))
+    noise = _t(z["noise_embed"])
+    q, ctx = noise.shape[1], tctx.shape[1]
+    out = bb(noise.to(DEV), tctx, *rope_tables(torch.arange(ctx + q), DIMS["hd"], DIMS["theta"]))
+    torch.cuda.synchronize()
+    assert max_rel_err(tctx, _t(z["target_ctx"])) < 2e-2
+    ref = _t(z["full_out"])
+    assert out.dtype == ref.dtype and max_rel_err(out, ref) < 2e-2, max_rel_err(out, ref)
+    assert _lib.device_error() == 0

@@ -18,6 +18,7 @@ import oracle
 HERE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(HERE, "qwen3_attn_*.npz")))
 LAYER_CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(HERE, "qwen3_layer_*.npz")))
+BACKBONE_CASES = sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(HERE, "qwen3_backbone_*.npz")))
 LAYER_KEYS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "q_norm", "k_norm",
               "input_layernorm", "post_attention_layernorm")
 DIMS = dict(nh=4, nkv=2, hd=32, eps=1e-6, theta=1000000.0)
@@ -34,7 +35,26 @@ def _weights(z):
 
 
 def test_golden_cases_exist():
-    assert len(CASES) == 2 and len(LAYER_CASES) == 2
+    assert len(CASES) == 2 and len(LAYER_CASES) == 2 and len(BACKBONE_CASES) == 1
+
+
+def backbone_tensors(z):
+    return {k: _t(v) for k, v in z.items() if k.endswith(".weight")}
+
+
+@pytest.mark.parametrize("name", BACKBONE_CASES)
+def test_backbone_oracle_matches_reference_goldens(name):
+    z = dict(np.load(os.path.join(HERE, name + ".npz")))
+    t = backbone_tensors(z)
+    nh, nkv, hd, eps, theta = (DIMS[k] for k in ("nh", "nkv", "hd", "eps", "theta"))
+    tctx = oracle.qwen3_project_context(t, eps, _t(z["target_hidden"]))
+    assert torch.equal(tctx, _t(z["target_ctx"]))
+    noise = _t(z["noise_embed"])
+    q, ctx = noise.shape[1], tctx.shape[1]
+    n_layers = len({k.split(".")[1] for k in t if k.startswith("layers.")})
+    cos, sin = oracle.qwen3_rope_tables(torch.arange(ctx + q), hd, theta)
+    out = oracle.qwen3_backbone(t, n_layers, nh, nkv, hd, eps, noise, tctx, cos, sin)
+    assert torch.equal(out, _t(z["full_out"]))
 
 
 @pytest.mark.parametrize("name", LAYER_CASES)
