@@ -91,3 +91,43 @@ def test_qwen3_attention_oracle_matches_reference_torch_model(reference):
     got = oracle.qwen3_attention(p, nh, nkv, hd, eps, noise, target, torch.from_numpy(cos_np),
                                  torch.from_numpy(sin_np))
     assert float((got - want).abs().max()) <= 1e-5 * float(want.abs().max())
+
+
+def test_qwen3_backbone_oracle_matches_reference_torch_model(reference):
+    """The reference's own backbone parity test (``tests/test_qwen3_arch.py:30-60``) holds the MLX
+    backbone to ``RefQwen3Backbone`` within 2e-3 on its shapes and weight scale; the oracle's
+    backbone is held to the same torch model in fp32, within 1e-5 relative."""
+    import sys
+    import types
+
+    import numpy as np
+    import torch
+
+    import oracle
+
+    shim_mods = {k: sys.modules.pop(k) for k in list(sys.modules) if k == "mlx" or k.startswith("mlx.")}
+    try:
+        ref = _load_test_module(os.path.join(REF, "tests", "qwen3_ref.py"))
+    finally:
+        sys.modules.update(shim_mods)
+    args = types.SimpleNamespace(hidden_size=32, num_attention_heads=4, num_key_value_heads=2, head_dim=16,
+                                 intermediate_size=24, num_hidden_layers=2, rms_norm_eps=1e-6, fc_in=64)
+    rng = np.random.default_rng(0)
+    bb = ref.RefQwen3Backbone(args)
+    weights = {k: torch.tensor((rng.standard_normal(tuple(v.shape)) * 0.05).astype(np.float32))
+               for k, v in bb.state_dict().items()}
+    for k in weights:
+        if k.endswith("norm.weight"):
+            weights[k] = weights[k] + 1
+    bb.load_state_dict(weights)
+    b, ctx, block = 1, 5, 3
+    noise = torch.tensor((rng.standard_normal((b, block, 32)) * 0.3).astype(np.float32))
+    target_hidden = torch.tensor((rng.standard_normal((b, ctx, 64)) * 0.3).astype(np.float32))
+    cos, sin = oracle.qwen3_rope_tables(torch.arange(ctx + block), 16, 1_000_000.0)
+    with torch.no_grad():
+        tctx_ref = bb.project_context(target_hidden)
+        want = bb(noise, tctx_ref, cos, sin)
+    tctx = oracle.qwen3_project_context(weights, 1e-6, target_hidden)
+    assert float((tctx - tctx_ref).abs().max()) <= 1e-5 * float(tctx_ref.abs().max())
+    got = oracle.qwen3_backbone(weights, 2, 4, 2, 16, 1e-6, noise, tctx, cos, sin)
+    assert float((got - want).abs().max()) <= 1e-5 * float(want.abs().max())
