@@ -130,3 +130,29 @@ def test_qwen3_backbone_matches_reference_goldens(name):
     ref = _t(z["full_out"])
     assert out.dtype == ref.dtype and max_rel_err(out, ref) < 2e-2, max_rel_err(out, ref)
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_add_rms_norm_entry_point(dtype):
+    """``dsm_add_rms_norm`` through the C ABI: s = x + delta rounded once, y = RMSNorm(s) * w, each
+    output optional; against the oracle's add and RMSNorm (bf16 within one rounding, fp32 1e-6)."""
+    from dsm._lib import dtype_code, lib, ptr, stream_ptr
+
+    g = torch.Generator().manual_seed(3)
+    n, dim = 37, 2560
+    x = torch.randn(n, dim, generator=g).to(dtype)
+    d = torch.randn(n, dim, generator=g).to(dtype)
+    w = 1 + 0.1 * torch.randn(dim, generator=g)
+    xs, ds, ws = x.to(DEV), d.to(DEV), w.to(DEV)
+    s, y, y0 = torch.empty_like(xs), torch.empty_like(xs), torch.empty_like(xs)
+    L = lib()
+    _lib.check(L.dsm_add_rms_norm(ptr(xs), ptr(ds), dtype_code(dtype), n, dim, ptr(ws), 1e-6, ptr(s), ptr(y),
+                                  stream_ptr()), "dsm_add_rms_norm")
+    _lib.check(L.dsm_add_rms_norm(ptr(xs), None, dtype_code(dtype), n, dim, ptr(ws), 1e-6, None, ptr(y0),
+                                  stream_ptr()), "dsm_add_rms_norm")
+    torch.cuda.synchronize()
+    ref_s = (x.float() + d.float()).to(dtype)
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-6
+    assert torch.equal(s.cpu(), ref_s)
+    assert max_rel_err(y, oracle.rms_norm(ref_s, w, 1e-6)) < tol
+    assert max_rel_err(y0, oracle.rms_norm(x, w, 1e-6)) < tol
