@@ -15,7 +15,7 @@
 //                       (kernels.py:20-57) over the window's filled slots and the block's own
 //                       rows (attention.py:65-69), then the inverse rotation of the output
 //                       (attention.py:117); written group-major for the grouped output
-//                       projection (attention.py:119-121).
+//                       projection (attention.py:124-128).
 //
 // Everything is fp32 inside; values are rounded to the activation dtype where the reference's
 // arrays carry it. One CTA per row (norms), per (token, head) warp (attention).

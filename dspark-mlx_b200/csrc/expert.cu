@@ -515,6 +515,43 @@ extern "C" int dsm_linear(const void* x_staged, const float* x_row_scale, int64_
   return dispatch<false>(wfmt, pick_nt(n_rows, 1, a.rt_count), a, as_stream(stream));
 }
 
+extern "C" int dsm_grouped_linear(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int k_dim,
+                                  int wfmt, int group_size, const void* w_packed, int n_groups,
+                                  const int32_t* offsets, int out_dim, float* o_rows, int ldo,
+                                  const int32_t* o_row_map, int64_t n_rows, void* stream) {
+  using namespace dsm;
+  if (int rc = check_common(wfmt, group_size, offsets, n_groups)) return rc;
+  DSM_REQUIRE(out_dim > 0 && k_dim > 0 && n_rows >= 0 && ldo >= out_dim, "dsm_grouped_linear: bad shape");
+  DSM_REQUIRE(rows_cap >= dsm_stage_rows_cap(n_rows), "dsm_grouped_linear: rows_cap too small");
+  DSM_REQUIRE(x_staged && x_row_scale && w_packed && o_rows, "dsm_grouped_linear: NULL pointer");
+  if (n_rows == 0) return DSM_OK;
+  if (tm_supports(wfmt))
+    return expert_tm_down(wfmt, group_size, x_staged, 1.f, rows_cap, k_dim, offsets, n_groups, w_packed, out_dim, 0,
+                          o_rows, ldo, o_row_map, n_rows, stream, x_row_scale);
+  if (use_tc(wfmt, n_rows, n_groups))
+    return expert_tc_down(wfmt, x_staged, 1.f, rows_cap, k_dim, offsets, n_groups, w_packed, out_dim, 0, o_rows, ldo,
+                          o_row_map, n_rows, stream, x_row_scale);
+  ExpertArgs a{};
+  a.wa = static_cast<const uint8_t*>(w_packed);
+  a.wb = nullptr;
+  a.xin = static_cast<const __half*>(x_staged);
+  a.act_scale = x_row_scale;
+  a.act_scale_const = 1.f;
+  a.rows_cap = rows_cap;
+  a.offsets = offsets;
+  a.n_rows = n_rows;
+  a.n_experts = n_groups;
+  a.out_rows = out_dim;
+  a.rt_count = int(ceil_div(out_dim, kTileRows));
+  a.kc_count = int(ceil_div(k_dim, kChunkK));
+  a.group_size = group_size > 0 ? group_size : 64;
+  a.o_out = o_rows;
+  a.o_row_map = o_row_map;
+  a.ldo = ldo;
+  a.round_o = 0;
+  return dispatch<false>(wfmt, pick_nt(n_rows, n_groups, a.rt_count), a, as_stream(stream));
+}
+
 namespace dsm {
 int expert_regime() { return g_regime.load(); }
 }  // namespace dsm

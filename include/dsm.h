@@ -216,6 +216,16 @@ int dsm_dense_mlp(const void* x, int x_dtype, int64_t n_tokens, int dim, int int
  * n_experts = 1. */
 int dsm_linear(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int k_dim, int wfmt, int group_size,
                const void* w_packed, int out_dim, float* o_rows, int ldo, int64_t n_rows, void* stream);
+/* grouped_linear: dsm_linear over n_groups weight matrices in one launch. Staged rows
+ * [offsets[g], offsets[g+1]) (device offsets, n_groups + 1 entries) are multiplied by group g's
+ * matrix of w_packed (dsm_pack_weights with n_experts = n_groups); row r of the product goes
+ * to output row o_row_map[r] (NULL: r) with row stride ldo. The grouped low-rank output
+ * projection of the draft attention (model/attention.py:124-128: o [b, s, groups, d] x wo_a
+ * [groups, rank, d]) is one call: group-major rows, o_row_map[g * n + t] = t * groups + g,
+ * ldo = rank. */
+int dsm_grouped_linear(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int k_dim, int wfmt,
+                       int group_size, const void* w_packed, int n_groups, const int32_t* offsets, int out_dim,
+                       float* o_rows, int ldo, const int32_t* o_row_map, int64_t n_rows, void* stream);
 /* dsm_linear with K split across the GPU for the tensor-memory formats (fp4, affine), whose
  * units hold up to 128 rows each: a few row tiles of a decode-sized product would leave most
  * SMs idle. fp32 partial slabs per K range go to the workspace

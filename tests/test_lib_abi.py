@@ -173,3 +173,12 @@ def test_desc_struct_layout_matches_header():
     body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
     c_fields = re.findall(r"\*?\s*([a-z_0-9]+)\s*[,;]", body)
     assert c_fields == names
+
+
+def test_grouped_linear_rejects_bad_arguments_on_the_host():
+    L = _lib.lib()
+    # no offsets for several groups, ldo below out_dim, unknown format
+    assert L.dsm_grouped_linear(1, 1, 1 << 10, 512, _lib.WFMT_F16, 0, 1, 4, None, 256, 1, 256, None, 224, None) != 0
+    assert L.dsm_grouped_linear(1, 1, 1 << 10, 512, _lib.WFMT_F16, 0, 1, 4, 1, 256, 1, 128, None, 224, None) != 0
+    assert L.dsm_grouped_linear(1, 1, 1 << 10, 512, 9, 0, 1, 4, 1, 256, 1, 256, None, 224, None) != 0
+    assert L.dsm_last_error_message().decode()
