@@ -195,10 +195,15 @@ __global__ void __launch_bounds__(kAttnThreads) sparse_attn_kernel(
   }
   __syncwarp();
   float den = 0.f;
-  for (int k = lane; k < nk; k += 32) den += expf(sc[k] - mx);
+  for (int k = lane; k < nk; k += 32) {  // each weight once: the lane owning k replaces its score
+    const float e = expf(sc[k] - mx);
+    sc[k] = e;
+    den += e;
+  }
 #pragma unroll
   for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
   den += expf(sink[h] - mx);
+  __syncwarp();  // every lane reads every weight below
   const int hpg = n_heads / n_groups, g = h / hpg;
   const int64_t dg = int64_t(hpg) * head_dim;
   T* oh = out + (int64_t(g) * n_tok + t) * dg + int64_t(h % hpg) * head_dim;
@@ -206,7 +211,7 @@ __global__ void __launch_bounds__(kAttnThreads) sparse_attn_kernel(
   for (int d0 = lane * 2; d0 < head_dim; d0 += 64) {
     float a = 0.f, c = 0.f;
     for (int k = 0; k < nk; ++k) {
-      const float w = expf(sc[k] - mx);
+      const float w = sc[k];
       const T* kr = key(k);
       a = fmaf(w, ld_f(kr, d0), a);
       c = fmaf(w, ld_f(kr, d0 + 1), c);
