@@ -907,6 +907,11 @@ GQA_METRIC = ("Qwen3 draft-layer attention tokens/s (attend_cached over 2048 cac
 # staging, q/k/v products (split K: product + sum each), head norms + RoPE, attention, range
 # combine, staging, o_proj (product + sum), cast
 GQA_KERNELS_PER_STEP = 1 + 3 * 2 + 1 + 1 + 1 + 1 + 2 + 1
+LAYER_METRIC = ("Qwen3 draft layer tokens/s (forward_cached over 2048 cached context rows, every Linear 8-bit "
+                "affine); HBM GB/s")
+# input norm, the attention, residual add + post-attention norm, the MLP (staging, gate/up, split
+# down, split sum + cast), the last residual add
+LAYER_KERNELS_PER_STEP = 1 + GQA_KERNELS_PER_STEP + 1 + 4 + 1
 
 
 def _gqa_cpu_setup(t, wl):
@@ -916,19 +921,24 @@ def _gqa_cpu_setup(t, wl):
     from dsm.qwen3_attention import rope_tables
 
     a, ctx, s = wl.args, wl.extra["ctx"], wl.block
-    w = {k: t[k].cpu() for k in ("q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm")}
+    names = ("q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm")
+    if "gate_proj" in t:  # the whole layer
+        names += ("gate_proj", "up_proj", "down_proj", "input_layernorm", "post_attention_layernorm")
+    w = {k: t[k].cpu() for k in names}
     cos, sin = rope_tables(torch.arange(ctx, ctx + s), a["head_dim"], a["rope_theta"])
     return w, t["x"][:1].cpu(), t["ctx_k"][:1].cpu(), t["ctx_v"][:1].cpu(), cos, sin
 
 
 def _gqa_cpu_timed(wl, setup, budget_s, max_calls=50):
-    """The oracle's attend_cached on one sequence per call, all host threads."""
+    """The oracle's attend_cached (or the whole layer's forward_cached) on one sequence per call,
+    all host threads."""
     import oracle
 
     a = wl.args
     w, x, ck, cv, cos, sin = setup
-    call = lambda: oracle.qwen3_attend_cached(w, a["num_attention_heads"], a["num_key_value_heads"],  # noqa: E731
-                                              a["head_dim"], a["rms_norm_eps"], x, ck, cv, cos, sin)
+    fn = oracle.qwen3_layer_cached if "gate_proj" in w else oracle.qwen3_attend_cached
+    call = lambda: fn(w, a["num_attention_heads"], a["num_key_value_heads"],  # noqa: E731
+                      a["head_dim"], a["rms_norm_eps"], x, ck, cv, cos, sin)
     n, t0 = 0, time.perf_counter()
     while n < max_calls and (n == 0 or time.perf_counter() - t0 < budget_s):
         call()
@@ -940,7 +950,8 @@ def _gqa_cpu_timed(wl, setup, budget_s, max_calls=50):
 def run_gqa(args):
     """One step = ``attend_cached`` of 16 sequences' 7-token blocks over 2048 cached context rows
     each (Qwen3-4B widths). The cached K/V (134 MB) and the projections (~28 MB) exceed L2, so
-    every step streams them from HBM."""
+    every step streams them from HBM. With ``--workload qwen3_layer_q8`` a step is the whole
+    layer's ``forward_cached`` (norms, that attention, the 9728-wide MLP: ~107 MB of weights)."""
     import torch
 
     from dsm import _lib, workloads as W
@@ -955,10 +966,18 @@ def run_gqa(args):
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    wl = W.WORKLOADS["qwen3_attn_q8"]
+    layer_mode = args.workload == "qwen3_layer_q8"
+    wl = W.WORKLOADS[args.workload]
     a = wl.args
-    t = W.make_gqa_tensors(wl, device=dev, seed=rank)
-    attn = W.build_gqa(wl, t, dev)
+    if layer_mode:
+        t = W.make_qwen3_layer_tensors(wl, device=dev, seed=rank)
+        layer = W.build_qwen3_layer(wl, t, dev)
+        attn = layer.self_attn
+        step = lambda x: layer.forward_cached(x, kc, vc, cos, sin)  # noqa: E731
+    else:
+        t = W.make_gqa_tensors(wl, device=dev, seed=rank)
+        attn = W.build_gqa(wl, t, dev)
+        step = lambda x: attn.attend_cached(x, kc, vc, cos, sin)  # noqa: E731
     b, s, ctx = wl.batch, wl.block, wl.extra["ctx"]
     nh, nkv, hd, h = a["num_attention_heads"], a["num_key_value_heads"], a["head_dim"], a["hidden_size"]
     cos, sin = rope_tables(torch.arange(ctx, ctx + s), hd, a["rope_theta"])
@@ -969,7 +988,7 @@ def run_gqa(args):
     kc, vc = t["ctx_k"], t["ctx_v"]
     stream = torch.cuda.current_stream()
     for i in range(args.warmup):
-        attn.attend_cached(xs[i % 4], kc, vc, cos, sin)
+        step(xs[i % 4])
     torch.cuda.synchronize()
 
     def timed(fn):
@@ -983,10 +1002,12 @@ def run_gqa(args):
 
     _barrier(ws)
     with ClockSampler(local) as clk:
-        ms = timed(lambda i: attn.attend_cached(xs[i % 4], kc, vc, cos, sin))
+        ms = timed(lambda i: step(xs[i % 4]))
     ms = _max_over_ranks(ms, ws, dev)
     kv_bytes = 2 * b * nkv * ctx * hd * 2
     w_bytes = sum(getattr(attn, n).packed().nbytes for n in ("q_proj", "k_proj", "v_proj", "o_proj"))
+    if layer_mode:
+        w_bytes += sum(getattr(layer.mlp, n).packed().nbytes for n in ("gate_proj", "up_proj", "down_proj"))
     act_bytes = b * s * h * 2 * 2  # the block in, the output out
     step_bytes = w_bytes + kv_bytes + act_bytes
     hbm_peak, _, peak_kind = _peaks()
@@ -1018,7 +1039,7 @@ def run_gqa(args):
         yh = torch.empty(b, s, h, dtype=torch.bfloat16).pin_memory()
 
         def e2e(i):
-            y = attn.attend_cached(xh[i % 4].to(dev, non_blocking=True), kc, vc, cos, sin)
+            y = step(xh[i % 4].to(dev, non_blocking=True))
             yh.copy_(y, non_blocking=True)
 
         for i in range(3):
@@ -1032,10 +1053,11 @@ def run_gqa(args):
             v, calls, el = _gqa_cpu_timed(wl, _gqa_cpu_setup(t, wl), args.cpu_seconds)
             cpu = {"value": v, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
                    "sample": f"1 of the {b} sequences ({s} block tokens over {ctx} context rows) per call, {calls} "
-                             f"calls in {el:.1f} s; CPU restatement of Qwen3DSparkAttention.attend_cached in "
-                             f"PyTorch with the bf16 weights before quantisation"}
+                             f"calls in {el:.1f} s; CPU restatement of "
+                             f"{'Qwen3DSparkLayer.forward_cached' if layer_mode else 'Qwen3DSparkAttention.attend_cached'}"
+                             f" in PyTorch with the bf16 weights before quantisation"}
         line = {
-            "metric": GQA_METRIC, "value": ws * b * s / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws,
+            "metric": LAYER_METRIC if layer_mode else GQA_METRIC, "value": ws * b * s / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None,
             "dtype": "int8 affine weights x bf16 activations (f16 MMA, fp32 accumulate); fp32 attention",
@@ -1043,7 +1065,8 @@ def run_gqa(args):
             "config": {"workload": wl.name, "tokens_per_step_per_gpu": b * s, "batch": b, "draft_block": s,
                        "context_rows": ctx, "hidden": h, "heads": nh, "kv_heads": nkv, "head_dim": hd,
                        "parallelism": f"replicas{ws}" if ws > 1 else "single",
-                       "l2": "inputs larger than L2 (134 MB of cached K/V + 28 MB of weights streamed every step)"},
+                       "l2": "inputs larger than L2 (134 MB of cached K/V + "
+                             f"{w_bytes / 1e6:.0f} MB of weights streamed every step)"},
             "hbm_gbs_step": step_bytes / (ms * 1e-3) / 1e9,
             "roofline": roofline,
             "cpu_baseline": cpu,
@@ -1051,7 +1074,7 @@ def run_gqa(args):
                 "value": ws * b * s / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": xs[0].numel() * 2, "d2h_bytes_per_step": b * s * h * 2,
                 "ms_per_step": e2e_ms},
-            "gpu_launches": GQA_KERNELS_PER_STEP * args.steps,
+            "gpu_launches": (LAYER_KERNELS_PER_STEP if layer_mode else GQA_KERNELS_PER_STEP) * args.steps,
             "clocks": clk.summary(),
         }
         print(json.dumps(line))
@@ -1067,8 +1090,9 @@ def run_reference_gqa(args):
         return
     from dsm import workloads as W
 
-    wl = W.WORKLOADS["qwen3_attn_q8"]
-    t = W.make_gqa_tensors(wl, device="cpu")
+    layer_mode = args.workload == "qwen3_layer_q8"
+    wl = W.WORKLOADS[args.workload]
+    t = (W.make_qwen3_layer_tensors if layer_mode else W.make_gqa_tensors)(wl, device="cpu")
     setup = _gqa_cpu_setup(t, wl)
     vals = []
     for i in range(args.warmup + args.steps):
@@ -1077,7 +1101,8 @@ def run_reference_gqa(args):
             vals.append(v)
     value = statistics.median(vals)
     line = {
-        "impl": "reference", "metric": GQA_METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": LAYER_METRIC if layer_mode else GQA_METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wl.n_tokens / value,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (bf16 weights)",
         "data": "synthetic",
@@ -1085,8 +1110,9 @@ def run_reference_gqa(args):
                    "context_rows": wl.extra["ctx"]},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
                          "sample": f"one sequence ({wl.block} block tokens over {wl.extra['ctx']} context rows) per "
-                                   f"step; CPU restatement of Qwen3DSparkAttention.attend_cached in PyTorch (mlx is "
-                                   f"not installable here)"},
+                                   f"step; CPU restatement of "
+                                   f"{'Qwen3DSparkLayer.forward_cached' if layer_mode else 'Qwen3DSparkAttention.attend_cached'}"
+                                   f" in PyTorch (mlx is not installable here)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -1304,7 +1330,7 @@ def main():
     qwen3 = args.workload.startswith("qwen3")
     if args.workload == "draft_head":
         (run_reference_head if args.impl == "reference" else run_head)(args)
-    elif args.workload == "qwen3_attn_q8":
+    elif args.workload in ("qwen3_attn_q8", "qwen3_layer_q8"):
         (run_reference_gqa if args.impl == "reference" else run_gqa)(args)
     elif args.workload == "draft_attn_dsv4":
         (run_reference_dsattn if args.impl == "reference" else run_dsattn)(args)

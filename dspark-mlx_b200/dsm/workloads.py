@@ -90,6 +90,12 @@ WORKLOADS = {
         "qwen3_attn_q8", dict(hidden_size=2560, num_attention_heads=32, num_key_value_heads=8, head_dim=128,
                               rms_norm_eps=1e-6, rope_theta=1000000.0),
         n_tokens=112, wfmt="affine8", batch=16, block=7, extra={"ctx": 2048}),
+    # the whole Qwen3-4B draft layer (norms, the attention above, the 9728-wide MLP) on the
+    # cached path, every Linear 8-bit affine as quantize_drafter leaves it
+    "qwen3_layer_q8": Workload(
+        "qwen3_layer_q8", dict(hidden_size=2560, num_attention_heads=32, num_key_value_heads=8, head_dim=128,
+                               rms_norm_eps=1e-6, rope_theta=1000000.0, intermediate_size=9728),
+        n_tokens=112, wfmt="affine8", batch=16, block=7, extra={"ctx": 2048}),
     # the DeepSeek-V4 draft attention (compress_ratio 0 MLA: 64 heads of 512, q rank 1024,
     # 8 output groups of rank 1024, a 128-slot window) decoding 7-token blocks for 8
     # sequences after a 160-token prefill: the window is full
@@ -314,6 +320,40 @@ def make_gqa_tensors(wl: Workload, device="cpu", seed: Optional[int] = None) -> 
             "q_norm": 1 + r(hd, std=0.1), "k_norm": 1 + r(hd, std=0.1),
             "x": r(b, s, h).to(torch.bfloat16),
             "ctx_k": r(b, nkv, ctx, hd).to(torch.bfloat16), "ctx_v": r(b, nkv, ctx, hd).to(torch.bfloat16)}
+
+
+def make_qwen3_layer_tensors(wl: Workload, device="cpu", seed: Optional[int] = None) -> Dict[str, torch.Tensor]:
+    """The attention workload's tensors plus the MLP's bf16 weights and the two layer norms."""
+    t = make_gqa_tensors(wl, device=device, seed=seed)
+    a = wl.args
+    g = torch.Generator(device=device)
+    g.manual_seed((wl.seed if seed is None else seed) + 1)
+    h, i = a["hidden_size"], a["intermediate_size"]
+    r = lambda *shape, std=1.0: torch.randn(shape, generator=g, device=device) * std  # noqa: E731
+    t.update({"gate_proj": r(i, h, std=h ** -0.5).to(torch.bfloat16), "up_proj": r(i, h, std=h ** -0.5).to(torch.bfloat16),
+              "down_proj": r(h, i, std=i ** -0.5).to(torch.bfloat16),
+              "input_layernorm": 1 + r(h, std=0.1), "post_attention_layernorm": 1 + r(h, std=0.1)})
+    return t
+
+
+def build_qwen3_layer(wl: Workload, t: Dict[str, torch.Tensor], device="cuda", bits: int = 8, group_size: int = 64):
+    """A :class:`dsm.qwen3_layer.Qwen3DSparkLayer` holding ``t``'s weights, quantised like
+    ``quantize_drafter`` when the workload is affine."""
+    from .qwen3_layer import Qwen3DSparkLayer
+
+    layer = Qwen3DSparkLayer(wl.args).to(device)
+    for n in ("q_proj", "k_proj", "v_proj", "o_proj"):
+        getattr(layer.self_attn, n).weight = torch.nn.Parameter(t[n].to(device), requires_grad=False)
+    for n in ("gate_proj", "up_proj", "down_proj"):
+        getattr(layer.mlp, n).weight = torch.nn.Parameter(t[n].to(device), requires_grad=False)
+    with torch.no_grad():
+        layer.self_attn.q_norm.weight.copy_(t["q_norm"])
+        layer.self_attn.k_norm.weight.copy_(t["k_norm"])
+        layer.input_layernorm.weight.copy_(t["input_layernorm"])
+        layer.post_attention_layernorm.weight.copy_(t["post_attention_layernorm"])
+    if wl.wfmt == "affine8":
+        layer.quantize(bits=bits, group_size=group_size)
+    return layer
 
 
 def build_gqa(wl: Workload, t: Dict[str, torch.Tensor], device="cuda", bits: int = 8, group_size: int = 64):
