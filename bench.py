@@ -959,6 +959,7 @@ def run_gqa(args):
 
     ws, rank, local = _dist()
     torch.cuda.set_device(local)
+    _lib.check(_lib.lib().dsm_set_attn_kernel(0 if args.attn_kernel == "mma" else 1), "dsm_set_attn_kernel")
     dev = torch.device("cuda", local)
     if ws > 1:
         import datetime
@@ -1028,7 +1029,8 @@ def run_gqa(args):
             "dsm_gqa_attn"))
         k_bytes = kv_bytes + 2 * b * nkv * s * hd * 2 + 2 * b * s * nh * hd * 2
         achieved = k_bytes / (k_ms * 1e-3) / 1e9
-        roofline = {"bound": "hbm", "kernel": "gqa_attn_kernel<bf16, 128> + gqa_combine_kernel",
+        kname = "gqa_mma_kernel<128>" if args.attn_kernel == "mma" else "gqa_attn_kernel<bf16, 128>"
+        roofline = {"bound": "hbm", "kernel": kname + " + gqa_combine_kernel",
                     "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                     "peak_kind": peak_kind, "frac_of_8tbs": achieved / SPEC_HBM_GBS,
                     "algorithmic_bytes_per_launch": k_bytes, "launch_ms": k_ms, "traffic": None}
@@ -1064,6 +1066,7 @@ def run_gqa(args):
             "data": "synthetic",
             "config": {"workload": wl.name, "tokens_per_step_per_gpu": b * s, "batch": b, "draft_block": s,
                        "context_rows": ctx, "hidden": h, "heads": nh, "kv_heads": nkv, "head_dim": hd,
+                       "attn_kernel": args.attn_kernel,
                        "parallelism": f"replicas{ws}" if ws > 1 else "single",
                        "l2": "inputs larger than L2 (134 MB of cached K/V + "
                              f"{w_bytes / 1e6:.0f} MB of weights streamed every step)"},
@@ -1168,6 +1171,7 @@ def run_dsattn(args):
 
     ws, rank, local = _dist()
     torch.cuda.set_device(local)
+    _lib.check(_lib.lib().dsm_set_attn_kernel(0 if args.attn_kernel == "mma" else 1), "dsm_set_attn_kernel")
     dev = torch.device("cuda", local)
     if ws > 1:
         import datetime
@@ -1263,6 +1267,7 @@ def run_dsattn(args):
             "data": "synthetic",
             "config": {"workload": wl.name, "tokens_per_step_per_gpu": b * s, "batch": b, "draft_block": s,
                        "dim": d, "heads": h, "head_dim": hd, "window": a["window_size"],
+                       "attn_kernel": args.attn_kernel,
                        "parallelism": f"replicas{ws}" if ws > 1 else "single",
                        "l2": "inputs larger than L2 (214 MB of projection weights streamed every step)"},
             "hbm_gbs_step": step_bytes / (ms * 1e-3) / 1e9,
@@ -1324,6 +1329,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-kernel-timing", action="store_true")
     ap.add_argument("--experts", type=int, default=0, help="shrink the routed expert pool (profiling)")
+    ap.add_argument("--attn-kernel", default="cuda", choices=["cuda", "mma"],
+                    help="attention workloads: CUDA-core kernels, or the tensor-core ones where they apply")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
