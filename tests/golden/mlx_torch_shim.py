@@ -461,6 +461,37 @@ class Module(dict):
         else:
             object.__delattr__(self, key)
 
+    def parameters(self):
+        """The arrays of this module and its children as a nested dict (lists stay lists), as
+        ``mlx.nn.Module.parameters`` returns them."""
+
+        def conv(v):
+            if isinstance(v, Module):
+                return v.parameters()
+            if isinstance(v, (list, tuple)):
+                return [conv(x) for x in v]
+            return v
+
+        return {k: conv(v) for k, v in self.items() if isinstance(v, (array, Module, list, tuple))}
+
+    def update(self, tree):
+        """Replace arrays from a nested dict as ``mlx.nn.Module.update`` does."""
+
+        def put(cur, new):
+            if isinstance(cur, Module):
+                for k, v in new.items():
+                    if isinstance(cur.get(k), (Module, list)):
+                        put(cur[k], v)
+                    else:
+                        cur[k] = v
+            elif isinstance(cur, list):
+                items = new.items() if isinstance(new, dict) else enumerate(new)
+                for i, v in items:
+                    put(cur[int(i)], v)
+
+        put(self, tree)
+        return self
+
     def named_modules(self):
         out = [("", self)]
 
@@ -548,6 +579,9 @@ def _tree_flatten(tree, prefix=""):
     if isinstance(tree, dict):
         for k, v in tree.items():
             out.extend(_tree_flatten(v, f"{prefix}{k}."))
+    elif isinstance(tree, (list, tuple)):
+        for i, v in enumerate(tree):
+            out.extend(_tree_flatten(v, f"{prefix}{i}."))
     else:
         out.append((prefix[:-1], tree))
     return out

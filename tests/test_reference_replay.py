@@ -131,3 +131,62 @@ def test_qwen3_backbone_oracle_matches_reference_torch_model(reference):
     assert float((tctx - tctx_ref).abs().max()) <= 1e-5 * float(tctx_ref.abs().max())
     got = oracle.qwen3_backbone(weights, 2, 4, 2, 16, 1e-6, noise, tctx, cos, sin)
     assert float((got - want).abs().max()) <= 1e-5 * float(want.abs().max())
+
+
+def _load_with_ref_tests(name):
+    """A reference test module whose helpers (``cpu_kernels``, ``torch_ref_heads``,
+    ``reference_model``) sit beside it in the reference's tests folder."""
+    import sys
+
+    ref_tests = os.path.join(REF, "tests")
+    if ref_tests not in sys.path:
+        sys.path.insert(0, ref_tests)
+    return _load_test_module(os.path.join(ref_tests, name))
+
+
+def test_reference_kernel_parity_tests(reference):
+    """The reference's own kernel parity tests (``tests/test_kernels_parity.py``): its
+    ``sparse_attn`` and ``hc_split_sinkhorn`` against its torch CPU kernels, run on the stand-in
+    that generated the attention and hyper-connection golden vectors."""
+    mod = _load_with_ref_tests("test_kernels_parity.py")
+    mod.test_sparse_attn_matches_reference()
+    mod.test_sparse_attn_equals_dense_when_full_and_no_sink()
+    mod.test_hc_sinkhorn_matches_reference()
+    mod.test_hc_sinkhorn_columns_normalized()
+
+
+def test_reference_head_parity_tests(reference):
+    """``tests/test_heads_parity.py``: the Markov and confidence heads against the reference's
+    torch heads, on the stand-in that generated the draft-head golden vectors."""
+    mod = _load_with_ref_tests("test_heads_parity.py")
+    mod.test_markov_head_parity()
+    mod.test_confidence_head_parity()
+    mod.test_config_from_dict_parses_dspark_fields()
+
+
+def test_reference_rope_roundtrip_test(reference):
+    """``tests/test_layers_parity.py``'s RoPE inverse round trip (its other cases need the
+    DeepSeek torch model, which is not in the reference tree)."""
+    mod = _load_with_ref_tests("test_layers_parity.py")
+    mod.test_rope_inverse_roundtrips()
+
+
+def test_reference_qwen3_backbone_parity_test(reference):
+    """The reference's own Qwen3 backbone parity test (``tests/test_qwen3_arch.py:30-60``): its
+    MLX backbone against the torch transcription of DeepSpec's model within 2e-3, run on the
+    stand-in that generated the Qwen3 attention, layer and backbone golden vectors."""
+    import sys
+    import types
+
+    if "dspark_mlx.arch" not in sys.modules:
+        arch = types.ModuleType("dspark_mlx.arch")
+        arch.__path__ = [os.path.join(REF, "dspark_mlx", "arch")]
+        sys.modules["dspark_mlx.arch"] = arch
+    # transformers probes for an installed mlx when its Qwen3 module loads: hide the stand-in
+    shim_mods = {k: sys.modules.pop(k) for k in list(sys.modules) if k == "mlx" or k.startswith("mlx.")}
+    try:
+        import transformers.models.qwen3.modeling_qwen3  # noqa: F401
+    finally:
+        sys.modules.update(shim_mods)
+    mod = _load_with_ref_tests("test_qwen3_arch.py")
+    mod.test_qwen3_backbone_parity()
