@@ -36,6 +36,17 @@ def test_map_checkpoint_key():
     assert loading.map_checkpoint_key("layers.0.attn.wkv.weight") is None
 
 
+def test_draft_shards_selects_only_the_draft():
+    # the reference's own case (tests/test_loader_deepseek.py:31-46)
+    wm = {"embed.weight": "s1", "head.weight": "s1", "layers.0.attn.wq_a.weight": "s2",
+          "layers.30.ffn.experts.3.w1.weight": "s3", "mtp.0.attn.wq_a.weight": "s9",
+          "mtp.0.ffn.experts.5.w1.weight": "s9", "mtp.2.markov_head.markov_w1.weight": "s10"}
+    keep, shards = loading.draft_shards(wm)
+    assert keep == {"embed.weight", "head.weight", "mtp.0.attn.wq_a.weight", "mtp.0.ffn.experts.5.w1.weight",
+                    "mtp.2.markov_head.markov_w1.weight"}
+    assert shards == ["s1", "s10", "s9"]  # sorted, unique; the base-only shards are never opened
+
+
 def test_e8m0_to_fp32_every_code_exact():
     codes = torch.arange(255, dtype=torch.uint8)
     exp = oracle.e8m0_decode(codes.numpy())
