@@ -141,3 +141,27 @@ def test_qwen3_attention_matches_oracle(dtype, b, q, ctx, h, nh, nkv, hd):
         torch.cuda.synchronize()
         assert max_rel_err(k, rk) < tol and max_rel_err(v, rv) < tol
     assert _lib.device_error() == 0
+
+
+def test_qwen3_attention_context_order_invariance_at_bench_shape():
+    """At the bench's shape (16 sequences x 7 block tokens over 2048 cached context rows,
+    Qwen3-4B widths) the CPU oracle is too slow, so a size-independent property stands in:
+    attention over the cached rows does not depend on their order. Permuting the context rows
+    (K and V alike) moves them across the kernel's key ranges and tiles; the output must agree
+    to bf16 rounding of the same sums in another order."""
+    from dsm import workloads as W
+
+    wl = W.WORKLOADS["qwen3_attn_q8"]
+    t = W.make_gqa_tensors(wl, device=DEV, seed=3)
+    attn = W.build_gqa(wl, t, DEV)
+    a = wl.args
+    s, ctx = wl.block, wl.extra["ctx"]
+    cos, sin = rope_tables(torch.arange(ctx, ctx + s), a["head_dim"], a["rope_theta"])
+    kc, vc = t["ctx_k"], t["ctx_v"]
+    perm = torch.randperm(ctx, generator=torch.Generator().manual_seed(1)).to(DEV)
+    y0 = attn.attend_cached(t["x"], kc, vc, cos, sin)
+    y1 = attn.attend_cached(t["x"], kc[:, :, perm].contiguous(), vc[:, :, perm].contiguous(), cos, sin)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y0.float()).all()
+    assert max_rel_err(y1, y0) < 1e-2, max_rel_err(y1, y0)
+    assert _lib.device_error() == 0
