@@ -351,7 +351,8 @@ __global__ void __launch_bounds__(kSaThreads) sparse_attn_mma_kernel(
     if (c < nchunks) {
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
-        const float pv = expf(s[c][cc] - m_row[cc >> 1]);
+        // rounded to bf16 here, so the denominator sums the weights the p.v products use
+        const float pv = __bfloat162float(__float2bfloat16_rn(expf(s[c][cc] - m_row[cc >> 1])));
         s[c][cc] = pv;
         ls[cc >> 1] += pv;
       }

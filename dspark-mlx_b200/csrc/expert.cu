@@ -374,13 +374,14 @@ int pick_nt(int64_t n_rows, int n_experts, int rt_count) {
   return nt;
 }
 
-std::atomic<int> g_regime{0};
+// per host thread: a caller's choice never changes another thread's launches
+thread_local int g_regime = 0;
 
 // The tcgen05 kernel pays off once an expert's weight tile is reused by many rows: with
 // 128-row MMA tiles, from about 64 rows per busy expert on average.
 bool use_tc(int wfmt, int64_t n_rows, int n_experts) {
   if (!tc_supports(wfmt)) return false;
-  const int r = g_regime.load(std::memory_order_relaxed);
+  const int r = g_regime;
   if (r == 1) return false;
   if (r == 2) return true;
   const int64_t busy = std::max<int64_t>(1, std::min<int64_t>(n_rows, n_experts));
@@ -553,11 +554,11 @@ extern "C" int dsm_grouped_linear(const void* x_staged, const float* x_row_scale
 }
 
 namespace dsm {
-int expert_regime() { return g_regime.load(); }
+int expert_regime() { return g_regime; }
 }  // namespace dsm
 
 extern "C" int dsm_set_expert_regime(int regime) {
   DSM_REQUIRE(regime >= 0 && regime <= 2, "dsm_set_expert_regime: regime must be 0, 1 or 2");
-  dsm::g_regime.store(regime);
+  dsm::g_regime = regime;
   return DSM_OK;
 }

@@ -24,7 +24,7 @@
 //                    q.k and p.v on mma.m16n8k16 (bf16 in, fp32 accumulate; p rounded to
 //                    bf16 for the second product), each warp an online softmax over half of
 //                    every tile, so each key range leaves two partials.
-// dsm_set_attn_kernel picks between them (process-wide).
+// dsm_set_attn_kernel picks between them (per host thread).
 #include <atomic>
 
 #include "common.cuh"
@@ -375,7 +375,8 @@ __global__ void __launch_bounds__(kMmaThreads) gqa_mma_kernel(
     for (int n = 0; n < 4; ++n)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const float pv = expf(s[n][c] - mx[c >> 1]);
+        // rounded to bf16 here, so the denominator sums the weights the p.v products use
+        const float pv = __bfloat162float(__float2bfloat16_rn(expf(s[n][c] - mx[c >> 1])));
         s[n][c] = pv;
         ls[c >> 1] += pv;
       }
@@ -653,14 +654,15 @@ extern "C" int dsm_gqa_attn(const void* q, const void* ctx_k, const void* ctx_v,
 
 namespace dsm {
 namespace {
-// 0: the tensor-core attention kernels wherever they apply, 1: the CUDA-core kernels
-std::atomic<int> g_attn_kernel{1};
+// 0: the tensor-core attention kernels wherever they apply, 1: the CUDA-core kernels; per
+// host thread, so one caller's choice never changes another thread's launches
+thread_local int g_attn_kernel = 1;
 }  // namespace
-int attn_kernel() { return g_attn_kernel.load(std::memory_order_relaxed); }
+int attn_kernel() { return g_attn_kernel; }
 }  // namespace dsm
 
 extern "C" int dsm_set_attn_kernel(int kernel) {
   DSM_REQUIRE(kernel == 0 || kernel == 1, "dsm_set_attn_kernel: kernel must be 0 or 1");
-  dsm::g_attn_kernel.store(kernel);
+  dsm::g_attn_kernel = kernel;
   return DSM_OK;
 }

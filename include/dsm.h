@@ -121,7 +121,9 @@ int dsm_router(const void* x, int x_dtype, int64_t n_tokens, int dim, const floa
  * DSM_ROUTER_NOALLOC_MAX_SCRATCH_BYTES inside the library, held on every GPU that loads it
  * until exit. Calls needing more (dsm_router_workspace_bytes) fail with DSM_ERR_WORKSPACE.
  * The first call on a device resolves the array's address there: make it before any stream
- * capture. All calls share the array: calls that can overlap on the GPU race on it. */
+ * capture. After cudaDeviceReset the first call resolves it again (the address is cached per
+ * CUDA context), so make that call before any capture too. All calls share the array: calls
+ * that can overlap on the GPU race on it. */
 #define DSM_ROUTER_NOALLOC_MAX_SCRATCH_BYTES (8u << 20)
 int dsm_router_noalloc(const void* x, int x_dtype, int64_t n_tokens, int dim, const float* gate_weight,
                        int n_experts, const float* gate_bias, const int32_t* tid2eid, int64_t vocab,
@@ -325,7 +327,8 @@ int dsm_round_rows(const float* in, const float* in_lo, int64_t n, void* out, in
  *   they apply: dsm_gqa_attn with head_dim 64 / 128, every pointer 16-byte aligned and the
  *   context strides multiples of 8; dsm_sparse_attn with head_dim 64..512 (a multiple of 64),
  *   at most 256 keys, q / window / block rows 16-byte aligned. Elsewhere the CUDA-core kernels
- *   run. 1 (the default) runs the CUDA-core kernels everywhere. Process-wide. */
+ *   run. 1 (the default) runs the CUDA-core kernels everywhere. The choice holds for the
+ *   calling host thread only (thread-local): other threads keep their own. */
 int dsm_qkv_norm_rope(const float* in, const float* in_lo, int64_t n_rows, int n_q, int n_kv, int head_dim,
                       const float* q_norm_w, const float* k_norm_w, float eps, const float* cos_t, const float* sin_t,
                       int tab_rows, int tab0, int period, void* q_out, void* k_out, void* v_out, int kv_cap, int row0,
@@ -348,7 +351,8 @@ int dsm_add_rms_norm(const void* x, const void* delta, int dtype, int64_t n_rows
 /* Kernel regime of the grouped expert products: 0 (default) picks by rows per busy
  * expert -- the mma.sync weight-streaming kernel at decode sizes, the tcgen05/TMEM kernel
  * (fp8 block-scaled experts) from ~64 rows per expert; 1 forces the streaming kernel;
- * 2 forces tcgen05 wherever the format supports it. Process-wide. */
+ * 2 forces tcgen05 wherever the format supports it. The choice holds for the calling host
+ * thread only (thread-local): other threads keep their own. */
 int dsm_set_expert_regime(int regime);
 
 /* ---- expert-parallel helpers -----------------------------------------------------------

@@ -26,3 +26,18 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(params=[1, 0], ids=["cuda_core_attn", "tensor_core_attn"])
+def attn_kernel(request):
+    """Runs a test once per attention kernel family: 1 the CUDA-core kernels, 0 the tensor-core
+    (mma.m16n8k16) kernels wherever they apply (bf16). The switch is per host thread; it is put
+    back to the default (1) afterwards."""
+    from dsm import _lib
+
+    L = _lib.lib()
+    _lib.check(L.dsm_set_attn_kernel(request.param))
+    try:
+        yield request.param
+    finally:
+        _lib.check(L.dsm_set_attn_kernel(1))

@@ -44,8 +44,10 @@ def _golden_args():
 
 
 @pytest.mark.parametrize("name", CASES)
-def test_qwen3_attention_matches_reference_goldens(name):
+def test_qwen3_attention_matches_reference_goldens(name, attn_kernel):
     z = dict(np.load(os.path.join(HERE, name + ".npz")))
+    if attn_kernel == 0 and not bool(z["dtype_bf16"]):
+        pytest.skip("fp32 attention always runs the CUDA-core kernels")
     tol = 2e-2 if bool(z["dtype_bf16"]) else 2e-3
     a = _module(_golden_args(), _weights(z))
     hidden, target = _t(z["hidden"]), _t(z["target_ctx"])
@@ -93,7 +95,7 @@ def _oracle_case(dtype, b, q, ctx, h, nh, nkv, hd, seed):
     return w, hidden, target
 
 
-def test_qwen3_attention_8bit_projections_match_oracle():
+def test_qwen3_attention_8bit_projections_match_oracle(attn_kernel):
     """Projections quantised as quantize_drafter leaves them (MLX affine, 8 bits, groups of 64)
     run split along K (dsm_linear_splitk). The oracle multiplies by the dequantised weights in
     fp32; the GPU's bf16 activations round after every product."""
@@ -124,7 +126,9 @@ def test_qwen3_attention_8bit_projections_match_oracle():
     (torch.float32, 1, 5, 1000, 512, 4, 1, 256),      # head_dim 256, one KV head
     (torch.bfloat16, 4, 7, 0, 512, 8, 4, 128),        # no context at all
 ])
-def test_qwen3_attention_matches_oracle(dtype, b, q, ctx, h, nh, nkv, hd):
+def test_qwen3_attention_matches_oracle(dtype, b, q, ctx, h, nh, nkv, hd, attn_kernel):
+    if attn_kernel == 0 and not dtype == torch.bfloat16:
+        pytest.skip("fp32 attention always runs the CUDA-core kernels")
     theta, eps = 1000000.0, 1e-6
     w, hidden, target = _oracle_case(dtype, b, q, ctx, h, nh, nkv, hd, seed=ctx + hd)
     a = _module(dict(hidden_size=h, num_attention_heads=nh, num_key_value_heads=nkv, head_dim=hd, rms_norm_eps=eps),
@@ -143,7 +147,7 @@ def test_qwen3_attention_matches_oracle(dtype, b, q, ctx, h, nh, nkv, hd):
     assert _lib.device_error() == 0
 
 
-def test_qwen3_attention_context_order_invariance_at_bench_shape():
+def test_qwen3_attention_context_order_invariance_at_bench_shape(attn_kernel):
     """At the bench's shape (16 sequences x 7 block tokens over 2048 cached context rows,
     Qwen3-4B widths) the CPU oracle is too slow, so a size-independent property stands in:
     attention over the cached rows does not depend on their order. Permuting the context rows
@@ -164,4 +168,35 @@ def test_qwen3_attention_context_order_invariance_at_bench_shape():
     torch.cuda.synchronize()
     assert torch.isfinite(y0.float()).all()
     assert max_rel_err(y1, y0) < 1e-2, max_rel_err(y1, y0)
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("ctx", [2048, 2011, 25])
+def test_qwen3_attention_kernels_agree(ctx):
+    """The tensor-core kernel (gqa_mma_kernel) against the CUDA-core one on the same inputs at
+    Qwen3-4B widths: 2048 context rows (the bench shape), 2011 (the last 64-key tile of each
+    range partly filled) and 25 (with the 7 block rows, one tile of 32 keys: the second key half
+    of every tile is empty). The tensor-core kernel rounds the softmax weights to bf16 for the
+    p.v products and sums the same rounded weights in the denominator, so the two agree to a
+    few bf16 ulps of the output."""
+    from dsm import workloads as W
+
+    L = _lib.lib()
+    wl = W.WORKLOADS["qwen3_attn_q8"]
+    t = W.make_gqa_tensors(wl, device=DEV, seed=5)
+    attn = W.build_gqa(wl, t, DEV)
+    a = wl.args
+    s = wl.block
+    cos, sin = rope_tables(torch.arange(ctx, ctx + s), a["head_dim"], a["rope_theta"])
+    kc, vc = t["ctx_k"][:, :, :ctx], t["ctx_v"][:, :, :ctx]
+    outs = []
+    for k in (1, 0):
+        _lib.check(L.dsm_set_attn_kernel(k))
+        try:
+            outs.append(attn.attend_cached(t["x"], kc, vc, cos, sin))
+            torch.cuda.synchronize()
+        finally:
+            _lib.check(L.dsm_set_attn_kernel(1))
+    assert torch.isfinite(outs[1].float()).all()
+    assert max_rel_err(outs[1], outs[0]) < 1e-2, max_rel_err(outs[1], outs[0])
     assert _lib.device_error() == 0
