@@ -12,10 +12,16 @@
 //     rejected with DSM_ERR_WORKSPACE before any GPU work.
 //   - The first call on a device resolves the array's device address there (once per
 //     device, with that device current); make that first call before any stream capture.
+//     The address is cached together with the unique id of the CUDA context it belongs to.
+//     cudaDeviceReset destroys that context and the array with it; the first call after a
+//     reset sees a new context id and resolves the address again (again: before any
+//     capture), so a stale address is never passed to a kernel.
 //   - Every call shares the one array and leaves its contents behind. The router overwrites
 //     every scratch cell it reads, so nothing has to start at zero; but two calls that can
 //     overlap on the GPU (different streams without ordering between them) race on it.
 //   - Nothing here calls cudaMalloc, cudaFree or any allocating library routine.
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -29,24 +35,66 @@ static_assert(kNoAllocScratchBytes == DSM_ROUTER_NOALLOC_MAX_SCRATCH_BYTES, "hea
 static __device__ __align__(256) unsigned char g_router_scratch[kNoAllocScratchBytes];
 
 constexpr int kMaxDevices = 64;
+struct ScratchSlot {
+  void* addr = nullptr;
+  unsigned long long ctx_id = 0;  // unique id of the context the address belongs to
+};
 std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
+ScratchSlot g_scratch[kMaxDevices];
 
-// Device address of g_router_scratch on the current device (resolved once per device).
+// The driver's current-context queries, reached through the runtime (no libcuda link).
+struct CtxFns {
+  PFN_cuCtxGetCurrent_v4000 current = nullptr;
+  PFN_cuCtxGetId_v12000 id = nullptr;
+};
+const CtxFns& ctx_fns() {
+  static CtxFns f;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      f.current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      f.id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+  });
+  return f;
+}
+
+// Unique id of the calling thread's current context, 0 when there is none yet.
+unsigned long long current_ctx_id() {
+  const CtxFns& f = ctx_fns();
+  if (!f.current || !f.id) return 0;
+  CUcontext c = nullptr;
+  if (f.current(&c) != CUDA_SUCCESS || c == nullptr) return 0;
+  unsigned long long id = 0;
+  return f.id(c, &id) == CUDA_SUCCESS ? id : 0;
+}
+
+// Device address of g_router_scratch on the current device: resolved on the first call on a
+// device, and again whenever the device's context has changed since (after cudaDeviceReset).
 int scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(DSM_ERR_CUDA, std::string("dsm_router_noalloc: cudaGetDevice: ") + cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return fail(DSM_ERR_UNSUPPORTED, "dsm_router_noalloc: device ordinal >= 64");
+  if (!ctx_fns().current || !ctx_fns().id)
+    return fail(DSM_ERR_CUDA, "dsm_router_noalloc: cuCtxGetCurrent / cuCtxGetId unavailable");
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[dev]) {
+  ScratchSlot& slot = g_scratch[dev];
+  const unsigned long long id = current_ctx_id();
+  if (!slot.addr || id == 0 || id != slot.ctx_id) {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_router_scratch);
+    e = cudaGetSymbolAddress(&p, g_router_scratch);  // makes the device's primary context current
     if (e != cudaSuccess || p == nullptr)
       return fail(DSM_ERR_CUDA, std::string("dsm_router_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-    g_scratch_addr[dev] = p;
+    slot.addr = p;
+    slot.ctx_id = current_ctx_id();
   }
-  *out = g_scratch_addr[dev];
+  *out = slot.addr;
   return DSM_OK;
 }
 
