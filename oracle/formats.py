@@ -43,9 +43,8 @@ __all__ = [
 ]
 
 
-def e4m3_decode(codes) -> torch.Tensor:
-    """e4m3 (fn) bit patterns -> fp32 values, from the bit fields."""
-    c = torch.as_tensor(np.asarray(codes, dtype=np.uint8)).to(torch.int32)
+def _e4m3_fields(c: torch.Tensor) -> torch.Tensor:
+    """e4m3 (fn) bit patterns (int32) -> fp32 values, from the bit fields."""
     sign = torch.where((c & 0x80) != 0, -1.0, 1.0)
     exp = (c >> 3) & 0xF
     man = (c & 0x7).to(torch.float64)
@@ -56,15 +55,36 @@ def e4m3_decode(codes) -> torch.Tensor:
     return val.to(torch.float32)
 
 
-def e2m1_decode(codes) -> torch.Tensor:
-    """e2m1 nibbles (values 0..15) -> fp32 values, from the bit fields."""
-    c = torch.as_tensor(np.asarray(codes, dtype=np.uint8)).to(torch.int32) & 0xF
+def _e2m1_fields(c: torch.Tensor) -> torch.Tensor:
+    """e2m1 nibbles (int32, 0..15) -> fp32 values, from the bit fields."""
     sign = torch.where((c & 0x8) != 0, -1.0, 1.0)
     exp = (c >> 1) & 0x3
     man = (c & 0x1).to(torch.float64)
     normal = (1.0 + man / 2.0) * torch.pow(2.0, (exp - 1).to(torch.float64))
     sub = man * 0.5
     return (torch.where(exp == 0, sub, normal) * sign).to(torch.float32)
+
+
+# Every code's value, decoded once from the bit fields above; decoding a tensor of codes is
+# then a table lookup (the same values, without re-running the field arithmetic per element).
+_E4M3_TABLE = _e4m3_fields(torch.arange(256, dtype=torch.int32))
+_E2M1_TABLE = _e2m1_fields(torch.arange(16, dtype=torch.int32))
+
+
+def _code_index(codes) -> torch.Tensor:
+    if isinstance(codes, torch.Tensor):
+        return codes.to(torch.int64) & 0xFF
+    return torch.as_tensor(np.asarray(codes, dtype=np.uint8)).to(torch.int64)
+
+
+def e4m3_decode(codes) -> torch.Tensor:
+    """e4m3 (fn) bit patterns -> fp32 values (the bit-field decode of each code)."""
+    return _E4M3_TABLE[_code_index(codes)]
+
+
+def e2m1_decode(codes) -> torch.Tensor:
+    """e2m1 nibbles (values 0..15) -> fp32 values (the bit-field decode of each code)."""
+    return _E2M1_TABLE[_code_index(codes) & 0xF]
 
 
 def e8m0_decode(codes) -> torch.Tensor:
@@ -122,11 +142,8 @@ def fp4_weight_dequant(codes: torch.Tensor, gscales: torch.Tensor, tscale: torch
     ``(code * group_scale)`` is the reference's ``dequant_fp4_groupwise`` (exact in fp32);
     the per-tensor fp32 scale multiplies that product.
     """
-    c = codes.numpy()
-    lo = c & 0xF
-    hi = c >> 4
-    nib = np.stack([lo, hi], axis=-1).reshape(*c.shape[:-1], c.shape[-1] * 2)
-    w = e2m1_decode(nib)
+    c = codes.to(torch.int64)
+    w = torch.stack([e2m1_decode(c & 0xF), e2m1_decode(c >> 4)], dim=-1).reshape(*c.shape[:-1], c.shape[-1] * 2)
     gs = e4m3_decode(gscales.numpy())
     wg = dequant_fp4_groupwise(w, gs, 32)
     ts = tscale.to(torch.float32).reshape(*tscale.shape, 1, 1)

@@ -66,3 +66,31 @@ def small_workload(base: str, *, dim=512, inter=256, experts=16, topk=4, n_token
     args.update(over.pop("args", {}))
     return W.Workload(f"{base}_small", args, n_tokens=n_tokens, wfmt=over.pop("wfmt", wl.wfmt),
                       layer_id=wl.layer_id, zipf_alpha=over.pop("zipf_alpha", wl.zipf_alpha), seed=seed, **over)
+
+
+def check_routing(idx_gpu: torch.Tensor, x: torch.Tensor, gate_weight: torch.Tensor, gate_bias: torch.Tensor,
+                  topk: int, score_func: str, route_scale: float, tie_eps: float = 1e-6):
+    """Routing indices of the GPU against the oracle's, with the near-tie rule.
+
+    A token whose top-(k+1) biased scores hold two neighbours within ``tie_eps`` of each
+    other may legitimately order them differently (the last bit of the activation function
+    decides). Such tokens are counted and must be rare (< 1%); for them the GPU's set of
+    experts must still lie within the oracle's top-(k+1) and hold its top-(k-1) whenever the
+    only near tie is the k-th/(k+1)-th. Every other token must match bit for bit, slot order
+    included. Returns ``(clear mask, oracle indices, number of near-tie tokens)``."""
+    x, gw, gb = x.cpu(), gate_weight.cpu(), gate_bias.cpu()
+    _, ref_idx = oracle.gate_forward(x, gw, topk=topk, score_func=score_func, route_scale=route_scale, bias=gb)
+    scores = oracle.moe_oracle._scores(x, gw, score_func) + gb.to(torch.float32)
+    top = torch.topk(scores.to(torch.float64), topk + 1, dim=-1)
+    gaps = top.values[:, :-1] - top.values[:, 1:]  # neighbours in descending order
+    clear = gaps.min(dim=-1).values > tie_eps
+    got = idx_gpu.cpu().to(torch.int64)
+    assert torch.equal(got[clear], ref_idx[clear].to(torch.int64)), "routing indices differ on clear tokens"
+    n_ties = int((~clear).sum())
+    for t in torch.nonzero(~clear).flatten().tolist():
+        allowed = set(top.indices[t].tolist())
+        assert set(got[t].tolist()) <= allowed, f"token {t}: an expert outside the oracle's top-{topk + 1}"
+        if float(gaps[t, :-1].min()) > tie_eps:  # only the k-th / (k+1)-th are near
+            assert set(top.indices[t, :topk - 1].tolist()) <= set(got[t].tolist()), f"token {t}: top-(k-1) lost"
+    assert n_ties < max(1, 0.01 * got.shape[0]), f"{n_ties} near-tie tokens of {got.shape[0]}"
+    return clear, ref_idx, n_ties

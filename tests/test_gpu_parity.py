@@ -15,7 +15,7 @@ from dsm import _lib, workloads as W
 from dsm.config import DSparkArgs
 from dsm.moe import MoE
 from dsm.weights import affine_quantize
-from helpers import MOE_TOL, max_rel_err, oracle_moe, small_workload
+from helpers import MOE_TOL, check_routing, max_rel_err, oracle_moe, small_workload
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -246,35 +246,79 @@ def test_shared_expert_standalone():
     assert max_rel_err(y, ref) < MOE_TOL
 
 
-def test_fp8_decode_full_size_sampled_tokens():
-    """The 56-token fp8 decode block at full size; the oracle checks a sample of tokens."""
-    wl = W.WORKLOADS["fp8_decode"]
+def _full_size_case(name: str):
+    """Runs the full-size workload on the GPU and checks, against the oracle:
+    routing indices (near-tie rule, count reported), per-expert counts / offsets /
+    permutation of the GPU's routing (bit-exact against ``oracle.permutation``), and the MoE
+    output of every token whose routing is clear of near ties."""
+    wl = W.WORKLOADS[name]
     t = W.make_moe_tensors(wl, device=DEV)
     moe = W.build_moe(wl, t, DEV)
     y, rw, ri = moe(t["x"], None, return_routing=True)
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
     assert bool(torch.isfinite(y.float()).all())
-    sample = [0, 13, 27, 55]
-    ref_y, _, ref_i = oracle_moe(wl, t, tokens=sample)
-    assert torch.equal(ri.cpu()[sample], ref_i)
-    assert max_rel_err(y[sample], ref_y) < MOE_TOL
+    a = t["args"]
+    clear, ref_i, n_ties = check_routing(ri, t["x"], t["gate_weight"], t["gate_bias"], a["n_activated_experts"],
+                                         a["score_func"], a["route_scale"])
+    print(f"{name}: {n_ties} near-tie tokens of {wl.n_tokens} excluded from the bit-exact routing check")
+    got = _permute(ri.cpu(), a["n_routed_experts"])
+    for g_, r_, what in zip(got, oracle.permutation(ri.cpu(), a["n_routed_experts"]), ("counts", "offsets", "perm",
+                                                                                      "inv")):
+        assert torch.equal(g_, r_), what
+    return wl, t, moe, y, ri, clear
 
 
-def test_fp4_decode_full_size_sampled_tokens():
-    """The 448-token fp4 block (Zipf-skewed routing) at full size; the oracle checks a sample."""
-    wl = W.WORKLOADS["fp4_decode"]
-    t = W.make_moe_tensors(wl, device=DEV)
-    moe = W.build_moe(wl, t, DEV)
-    y, rw, ri = moe(t["x"], None, return_routing=True)
-    torch.cuda.synchronize()
-    assert _lib.device_error() == 0
+def test_fp8_decode_full_size_all_tokens():
+    """The 56-token fp8 decode block at full size (hidden 4096, 256 experts, top-6): every
+    token against the oracle, which dequantises one expert at a time."""
+    wl, t, moe, y, ri, clear = _full_size_case("fp8_decode")
+    tokens = torch.nonzero(clear).flatten().tolist()
+    ref_y, _, ref_i = oracle_moe(wl, t, tokens=tokens)
+    assert torch.equal(ri.cpu()[tokens], ref_i)
+    assert max_rel_err(y[tokens], ref_y) < MOE_TOL, max_rel_err(y[tokens], ref_y)
+
+
+def test_fp4_decode_full_size_all_tokens():
+    """The 448-token fp4 block (Zipf-skewed routing) at full size: every token against the
+    oracle."""
+    wl, t, moe, y, ri, clear = _full_size_case("fp4_decode")
     counts = torch.bincount(ri.flatten().long(), minlength=256)
     assert int(counts.max()) > 4 * int(counts.float().mean())  # the skew is there
-    sample = [1, 100, 333, 447]
-    ref_y, _, ref_i = oracle_moe(wl, t, tokens=sample)
-    assert torch.equal(ri.cpu()[sample], ref_i)
-    assert max_rel_err(y[sample], ref_y) < MOE_TOL
+    tokens = torch.nonzero(clear).flatten().tolist()
+    ref_y, _, ref_i = oracle_moe(wl, t, tokens=tokens)
+    assert torch.equal(ri.cpu()[tokens], ref_i)
+    assert max_rel_err(y[tokens], ref_y) < MOE_TOL, max_rel_err(y[tokens], ref_y)
+
+
+def test_prefill_full_size():
+    """The prefill stress case at its own shapes: 16384 tokens, 256 experts, top-8, hidden
+    4096, inter 2048, fp8 128x128 block scales, Zipf(1.2) popularity, on the tcgen05 regime.
+    Routing and the permutation are checked for all 16384 tokens; the MoE output on a sample
+    that holds rows of the most-loaded expert (first, last and middle), every row of the
+    least-loaded busy expert, and random tokens."""
+    wl, t, moe, y, ri, clear = _full_size_case("prefill_fp8")
+    E = wl.args["n_routed_experts"]
+    counts = torch.bincount(ri.cpu().flatten().long(), minlength=E)
+    assert int(counts.max()) > 1000 and int(counts.min()) <= 4  # the Zipf skew: >1000 rows and (near-)empty experts
+    pairs_tok = torch.arange(ri.shape[0]).repeat_interleave(ri.shape[1])
+    flat = ri.cpu().flatten().long()
+    e_max = int(counts.argmax())
+    busy = torch.nonzero(counts > 0).flatten()
+    e_min = int(busy[counts[busy].argmin()])
+    tok_max = pairs_tok[flat == e_max]
+    tok_min = pairs_tok[flat == e_min]
+    g = torch.Generator().manual_seed(99)
+    sample = {int(tok_max[0]), int(tok_max[len(tok_max) // 2]), int(tok_max[-1])}
+    sample |= {int(v) for v in tok_min[:4]}
+    sample |= {int(v) for v in torch.randint(0, wl.n_tokens, (6,), generator=g)}
+    tokens = sorted(v for v in sample if bool(clear[v]))
+    print(f"prefill: expert {e_max} has {int(counts[e_max])} rows, expert {e_min} {int(counts[e_min])}; "
+          f"{int((counts == 0).sum())} experts empty; output checked on tokens {tokens}")
+    assert len(tokens) >= 8
+    ref_y, _, ref_i = oracle_moe(wl, t, tokens=tokens)
+    assert torch.equal(ri.cpu()[tokens], ref_i)
+    assert max_rel_err(y[tokens], ref_y) < MOE_TOL, max_rel_err(y[tokens], ref_y)
 
 
 def test_fp8_decode_batch_invariance():
