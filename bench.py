@@ -112,6 +112,25 @@ def _dist():
     return ws, rank, local
 
 
+def _init_dist(ws, dev):
+    """One NCCL process group per run (several workloads may run in one process)."""
+    if ws <= 1:
+        return
+    import datetime
+
+    import torch.distributed as dist
+
+    if not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+
+def _finish_dist():
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        dist.destroy_process_group()
+
+
 def _barrier(ws):
     if ws > 1:
         import torch.distributed as dist
@@ -207,7 +226,9 @@ def run_reference(args):
     wl = W.WORKLOADS[args.workload]
     t = W.make_moe_tensors(wl, device="cpu", routed=False)
     threads = os.cpu_count() or 1
-    sample = min(8, wl.n_tokens)
+    # the whole call for the decode workloads (the GPU arm's own config); a bounded sample of
+    # the 16384-token prefill call
+    sample = wl.n_tokens if wl.n_tokens <= 512 else 16
     ref = CpuReference(wl, t, lambda ids: W.expert_tensors(wl, ids), sample, threads)
     vals = []
     for i in range(args.warmup + args.steps):
@@ -222,19 +243,38 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wl.n_tokens / value,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (bf16 in/out)",
         "data": "synthetic",
-        "config": {"workload": wl.name, "tokens_per_step": wl.n_tokens, "dim": wl.args["dim"],
-                   "n_experts": wl.args["n_routed_experts"], "topk": wl.args["n_activated_experts"],
-                   "inter": wl.args["moe_inter_dim"], "weights": wl.wfmt},
+        "config": moe_config(wl, args.gpus),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"one call per step on {sample} of the {wl.n_tokens} tokens, experts dequantised "
-                                   f"to fp32 before timing (the reference dequantises at load); CPU restatement of "
-                                   f"MoE.__call__ in PyTorch (mlx is not installable here)"},
+                         "sample": (f"the whole {wl.n_tokens}-token call per step" if sample == wl.n_tokens else
+                                    f"one call per step on {sample} of the {wl.n_tokens} tokens") +
+                                   ", the touched experts dequantised to fp32 before timing (the reference dequantises "
+                                   "at load); CPU restatement of MoE.__call__ in PyTorch (mlx is not installable "
+                                   "here)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
 
 
-def run_gpu(args):
+def moe_config(wl, ws: int) -> dict:
+    """The ``config`` object of a MoE workload's line (the same for the GPU and the reference arm)."""
+    a = wl.args
+    return {"workload": wl.name, "tokens_per_step_per_gpu": wl.n_tokens, "batch": wl.batch, "draft_block": wl.block,
+            "dim": a["dim"], "n_experts": a["n_routed_experts"], "topk": a["n_activated_experts"],
+            "inter": a["moe_inter_dim"], "weights": wl.wfmt, "score_func": a["score_func"],
+            "routing": "hash" if wl.layer_id < a.get("n_hash_layers", 0) else
+            (f"zipf({wl.zipf_alpha})" if wl.zipf_alpha else "uniform"),
+            "parallelism": f"ep{ws} (experts sharded, NCCL all-to-all)" if ws > 1 else "single",
+            "l2": "inputs larger than L2 (touched expert weights exceed L2, 4 rotating token batches)"
+            if wl.name != "tiny_hash" else "tiny: weights (3 MB) L2-resident, as in the reference's latency case"}
+
+
+# Tokens of each MoE workload that the CPU baseline inside the GPU run takes per call (None:
+# the whole call). The large calls are bounded so the default run ends within minutes.
+CPU_SAMPLE = {"fp8_decode": None, "tiny_hash": None, "fp4_decode": 56, "prefill_fp8": 16}
+
+
+def run_gpu(args, wl_name=None, emit=True):
+    """One MoE workload on this rank's GPU; returns (and with ``emit`` prints) its JSON line."""
     import ctypes
 
     import torch
@@ -244,18 +284,18 @@ def run_gpu(args):
     ws, rank, local = _dist()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if ws > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    wl = W.WORKLOADS[args.workload]
+    _init_dist(ws, dev)
+    wl = W.WORKLOADS[wl_name or args.workload]
     if args.experts:
         # a smaller expert pool with every per-expert shape unchanged (profiling captures)
         import dataclasses
 
         wl = dataclasses.replace(wl, args=dict(wl.args, n_routed_experts=args.experts))
+    if args.tokens:
+        # fewer tokens per call, every other shape unchanged (small profiling captures)
+        import dataclasses
+
+        wl = dataclasses.replace(wl, n_tokens=args.tokens)
     # every rank holds the same weights; each rank routes its own tokens
     t = W.make_moe_tensors(wl, device=dev, seed=wl.seed)
     moe = W.build_moe(wl, t, dev)
@@ -388,21 +428,21 @@ def run_gpu(args):
                 keys = [k for k in t if k[:2] in ("w1", "w2", "w3")]
                 return {k: t[k][ids].cpu() for k in keys}
 
-            v, n, el = CpuReference(wl, t, experts, min(8, N), threads).timed(args.cpu_seconds)
+            cpu_n = CPU_SAMPLE.get(wl.name) or N
+            budget = args.cpu_seconds if wl.name == "fp8_decode" else min(args.cpu_seconds, 8.0)
+            v, n, el = CpuReference(wl, t, experts, cpu_n, threads).timed(budget)
+            what = f"the whole {N}-token call" if cpu_n >= N else f"{cpu_n} of the {N} tokens per call"
             cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                   "sample": f"{min(8, N)} of the {N} tokens, {n} calls in {el:.1f} s; experts dequantised to fp32 "
-                             f"before timing; CPU restatement of MoE.__call__ in PyTorch"}
+                   "sample": f"{what}, {n} calls in {el:.1f} s; the touched experts dequantised to fp32 before "
+                             f"timing (the reference dequantises at load); CPU restatement of MoE.__call__ in "
+                             f"PyTorch"}
         value = ws * N / (ms * 1e-3)
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": DTYPE_DESC.get(wl.wfmt, wl.wfmt),
             "data": "synthetic",
-            "config": {"workload": wl.name, "tokens_per_step_per_gpu": N, "batch": wl.batch, "draft_block": wl.block,
-                       "dim": dim, "n_experts": wl.args["n_routed_experts"], "topk": wl.args["n_activated_experts"],
-                       "inter": wl.args["moe_inter_dim"], "weights": wl.wfmt,
-                       "parallelism": f"ep{ws} (experts sharded, NCCL all-to-all)" if ws > 1 else "single",
-                       "l2": "inputs larger than L2 (touched expert weights ~GB per step, 4 rotating token batches)"},
+            "config": moe_config(wl, ws),
             "draft_block_latency_ms": ms,
             "hbm_gbs_step": avg_step_bytes / (ms * 1e-3) / 1e9,
             "hbm_frac_of_8tbs_step": avg_step_bytes / (ms * 1e-3) / 1e9 / SPEC_HBM_GBS,
@@ -415,11 +455,10 @@ def run_gpu(args):
             "gpu_launches": (KERNELS_PER_STEP if ws == 1 else KERNELS_PER_STEP_EP) * args.steps,
             "clocks": clk.summary(),
         }
-        print(json.dumps(line))
-    if ws > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
+        if emit:
+            print(json.dumps(line))
+        return line
+    return None
 
 
 # arithmetic of the routed expert products per weight format
@@ -550,7 +589,7 @@ def _qwen3_cpu_timed(x, weights, sample, budget_s, max_calls=1000):
     return sample * n / el, n, el
 
 
-def run_qwen3(args):
+def run_qwen3(args, emit=True):
     """One step = one Qwen3 MLP call (hidden 2560, inter 9728, 8-bit affine g64) on 16 x 7
     draft tokens. The quantised weights (79 MB) fit in L2, so L2 is flushed (a 256 MB write)
     before every timed call, outside the CUDA-event bracket of that call."""
@@ -563,13 +602,8 @@ def run_qwen3(args):
     ws, rank, local = _dist()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if ws > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    wl = W.WORKLOADS[args.workload]
+    _init_dist(ws, dev)
+    wl = W.WORKLOADS["qwen3_mlp_q8"]
     t = W.make_qwen3_tensors(wl, device=dev)
     mlp = W.build_qwen3_mlp(wl, t, dev)
     N, h, inter = wl.n_tokens, wl.args["hidden_size"], wl.args["intermediate_size"]
@@ -642,9 +676,9 @@ def run_qwen3(args):
     if rank == 0:
         cpu = None
         if ws == 1 and not args.no_cpu_baseline:
-            v, n, el = _qwen3_cpu_timed(t["x"], _qwen3_cpu_weights(mlp), min(8, N), args.cpu_seconds)
+            v, n, el = _qwen3_cpu_timed(t["x"], _qwen3_cpu_weights(mlp), N, min(args.cpu_seconds, 8.0))
             cpu = {"value": v, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
-                   "sample": f"{min(8, N)} of the {N} tokens, {n} calls in {el:.1f} s; weights dequantised to "
+                   "sample": f"the whole {N}-token call, {n} calls in {el:.1f} s; weights dequantised to "
                              f"fp32 before timing; CPU restatement of Qwen3MLP.__call__ in PyTorch"}
         line = {
             "metric": QWEN3_METRIC, "value": ws * N / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws,
@@ -664,11 +698,10 @@ def run_qwen3(args):
             "gpu_launches": QWEN3_KERNELS_PER_STEP * args.steps,
             "clocks": clk.summary(),
         }
-        print(json.dumps(line))
-    if ws > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
+        if emit:
+            print(json.dumps(line))
+        return line
+    return None
 
 
 def run_reference_qwen3(args):
@@ -764,12 +797,7 @@ def run_head(args):
     ws, rank, local = _dist()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if ws > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    _init_dist(ws, dev)
     wl = W.WORKLOADS["draft_head"]
     t = W.make_head_tensors(wl, device=dev, seed=rank)
     head = W.build_head(wl, t, dev)
@@ -866,10 +894,6 @@ def run_head(args):
             "clocks": clk.summary(),
         }
         print(json.dumps(line))
-    if ws > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
 
 
 def run_reference_head(args):
@@ -961,12 +985,7 @@ def run_gqa(args):
     torch.cuda.set_device(local)
     _lib.check(_lib.lib().dsm_set_attn_kernel(0 if args.attn_kernel == "mma" else 1), "dsm_set_attn_kernel")
     dev = torch.device("cuda", local)
-    if ws > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    _init_dist(ws, dev)
     layer_mode = args.workload == "qwen3_layer_q8"
     wl = W.WORKLOADS[args.workload]
     a = wl.args
@@ -1081,10 +1100,6 @@ def run_gqa(args):
             "clocks": clk.summary(),
         }
         print(json.dumps(line))
-    if ws > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
 
 
 def run_reference_gqa(args):
@@ -1173,12 +1188,7 @@ def run_dsattn(args):
     torch.cuda.set_device(local)
     _lib.check(_lib.lib().dsm_set_attn_kernel(0 if args.attn_kernel == "mma" else 1), "dsm_set_attn_kernel")
     dev = torch.device("cuda", local)
-    if ws > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    _init_dist(ws, dev)
     wl = W.WORKLOADS["draft_attn_dsv4"]
     a = wl.args
     t = W.make_dsattn_tensors(wl, device=dev, seed=rank)
@@ -1281,10 +1291,6 @@ def run_dsattn(args):
             "clocks": clk.summary(),
         }
         print(json.dumps(line))
-    if ws > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
 
 
 def run_reference_dsattn(args):
@@ -1317,23 +1323,62 @@ def run_reference_dsattn(args):
     print(json.dumps(line))
 
 
+# The other single-GPU configurations, measured in the same process and run as the headline
+# (fp8 decode) and carried in its line under "configs": the tiny hash-routed layer (latency),
+# fp4 decode (448 tokens, Zipf 1.1), the Qwen3 q8 MLP and the 16384-token prefill.
+SIDE_CONFIGS = ("tiny_hash", "fp4_decode", "qwen3_mlp_q8", "prefill_fp8")
+# expert parallelism: fp4 decode is the other configuration the reference quotes at 1/2/4/8 GPUs
+SIDE_CONFIGS_EP = ("fp4_decode",)
+CONFIG_KEYS = ("metric", "value", "unit", "ms_per_step", "higher_is_better", "dtype", "config", "hbm_gbs_step",
+               "roofline", "cpu_baseline", "e2e", "gpu_launches", "clocks")
+
+
+def run_all(args):
+    """The default run: the fp8 decode headline line, with every other configuration's numbers
+    (value, roofline, CPU baseline, e2e, clocks) under ``configs``."""
+    import torch
+
+    ws, rank, _ = _dist()
+    head = run_gpu(args, "fp8_decode", emit=False)
+    configs = {}
+    for name in (SIDE_CONFIGS if ws == 1 else SIDE_CONFIGS_EP):
+        torch.cuda.empty_cache()
+        line = run_qwen3(args, emit=False) if name.startswith("qwen3") else run_gpu(args, name, emit=False)
+        if rank == 0:
+            configs[name] = {k: line.get(k) for k in CONFIG_KEYS}
+    if rank == 0:
+        head["configs"] = configs
+        print(json.dumps(head))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--workload", default="fp8_decode")
+    ap.add_argument("--workload", default=None,
+                    help="one workload alone (default: fp8 decode with every other configuration under configs)")
     ap.add_argument("--impl", default="dsm", choices=["dsm", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-kernel-timing", action="store_true")
     ap.add_argument("--experts", type=int, default=0, help="shrink the routed expert pool (profiling)")
+    ap.add_argument("--tokens", type=int, default=0, help="override a MoE workload's tokens per call (profiling)")
     ap.add_argument("--attn-kernel", default="cuda", choices=["cuda", "mma"],
                     help="attention workloads: CUDA-core kernels, or the tensor-core ones where they apply")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload is None:
+        if args.impl == "reference":
+            args.workload = "fp8_decode"
+        else:
+            try:
+                run_all(args)
+            finally:
+                _finish_dist()
+            return
     qwen3 = args.workload.startswith("qwen3")
     if args.workload == "draft_head":
         (run_reference_head if args.impl == "reference" else run_head)(args)
@@ -1344,7 +1389,12 @@ def main():
     elif args.impl == "reference":
         (run_reference_qwen3 if qwen3 else run_reference)(args)
     else:
-        (run_qwen3 if qwen3 else run_gpu)(args)
+        try:
+            (run_qwen3 if qwen3 else run_gpu)(args)
+        finally:
+            _finish_dist()
+        return
+    _finish_dist()
 
 
 if __name__ == "__main__":
