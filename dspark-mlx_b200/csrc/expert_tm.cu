@@ -376,12 +376,14 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
           uint32_t out[C::kCols];
           if constexpr (!C::kAffine) {
             const uint32_t sw = lds32(meta + row * 4);  // e4m3 scales of the row's 4 groups
+            uint32_t sp_lo, sp_hi;  // the 4 scales as f16 pairs: two conversions per row and stage
+            e4m3x4_to_f16(sw, sp_lo, sp_hi);
 #pragma unroll
             for (int c = 0; c < C::kChunks; ++c) {
               const int cc = part * C::kChunks + c;
               const uint4 v = lds128(raw + (cc * kTmM + row) * 16);
-              const uint32_t sf = e4m3_to_f16_bits((sw >> (8 * cc)) & 0xFFu);
-              const uint32_t s2 = sf | (sf << 16);
+              const uint32_t sp = (cc >> 1) ? sp_hi : sp_lo;
+              const uint32_t s2 = __byte_perm(sp, 0, (cc & 1) ? 0x3232 : 0x1010);
               const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
               for (int wi = 0; wi < 4; ++wi) {
