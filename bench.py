@@ -1365,7 +1365,7 @@ def main():
     ap.add_argument("--no-kernel-timing", action="store_true")
     ap.add_argument("--experts", type=int, default=0, help="shrink the routed expert pool (profiling)")
     ap.add_argument("--tokens", type=int, default=0, help="override a MoE workload's tokens per call (profiling)")
-    ap.add_argument("--attn-kernel", default="cuda", choices=["cuda", "mma"],
+    ap.add_argument("--attn-kernel", default="mma", choices=["cuda", "mma"],
                     help="attention workloads: CUDA-core kernels, or the tensor-core ones where they apply")
     args = ap.parse_args()
     if args.warmup < 3:

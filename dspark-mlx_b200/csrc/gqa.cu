@@ -654,9 +654,9 @@ extern "C" int dsm_gqa_attn(const void* q, const void* ctx_k, const void* ctx_v,
 
 namespace dsm {
 namespace {
-// 0: the tensor-core attention kernels wherever they apply, 1: the CUDA-core kernels; per
+// 0 (default): the tensor-core attention kernels wherever they apply, 1: the CUDA-core kernels; per
 // host thread, so one caller's choice never changes another thread's launches
-thread_local int g_attn_kernel = 1;
+thread_local int g_attn_kernel = 0;
 }  // namespace
 int attn_kernel() { return g_attn_kernel; }
 }  // namespace dsm

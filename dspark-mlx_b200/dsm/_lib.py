@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libdsm.so")
 # status / enums (mirror include/dsm.h)
 DSM_OK = 0
 DT_F32, DT_BF16, DT_F16, DT_I32, DT_I64 = 0, 1, 2, 3, 4
+ATTN_KERNEL_DEFAULT = 0  # dsm_set_attn_kernel's default: the tensor-core attention kernels
 SCORE = {"softmax": 0, "sigmoid": 1, "sqrtsoftplus": 2}
 WFMT_F16, WFMT_FP8_B128, WFMT_FP4_G32, WFMT_AFFINE8, WFMT_AFFINE4 = 0, 1, 2, 3, 4
 ACT_SWIGLU_CLAMP, ACT_SILU_MUL_BF16 = 0, 1

@@ -323,11 +323,11 @@ int dsm_round_rows(const float* in, const float* in_lo, int64_t n, void* out, in
  *   blk_k / blk_v [batch, n_kv, block, head_dim]; q is [batch, block, n_heads, head_dim].
  *   head_dim 32, 64, 128 or 256. workspace: dsm_gqa_attn_workspace_bytes (fp32 partials of
  *   the key ranges).
- * set_attn_kernel: 0 runs bf16 attention on the tensor-core kernels (mma.m16n8k16) where
+ * set_attn_kernel: 0 (the default) runs bf16 attention on the tensor-core kernels (mma.m16n8k16) where
  *   they apply: dsm_gqa_attn with head_dim 64 / 128, every pointer 16-byte aligned and the
  *   context strides multiples of 8; dsm_sparse_attn with head_dim 64..512 (a multiple of 64),
  *   at most 256 keys, q / window / block rows 16-byte aligned. Elsewhere the CUDA-core kernels
- *   run. 1 (the default) runs the CUDA-core kernels everywhere. The choice holds for the
+ *   run. 1 runs the CUDA-core kernels everywhere. The choice holds for the
  *   calling host thread only (thread-local): other threads keep their own. */
 int dsm_qkv_norm_rope(const float* in, const float* in_lo, int64_t n_rows, int n_q, int n_kv, int head_dim,
                       const float* q_norm_w, const float* k_norm_w, float eps, const float* cos_t, const float* sin_t,

@@ -32,7 +32,7 @@ def pytest_collection_modifyitems(config, items):
 def attn_kernel(request):
     """Runs a test once per attention kernel family: 1 the CUDA-core kernels, 0 the tensor-core
     (mma.m16n8k16) kernels wherever they apply (bf16). The switch is per host thread; it is put
-    back to the default (1) afterwards."""
+    back to the library default afterwards."""
     from dsm import _lib
 
     L = _lib.lib()
@@ -40,4 +40,4 @@ def attn_kernel(request):
     try:
         yield request.param
     finally:
-        _lib.check(L.dsm_set_attn_kernel(1))
+        _lib.check(L.dsm_set_attn_kernel(_lib.ATTN_KERNEL_DEFAULT))

@@ -196,7 +196,7 @@ def test_qwen3_attention_kernels_agree(ctx):
             outs.append(attn.attend_cached(t["x"], kc, vc, cos, sin))
             torch.cuda.synchronize()
         finally:
-            _lib.check(L.dsm_set_attn_kernel(1))
+            _lib.check(L.dsm_set_attn_kernel(_lib.ATTN_KERNEL_DEFAULT))
     assert torch.isfinite(outs[1].float()).all()
     assert max_rel_err(outs[1], outs[0]) < 1e-2, max_rel_err(outs[1], outs[0])
     assert _lib.device_error() == 0

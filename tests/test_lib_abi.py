@@ -135,6 +135,7 @@ def test_gqa_attention_entry_points_reject_bad_arguments_on_the_host():
     assert L.dsm_gqa_attn_workspace_bytes(1, 7, 32, 8, 128, 2048) == 32 * 7 * 66 * 130 * 4
     assert L.dsm_gqa_attn_workspace_bytes(1, 7, 32, 8, 128, 0) == 32 * 7 * 2 * 130 * 4
     assert L.dsm_set_attn_kernel(2) != 0 and L.dsm_set_attn_kernel(1) == 0
+    assert L.dsm_set_attn_kernel(_lib.ATTN_KERNEL_DEFAULT) == 0
     # split-K linear: up to 8 fp32 partial slabs; bad format, group size and shapes rejected
     assert L.dsm_linear_splitk_workspace_bytes(112, 1024) == 8 * 112 * 1024 * 4
     assert L.dsm_linear_splitk(1, 1, 1 << 10, 2560, 9, 64, 1, 1024, 1, 1024, 112, 1, 1 << 30, None) != 0
