@@ -123,19 +123,27 @@ class DSparkBlock(nn.Module):
             self._main_cache = (key, pack("dense", data=w.detach(), device=w.device))
         return self._main_cache[1]
 
+    def project_main(self, main_hidden: torch.Tensor) -> torch.Tensor:
+        """``main_norm(main_proj(main_hidden))`` over the last dimension (stage 0), the rows the
+        window and the attention read (``block.py:96`` and ``drafter.py:50-51``)."""
+        if self.stage_id != 0:
+            raise ValueError("the main projection belongs to stage 0")
+        if not main_hidden.is_cuda:
+            raise ValueError("DSparkBlock runs on the GPU only")
+        dt = main_hidden.dtype if main_hidden.dtype in (torch.bfloat16, torch.float32) else torch.float32
+        mh = main_hidden.to(dt).contiguous()
+        lead = mh.shape[:-1]
+        mh2 = mh.reshape(-1, mh.shape[-1])
+        main_x = self.attn._norm_rope(mh2, self._packed_main(), self.main_norm.weight, False, 0, 1)
+        return main_x.reshape(*lead, self.dim)
+
     def forward_embed(self, main_hidden: torch.Tensor, input_ids: torch.Tensor, embed: nn.Module):
         """``(x [b, block, hc, dim], main_x [b, seqlen, dim])``; ``embed`` holds ``weight [vocab, dim]``."""
         if self.stage_id != 0:
             raise ValueError("forward_embed belongs to stage 0")
         if not (main_hidden.is_cuda and input_ids.is_cuda):
             raise ValueError("DSparkBlock runs on the GPU only")
-        dt = main_hidden.dtype if main_hidden.dtype in (torch.bfloat16, torch.float32) else torch.float32
-        mh = main_hidden.to(dt).contiguous()
-        lead = mh.shape[:-1]
-        mh2 = mh.reshape(-1, mh.shape[-1])
-        n = mh2.shape[0]
-        main_x = self.attn._norm_rope(mh2, self._packed_main(), self.main_norm.weight, False, 0, 1)
-        main_x = main_x.reshape(*lead, self.dim)
+        main_x = self.project_main(main_hidden)
         b = input_ids.shape[0]
         w = embed.weight.detach()
         if w.dtype not in (torch.bfloat16, torch.float32):

@@ -12,3 +12,4 @@ from .head_oracle import *  # noqa: F401,F403
 from .attention_oracle import *  # noqa: F401,F403
 from .qwen3_attn_oracle import *  # noqa: F401,F403
 from .draft_block_oracle import *  # noqa: F401,F403
+from .drafter_oracle import *  # noqa: F401,F403
