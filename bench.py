@@ -32,8 +32,9 @@ sys.path.insert(0, ROOT)
 METRIC = "MoE-layer tokens/s & draft-block latency; HBM GB/s vs 8 TB/s at 1/2/4/8 B200"
 SPEC_HBM_GBS = 8000.0
 KERNELS_PER_STEP = 10  # router 3, permute 1, staging 1, routed gate/up + down 2, shared gate/up + down 2, combine 1
-# expert-parallel step: router 3, permute 2, gather 1, shared 3, segment ids 1, staging 1, gate/up + down 2, combine 1
-KERNELS_PER_STEP_EP = 14
+# expert-parallel step: router 3, permute 1, dispatch 1, shared expert 3 (staging, gate/up, down), receive 1,
+# staging 1, gate/up + down 2, return 1, wait 1, combine 1
+KERNELS_PER_STEP_EP = 15
 
 
 def _peaks():
@@ -263,7 +264,7 @@ def moe_config(wl, ws: int) -> dict:
             "inter": a["moe_inter_dim"], "weights": wl.wfmt, "score_func": a["score_func"],
             "routing": "hash" if wl.layer_id < a.get("n_hash_layers", 0) else
             (f"zipf({wl.zipf_alpha})" if wl.zipf_alpha else "uniform"),
-            "parallelism": f"ep{ws} (experts sharded, NCCL all-to-all)" if ws > 1 else "single",
+            "parallelism": f"ep{ws} (experts sharded, peer stores over NVLink)" if ws > 1 else "single",
             "l2": "inputs larger than L2 (touched expert weights exceed L2, 4 rotating token batches)"
             if wl.name != "tiny_hash" else "tiny: weights (3 MB) L2-resident, as in the reference's latency case"}
 
@@ -334,7 +335,7 @@ def run_gpu(args, wl_name=None, emit=True):
         from dsm.config import DSparkArgs
         from dsm.ep import ExpertParallelMoE
 
-        model = ExpertParallelMoE.from_moe(moe, DSparkArgs.from_dict(t["args"]), wl.layer_id)
+        model = ExpertParallelMoE.from_moe(moe, DSparkArgs.from_dict(t["args"]), wl.layer_id, max_tokens=N)
         del moe
         t = {k: v for k, v in t.items() if not (k[:2] in ("w1", "w2", "w3"))}
         torch.cuda.empty_cache()

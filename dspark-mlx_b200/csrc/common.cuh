@@ -79,7 +79,7 @@ int attn_kernel();
 // n_rows_b > 0, the first n_rows_b tokens in order (job b). Arguments as dsm_stage_rows.
 int stage_rows_pair(const void* x, int x_dtype, int64_t n_tokens, int dim, const int32_t* perm, int64_t n_rows,
                     int topk, void* staged, int64_t rows_cap, float* row_scale, int64_t n_rows_b, void* staged_b,
-                    int64_t rows_cap_b, float* row_scale_b, void* stream);
+                    int64_t rows_cap_b, float* row_scale_b, void* stream, const int32_t* n_valid = nullptr);
 
 // Stage fp32 rows as two f16 rows each: row r the row itself (as dsm_stage_rows does), row
 // n_rows + r the residual x - hi, with its own power-of-two scale, so that a product over both

@@ -11,6 +11,8 @@
 // the scaled range sits inside f16's normal range; only entries below 2^-28 of the row
 // maximum lose bits), so the f16 tensor-core products see the reference's bf16 operand.
 // row_scale[r] = 2^-s undoes it in the epilogue.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace dsm {
@@ -47,23 +49,18 @@ struct StageJob {
   __half* staged;
   int64_t rows_cap;
   float* row_scale;
+  const int32_t* n_valid;  // the count of rows to stage (stage_rows_count_kernel only)
 };
 
-// One CTA per staged row: 16-byte loads, block max, one 16-byte store per 8 columns.
-// Blocks [0, n_rows) serve job a; blocks [n_rows, n_rows + n_rows_b) serve job b.
+// One staged row: 16-byte loads, block max, one 16-byte store per 8 columns (the whole CTA).
 template <typename XT>
-__global__ void __launch_bounds__(kStageThreads) stage_rows_kernel(const XT* __restrict__ x, int64_t n_tokens, int dim,
-                                                                   int64_t n_rows, StageJob ja, StageJob jb,
-                                                                   int k_chunks) {
-  __shared__ float red[kStageThreads / 32];
-  const bool second = int64_t(blockIdx.x) >= n_rows;
-  const StageJob& j = second ? jb : ja;
+__device__ __forceinline__ void stage_one_row(const XT* __restrict__ x, int64_t n_tokens, int dim, int64_t r,
+                                              const StageJob& j, int k_chunks, float* red) {
   const int32_t* __restrict__ perm = j.perm;
   const int topk = j.topk;
   __half* __restrict__ staged = j.staged;
   const int64_t rows_cap = j.rows_cap;
   float* __restrict__ row_scale = j.row_scale;
-  const int64_t r = second ? int64_t(blockIdx.x) - n_rows : int64_t(blockIdx.x);
   int64_t t = perm ? int64_t(perm[r]) / topk : r;
   if (t < 0 || t >= n_tokens) {
     if (threadIdx.x == 0) raise_device_error(DSM_DEV_ERR_TOKEN_RANGE);
@@ -81,6 +78,7 @@ __global__ void __launch_bounds__(kStageThreads) stage_rows_kernel(const XT* __r
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  __syncthreads();  // red is reused by the next row of a looping CTA
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
   amax = red[0];
@@ -107,6 +105,27 @@ __global__ void __launch_bounds__(kStageThreads) stage_rows_kernel(const XT* __r
     const int c = k / kChunkK, col = k % kChunkK;
     *reinterpret_cast<uint4*>(staged + (int64_t(c) * rows_cap + r) * kStagePitch + col) = make_uint4(h[0], h[1], h[2], h[3]);
   }
+}
+
+// One CTA per staged row. Blocks [0, n_rows) serve job a; blocks [n_rows, n_rows + n_rows_b)
+// serve job b.
+template <typename XT>
+__global__ void __launch_bounds__(kStageThreads) stage_rows_kernel(const XT* __restrict__ x, int64_t n_tokens, int dim,
+                                                                   int64_t n_rows, StageJob ja, StageJob jb,
+                                                                   int k_chunks) {
+  __shared__ float red[kStageThreads / 32];
+  const bool second = int64_t(blockIdx.x) >= n_rows;
+  const int64_t r = second ? int64_t(blockIdx.x) - n_rows : int64_t(blockIdx.x);
+  stage_one_row(x, n_tokens, dim, r, second ? jb : ja, k_chunks, red);
+}
+
+// Rows r < *j.n_valid (a device count), the CTAs striding over them.
+template <typename XT>
+__global__ void __launch_bounds__(kStageThreads) stage_rows_count_kernel(const XT* __restrict__ x, int64_t n_tokens,
+                                                                         int dim, StageJob j, int k_chunks) {
+  __shared__ float red[kStageThreads / 32];
+  const int64_t n = *j.n_valid;
+  for (int64_t r = blockIdx.x; r < n; r += gridDim.x) stage_one_row(x, n_tokens, dim, r, j, k_chunks, red);
 }
 
 // One CTA per fp32 row: the row staged as stage_rows_kernel does (row r), then the residual
@@ -202,6 +221,23 @@ extern "C" int dsm_stage_rows(const void* x, int x_dtype, int64_t n_tokens, int 
                          nullptr, stream);
 }
 
+extern "C" int dsm_stage_rows_count(const void* x, int x_dtype, int64_t n_tokens, int dim, const int32_t* perm,
+                                    int64_t max_rows, int topk, void* staged, int64_t rows_cap, float* row_scale,
+                                    const int32_t* n_valid, void* stream) {
+  using namespace dsm;
+  DSM_REQUIRE(n_valid != nullptr, "dsm_stage_rows_count: n_valid is NULL");
+  DSM_REQUIRE(dim > 0 && max_rows >= 0 && n_tokens >= 0, "dsm_stage_rows_count: bad shape");
+  DSM_REQUIRE(rows_cap >= dsm_stage_rows_cap(max_rows), "dsm_stage_rows_count: rows_cap too small");
+  DSM_REQUIRE(x_dtype == DSM_DT_F32 || x_dtype == DSM_DT_BF16, "dsm_stage_rows_count: x must be F32 or BF16");
+  DSM_REQUIRE(!perm || topk >= 1, "dsm_stage_rows_count: topk must be >= 1 with a permutation");
+  if (max_rows == 0) return DSM_OK;
+  DSM_REQUIRE(x && staged && row_scale, "dsm_stage_rows_count: NULL pointer");
+  DSM_REQUIRE((reinterpret_cast<uintptr_t>(staged) & 15) == 0, "dsm_stage_rows_count: staged must be 16-byte aligned");
+  DSM_REQUIRE(max_rows < (int64_t(1) << 31), "dsm_stage_rows_count: too many rows");
+  return stage_rows_pair(x, x_dtype, n_tokens, dim, perm, max_rows, topk, staged, rows_cap, row_scale, 0, nullptr, 0,
+                         nullptr, stream, n_valid);
+}
+
 extern "C" int dsm_stage_rows_hilo(const float* x, int64_t n_rows, int dim, void* staged, int64_t rows_cap,
                                    float* row_scale, void* stream) {
   using namespace dsm;
@@ -228,10 +264,22 @@ int stage_rows_hilo(const float* x, int64_t n_rows, int dim, void* staged, int64
 
 int stage_rows_pair(const void* x, int x_dtype, int64_t n_tokens, int dim, const int32_t* perm, int64_t n_rows,
                     int topk, void* staged, int64_t rows_cap, float* row_scale, int64_t n_rows_b, void* staged_b,
-                    int64_t rows_cap_b, float* row_scale_b, void* stream) {
+                    int64_t rows_cap_b, float* row_scale_b, void* stream, const int32_t* n_valid) {
   const int kc = int(ceil_div(dim, kChunkK));
-  const StageJob ja{perm, topk, static_cast<__half*>(staged), rows_cap, row_scale};
-  const StageJob jb{nullptr, 1, static_cast<__half*>(staged_b), rows_cap_b, row_scale_b};
+  const StageJob ja{perm, topk, static_cast<__half*>(staged), rows_cap, row_scale, n_valid};
+  const StageJob jb{nullptr, 1, static_cast<__half*>(staged_b), rows_cap_b, row_scale_b, nullptr};
+  if (n_valid) {  // job a only, over a device count of at most n_rows rows
+    const unsigned grid = unsigned(std::min<int64_t>(n_rows, 8 * int64_t(num_sms())));
+    cudaStream_t s = as_stream(stream);
+    if (grid == 0) return DSM_OK;
+    if (x_dtype == DSM_DT_BF16)
+      stage_rows_count_kernel<__nv_bfloat16><<<grid, kStageThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                                            n_tokens, dim, ja, kc);
+    else
+      stage_rows_count_kernel<float><<<grid, kStageThreads, 0, s>>>(static_cast<const float*>(x), n_tokens, dim, ja,
+                                                                    kc);
+    return check_launch("stage_rows_count");
+  }
   const unsigned blocks = unsigned(n_rows + n_rows_b);
   if (blocks == 0) return DSM_OK;
   cudaStream_t s = as_stream(stream);

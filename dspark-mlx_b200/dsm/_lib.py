@@ -23,14 +23,18 @@ WFMT_F16, WFMT_FP8_B128, WFMT_FP4_G32, WFMT_AFFINE8, WFMT_AFFINE4 = 0, 1, 2, 3, 
 ACT_SWIGLU_CLAMP, ACT_SILU_MUL_BF16 = 0, 1
 STAGE_PITCH = 160
 DEVICE_ERRORS = {0x10: "expert id out of range", 0x11: "token id out of range",
-                 0x12: "pipeline wait ran out of its time budget"}
+                 0x12: "pipeline wait ran out of its time budget",
+                 0x13: "an expert-parallel peer did not signal in time",
+                 0x14: "more expert-parallel rows than the exchange buffer holds"}
 
 EXPORTED = (
     "dsm_abi_version", "dsm_status_string", "dsm_last_error_message", "dsm_device_error",
     "dsm_router_workspace_bytes", "dsm_router", "dsm_router_noalloc", "dsm_permute_workspace_bytes", "dsm_permute", "dsm_stage_bytes",
     "dsm_stage_rows_cap", "dsm_stage_rows", "dsm_packed_bytes", "dsm_pack_weights",
     "dsm_affine_quantize", "dsm_expert_gate_up", "dsm_expert_down", "dsm_combine",
-    "dsm_moe_workspace_bytes", "dsm_moe_forward", "dsm_gather_rows", "dsm_segment_ids",
+    "dsm_moe_workspace_bytes", "dsm_moe_forward", "dsm_gather_rows", "dsm_stage_rows_count",
+    "dsm_ep_buffer_bytes", "dsm_ep_rows_offset", "dsm_ep_results_offset", "dsm_ep_dispatch", "dsm_ep_receive", "dsm_ep_return",
+    "dsm_ep_wait_results", "dsm_enable_peer_access", "dsm_ipc_get_handle", "dsm_ipc_open", "dsm_ipc_close",
     "dsm_set_expert_regime", "dsm_hc_pre_norm", "dsm_hc_post", "dsm_dense_mlp_workspace_bytes",
     "dsm_dense_mlp", "dsm_linear", "dsm_hc_head_norm", "dsm_markov_head", "dsm_draft_head_workspace_bytes",
     "dsm_draft_head", "dsm_rows_norm_rope", "dsm_q_head_norm_rope", "dsm_kv_window_write",
@@ -59,6 +63,13 @@ class MoEDesc(ctypes.Structure):
         ("shared_inter", c_int), ("shared_round_gu", c_int), ("shared_round_o", c_int),
         ("act", c_int),
     ]
+
+
+class EpDesc(ctypes.Structure):
+    """``dsm_ep_desc`` (field order and types follow the C struct)."""
+
+    _fields_ = [("world", c_int), ("rank", c_int), ("e_local", c_int), ("dim", c_int), ("x_dtype", c_int),
+                ("capacity", c_int64)]
 
 
 class HeadDesc(ctypes.Structure):
@@ -106,7 +117,18 @@ def _declare(lib):
         "dsm_expert_gate_up": (I, [V, V, I64, I, V, I, I, I, V, V, I, I, F, I, V, F, I64, V]),
         "dsm_expert_down": (I, [V, F, I64, I, V, I, I, I, V, I, I, V, I, V, I64, V]),
         "dsm_gather_rows": (I, [V, I, I64, I, V, I64, I, V, V]),
-        "dsm_segment_ids": (I, [V, I, I, V, I64, V]),
+        "dsm_stage_rows_count": (I, [V, I, I64, I, V, I64, I, V, I64, V, V, V]),
+        "dsm_ep_buffer_bytes": (S, [POINTER(EpDesc)]),
+        "dsm_ep_rows_offset": (I64, [POINTER(EpDesc), ctypes.c_uint32]),
+        "dsm_ep_results_offset": (I64, [POINTER(EpDesc), ctypes.c_uint32]),
+        "dsm_ep_dispatch": (I, [POINTER(EpDesc), V, I64, V, V, V, V, I, V, V, V, ctypes.c_uint32, V]),
+        "dsm_ep_receive": (I, [POINTER(EpDesc), V, ctypes.c_uint32, V, V, V, V]),
+        "dsm_ep_return": (I, [POINTER(EpDesc), V, V, V, V, ctypes.c_uint32, V]),
+        "dsm_ep_wait_results": (I, [POINTER(EpDesc), V, ctypes.c_uint32, V]),
+        "dsm_enable_peer_access": (I, [I]),
+        "dsm_ipc_get_handle": (I, [V, V, POINTER(c_int64)]),
+        "dsm_ipc_open": (I, [V, POINTER(ctypes.c_uint64)]),
+        "dsm_ipc_close": (I, [ctypes.c_uint64]),
         "dsm_set_expert_regime": (I, [I]),
         "dsm_combine": (I, [V, V, V, I64, I, I, V, V, I, V]),
         "dsm_hc_pre_norm": (I, [V, I, I64, I, I, V, V, V, I, F, F, V, V, V, V, V]),

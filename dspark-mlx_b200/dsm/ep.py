@@ -3,25 +3,31 @@
 The reference runs the whole MoE on one device (``dspark_mlx/model/moe.py:151-161``; its test
 harness forces ``world_size=1``, ``tests/reference_model.py:55-56``). Here rank ``r`` of ``W``
 owns experts ``[r*E/W, (r+1)*E/W)``; the router and the shared expert are replicated and every
-rank routes its own tokens. One call:
+rank routes its own tokens. Every rank holds one exchange buffer that the other ranks map
+(CUDA IPC, set up once through the process group) and write into with plain stores over
+NVLink. One call, all on the current stream and with no host synchronisation:
 
-1. route the local tokens, sort the (token, slot) pairs by expert -- expert order is owner
-   order, so the sorted pairs are already grouped by destination rank;
-2. all-to-all the per-expert counts (equal splits of ``E/W``), and copy them to the host on a
-   side stream while the shared expert runs;
-3. all-to-all the pair rows (bf16) with those splits; the receiver groups the rows of all
-   sources by its local experts (segment ids + a local permutation);
-4. grouped gate/up + down on the local experts; the down kernel writes each result row back
-   to the position its input row arrived at;
-5. all-to-all the fp32 result rows back (reversed splits) and combine them with the routing
-   weights and the shared expert, exactly as the single-GPU path does.
+1. route the local tokens and sort the (token, slot) pairs by (global) expert;
+2. ``dsm_ep_dispatch``: every pair row goes straight into its owner's buffer, with the
+   sender's per-expert counts, and the sender raises its flag in every peer;
+3. the shared expert, on the local tokens, while the peers' rows arrive;
+4. ``dsm_ep_receive``: wait (bounded) for every sender's flag; lay the arrived rows out by
+   local expert (offsets, staging permutation, row count, all on the device);
+5. grouped gate/up + down on the local experts; the down product writes each result row at
+   the position its input row arrived at;
+6. ``dsm_ep_return``: every result row goes back into its sender's buffer; flags again;
+7. ``dsm_ep_wait_results`` and the weighted combine with the shared expert, exactly as the
+   single-GPU path does (``dsm_combine``), reading the returned rows through the row map.
 
-The exchanges are NCCL all-to-alls (torch.distributed); the compute is ``libdsm.so``.
+Two buffer sets alternate between calls, so no call waits for the previous one. Every
+exchange has the same geometry on every rank: ``max_tokens`` (tokens per rank per call)
+fixes it at construction.
 """
 
 from __future__ import annotations
 
 import copy
+import ctypes
 from typing import List, Optional, Tuple
 
 import torch
@@ -29,11 +35,10 @@ import torch.distributed as dist
 from torch import nn
 
 from . import _lib
-from ._lib import check, dtype_code, lib, ptr, stream_ptr
+from ._lib import EpDesc, check, dtype_code, lib, ptr, stream_ptr
 from .moe import Expert, Gate, MoE, _cuda_contig, _ids_arg
 
 
-# ---------------------------------------------------------------------------- exchange steps
 def rank_expert_range(n_experts: int, world: int, rank: int) -> Tuple[int, int]:
     if n_experts % world:
         raise ValueError(f"{n_experts} experts do not shard evenly over {world} ranks")
@@ -41,45 +46,123 @@ def rank_expert_range(n_experts: int, world: int, rank: int) -> Tuple[int, int]:
     return rank * el, el
 
 
-def exchange_counts(counts: torch.Tensor, world: int, group=None) -> torch.Tensor:
-    """``counts [E]`` (pairs this rank sends to each expert) -> ``[W * E/W]``: row ``s`` holds the
-    pairs source ``s`` sends to each of this rank's experts."""
-    recv = torch.empty_like(counts)
-    if world == 1:
-        recv.copy_(counts)
-    else:
-        dist.all_to_all_single(recv, counts, group=group)
-    return recv
+def capacity(max_tokens: int, topk: int, e_local: int) -> int:
+    """Rows one sender can put in one owner's block: each token sends at most min(topk,
+    e_local) of its slots to one owner (its experts are distinct)."""
+    return max(1, max_tokens * min(topk, e_local))
 
 
-def splits(counts: torch.Tensor, world: int) -> List[int]:
-    """Rows per rank from per-expert counts laid out rank-major ([W, E/W] or [E])."""
-    return counts.view(world, -1).sum(dim=1).tolist()
+# Peer allocations mapped into this process, by IPC handle: [base, users]. One allocation can
+# hold several exchange buffers (the caching allocator's segments), and CUDA maps a handle
+# once per process, so mappings are shared and unmapped with their last user.
+_IPC_MAPS = {}
 
 
-def exchange_rows(send: torch.Tensor, send_splits: List[int], recv_splits: List[int], world: int,
-                  group=None) -> torch.Tensor:
-    """Rows grouped by destination rank -> rows grouped by source rank (same order within)."""
-    recv = torch.empty((sum(recv_splits),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
-    if world == 1:
-        recv.copy_(send)
-    else:
-        dist.all_to_all_single(recv, send, recv_splits, send_splits, group=group)
-    return recv
+def _ipc_map(handle: bytes) -> int:
+    ent = _IPC_MAPS.get(handle)
+    if ent is None:
+        base = ctypes.c_uint64(0)
+        check(lib().dsm_ipc_open(handle, ctypes.byref(base)), "dsm_ipc_open")  # into this device's space
+        ent = _IPC_MAPS[handle] = [base.value, 0]
+    ent[1] += 1
+    return ent[0]
+
+
+def _ipc_unmap(handle: bytes) -> None:
+    ent = _IPC_MAPS.get(handle)
+    if ent is None:
+        return
+    ent[1] -= 1
+    if ent[1] == 0:
+        lib().dsm_ipc_close(ent[0])
+        del _IPC_MAPS[handle]
+
+
+class _Exchange:
+    """This rank's exchange buffer, the peers' mapped addresses and the step counter."""
+
+    def __init__(self, desc: EpDesc, group, device: torch.device, peers: Optional[List[torch.Tensor]] = None,
+                 buf: Optional[torch.Tensor] = None):
+        L = lib()
+        self.desc = desc
+        if peers is not None:  # ranks emulated on one device: the buffers are given
+            self.buf, self.peers, self.mapped = buf, peers, []
+            self.peer_base = torch.tensor([t.data_ptr() for t in peers], dtype=torch.int64, device=device)
+            self.done = torch.zeros(2, dtype=torch.int32, device=device)
+            self.epoch = 0
+            return
+        nbytes = L.dsm_ep_buffer_bytes(ctypes.byref(desc))
+        if nbytes == 0:
+            raise ValueError(L.dsm_last_error_message().decode())
+        self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)  # flags start at 0
+        torch.cuda.synchronize(device)
+        world = desc.world
+        self.mapped: List[bytes] = []
+        addrs = [self.buf.data_ptr()] * world
+        if world > 1:
+            handle = ctypes.create_string_buffer(64)
+            off = ctypes.c_int64(0)
+            check(L.dsm_ipc_get_handle(self.buf.data_ptr(), handle, ctypes.byref(off)), "dsm_ipc_get_handle")
+            shared: List = [None] * world
+            dist.all_gather_object(shared, (handle.raw, off.value, device.index), group=group)
+            for r, (h, o, peer_dev) in enumerate(shared):
+                if r == desc.rank:
+                    continue
+                check(L.dsm_enable_peer_access(peer_dev), "dsm_enable_peer_access")
+                addrs[r] = _ipc_map(h) + o
+                self.mapped.append(h)
+            dist.barrier(group=group)
+        self.peers = [self.buf]  # keeps this rank's buffer alive while peers map it
+        self.peer_base = torch.tensor(addrs, dtype=torch.int64, device=device)
+        self.done = torch.zeros(2, dtype=torch.int32, device=device)
+        self.epoch = 0
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers (also when the exchange is collected)."""
+        for h in self.mapped:
+            _ipc_unmap(h)
+        self.mapped = []
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown
+            pass
+
+    def next_epoch(self) -> int:
+        self.epoch = self.epoch % 0xFFFFFFFE + 1  # 1, 2, ...: never 0 (the flags' initial value)
+        return self.epoch
+
+
+def connect_on_one_device(modules: List["ExpertParallelMoE"], dtype: torch.dtype, device) -> None:
+    """Wire the exchanges of W ranks' modules that share one device and one process (rank r's
+    "peer" buffers are the other modules' local buffers). Drive them phase by phase: every
+    rank's ``dispatch``, then every ``compute``, then every ``combine``."""
+    device = torch.device(device)
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    L = lib()
+    descs = [m.exchange_desc(dtype) for m in modules]
+    bufs = [torch.zeros(L.dsm_ep_buffer_bytes(ctypes.byref(dd)), dtype=torch.uint8, device=device) for dd in descs]
+    for m, dd, b in zip(modules, descs, bufs):
+        m._ex[(dtype, device)] = _Exchange(dd, None, device, peers=bufs, buf=b)
 
 
 # ---------------------------------------------------------------------------- module
 class ExpertParallelMoE(nn.Module):
-    """``MoE`` with the routed experts sharded over ``group``; call it like ``MoE``."""
+    """``MoE`` with the routed experts sharded over ``group``; call it like ``MoE``. Calls carry
+    at most ``max_tokens`` tokens on every rank."""
 
-    def __init__(self, args, layer_id: int, group=None):
+    def __init__(self, args, layer_id: int, group=None, max_tokens: int = 512, world: Optional[int] = None,
+                 rank: Optional[int] = None):
         super().__init__()
         self.group = group
-        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
-        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = world if world is not None else (dist.get_world_size(group) if dist.is_initialized() else 1)
+        self.rank = rank if rank is not None else (dist.get_rank(group) if dist.is_initialized() else 0)
         self.dim, self.inter_dim = args.dim, args.moe_inter_dim
         self.n_routed_experts = args.n_routed_experts
         self.swiglu_limit = args.swiglu_limit
+        self.max_tokens = max_tokens
         self.e0, self.e_local = rank_expert_range(args.n_routed_experts, self.world, self.rank)
         self.gate = Gate(args, layer_id)
         self.shared_experts = Expert(args.dim, args.moe_inter_dim, args.swiglu_limit)
@@ -87,13 +170,14 @@ class ExpertParallelMoE(nn.Module):
         local_args.n_routed_experts = self.e_local
         self.local = MoE(local_args, layer_id)  # holds this rank's routed experts (any format)
         del self.local.gate, self.local.shared_experts
-        self._side = None
-        self._host = None
+        self._ex = {}
 
     @classmethod
-    def from_moe(cls, moe: MoE, args, layer_id: int, group=None) -> "ExpertParallelMoE":
-        """Shard a full ``MoE``'s routed experts; router and shared expert are copied."""
-        ep = cls(args, layer_id, group)
+    def from_moe(cls, moe: MoE, args, layer_id: int, group=None, max_tokens: int = 512, world: Optional[int] = None,
+                 rank: Optional[int] = None) -> "ExpertParallelMoE":
+        """Shard a full ``MoE``'s routed experts; router and shared expert are copied.
+        ``world`` / ``rank`` default to the process group's."""
+        ep = cls(args, layer_id, group, max_tokens, world, rank)
         # share the replicated modules as they are: their dtypes decide the reference's
         # rounding points (bf16 products for bf16 weights), so they must not be re-cast
         ep.gate = moe.gate
@@ -139,15 +223,41 @@ class ExpertParallelMoE(nn.Module):
                                 ptr(o), dim, None, n, s), "dsm_expert_down")
         return o
 
+    def exchange_desc(self, dtype: torch.dtype) -> EpDesc:
+        return EpDesc(self.world, self.rank, self.e_local, self.dim, dtype_code(dtype),
+                      capacity(self.max_tokens, self.gate.topk, self.e_local))
+
+    def exchange(self, dtype: torch.dtype, device: torch.device) -> "_Exchange":
+        """One exchange per activation dtype, set up collectively on first use (every rank
+        must make its first call with that dtype at the same point)."""
+        key = (dtype, device)
+        if key not in self._ex:
+            self._ex[key] = _Exchange(self.exchange_desc(dtype), self.group, device)
+        return self._ex[key]
+
     def forward(self, x: torch.Tensor, input_ids: Optional[torch.Tensor] = None, *, return_routing: bool = False):
+        st = self.dispatch(x, input_ids)
+        self.compute(st)
+        y = self.combine(st)
+        return (y, st["w"], st["idx"]) if return_routing else y
+
+    # The three phases of a call, in stream order on every rank: dispatch (rows out, shared
+    # expert), compute (rows in, local experts, results out), combine (results in). A caller
+    # that drives several ranks' modules from one process on one GPU (a test standing in for
+    # W GPUs) runs every rank's dispatch, then every rank's compute, then every combine: each
+    # wait then finds its peers' signals already raised by earlier launches.
+    def dispatch(self, x: torch.Tensor, input_ids: Optional[torch.Tensor] = None) -> dict:
         L = lib()
-        shape, in_dtype = x.shape, x.dtype
         x2 = _cuda_contig(x.reshape(-1, self.dim), "x")
         n, dim = x2.shape
+        if n > self.max_tokens:
+            raise ValueError(f"{n} tokens in one call; this module's exchange holds max_tokens={self.max_tokens}")
         dev = x2.device
-        E, El, W, k = self.n_routed_experts, self.e_local, self.world, self.gate.topk
+        E, k = self.n_routed_experts, self.gate.topk
         P = n * k
         s = stream_ptr()
+        ex = self.exchange(x2.dtype, dev)
+        epoch = ex.next_epoch()
         # 1. route and sort the pairs by (global) expert
         w, idx = self.gate(x2, input_ids)
         counts = torch.empty(E, dtype=torch.int32, device=dev)
@@ -157,64 +267,69 @@ class ExpertParallelMoE(nn.Module):
         pws = torch.empty(max(1, L.dsm_permute_workspace_bytes(P, E)), dtype=torch.uint8, device=dev)
         check(L.dsm_permute(ptr(idx), P, E, ptr(counts), ptr(offsets), ptr(perm), ptr(inv), ptr(pws), pws.numel(),
                             s), "dsm_permute")
-        x_send = torch.empty(P, dim, dtype=x2.dtype, device=dev)
-        check(L.dsm_gather_rows(ptr(x2), dtype_code(x2.dtype), n, dim, ptr(perm), P, k, ptr(x_send), s),
-              "dsm_gather_rows")
-        # 2. counts to the expert owners; to the host on a side stream while the shared expert runs
-        recv_counts = exchange_counts(counts, W, self.group)
-        if self._side is None:
-            self._side = torch.cuda.Stream(device=dev)
-            self._host = torch.empty(2 * E, dtype=torch.int32).pin_memory()
-        main = torch.cuda.current_stream(dev)
-        self._side.wait_stream(main)
-        with torch.cuda.stream(self._side):
-            self._host[:E].copy_(counts, non_blocking=True)
-            self._host[E:].copy_(recv_counts, non_blocking=True)
-        rgu, ro = self.local.routed_round_flags(x2.dtype)
+        # 2. rows to their owners
+        row_map = torch.empty(max(P, 1), dtype=torch.int32, device=dev)
+        check(L.dsm_ep_dispatch(ctypes.byref(ex.desc), ptr(x2), n, ptr(idx), ptr(perm), ptr(offsets), ptr(counts), k,
+                                ptr(ex.peer_base), ptr(row_map), ptr(ex.done), epoch, s), "dsm_ep_dispatch")
+        # 3. the shared expert while the peers' rows arrive
         if x2.dtype == torch.bfloat16:
             sgu = int(self.shared_experts.weight_dtype("w1") == torch.bfloat16) | 2
             so = int(self.shared_experts.weight_dtype("w2") == torch.bfloat16)
         else:
             sgu, so = 0, 0
-        hsc = 1.0 if 0 < self.swiglu_limit and self.swiglu_limit ** 2 < 30000 else 1.0 / 256
-        o_shared = self._shared(x2, sgu, so, hsc, s)
-        self._side.synchronize()
-        host = self._host.clone()
-        send_splits = splits(host[:E], W)
-        recv_splits = splits(host[E:], W)
-        # 3. rows to the owners; group all sources' rows by local expert
-        x_recv = exchange_rows(x_send, send_splits, recv_splits, W, self.group)
-        R = x_recv.shape[0]
-        o_recv = torch.empty(max(R, 1), dim, dtype=torch.float32, device=dev)
-        if R:
-            seg = torch.empty(R, dtype=torch.int32, device=dev)
-            check(L.dsm_segment_ids(ptr(recv_counts), W * El, El, ptr(seg), R, s), "dsm_segment_ids")
-            lc = torch.empty(El, dtype=torch.int32, device=dev)
-            lo = torch.empty(El + 1, dtype=torch.int32, device=dev)
-            lperm = torch.empty(R, dtype=torch.int32, device=dev)
-            linv = torch.empty(R, dtype=torch.int32, device=dev)
-            lws = torch.empty(max(1, L.dsm_permute_workspace_bytes(R, El)), dtype=torch.uint8, device=dev)
-            check(L.dsm_permute(ptr(seg), R, El, ptr(lc), ptr(lo), ptr(lperm), ptr(linv), ptr(lws), lws.numel(), s),
-                  "dsm_permute")
-            # 4. local grouped expert products; results land in arrival order
-            p1, p3, p2 = self.local.packed_experts()
-            cap = L.dsm_stage_rows_cap(R)
-            xs = torch.empty(L.dsm_stage_bytes(cap, dim), dtype=torch.uint8, device=dev)
-            xsc = torch.empty(cap, dtype=torch.float32, device=dev)
-            hs = torch.empty(L.dsm_stage_bytes(cap, self.inter_dim), dtype=torch.uint8, device=dev)
-            check(L.dsm_stage_rows(ptr(x_recv), dtype_code(x_recv.dtype), R, dim, ptr(lperm), R, 1, ptr(xs), cap,
-                                   ptr(xsc), s), "dsm_stage_rows")
-            check(L.dsm_expert_gate_up(ptr(xs), ptr(xsc), cap, dim, ptr(lo), El, p1.wfmt, p1.group_size,
-                                       ptr(p1.packed), ptr(p3.packed), self.inter_dim, _lib.ACT_SWIGLU_CLAMP,
-                                       float(self.swiglu_limit), rgu, ptr(hs), hsc, R, s), "dsm_expert_gate_up")
-            check(L.dsm_expert_down(ptr(hs), hsc, cap, self.inter_dim, ptr(lo), El, p2.wfmt, p2.group_size,
-                                    ptr(p2.packed), dim, ro, ptr(o_recv), dim, ptr(lperm), R, s), "dsm_expert_down")
-        # 5. results back to the token owners (in the order the rows were sent), combine
-        o_back = exchange_rows(o_recv[:R], recv_splits, send_splits, W, self.group)
+        o_shared = self._shared(x2, sgu, so, self._h_scale(), s)
+        return dict(x_shape=x.shape, in_dtype=x.dtype, x2=x2, ex=ex, epoch=epoch, w=w, idx=idx, row_map=row_map,
+                    o_shared=o_shared, keep=(counts, offsets, perm, inv, pws))
+
+    def _h_scale(self) -> float:
+        return 1.0 if 0 < self.swiglu_limit and self.swiglu_limit ** 2 < 30000 else 1.0 / 256
+
+    def compute(self, st: dict) -> None:
+        L = lib()
+        ex, epoch, x2 = st["ex"], st["epoch"], st["x2"]
+        d = ctypes.byref(ex.desc)
+        dev, dim = x2.device, self.dim
+        El, W, C = self.e_local, ex.desc.world, ex.desc.capacity
+        s = stream_ptr()
+        # 4. the arrived rows, laid out by local expert on the device
+        R = W * C
+        loff = torch.empty(El + 1, dtype=torch.int32, device=dev)
+        lperm = torch.empty(R, dtype=torch.int32, device=dev)
+        n_valid = torch.empty(1 + W, dtype=torch.int32, device=dev)
+        check(L.dsm_ep_receive(d, ptr(ex.buf), epoch, ptr(loff), ptr(lperm), ptr(n_valid), s), "dsm_ep_receive")
+        x_recv = ex.buf.data_ptr() + L.dsm_ep_rows_offset(d, epoch)
+        # 5. local grouped expert products; results land in arrival order
+        rgu, ro = self.local.routed_round_flags(x2.dtype)
+        hsc = self._h_scale()
+        p1, p3, p2 = self.local.packed_experts()
+        cap = L.dsm_stage_rows_cap(R)
+        xs = torch.empty(L.dsm_stage_bytes(cap, dim), dtype=torch.uint8, device=dev)
+        xsc = torch.empty(cap, dtype=torch.float32, device=dev)
+        hs = torch.empty(L.dsm_stage_bytes(cap, self.inter_dim), dtype=torch.uint8, device=dev)
+        o_recv = torch.empty(R, dim, dtype=torch.float32, device=dev)
+        check(L.dsm_stage_rows_count(x_recv, dtype_code(x2.dtype), R, dim, ptr(lperm), R, 1, ptr(xs), cap, ptr(xsc),
+                                     ptr(n_valid), s), "dsm_stage_rows_count")
+        hint = max(1, x2.shape[0] * self.gate.topk)  # rows an owner gets on average when every rank routes n tokens
+        check(L.dsm_expert_gate_up(ptr(xs), ptr(xsc), cap, dim, ptr(loff), El, p1.wfmt, p1.group_size, ptr(p1.packed),
+                                   ptr(p3.packed), self.inter_dim, _lib.ACT_SWIGLU_CLAMP, float(self.swiglu_limit),
+                                   rgu, ptr(hs), hsc, hint, s), "dsm_expert_gate_up")
+        check(L.dsm_expert_down(ptr(hs), hsc, cap, self.inter_dim, ptr(loff), El, p2.wfmt, p2.group_size,
+                                ptr(p2.packed), dim, ro, ptr(o_recv), dim, ptr(lperm), hint, s), "dsm_expert_down")
+        # 6. results back to the token owners
+        check(L.dsm_ep_return(d, ptr(o_recv), ptr(n_valid), ptr(ex.peer_base), ex.done.data_ptr() + 4, epoch, s),
+              "dsm_ep_return")
+        st["keep_compute"] = (loff, lperm, n_valid, xs, xsc, hs, o_recv)
+
+    def combine(self, st: dict) -> torch.Tensor:
+        L = lib()
+        ex, epoch, x2 = st["ex"], st["epoch"], st["x2"]
+        d = ctypes.byref(ex.desc)
+        s = stream_ptr()
+        n, dim = x2.shape
+        # 7. wait for every owner's results; the weighted combine with the shared expert
+        check(L.dsm_ep_wait_results(d, ptr(ex.buf), epoch, s), "dsm_ep_wait_results")
+        o_back = ex.buf.data_ptr() + L.dsm_ep_results_offset(d, epoch)
         y = torch.empty_like(x2)
-        check(L.dsm_combine(ptr(o_back), ptr(inv), ptr(w), n, k, dim, ptr(o_shared), ptr(y), dtype_code(x2.dtype), s),
-              "dsm_combine")
-        y = y.to(in_dtype).reshape(shape)
-        if return_routing:
-            return y, w, idx
-        return y
+        check(L.dsm_combine(o_back, ptr(st["row_map"]), ptr(st["w"]), n, self.gate.topk, dim, ptr(st["o_shared"]),
+                            ptr(y), dtype_code(x2.dtype), s), "dsm_combine")
+        return y.to(st["in_dtype"]).reshape(st["x_shape"])

@@ -41,9 +41,10 @@
  *   dsm_qkv_norm_rope, dsm_gqa_attn: Qwen3DSparkAttention.__call__ / context_kv /
  *                       attend_cached around dsm_linear (arch/qwen3.py:64-143)
  *   dsm_add_rms_norm    the residual adds and RMSNorms of Qwen3DSparkLayer (arch/qwen3.py:157-176)
- *   dsm_gather_rows, dsm_segment_ids: expert-parallel plumbing; the reference runs on one
- *                       device (tests/reference_model.py:55-56 forces world_size 1) and has
- *                       no counterpart.
+ *   dsm_gather_rows     the draft block's embedding rows (block.py:97-101)
+ *   dsm_ep_*            expert parallelism over peer stores; the reference runs on one device
+ *                       (tests/reference_model.py:55-56 forces world_size 1) and has no
+ *                       counterpart.
  */
 #ifndef DSM_H_
 #define DSM_H_
@@ -67,6 +68,8 @@ extern "C" {
 #define DSM_DEV_ERR_EXPERT_RANGE 0x10
 #define DSM_DEV_ERR_TOKEN_RANGE 0x11
 #define DSM_DEV_ERR_PIPELINE_TIMEOUT 0x12
+#define DSM_DEV_ERR_PEER_TIMEOUT 0x13   /* an expert-parallel peer did not signal within ~2 s */
+#define DSM_DEV_ERR_CAPACITY 0x14       /* more expert-parallel rows than the exchange buffer holds */
 
 /* element types */
 #define DSM_DT_F32 0
@@ -150,6 +153,11 @@ int64_t dsm_stage_rows_cap(int64_t n_rows);
 int dsm_stage_rows(const void* x, int x_dtype, int64_t n_tokens, int dim, const int32_t* perm,
                    int64_t n_rows, int topk, void* staged, int64_t rows_cap, float* row_scale,
                    void* stream);
+/* stage_rows_count: as stage_rows over rows r < *n_valid (a device count, <= max_rows); the
+ * expert-parallel receiver stages the rows that arrived without reading their count back. */
+int dsm_stage_rows_count(const void* x, int x_dtype, int64_t n_tokens, int dim, const int32_t* perm,
+                         int64_t max_rows, int topk, void* staged, int64_t rows_cap, float* row_scale,
+                         const int32_t* n_valid, void* stream);
 /* fp32 rows x [n_rows, dim] staged as 2 * n_rows f16 rows: row r as dsm_stage_rows stages it
  * (hi), row n_rows + r the residual x - hi with its own scale (lo); a product over all rows
  * then adds up, hi + lo, to the fp32 row's product within ~2^-22 relative.
@@ -355,16 +363,65 @@ int dsm_add_rms_norm(const void* x, const void* delta, int dtype, int64_t n_rows
  * thread only (thread-local): other threads keep their own. */
 int dsm_set_expert_regime(int regime);
 
-/* ---- expert-parallel helpers -----------------------------------------------------------
- * gather_rows: out[r] = x[perm[r] / topk] (perm NULL: x[r]), same dtype (F32/BF16), the
- *   rows a rank sends to the owners of its routed experts (expert order = owner order).
- * segment_ids: rows arriving from W sources, each source's rows grouped by the receiver's
- *   E_local experts with counts[s * E_local + e] rows; ids[row] = e (the local expert).
- *   n_segments = W * E_local <= 4096; n_rows = sum(counts). */
+/* ---- row gather and expert parallelism ---------------------------------------------------
+ * gather_rows: out[r] = x[perm[r] / topk] (perm NULL: x[r]), same dtype (F32/BF16).
+ *
+ * Expert parallelism: no counterpart in the reference, which runs the MoE on one device
+ * (tests/reference_model.py:55-56 forces world_size 1). Rank `rank` of `world` owns experts
+ * [rank * e_local, (rank + 1) * e_local) and routes its own tokens. Each rank allocates one
+ * exchange buffer of dsm_ep_buffer_bytes (zero-filled once) that every peer maps (CUDA IPC);
+ * peer_base [world] (device memory) holds the peers' mapped addresses, peer_base[rank] this
+ * rank's own buffer. A step, all stream-ordered, no host synchronisation:
+ *   dsm_ep_dispatch      the sender's expert-sorted (token, slot) rows (dsm_permute's perm,
+ *                        offsets, counts over all experts; indices = the routing [n*topk]) go
+ *                        into their owners' buffers; row_map[pair] = owner * capacity + slot
+ *                        for the combine; raises this rank's flag in every peer.
+ *   dsm_ep_receive       waits (bounded) for every sender, whose rows then sit at own_buffer +
+ *                        dsm_ep_rows_offset(epoch) ([world * capacity, dim], sender-major),
+ *                        and writes offsets [e_local + 1] of the
+ *                        arrived rows by local expert, lperm (staged position -> arrival row
+ *                        sender * capacity + slot, for dsm_stage_rows_count and as the down
+ *                        product's o_row_map) and n_valid [1 + world] (rows arrived, rows per
+ *                        sender).
+ *   dsm_ep_return        result rows [world * capacity, dim] fp32 (arrival order) go back to
+ *                        their senders; raises this rank's result flag in every peer.
+ *   dsm_ep_wait_results  waits (bounded) for every owner; dsm_combine then reads the results at
+ *                        own_buffer + dsm_ep_results_offset(epoch) through row_map.
+ * epoch: 1, 2, 3 ... one per step, the same on every rank (two buffer sets alternate by its
+ * parity). done: one zero-initialised uint32 per kernel (dispatch, return), reset by the kernel.
+ * capacity: rows per (sender, owner) block >= n_tokens * min(topk, e_local) of any rank.
+ * Waits give up after ~2 s with DSM_DEV_ERR_PEER_TIMEOUT. enable_peer_access: lets this
+ * device's kernels store into peer_device's memory. */
+typedef struct dsm_ep_desc {
+  int world;
+  int rank;
+  int e_local;
+  int dim;
+  int x_dtype; /* BF16 or F32: the rows the dispatch sends */
+  int64_t capacity;
+} dsm_ep_desc;
 int dsm_gather_rows(const void* x, int x_dtype, int64_t n_tokens, int dim, const int32_t* perm,
                     int64_t n_rows, int topk, void* out, void* stream);
-int dsm_segment_ids(const int32_t* counts, int n_segments, int e_local, int32_t* ids, int64_t n_rows,
+size_t dsm_ep_buffer_bytes(const dsm_ep_desc* d);
+int64_t dsm_ep_rows_offset(const dsm_ep_desc* d, uint32_t epoch);
+int64_t dsm_ep_results_offset(const dsm_ep_desc* d, uint32_t epoch);
+int dsm_ep_dispatch(const dsm_ep_desc* d, const void* x, int64_t n_tokens, const int32_t* indices,
+                    const int32_t* perm, const int32_t* offsets, const int32_t* counts, int topk,
+                    const uint64_t* peer_base, int32_t* row_map, uint32_t* done, uint32_t epoch,
                     void* stream);
+int dsm_ep_receive(const dsm_ep_desc* d, const void* own_buffer, uint32_t epoch, int32_t* offsets,
+                   int32_t* lperm, int32_t* n_valid, void* stream);
+int dsm_ep_return(const dsm_ep_desc* d, const float* o_rows, const int32_t* n_valid,
+                  const uint64_t* peer_base, uint32_t* done, uint32_t epoch, void* stream);
+int dsm_ep_wait_results(const dsm_ep_desc* d, const void* own_buffer, uint32_t epoch, void* stream);
+int dsm_enable_peer_access(int peer_device);
+/* The exchange buffers across processes: ipc_get_handle gives the 64-byte CUDA IPC handle of
+ * the allocation holding ptr and ptr's offset in it; ipc_open maps a peer's handle into the
+ * current device's address space (peer access enabled as needed) and returns the base, to
+ * which the peer's offset is added; ipc_close unmaps it. */
+int dsm_ipc_get_handle(const void* ptr, void* handle, int64_t* offset);
+int dsm_ipc_open(const void* handle, uint64_t* base);
+int dsm_ipc_close(uint64_t base);
 
 /* ---- combine: y = sum_s o[inv[t*k+s]] * w[t,s] (+ shared[t]) -> y_dtype --------------- */
 int dsm_combine(const float* o_sorted, const int32_t* inv, const float* route_weights,
