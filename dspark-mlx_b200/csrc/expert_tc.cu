@@ -2,20 +2,29 @@
 // accumulators, for fp8 128x128 block-scaled experts and f16-packed (bf16/fp32) experts --
 // the shared expert among them.
 //
-// Work unit = (expert e, 128 weight rows, BN staged rows of the expert). Persistent CTAs,
-// warp-specialised:
+// Work unit = (expert e, 128 weight rows, up to 256 staged rows of the expert). Persistent
+// CTAs, warp-specialised:
 //   warp 0      producer: per 64-wide K stage, bulk-copies the unit's fp8 codes (half of a
 //               packed 128x128 tile, already in the layout the decode kernel reads) plus the
-//               tile's fp32 block scale, and TMA-loads the BN x 64 f16 activation box (128B
-//               swizzle) from the staged rows;
+//               tile's fp32 block scale, and TMA-loads the 256 x 64 f16 activation box (128B
+//               swizzle) from the staged rows, into a ring of load slots (as many as shared
+//               memory holds: 3-4);
 //   warp 1      MMA issuer (one elected thread): tcgen05.mma kind::f16, M=128, N = the
-//               unit's rows rounded to 16, K=16 x 4 per stage, D in TMEM (double-buffered so
-//               the epilogue of one unit overlaps the main loop of the next); tcgen05.commit
-//               releases smem stages and hands accumulators to the epilogue;
+//               unit's rows rounded to 16 (up to 256), K=16 x 4 per stage, D in TMEM (two
+//               buffers where they fit -- the down product -- so an epilogue overlaps the next
+//               unit's main loop; the gate/up pair's two 256-column accumulators fill TMEM);
+//               tcgen05.commit releases load slots and A slots and hands accumulators to the
+//               epilogue;
 //   warps 2-9   converters: e4m3 -> f16 (hardware cvt) times the block scale (f16 multiply),
-//               written as the K-major SWIZZLE_128B f16 A operand;
-//   warps 10-13 epilogue: tcgen05.ld of the accumulators (each warp its 32-lane TMEM
-//               sub-partition), activation row scale, SwiGLU (gate/up) or output rows (down).
+//               written as the K-major SWIZZLE_128B f16 A operand into a two-slot ring of
+//               its own, with bank-conflict-free 16-byte stores;
+//   warps 10-21 epilogue: tcgen05.ld of the accumulators (warp w reads TMEM sub-partition
+//               w % 4; the three warps of a sub-partition take alternate 16-column blocks),
+//               activation row scale, SwiGLU (gate/up) or output rows (down).
+// Shared memory bandwidth sets the pace: every stage moves the widened A tiles in and out,
+// the activation rows in (TMA) and out (MMA) and the raw codes through the converters. The
+// 256-row units read each A tile once per 256 rows instead of per 128 (4 KB of A + 8 KB of B
+// per 128 tensor cycles of an N = 256 MMA).
 //
 // A and B of one kind::f16 MMA must share a type, and the bf16 activations rule out the fp8
 // MMA kinds (fp8 activations would cost ~2% relative error), so the weights are widened to
@@ -37,33 +46,43 @@ using namespace tc;
 constexpr int kTcM = 128;            // weight rows per unit = one scale row block
 constexpr int kTcK = 64;             // K per stage = one 128-byte swizzle row of f16
 constexpr int kTcConvWarps = 8;
-constexpr int kTcEpiWarps = 4;
+constexpr int kTcEpiWarps = 12;  // a multiple of 4: warps of one TMEM sub-partition share its columns
 constexpr int kTcConvWarp0 = 2;
 constexpr int kTcEpiWarp0 = kTcConvWarp0 + kTcConvWarps;  // 10
-constexpr int kTcThreads = 32 * (kTcEpiWarp0 + kTcEpiWarps);  // 448
+constexpr int kTcThreads = 32 * (kTcEpiWarp0 + kTcEpiWarps);
 constexpr int kABytes = kTcM * kTcK * 2;
+constexpr int kTcABufs = 2;     // widened A tiles: converted one stage ahead of the MMAs
+constexpr int kTcMaxLoads = 8;  // load slots (sized at launch from the shared memory left)
 
 // FMT: DSM_WFMT_FP8_B128 (codes widened and block-scaled by the converters) or DSM_WFMT_F16
 // (f16 codes reshuffled into the swizzled layout; the per-expert prescale is undone in the
-// epilogue). The raw stage holds the packed tile's codes for 64 K: slabs 2h, 2h+1 (fp8, 8 KB)
-// or 4h .. 4h+3 (f16, 16 KB) of the 128-K tile.
+// epilogue). A load slot holds one 64-K stage: the BN activation rows (TMA, 128-byte swizzle)
+// and the packed tile's codes for 64 K: slabs 2h, 2h+1 (fp8, 8 KB) or 4h .. 4h+3 (f16, 16 KB)
+// of the 128-K tile, per matrix; the fp8 block scales go to a small side array. The widened
+// A tiles live in their own two-slot ring, so the loads (whose latency sets the pace) keep
+// more stages in flight than a ring of whole stages would.
 template <int FMT, bool DUAL>
 struct TcCfg {
   static constexpr bool kFp8 = FMT == DSM_WFMT_FP8_B128;
   static constexpr int NM = DUAL ? 2 : 1;
-  static constexpr int BN = DUAL ? 128 : 256;
+  static constexpr int BN = 256;
   static constexpr int kRawBytes = kFp8 ? 8192 : 16384;
   static constexpr int kMetaBytes = kFp8 ? 16 : 0;
   static constexpr int kBBytes = BN * kTcK * 2;
-  // stage: [A x NM][B][raw x NM][meta x NM], 1024-aligned operand pieces
-  static constexpr int kOffB = NM * kABytes;
-  static constexpr int kOffRaw = kOffB + kBBytes;
-  static constexpr int kOffMeta = kOffRaw + NM * kRawBytes;
-  static constexpr int kStageBytes = ((kOffMeta + NM * 16) + 1023) / 1024 * 1024;
-  static constexpr int kStages = (3 * kStageBytes <= 204 * 1024) ? 3 : 2;
+  static constexpr int kOffRaw = kBBytes;                         // load slot: [B][raw x NM]
+  static constexpr int kLoadBytes = kBBytes + NM * kRawBytes;     // a multiple of 1024
+  static constexpr int kABufBytes = NM * kABytes;
   static constexpr int kTxBytes = NM * (kRawBytes + kMetaBytes) + kBBytes;
-  static constexpr int kTmemCols = 2 * NM * BN;  // double-buffered accumulators = 512
+  // accumulators double-buffered when two fit in the 512 TMEM columns
+  static constexpr int kNBuf = 2 * NM * BN <= 512 ? 2 : 1;
+  static constexpr int kTmemCols = kNBuf * NM * BN;
+  static_assert(kLoadBytes % 1024 == 0, "load slots keep the 1024-byte alignment of the swizzled B tiles");
 };
+
+// shared memory past the A and load slots: barriers, block scales, TMEM slot, flags, unit prefix
+constexpr size_t tc_tail_bytes(int n_experts) {
+  return 8 * (2 * kTcMaxLoads + 2 * kTcABufs + 5) + 16 * 2 * kTcMaxLoads + 16 + size_t(n_experts + 1) * 4;
+}
 
 struct TcArgs {
   const uint8_t* wa;
@@ -107,18 +126,23 @@ __device__ __forceinline__ int tc_find_expert(const int* pre, int n_experts, int
 
 template <int FMT, bool DUAL>
 __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a,
-                                                                  const __grid_constant__ CUtensorMap xmap) {
+                                                                  const __grid_constant__ CUtensorMap xmap,
+                                                                  const int n_loads) {
   using C = TcCfg<FMT, DUAL>;
-  constexpr int kTcStages = C::kStages;
+  const int S = n_loads;  // load slots, 2 .. kTcMaxLoads
   constexpr int NM = C::NM, BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw0 = smem_u32(smem_raw);
   const uint32_t base = (raw0 + 1023u) & ~1023u;
-  uint8_t* sbase = smem_raw + (base - raw0);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sbase + kTcStages * C::kStageBytes);
-  uint64_t* conv = full + kTcStages;
-  uint64_t* empty = conv + kTcStages;
-  uint64_t* tfull = empty + kTcStages;
+  // [A slots][load slots][block scales][barriers][TMEM slot, abort flag, unit prefix]
+  uint8_t* abase = smem_raw + (base - raw0);
+  uint8_t* lbase = abase + kTcABufs * C::kABufBytes;
+  uint8_t* metas = lbase + size_t(S) * C::kLoadBytes;  // [slot][matrix] 16 bytes (bulk-copy aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(metas + 16 * 2 * kTcMaxLoads);
+  uint64_t* empty = full + kTcMaxLoads;
+  uint64_t* conv = empty + kTcMaxLoads;
+  uint64_t* aempty = conv + kTcABufs;
+  uint64_t* tfull = aempty + kTcABufs;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -128,12 +152,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = a.n_experts;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&conv[s], kTcConvWarps);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kTcABufs; ++b) {
+      mbar_init(&conv[b], kTcConvWarps);
+      mbar_init(&aempty[b], 1);
+    }
+    for (int b = 0; b < C::kNBuf; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kTcEpiWarps);
     }
@@ -141,7 +168,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) {  // TMEM: 512 columns (two accumulator buffers)
+  if (warp == 1) {  // TMEM: the accumulator buffers
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(C::kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -196,17 +223,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
             ok = false;
             break;
           }
-          uint8_t* st = sbase + s * C::kStageBytes;
+          uint8_t* st = lbase + size_t(s) * C::kLoadBytes;
           const int kc = ks >> 1, half = ks & 1;
           mbar_arrive_expect_tx(&full[s], uint32_t(C::kTxBytes));
 #pragma unroll
           for (int m = 0; m < NM; ++m) {
             const uint8_t* tile = tiles[m] + (tile0 + kc) * tile_b;
             bulk_g2s(st + C::kOffRaw + m * C::kRawBytes, tile + half * C::kRawBytes, C::kRawBytes, &full[s], pol_w);
-            if (C::kFp8) bulk_g2s(st + C::kOffMeta + m * 16, tile + 16384, 16, &full[s], pol_w);
+            if (C::kFp8) bulk_g2s(metas + (s * NM + m) * 16, tile + 16384, 16, &full[s], pol_w);
           }
-          tma_load_3d(smem_u32(st + C::kOffB), &xmap, half * kTcK, row0, kc, &full[s]);
-          if (++s == kTcStages) {
+          tma_load_3d(smem_u32(st), &xmap, half * kTcK, row0, kc, &full[s]);
+          if (++s == S) {
             s = 0;
             ph ^= 1u;
           }
@@ -218,8 +245,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      int s = 0;
-      uint32_t ph = 0;
+      int s = 0, ab = 0;
+      uint32_t ph = 0, aph = 0;
       bool ok = true;
       int j = 0;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++j) {
@@ -230,35 +257,41 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
         const int rows = min(BN, cnt - chunk * BN);
         const int n_mma = min(BN, (rows + 15) / 16 * 16);
         const uint32_t idesc = umma_idesc_f16(kTcM, n_mma);
-        const int buf = j & 1;
-        if (*abort_flag || !mbar_wait(&tempty[buf], ((j >> 1) & 1) ^ 1u)) {
+        const int buf = j % C::kNBuf;
+        if (*abort_flag || !mbar_wait(&tempty[buf], ((j / C::kNBuf) & 1) ^ 1u)) {
           *abort_flag = 1;
           ok = false;
           break;
         }
         tc_fence_after();
         for (int ks = 0; ks < nks; ++ks) {
-          if (*abort_flag || !mbar_wait(&conv[s], ph) || !mbar_wait(&full[s], ph)) {
+          if (*abort_flag || !mbar_wait(&conv[ab], aph) || !mbar_wait(&full[s], ph)) {
             *abort_flag = 1;
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t st = smem_u32(sbase + s * C::kStageBytes);
+          const uint32_t sb = smem_u32(lbase + size_t(s) * C::kLoadBytes);
+          const uint32_t sa = smem_u32(abase + ab * C::kABufBytes);
 #pragma unroll
           for (int kk = 0; kk < kTcK / 16; ++kk) {
-            const uint64_t bdesc = umma_desc_sw128(st + C::kOffB) + uint64_t(kk * 2);
+            const uint64_t bdesc = umma_desc_sw128(sb) + uint64_t(kk * 2);
 #pragma unroll
             for (int m = 0; m < NM; ++m) {
-              const uint64_t adesc = umma_desc_sw128(st + m * kABytes) + uint64_t(kk * 2);
+              const uint64_t adesc = umma_desc_sw128(sa + m * kABytes) + uint64_t(kk * 2);
               const uint32_t d = tmem + uint32_t((buf * NM + m) * BN);
               umma_f16(d, adesc, bdesc, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
             }
           }
-          umma_commit(&empty[s]);  // smem stage free once these MMAs have read it
-          if (++s == kTcStages) {
+          umma_commit(&empty[s]);    // load slot free once these MMAs have read B (the
+          umma_commit(&aempty[ab]);  // converters were done with its codes before) and A
+          if (++s == S) {
             s = 0;
             ph ^= 1u;
+          }
+          if (++ab == kTcABufs) {
+            ab = 0;
+            aph ^= 1u;
           }
         }
         if (!ok) break;
@@ -272,21 +305,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
     // ------------------------------------------------------------------ converters
     const int cw = warp - kTcConvWarp0;  // 0..7
     const int g = lane >> 2, q = lane & 3;
-    int s = 0;
-    uint32_t ph = 0;
+    int s = 0, ab = 0;
+    uint32_t ph = 0, aph = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x) {
       bool ok = true;
       for (int ks = 0; ks < nks; ++ks) {
-        if (*abort_flag || !mbar_wait(&full[s], ph)) {
+        // the stage's codes have landed, and the MMAs two stages back have released A slot ab
+        if (*abort_flag || !mbar_wait(&full[s], ph) || !mbar_wait(&aempty[ab], aph ^ 1u)) {
           *abort_flag = 1;
           ok = false;
           break;
         }
-        uint8_t* st = sbase + s * C::kStageBytes;
+        uint8_t* st = lbase + size_t(s) * C::kLoadBytes;
 #pragma unroll
         for (int m = 0; m < NM; ++m) {
           const uint32_t rawm = smem_u32(st + C::kOffRaw + m * C::kRawBytes);
-          const uint32_t am = smem_u32(st + m * kABytes);
+          const uint32_t am = smem_u32(abase + ab * C::kABufBytes + m * kABytes);
           if constexpr (!C::kFp8) {
             // f16 codes: 4 k16 slabs x 8 m16 tiles of 512 B; lane holds rows r0, r0+8 at k 4q..4q+3
 #pragma unroll
@@ -304,40 +338,54 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
             }
             continue;
           }
-          const float sc = *reinterpret_cast<const float*>(st + C::kOffMeta + m * 16);
+          const float sc = *reinterpret_cast<const float*>(metas + (s * NM + m) * 16);
           const __half2 s2 = __float2half2_rn(sc);
           const uint32_t sbits = *reinterpret_cast<const uint32_t*>(&s2);
-          // 16 blocks of 512 B (2 slabs x 8 m16 tiles); warp cw converts blocks cw and cw + 8
+          // 16 blocks of 512 B (2 slabs x 8 m16 tiles); warp cw converts blocks cw (slab 0) and
+          // cw + 8 (slab 1): lane (g, q) holds rows r0 = 16 cw + g and r0 + 8 at k 8q..8q+7 of each
+          // slab, i.e. 16-byte chunk q of slab 0 and chunk 4 + q of slab 1 in the swizzled rows.
+          // A 16-byte store serves 8 lanes per pass (g = 2p, 2p + 1); lanes of odd g store the
+          // slab-1 chunk first, so the pass covers chunks {q ^ g} and {(4 + q) ^ g'}: all eight
+          // 16-byte bank groups, no conflict.
+          uint32_t h[2][8];
 #pragma unroll
           for (int bi = 0; bi < 2; ++bi) {
-            const int blk = cw + 8 * bi;
-            const int sl = blk >> 3, mt = blk & 7;
-            const uint4 v = lds128(rawm + (blk * 32 + lane) * 16);
-            uint32_t h[8];
-            e4m3x4_to_f16(v.x, h[0], h[1]);  // row r0, k 8q..8q+3
-            e4m3x4_to_f16(v.y, h[2], h[3]);  // row r0, k 8q+4..8q+7
-            e4m3x4_to_f16(v.z, h[4], h[5]);  // row r0+8
-            e4m3x4_to_f16(v.w, h[6], h[7]);
+            const uint4 v = lds128(rawm + ((cw + 8 * bi) * 32 + lane) * 16);
+            e4m3x4_to_f16(v.x, h[bi][0], h[bi][1]);  // row r0, k 8q..8q+3
+            e4m3x4_to_f16(v.y, h[bi][2], h[bi][3]);  // row r0, k 8q+4..8q+7
+            e4m3x4_to_f16(v.z, h[bi][4], h[bi][5]);  // row r0+8
+            e4m3x4_to_f16(v.w, h[bi][6], h[bi][7]);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) h[i] = hmul2_bits(h[i], sbits);
-            const int r0 = mt * 16 + g, r1 = r0 + 8;
-            const int ch = sl * 4 + q;  // 16-byte chunk (8 halves) of the 128-byte row
-            const uint32_t p0 = am + r0 * 128 + ((ch ^ (r0 & 7)) << 4);
-            const uint32_t p1 = am + r1 * 128 + ((ch ^ (r1 & 7)) << 4);
-            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(p0), "r"(h[0]), "r"(h[1]), "r"(h[2]),
-                         "r"(h[3])
+            for (int i = 0; i < 8; ++i) h[bi][i] = hmul2_bits(h[bi][i], sbits);
+          }
+          const int odd = g & 1;
+          const int r0 = cw * 16 + g;
+          const uint32_t row0 = am + r0 * 128, row1 = row0 + 8 * 128;
+#pragma unroll
+          for (int o = 0; o < 2; ++o) {
+            const int bi = o ^ odd;  // slab this lane stores in pass o
+            uint32_t w[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w[i] = bi ? h[1][i] : h[0][i];
+            const uint32_t cx = uint32_t(((bi * 4 + q) ^ g) << 4);  // r0 & 7 == r1 & 7 == g
+            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(row0 + cx), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+                         "r"(w[3])
                          : "memory");
-            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(p1), "r"(h[4]), "r"(h[5]), "r"(h[6]),
-                         "r"(h[7])
+            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(row1 + cx), "r"(w[4]), "r"(w[5]), "r"(w[6]),
+                         "r"(w[7])
                          : "memory");
           }
         }
         fence_async_smem();  // generic-proxy writes -> visible to the tensor core's async proxy
         __syncwarp();
-        if (lane == 0) mbar_arrive(&conv[s]);
-        if (++s == kTcStages) {
+        if (lane == 0) mbar_arrive(&conv[ab]);
+        if (++s == S) {
           s = 0;
           ph ^= 1u;
+        }
+        if (++ab == kTcABufs) {
+          ab = 0;
+          aph ^= 1u;
         }
       }
       if (!ok) break;
@@ -345,6 +393,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
   } else {
     // ------------------------------------------------------------------ epilogue
     const int sp = warp & 3;  // TMEM sub-partition of this warp: lanes 32*sp .. 32*sp+31
+    const int eh = (warp - kTcEpiWarp0) >> 2;  // which of the sub-partition's column blocks
     const int rloc = 32 * sp + lane;
     int j = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++j) {
@@ -355,8 +404,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
       const int local = u - pre[e];
       const int rt = local / nch, chunk = local % nch;
       const int rows = min(BN, cnt - chunk * BN);
-      const int buf = j & 1;
-      if (*abort_flag || !mbar_wait(&tfull[buf], (j >> 1) & 1)) {
+      const int buf = j % C::kNBuf;
+      if (*abort_flag || !mbar_wait(&tfull[buf], (j / C::kNBuf) & 1)) {
         *abort_flag = 1;
         break;
       }
@@ -364,7 +413,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
       const float wmul_a = reinterpret_cast<const float*>(a.wa)[e];
       const float wmul_b = DUAL ? reinterpret_cast<const float*>(a.wb)[e] : 1.f;
       const uint32_t lane_base = tmem + (uint32_t(32 * sp) << 16);
-      for (int cb = 0; cb < rows; cb += 16) {
+      for (int cb = 16 * eh; cb < rows; cb += 16 * (kTcEpiWarps / 4)) {
         uint32_t gv[16], uv[16];
         tmem_ld16(lane_base + uint32_t(buf * NM * BN + cb), gv);
         if (DUAL) tmem_ld16(lane_base + uint32_t((buf * NM + 1) * BN + cb), uv);
@@ -431,15 +480,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
 template <int FMT, bool DUAL>
 int launch_tc(const TcArgs& a, const void* staged, int64_t rows_cap, cudaStream_t stream) {
   using C = TcCfg<FMT, DUAL>;
-  constexpr int kTcStages = C::kStages;
   CUtensorMap map;
   if (int rc = make_stage_map(&map, staged, rows_cap, a.kc_count, C::BN)) return rc;
-  const size_t smem = 1024 + size_t(kTcStages) * C::kStageBytes + 8 * (3 * kTcStages + 5) + 16 +
-                      size_t(a.n_experts + 1) * 4;
+  int dev = 0, optin = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+    return check_launch("expert_tc device attribute");
+  // as many load slots as the shared memory left by the A slots holds
+  const size_t fixed = 1024 + size_t(kTcABufs) * C::kABufBytes + tc_tail_bytes(a.n_experts);
+  const int n_loads = size_t(optin) > fixed ? int(std::min<size_t>(kTcMaxLoads, (size_t(optin) - fixed) / C::kLoadBytes)) : 0;
+  if (n_loads < 2) return fail(DSM_ERR_UNSUPPORTED, "expert_tc: too many experts for the shared-memory ring");
+  const size_t smem = fixed + size_t(n_loads) * C::kLoadBytes;
   auto kern = expert_tc_kernel<FMT, DUAL>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return check_launch("expert_tc smem attribute");
-  kern<<<persistent_ctas(), kTcThreads, smem, stream>>>(a, map);
+  kern<<<persistent_ctas(), kTcThreads, smem, stream>>>(a, map, n_loads);
   return check_launch("expert_tc");
 }
 
