@@ -231,6 +231,117 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
   const uint8_t* tiles_b = DUAL ? a.wb + hdr_bytes : nullptr;
   const int kcs = a.kc_count;
 
+  // Epilogue of the CTA's j-th unit u for TMEM sub-partition sp: its 16-column blocks part,
+  // part + nparts, ... . The epilogue warps take every unit; the converter warps, idle once
+  // their last stage is written, take a share of the CTA's last unit (the whole epilogue when
+  // a CTA has one unit, as the dense layers' wide units do). False on abort.
+  auto epilogue_unit = [&](int j, int u, int sp, int part, int nparts) -> bool {
+    const int rloc = 32 * sp + lane;
+    const uint32_t lane_base = tmem + (uint32_t(32 * sp) << 16);
+    const TmUnit w = tm_unit<BN>(a, pre, E, u, kcs);
+    const int e = w.e, rt = w.rt, chunk = w.chunk;
+    const int off = tm_first(a, e);
+    const int rows = min(BN, w.cnt - chunk * BN);
+    float* const o_out = a.o_out + w.ks * a.o_split_stride;
+    const int buf = j % C::DB;
+    if (*abort_flag || !mbar_wait(&tfull[buf], (j / C::DB) & 1)) {
+      *abort_flag = 1;
+      return false;
+    }
+    tc_fence_after();
+    const float wmul_a = reinterpret_cast<const float*>(a.wa)[e];
+    const float wmul_b = DUAL ? reinterpret_cast<const float*>(a.wb)[e] : 1.f;
+    for (int cb = 16 * part; cb < rows; cb += 16 * nparts) {
+      // partial accumulators, added in issuer order: issuer q holds matrix q % NM
+      float gsum[16], usum[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) gsum[i] = usum[i] = 0.f;
+#pragma unroll
+      for (int q = 0; q < P; ++q) {
+        uint32_t pv[16];
+        tmem_ld16(lane_base + uint32_t((buf * P + q) * BN + cb), pv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          if (q % NM == 0)
+            gsum[i] += __uint_as_float(pv[i]);
+          else
+            usum[i] += __uint_as_float(pv[i]);
+        }
+      }
+      if constexpr (DUAL && P >= 4) {
+        // decode widths: the epilogue overlaps the next unit's main loop (two accumulator
+        // buffers), and the branch-free form below would not fit the register budget of
+        // this thread count
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int col = cb + i;
+          if (col >= rows) break;
+          const int64_t r = int64_t(off) + chunk * BN + col;
+          const float xs = a.act_scale ? a.act_scale[r] : a.act_scale_const;
+          float gg = gsum[i] * xs * wmul_a;
+          float uu = usum[i] * xs * wmul_b;
+          if (a.round_gu & 1) {
+            gg = bf16_round(gg);
+            uu = bf16_round(uu);
+          }
+          float h = swiglu(gg, uu, a.act, a.limit);
+          if (a.round_gu & 2) h = bf16_round(h);
+          a.h_out[(int64_t(rt) * a.h_rows_cap + r) * kStagePitch + rloc] = __float2half_rn(h * a.h_scale);
+        }
+        continue;
+      }
+      // the block's 16 row scales (and output rows): one guarded load per lane, broadcast
+      // with a constant source lane per column
+      const int cl = cb + (lane & 15);
+      const int rl = off + chunk * BN + cl;
+      const float xs_b = (cl < rows && a.act_scale) ? a.act_scale[rl] : a.act_scale_const;
+      if constexpr (DUAL) {
+        // all 16 columns are computed without a branch (columns past `rows` hold unused
+        // accumulators), so their activation chains interleave; only the stores are guarded
+        const bool rg = a.round_gu & 1, rh = a.round_gu & 2;
+        __half* hp = a.h_out + (int64_t(rt) * a.h_rows_cap + off + chunk * BN + cb) * kStagePitch + rloc;
+        auto block = [&](auto silu_tag) {
+#pragma unroll
+          for (int i0 = 0; i0 < 16; i0 += 8) {  // 8 chains at a time: ILP within the register budget
+            float hv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float xs = __shfl_sync(0xffffffffu, xs_b, i0 + i);
+              float gg = gsum[i0 + i] * xs * wmul_a;
+              float uu = usum[i0 + i] * xs * wmul_b;
+              gg = rg ? bf16_round(gg) : gg;
+              uu = rg ? bf16_round(uu) : uu;
+              const float h = swiglu<decltype(silu_tag)::value>(gg, uu, a.limit);
+              hv[i] = (rh ? bf16_round(h) : h) * a.h_scale;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              if (cb + i0 + i < rows) hp[int64_t(i0 + i) * kStagePitch] = __float2half_rn(hv[i]);
+          }
+        };
+        if (a.act == DSM_ACT_SILU_MUL_BF16)
+          block(std::true_type{});
+        else
+          block(std::false_type{});
+      } else {
+        const int or_b = (cl < rows && a.o_row_map) ? a.o_row_map[rl] : rl;
+        const int d = rt * kTmM + rloc;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float xs = __shfl_sync(0xffffffffu, xs_b, i);
+          const int orow = __shfl_sync(0xffffffffu, or_b, i);
+          float v = gsum[i] * xs * wmul_a;
+          v = a.round_o ? bf16_round(v) : v;
+          if (cb + i < rows && d < a.out_rows) o_out[int64_t(orow) * a.ldo + d] = v;
+        }
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    return true;
+  };
+
   if (warp == kTmProducer) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
@@ -439,114 +550,18 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
         if (++ab == NA) ab = 0;
       }
     }
+    // this warp's share of the CTA's last unit's epilogue
+    if (ok && int(blockIdx.x) < total) {
+      const int j = (total - 1 - int(blockIdx.x)) / int(gridDim.x);
+      epilogue_unit(j, int(blockIdx.x) + j * int(gridDim.x), warp & 3, 1 + part, 1 + CW / 4);
+    }
   } else if (warp < kTmEpiWarps) {
     // ------------------------------------------------------------------ epilogue
-    const int rloc = 32 * warp + lane;
-    const uint32_t lane_base = tmem + (uint32_t(32 * warp) << 16);
     int j = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++j) {
-      const TmUnit w = tm_unit<BN>(a, pre, E, u, kcs);
-      const int e = w.e, rt = w.rt, chunk = w.chunk;
-      const int off = tm_first(a, e);
-      const int rows = min(BN, w.cnt - chunk * BN);
-      float* const o_out = a.o_out + w.ks * a.o_split_stride;
-      const int buf = j % C::DB;
-      if (*abort_flag || !mbar_wait(&tfull[buf], (j / C::DB) & 1)) {
-        *abort_flag = 1;
-        break;
-      }
-      tc_fence_after();
-      const float wmul_a = reinterpret_cast<const float*>(a.wa)[e];
-      const float wmul_b = DUAL ? reinterpret_cast<const float*>(a.wb)[e] : 1.f;
-      for (int cb = 0; cb < rows; cb += 16) {
-        // partial accumulators, added in issuer order: issuer q holds matrix q % NM
-        float gsum[16], usum[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) gsum[i] = usum[i] = 0.f;
-#pragma unroll
-        for (int q = 0; q < P; ++q) {
-          uint32_t pv[16];
-          tmem_ld16(lane_base + uint32_t((buf * P + q) * BN + cb), pv);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            if (q % NM == 0)
-              gsum[i] += __uint_as_float(pv[i]);
-            else
-              usum[i] += __uint_as_float(pv[i]);
-          }
-        }
-        if constexpr (DUAL && P >= 4) {
-          // decode widths: the epilogue overlaps the next unit's main loop (two accumulator
-          // buffers), and the branch-free form below would not fit the register budget of
-          // this thread count
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int col = cb + i;
-            if (col >= rows) break;
-            const int64_t r = int64_t(off) + chunk * BN + col;
-            const float xs = a.act_scale ? a.act_scale[r] : a.act_scale_const;
-            float gg = gsum[i] * xs * wmul_a;
-            float uu = usum[i] * xs * wmul_b;
-            if (a.round_gu & 1) {
-              gg = bf16_round(gg);
-              uu = bf16_round(uu);
-            }
-            float h = swiglu(gg, uu, a.act, a.limit);
-            if (a.round_gu & 2) h = bf16_round(h);
-            a.h_out[(int64_t(rt) * a.h_rows_cap + r) * kStagePitch + rloc] = __float2half_rn(h * a.h_scale);
-          }
-          continue;
-        }
-        // the block's 16 row scales (and output rows): one guarded load per lane, broadcast
-        // with a constant source lane per column
-        const int cl = cb + (lane & 15);
-        const int rl = off + chunk * BN + cl;
-        const float xs_b = (cl < rows && a.act_scale) ? a.act_scale[rl] : a.act_scale_const;
-        if constexpr (DUAL) {
-          // all 16 columns are computed without a branch (columns past `rows` hold unused
-          // accumulators), so their activation chains interleave; only the stores are guarded
-          const bool rg = a.round_gu & 1, rh = a.round_gu & 2;
-          __half* hp = a.h_out + (int64_t(rt) * a.h_rows_cap + off + chunk * BN + cb) * kStagePitch + rloc;
-          auto block = [&](auto silu_tag) {
-#pragma unroll
-            for (int i0 = 0; i0 < 16; i0 += 8) {  // 8 chains at a time: ILP within the register budget
-              float hv[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float xs = __shfl_sync(0xffffffffu, xs_b, i0 + i);
-                float gg = gsum[i0 + i] * xs * wmul_a;
-                float uu = usum[i0 + i] * xs * wmul_b;
-                gg = rg ? bf16_round(gg) : gg;
-                uu = rg ? bf16_round(uu) : uu;
-                const float h = swiglu<decltype(silu_tag)::value>(gg, uu, a.limit);
-                hv[i] = (rh ? bf16_round(h) : h) * a.h_scale;
-              }
-#pragma unroll
-              for (int i = 0; i < 8; ++i)
-                if (cb + i0 + i < rows) hp[int64_t(i0 + i) * kStagePitch] = __float2half_rn(hv[i]);
-            }
-          };
-          if (a.act == DSM_ACT_SILU_MUL_BF16)
-            block(std::true_type{});
-          else
-            block(std::false_type{});
-        } else {
-          const int or_b = (cl < rows && a.o_row_map) ? a.o_row_map[rl] : rl;
-          const int d = rt * kTmM + rloc;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float xs = __shfl_sync(0xffffffffu, xs_b, i);
-            const int orow = __shfl_sync(0xffffffffu, or_b, i);
-            float v = gsum[i] * xs * wmul_a;
-            v = a.round_o ? bf16_round(v) : v;
-            if (cb + i < rows && d < a.out_rows) o_out[int64_t(orow) * a.ldo + d] = v;
-          }
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);
+      const bool last = u + int(gridDim.x) >= total;
+      if (!epilogue_unit(j, u, warp, 0, last ? 1 + CW / 4 : 1)) break;
+      if (lane == 0) mbar_arrive(&tempty[j % C::DB]);
     }
   }
   tc_fence_before();
