@@ -375,6 +375,7 @@ def run_gpu(args, wl_name=None, emit=True):
     ms = e0_.elapsed_time(e1_) / args.steps
     ms = _max_over_ranks(ms, ws, dev)
     _barrier(ws)
+    ep_info = ep_measure(model, step, routing, ws, rank, dev, wl) if ws > 1 else None
 
     # ---- dominant kernel: the fused gate/up expert kernel, timed alone with events (1 GPU)
     sh_bytes = 3 * wl.args["moe_inter_dim"] * dim * 2
@@ -448,7 +449,7 @@ def run_gpu(args, wl_name=None, emit=True):
             "hbm_gbs_step": avg_step_bytes / (ms * 1e-3) / 1e9,
             "hbm_frac_of_8tbs_step": avg_step_bytes / (ms * 1e-3) / 1e9 / SPEC_HBM_GBS,
             "roofline": roofline_entry(ws, k_ms, k_bytes, k_touched, k_flops, k_tc, achieved, avg_step_bytes, ms,
-                                       hbm_peak, tc_peak, peak_kind, traffic, wl.wfmt),
+                                       hbm_peak, tc_peak, peak_kind, traffic, wl.wfmt, ep_info),
             "cpu_baseline": cpu,
             "e2e": None if e2e_ms is None else {
                 "value": ws * N / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": N * dim * 2,
@@ -456,10 +457,71 @@ def run_gpu(args, wl_name=None, emit=True):
             "gpu_launches": (KERNELS_PER_STEP if ws == 1 else KERNELS_PER_STEP_EP) * args.steps,
             "clocks": clk.summary(),
         }
+        if ep_info is not None:
+            line["expert_parallel"] = ep_info
         if emit:
             print(json.dumps(line))
         return line
     return None
+
+
+def ep_measure(model, step, routing, ws, rank, dev, wl, n=3):
+    """Expert parallelism, per rank: the row exchange (dispatch of the routed rows to their
+    owners, return of the fp32 results) and the local gate/up product, timed with CUDA events
+    around those launches over ``n`` further steps, and the NVLink bytes each rank stores into
+    its peers' buffers (from the same steps' routing). Every rank takes the same collective
+    steps."""
+    import torch
+    import torch.distributed as dist
+
+    dim, inter = wl.args["dim"], wl.args["moe_inter_dim"]
+    model.phase_events = []
+    for i in range(n):
+        step(i)
+    torch.cuda.synchronize()
+    acc = {}
+    for name, a, b in model.phase_events:
+        acc.setdefault(name, []).append(a.elapsed_time(b))
+    model.phase_events = None
+    names = ("dispatch", "return", "gate_up")
+    t = torch.zeros(ws, len(names), dtype=torch.float64, device=dev)
+    for j, name in enumerate(names):
+        v = acc.get(name, [])
+        t[rank, j] = sum(v) / len(v) if v else 0.0
+    pairs = torch.zeros(ws, ws, dtype=torch.float64, device=dev)  # [sender, owner] routed rows
+    for i in range(n):
+        owner = routing(i).flatten().long() // model.e_local
+        pairs[rank] += torch.bincount(owner, minlength=ws).double()
+    dist.all_reduce(t)
+    dist.all_reduce(pairs)
+    t, pairs = t.cpu(), (pairs / n).cpu()
+    own = pairs.diagonal()
+    rows_in = pairs.sum(0)                        # rows each owner's experts compute
+    sent = (pairs.sum(1) - own) * dim * 2         # bf16 rows stored into peers
+    back = (rows_in - own) * dim * 4              # fp32 results stored back to their senders
+    out_bytes = sent + back
+    ex_ms = t[:, 0] + t[:, 1]
+    gbs = [float(b / (m * 1e-3) / 1e9) if m > 0 else None for b, m in zip(out_bytes, ex_ms)]
+    topk = wl.args["n_activated_experts"]
+    hint, busy = wl.n_tokens * topk, min(wl.n_tokens * topk, model.e_local)
+    tc = wl.wfmt == "fp8" and hint >= 64 * busy  # the expert products' dispatch rule
+    info = {
+        "exchange": "peer stores into CUDA-IPC buffers over NVLink (no NCCL on the data path)",
+        "dispatch_ms": [float(v) for v in t[:, 0]],
+        "return_ms": [float(v) for v in t[:, 1]],
+        "a2a_bytes_out_per_step": [float(v) for v in out_bytes],
+        "a2a_gbs_per_gpu": gbs,
+        "a2a_gbs_per_gpu_mean": sum(g for g in gbs if g) / max(1, sum(1 for g in gbs if g)),
+        "nvlink_nominal_gbs_per_direction": 900,
+        "rows_per_rank": [float(v) for v in rows_in],
+        "gate_up_ms": [float(v) for v in t[:, 2]],
+        "gate_up_regime": "tcgen05 (tensor)" if tc else "weight streaming (HBM)",
+        "sample": f"{n} steps after the timed ones",
+    }
+    if tc:
+        info["gate_up_tflops"] = [float(2 * 2 * r * dim * inter / (m * 1e-3) / 1e12) if m > 0 else None
+                                  for r, m in zip(rows_in, t[:, 2])]
+    return info
 
 
 # arithmetic of the routed expert products per weight format
@@ -472,8 +534,16 @@ DTYPE_DESC = {
 
 
 def roofline_entry(ws, k_ms, k_bytes, k_touched, k_flops, k_tc, achieved, step_bytes, ms, hbm_peak, tc_peak,
-                   peak_kind, traffic, wfmt="fp8"):
-    """The roofline figure of the dominant kernel (or, for expert parallelism, of the step)."""
+                   peak_kind, traffic, wfmt="fp8", ep_info=None):
+    """The roofline figure of the dominant kernel (or, for expert parallelism, of the step;
+    of the local gate/up product on the slowest rank when it runs on the tensor pipe)."""
+    if ws > 1 and ep_info and ep_info.get("gate_up_tflops"):
+        ms_r = ep_info["gate_up_ms"]
+        r = max(range(len(ms_r)), key=lambda i: ms_r[i])  # the rank that bounds the step
+        tflops = ep_info["gate_up_tflops"][r]
+        return {"bound": "tensor", "kernel": f"expert_tc_kernel<gate_up> on rank {r} (the slowest)",
+                "achieved": tflops, "peak": tc_peak, "unit": "TFLOP/s", "frac": tflops / tc_peak,
+                "peak_kind": peak_kind + " (dense bf16/f16 burst)", "launch_ms": ms_r[r], "traffic": None}
     if ws > 1:
         gbs = step_bytes / (ms * 1e-3) / 1e9
         return {"bound": "hbm", "kernel": "whole step per rank (expert-parallel)", "achieved": gbs, "peak": hbm_peak,
@@ -699,10 +769,71 @@ def run_qwen3(args, emit=True):
             "gpu_launches": QWEN3_KERNELS_PER_STEP * args.steps,
             "clocks": clk.summary(),
         }
+        if ep_info is not None:
+            line["expert_parallel"] = ep_info
         if emit:
             print(json.dumps(line))
         return line
     return None
+
+
+def ep_measure(model, step, routing, ws, rank, dev, wl, n=3):
+    """Expert parallelism, per rank: the row exchange (dispatch of the routed rows to their
+    owners, return of the fp32 results) and the local gate/up product, timed with CUDA events
+    around those launches over ``n`` further steps, and the NVLink bytes each rank stores into
+    its peers' buffers (from the same steps' routing). Every rank takes the same collective
+    steps."""
+    import torch
+    import torch.distributed as dist
+
+    dim, inter = wl.args["dim"], wl.args["moe_inter_dim"]
+    model.phase_events = []
+    for i in range(n):
+        step(i)
+    torch.cuda.synchronize()
+    acc = {}
+    for name, a, b in model.phase_events:
+        acc.setdefault(name, []).append(a.elapsed_time(b))
+    model.phase_events = None
+    names = ("dispatch", "return", "gate_up")
+    t = torch.zeros(ws, len(names), dtype=torch.float64, device=dev)
+    for j, name in enumerate(names):
+        v = acc.get(name, [])
+        t[rank, j] = sum(v) / len(v) if v else 0.0
+    pairs = torch.zeros(ws, ws, dtype=torch.float64, device=dev)  # [sender, owner] routed rows
+    for i in range(n):
+        owner = routing(i).flatten().long() // model.e_local
+        pairs[rank] += torch.bincount(owner, minlength=ws).double()
+    dist.all_reduce(t)
+    dist.all_reduce(pairs)
+    t, pairs = t.cpu(), (pairs / n).cpu()
+    own = pairs.diagonal()
+    rows_in = pairs.sum(0)                        # rows each owner's experts compute
+    sent = (pairs.sum(1) - own) * dim * 2         # bf16 rows stored into peers
+    back = (rows_in - own) * dim * 4              # fp32 results stored back to their senders
+    out_bytes = sent + back
+    ex_ms = t[:, 0] + t[:, 1]
+    gbs = [float(b / (m * 1e-3) / 1e9) if m > 0 else None for b, m in zip(out_bytes, ex_ms)]
+    topk = wl.args["n_activated_experts"]
+    hint, busy = wl.n_tokens * topk, min(wl.n_tokens * topk, model.e_local)
+    tc = wl.wfmt == "fp8" and hint >= 64 * busy  # the expert products' dispatch rule
+    info = {
+        "exchange": "peer stores into CUDA-IPC buffers over NVLink (no NCCL on the data path)",
+        "dispatch_ms": [float(v) for v in t[:, 0]],
+        "return_ms": [float(v) for v in t[:, 1]],
+        "a2a_bytes_out_per_step": [float(v) for v in out_bytes],
+        "a2a_gbs_per_gpu": gbs,
+        "a2a_gbs_per_gpu_mean": sum(g for g in gbs if g) / max(1, sum(1 for g in gbs if g)),
+        "nvlink_nominal_gbs_per_direction": 900,
+        "rows_per_rank": [float(v) for v in rows_in],
+        "gate_up_ms": [float(v) for v in t[:, 2]],
+        "gate_up_regime": "tcgen05 (tensor)" if tc else "weight streaming (HBM)",
+        "sample": f"{n} steps after the timed ones",
+    }
+    if tc:
+        info["gate_up_tflops"] = [float(2 * 2 * r * dim * inter / (m * 1e-3) / 1e12) if m > 0 else None
+                                  for r, m in zip(rows_in, t[:, 2])]
+    return info
 
 
 def run_reference_qwen3(args):
@@ -1328,10 +1459,11 @@ def run_reference_dsattn(args):
 # (fp8 decode) and carried in its line under "configs": the tiny hash-routed layer (latency),
 # fp4 decode (448 tokens, Zipf 1.1), the Qwen3 q8 MLP and the 16384-token prefill.
 SIDE_CONFIGS = ("tiny_hash", "fp4_decode", "qwen3_mlp_q8", "prefill_fp8")
-# expert parallelism: fp4 decode is the other configuration the reference quotes at 1/2/4/8 GPUs
-SIDE_CONFIGS_EP = ("fp4_decode",)
+# expert parallelism: fp4 decode (quoted at 1/2/4/8 GPUs) and the 16384-token prefill (quoted at
+# 8 GPUs with its all-to-all GB/s and tensor-pipe figures)
+SIDE_CONFIGS_EP = ("fp4_decode", "prefill_fp8")
 CONFIG_KEYS = ("metric", "value", "unit", "ms_per_step", "higher_is_better", "dtype", "config", "hbm_gbs_step",
-               "roofline", "cpu_baseline", "e2e", "gpu_launches", "clocks")
+               "roofline", "cpu_baseline", "e2e", "gpu_launches", "clocks", "expert_parallel")
 
 
 def run_all(args):

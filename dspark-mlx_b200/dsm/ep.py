@@ -26,6 +26,7 @@ fixes it at construction.
 
 from __future__ import annotations
 
+import contextlib
 import copy
 import ctypes
 from typing import List, Optional, Tuple
@@ -171,6 +172,21 @@ class ExpertParallelMoE(nn.Module):
         self.local = MoE(local_args, layer_id)  # holds this rank's routed experts (any format)
         del self.local.gate, self.local.shared_experts
         self._ex = {}
+        # a list to collect (name, start, end) CUDA events around the row exchange launches
+        # ("dispatch", "return") and the local gate/up product ("gate_up"), for bandwidth and
+        # tensor-pipe measurements; None (the default) records nothing
+        self.phase_events: Optional[list] = None
+
+    @contextlib.contextmanager
+    def _timed(self, name: str):
+        if self.phase_events is None:
+            yield
+            return
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        yield
+        b.record()
+        self.phase_events.append((name, a, b))
 
     @classmethod
     def from_moe(cls, moe: MoE, args, layer_id: int, group=None, max_tokens: int = 512, world: Optional[int] = None,
@@ -269,8 +285,9 @@ class ExpertParallelMoE(nn.Module):
                             s), "dsm_permute")
         # 2. rows to their owners
         row_map = torch.empty(max(P, 1), dtype=torch.int32, device=dev)
-        check(L.dsm_ep_dispatch(ctypes.byref(ex.desc), ptr(x2), n, ptr(idx), ptr(perm), ptr(offsets), ptr(counts), k,
-                                ptr(ex.peer_base), ptr(row_map), ptr(ex.done), epoch, s), "dsm_ep_dispatch")
+        with self._timed("dispatch"):
+            check(L.dsm_ep_dispatch(ctypes.byref(ex.desc), ptr(x2), n, ptr(idx), ptr(perm), ptr(offsets), ptr(counts),
+                                    k, ptr(ex.peer_base), ptr(row_map), ptr(ex.done), epoch, s), "dsm_ep_dispatch")
         # 3. the shared expert while the peers' rows arrive
         if x2.dtype == torch.bfloat16:
             sgu = int(self.shared_experts.weight_dtype("w1") == torch.bfloat16) | 2
@@ -310,14 +327,16 @@ class ExpertParallelMoE(nn.Module):
         check(L.dsm_stage_rows_count(x_recv, dtype_code(x2.dtype), R, dim, ptr(lperm), R, 1, ptr(xs), cap, ptr(xsc),
                                      ptr(n_valid), s), "dsm_stage_rows_count")
         hint = max(1, x2.shape[0] * self.gate.topk)  # rows an owner gets on average when every rank routes n tokens
-        check(L.dsm_expert_gate_up(ptr(xs), ptr(xsc), cap, dim, ptr(loff), El, p1.wfmt, p1.group_size, ptr(p1.packed),
-                                   ptr(p3.packed), self.inter_dim, _lib.ACT_SWIGLU_CLAMP, float(self.swiglu_limit),
-                                   rgu, ptr(hs), hsc, hint, s), "dsm_expert_gate_up")
+        with self._timed("gate_up"):
+            check(L.dsm_expert_gate_up(ptr(xs), ptr(xsc), cap, dim, ptr(loff), El, p1.wfmt, p1.group_size,
+                                       ptr(p1.packed), ptr(p3.packed), self.inter_dim, _lib.ACT_SWIGLU_CLAMP,
+                                       float(self.swiglu_limit), rgu, ptr(hs), hsc, hint, s), "dsm_expert_gate_up")
         check(L.dsm_expert_down(ptr(hs), hsc, cap, self.inter_dim, ptr(loff), El, p2.wfmt, p2.group_size,
                                 ptr(p2.packed), dim, ro, ptr(o_recv), dim, ptr(lperm), hint, s), "dsm_expert_down")
         # 6. results back to the token owners
-        check(L.dsm_ep_return(d, ptr(o_recv), ptr(n_valid), ptr(ex.peer_base), ex.done.data_ptr() + 4, epoch, s),
-              "dsm_ep_return")
+        with self._timed("return"):
+            check(L.dsm_ep_return(d, ptr(o_recv), ptr(n_valid), ptr(ex.peer_base), ex.done.data_ptr() + 4, epoch, s),
+                  "dsm_ep_return")
         st["keep_compute"] = (loff, lperm, n_valid, xs, xsc, hs, o_recv)
 
     def combine(self, st: dict) -> torch.Tensor:
