@@ -769,71 +769,10 @@ def run_qwen3(args, emit=True):
             "gpu_launches": QWEN3_KERNELS_PER_STEP * args.steps,
             "clocks": clk.summary(),
         }
-        if ep_info is not None:
-            line["expert_parallel"] = ep_info
         if emit:
             print(json.dumps(line))
         return line
     return None
-
-
-def ep_measure(model, step, routing, ws, rank, dev, wl, n=3):
-    """Expert parallelism, per rank: the row exchange (dispatch of the routed rows to their
-    owners, return of the fp32 results) and the local gate/up product, timed with CUDA events
-    around those launches over ``n`` further steps, and the NVLink bytes each rank stores into
-    its peers' buffers (from the same steps' routing). Every rank takes the same collective
-    steps."""
-    import torch
-    import torch.distributed as dist
-
-    dim, inter = wl.args["dim"], wl.args["moe_inter_dim"]
-    model.phase_events = []
-    for i in range(n):
-        step(i)
-    torch.cuda.synchronize()
-    acc = {}
-    for name, a, b in model.phase_events:
-        acc.setdefault(name, []).append(a.elapsed_time(b))
-    model.phase_events = None
-    names = ("dispatch", "return", "gate_up")
-    t = torch.zeros(ws, len(names), dtype=torch.float64, device=dev)
-    for j, name in enumerate(names):
-        v = acc.get(name, [])
-        t[rank, j] = sum(v) / len(v) if v else 0.0
-    pairs = torch.zeros(ws, ws, dtype=torch.float64, device=dev)  # [sender, owner] routed rows
-    for i in range(n):
-        owner = routing(i).flatten().long() // model.e_local
-        pairs[rank] += torch.bincount(owner, minlength=ws).double()
-    dist.all_reduce(t)
-    dist.all_reduce(pairs)
-    t, pairs = t.cpu(), (pairs / n).cpu()
-    own = pairs.diagonal()
-    rows_in = pairs.sum(0)                        # rows each owner's experts compute
-    sent = (pairs.sum(1) - own) * dim * 2         # bf16 rows stored into peers
-    back = (rows_in - own) * dim * 4              # fp32 results stored back to their senders
-    out_bytes = sent + back
-    ex_ms = t[:, 0] + t[:, 1]
-    gbs = [float(b / (m * 1e-3) / 1e9) if m > 0 else None for b, m in zip(out_bytes, ex_ms)]
-    topk = wl.args["n_activated_experts"]
-    hint, busy = wl.n_tokens * topk, min(wl.n_tokens * topk, model.e_local)
-    tc = wl.wfmt == "fp8" and hint >= 64 * busy  # the expert products' dispatch rule
-    info = {
-        "exchange": "peer stores into CUDA-IPC buffers over NVLink (no NCCL on the data path)",
-        "dispatch_ms": [float(v) for v in t[:, 0]],
-        "return_ms": [float(v) for v in t[:, 1]],
-        "a2a_bytes_out_per_step": [float(v) for v in out_bytes],
-        "a2a_gbs_per_gpu": gbs,
-        "a2a_gbs_per_gpu_mean": sum(g for g in gbs if g) / max(1, sum(1 for g in gbs if g)),
-        "nvlink_nominal_gbs_per_direction": 900,
-        "rows_per_rank": [float(v) for v in rows_in],
-        "gate_up_ms": [float(v) for v in t[:, 2]],
-        "gate_up_regime": "tcgen05 (tensor)" if tc else "weight streaming (HBM)",
-        "sample": f"{n} steps after the timed ones",
-    }
-    if tc:
-        info["gate_up_tflops"] = [float(2 * 2 * r * dim * inter / (m * 1e-3) / 1e12) if m > 0 else None
-                                  for r, m in zip(rows_in, t[:, 2])]
-    return info
 
 
 def run_reference_qwen3(args):
