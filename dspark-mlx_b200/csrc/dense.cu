@@ -31,16 +31,24 @@ template <typename YT>
 __global__ void __launch_bounds__(256) reduce_splits_kernel(const float* __restrict__ parts, int n_splits,
                                                             int64_t stride, int64_t count, int round,
                                                             YT* __restrict__ y) {
-  // four consecutive elements per thread; count and stride are multiples of 4 (dim % 4 == 0)
+  // four consecutive elements per thread; count and stride are multiples of 4 (dim % 4 == 0).
+  // Every slab's load is issued before the first add (one memory latency, not n_splits), and
+  // the adds keep split order.
   for (int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < count;
        i += int64_t(gridDim.x) * blockDim.x * 4) {
-    float4 acc = *reinterpret_cast<const float4*>(parts + i);
-    for (int s = 1; s < n_splits; ++s) {
-      const float4 v = *reinterpret_cast<const float4*>(parts + s * stride + i);
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+    float4 v[kMaxSplits];
+#pragma unroll
+    for (int s = 0; s < kMaxSplits; ++s)
+      if (s < n_splits) v[s] = *reinterpret_cast<const float4*>(parts + s * stride + i);
+    float4 acc = v[0];
+#pragma unroll
+    for (int s = 1; s < kMaxSplits; ++s) {
+      if (s < n_splits) {
+        acc.x += v[s].x;
+        acc.y += v[s].y;
+        acc.z += v[s].z;
+        acc.w += v[s].w;
+      }
     }
     const float r[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
@@ -93,13 +101,19 @@ __global__ void __launch_bounds__(256) sum_splits_rows_kernel(const float* __res
   const int64_t count = n_rows * dim;
   for (int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < count;
        i += int64_t(gridDim.x) * blockDim.x * 4) {
-    float4 acc = *reinterpret_cast<const float4*>(parts + i);
-    for (int s = 1; s < n_splits; ++s) {
-      const float4 v = *reinterpret_cast<const float4*>(parts + s * count + i);
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+    float4 v[kMaxSplits];  // every slab's load in flight before the adds, which keep split order
+#pragma unroll
+    for (int s = 0; s < kMaxSplits; ++s)
+      if (s < n_splits) v[s] = *reinterpret_cast<const float4*>(parts + s * count + i);
+    float4 acc = v[0];
+#pragma unroll
+    for (int s = 1; s < kMaxSplits; ++s) {
+      if (s < n_splits) {
+        acc.x += v[s].x;
+        acc.y += v[s].y;
+        acc.z += v[s].z;
+        acc.w += v[s].w;
+      }
     }
     const int64_t r = i / dim;
     const int c = int(i % dim);
