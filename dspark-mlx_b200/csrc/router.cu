@@ -14,19 +14,29 @@
 // order of ``argsort(scores + bias)[..., -k:]``; equal scores rank by expert id (the
 // higher id ranks higher, as a stable ascending sort leaves them).
 #include <cfloat>
+#include <type_traits>
 
 #include "common.cuh"
 
 namespace dsm {
 namespace {
 
-// CTA tile: 64 tokens x 32 experts x one K slice, in 32-wide K sub-chunks; 8 warps, each
-// 16 tokens x 16 experts (2 x 2 m8n8 tiles). Shared pitch 36 doubles (4 mod 16) makes the
-// m8n8k4 fragment loads (8 rows x 4 consecutive K) conflict-free.
-constexpr int kPT = 64;
-constexpr int kPE = 32;
-constexpr int kPKS = 32;
-constexpr int kPitch = 36;
+// CTA tiles: PT tokens x PE experts x one K slice, in PKS-wide K sub-chunks; 8 warps in a
+// 4 x 2 grid, each (PT / 4) tokens x (PE / 2) experts of m8n8 tiles. Decode-sized calls take
+// 64 x 32 (32-wide sub-chunks, 16 x 16 per warp: little padding at 56-448 tokens); from
+// kWideTokens tokens, 128 x 64 (16-wide sub-chunks, 32 x 32 per warp: each fragment load
+// feeds twice the MMAs). Shared pitch PKS + 4 doubles (4 mod 16) makes the m8n8k4 fragment
+// loads (8 rows x 4 consecutive K) conflict-free.
+constexpr int64_t kWideTokens = 1024;
+template <int PT>
+struct RouterTile {
+  static constexpr int PE = PT == 128 ? 64 : 32;
+  static constexpr int PKS = PT == 128 ? 16 : 32;
+  static constexpr int kPitch = PKS + 4;
+  static constexpr int TI = PT / 4 / 8, TJ = PE / 2 / 8;  // m8n8 tiles per warp
+  static_assert(PT * PKS == 256 * 8 && PE * PKS == 256 * 4, "one 8-value x load and one 4-value w load per thread");
+};
+inline int router_tile_tokens(int64_t n_tokens) { return n_tokens >= kWideTokens ? 128 : 64; }
 
 __device__ __forceinline__ void dmma(double (&d)[2], double a, double b) {
   asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
@@ -42,29 +52,32 @@ __device__ __forceinline__ void dmma(double (&d)[2], double a, double b) {
 int router_k_slice(int64_t n_tokens, int dim, int n_experts) {
   if (n_tokens <= 256) return 256;
   constexpr int64_t kTargetCtas = 2 * 148;
-  const int64_t tiles = ceil_div(int64_t(n_experts), int64_t(kPE)) * ceil_div(n_tokens, int64_t(kPT));
+  const int pt = router_tile_tokens(n_tokens), pe = pt == 128 ? 64 : 32;
+  const int64_t tiles = ceil_div(int64_t(n_experts), int64_t(pe)) * ceil_div(n_tokens, int64_t(pt));
   int64_t slices = std::max<int64_t>(1, ceil_div(kTargetCtas, tiles));
   slices = std::min<int64_t>(slices, std::max<int64_t>(1, dim / 256));
-  return int(ceil_div(ceil_div(int64_t(dim), slices), int64_t(kPKS)) * kPKS);
+  return int(ceil_div(ceil_div(int64_t(dim), slices), int64_t(32)) * 32);
 }
 
-template <typename XT>
+template <typename XT, int PT>
 __global__ void __launch_bounds__(256) gate_partial_kernel(const XT* __restrict__ x, const float* __restrict__ w,
                                                            double* __restrict__ part, int64_t n, int dim,
                                                            int n_experts, int k_slice, int vec_ok) {
-  __shared__ double xs[kPT][kPitch];
-  __shared__ double ws[kPE][kPitch];
+  using T = RouterTile<PT>;
+  constexpr int PE = T::PE, PKS = T::PKS, TI = T::TI, TJ = T::TJ;
+  __shared__ double xs[PT][T::kPitch];
+  __shared__ double ws[PE][T::kPitch];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int e0 = blockIdx.x * kPE;
+  const int e0 = blockIdx.x * PE;
   const int ks = blockIdx.y;
-  const int64_t t0 = int64_t(blockIdx.z) * kPT;
+  const int64_t t0 = int64_t(blockIdx.z) * PT;
   const int kbeg = ks * k_slice, kend = min(dim, kbeg + k_slice);
-  const int tw = (warp & 3) * 16, ew = (warp >> 2) * 16;
-  double acc[2][2][2] = {};
-  // each thread stages 8 x values and 4 w values per 32-wide sub-chunk; the next
-  // sub-chunk's global loads are issued before the current one is multiplied
-  const int xr = tid >> 2, xc = (tid & 3) * 8;
-  const int wr = tid >> 3, wc = (tid & 7) * 4;
+  const int tw = (warp & 3) * (PT / 4), ew = (warp >> 2) * (PE / 2);
+  double acc[TI][TJ][2] = {};
+  // each thread stages 8 x values and 4 w values per sub-chunk; the next sub-chunk's global
+  // loads are issued before the current one is multiplied
+  const int xr = tid / (PKS / 8), xc = (tid % (PKS / 8)) * 8;
+  const int wr = tid / (PKS / 4), wc = (tid % (PKS / 4)) * 4;
   float xv[8], wv[4];
   auto fetch = [&](int k0) {
     const int64_t t = t0 + xr;
@@ -98,33 +111,32 @@ __global__ void __launch_bounds__(256) gate_partial_kernel(const XT* __restrict_
     }
   };
   fetch(kbeg);
-  for (int k0 = kbeg; k0 < kend; k0 += kPKS) {
+  for (int k0 = kbeg; k0 < kend; k0 += PKS) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) xs[xr][xc + i] = double(xv[i]);
 #pragma unroll
     for (int i = 0; i < 4; ++i) ws[wr][wc + i] = double(wv[i]);
     __syncthreads();
-    if (k0 + kPKS < kend) fetch(k0 + kPKS);
+    if (k0 + PKS < kend) fetch(k0 + PKS);
 #pragma unroll
-    for (int kk = 0; kk < kPKS / 4; ++kk) {
+    for (int kk = 0; kk < PKS / 4; ++kk) {
       const int kc = kk * 4 + (lane & 3);
-      double a[2], b[2];
+      double a[TI], b[TJ];
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        a[i] = xs[tw + 8 * i + (lane >> 2)][kc];
-        b[i] = ws[ew + 8 * i + (lane >> 2)][kc];
-      }
+      for (int i = 0; i < TI; ++i) a[i] = xs[tw + 8 * i + (lane >> 2)][kc];
 #pragma unroll
-      for (int i = 0; i < 2; ++i)
+      for (int j = 0; j < TJ; ++j) b[j] = ws[ew + 8 * j + (lane >> 2)][kc];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) dmma(acc[i][j], a[i], b[j]);
+      for (int i = 0; i < TI; ++i)
+#pragma unroll
+        for (int j = 0; j < TJ; ++j) dmma(acc[i][j], a[i], b[j]);
     }
     __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 2; ++i)
+  for (int i = 0; i < TI; ++i)
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+    for (int j = 0; j < TJ; ++j)
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int64_t t = t0 + tw + 8 * i + (lane >> 2);
@@ -305,13 +317,20 @@ extern "C" int dsm_router(const void* x, int x_dtype, int64_t n_tokens, int dim,
   float* logits = reinterpret_cast<float*>(part + int64_t(n_slices) * n_tokens * n_experts);
   const int vec_ok = (dim % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(gate_weight) & 15) == 0);
-  dim3 grid(unsigned(ceil_div(n_experts, kPE)), unsigned(n_slices), unsigned(ceil_div(n_tokens, kPT)));
-  if (x_dtype == DSM_DT_BF16)
-    gate_partial_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), gate_weight, part,
-                                                            n_tokens, dim, n_experts, k_slice, vec_ok);
+  auto partial = [&](auto tile) {
+    constexpr int PT = decltype(tile)::value;
+    dim3 grid(unsigned(ceil_div(n_experts, RouterTile<PT>::PE)), unsigned(n_slices), unsigned(ceil_div(n_tokens, PT)));
+    if (x_dtype == DSM_DT_BF16)
+      gate_partial_kernel<__nv_bfloat16, PT><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), gate_weight,
+                                                                  part, n_tokens, dim, n_experts, k_slice, vec_ok);
+    else
+      gate_partial_kernel<float, PT><<<grid, 256, 0, s>>>(static_cast<const float*>(x), gate_weight, part, n_tokens,
+                                                          dim, n_experts, k_slice, vec_ok);
+  };
+  if (router_tile_tokens(n_tokens) == 128)
+    partial(std::integral_constant<int, 128>{});
   else
-    gate_partial_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(x), gate_weight, part, n_tokens, dim,
-                                                    n_experts, k_slice, vec_ok);
+    partial(std::integral_constant<int, 64>{});
   if (int rc = check_launch("gate_partial")) return rc;
   const int64_t count = n_tokens * n_experts;
   gate_reduce_kernel<<<unsigned(ceil_div(count, 256)), 256, 0, s>>>(part, n_slices, count, logits);

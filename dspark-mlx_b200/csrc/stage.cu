@@ -69,27 +69,33 @@ __device__ __forceinline__ void stage_one_row(const XT* __restrict__ x, int64_t 
   const XT* row = x + t * dim;
   const bool vec_ok = (dim % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
   const int kpad = k_chunks * kChunkK;
-  // the row's power-of-two scale from the CTA's max |x|
-  auto row_scale_exp = [&](float amax) {
+  float amax = 0.f;
+  for (int k = threadIdx.x * 8; k < dim; k += kStageThreads * 8) {
+    float v[8];
+    load8(row, k, dim, vec_ok, v);
 #pragma unroll
-    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    __syncthreads();  // red is reused by the next row of a looping CTA
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
-    __syncthreads();
-    amax = red[0];
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  }
 #pragma unroll
-    for (int i = 1; i < kStageThreads / 32; ++i) amax = fmaxf(amax, red[i]);
-    int s = 0;
-    if (amax > 0.f && isfinite(amax)) {
-      int ex;
-      frexpf(amax, &ex);  // amax in [2^(ex-1), 2^ex)
-      s = 15 - ex;
-      s = s < -100 ? -100 : (s > 100 ? 100 : s);
-    }
-    if (threadIdx.x == 0) row_scale[r] = ldexpf(1.f, -s);
-    return ldexpf(1.f, s);
-  };
-  auto store8 = [&](int k, const float (&v)[8], float up) {
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  __syncthreads();  // red is reused by the next row of a looping CTA
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int i = 1; i < kStageThreads / 32; ++i) amax = fmaxf(amax, red[i]);
+  int s = 0;
+  if (amax > 0.f && isfinite(amax)) {
+    int ex;
+    frexpf(amax, &ex);  // amax in [2^(ex-1), 2^ex)
+    s = 15 - ex;
+    s = s < -100 ? -100 : (s > 100 ? 100 : s);
+  }
+  const float up = ldexpf(1.f, s);
+  if (threadIdx.x == 0) row_scale[r] = ldexpf(1.f, -s);
+  for (int k = threadIdx.x * 8; k < kpad; k += kStageThreads * 8) {
+    float v[8];
+    load8(row, k, dim, vec_ok, v);
     uint32_t h[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -98,41 +104,6 @@ __device__ __forceinline__ void stage_one_row(const XT* __restrict__ x, int64_t 
     }
     const int c = k / kChunkK, col = k % kChunkK;
     *reinterpret_cast<uint4*>(staged + (int64_t(c) * rows_cap + r) * kStagePitch + col) = make_uint4(h[0], h[1], h[2], h[3]);
-  };
-  constexpr int kStep = kStageThreads * 8;
-  constexpr int kRegIt = 4;  // rows of up to 4096 columns stay in registers: one read of x
-  if (kpad <= kRegIt * kStep) {
-    float v[kRegIt][8];
-    float amax = 0.f;
-#pragma unroll
-    for (int it = 0; it < kRegIt; ++it) {
-      const int k = threadIdx.x * 8 + it * kStep;
-      if (k < kpad) {
-        load8(row, k, dim, vec_ok, v[it]);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[it][i]));
-      }
-    }
-    const float up = row_scale_exp(amax);
-#pragma unroll
-    for (int it = 0; it < kRegIt; ++it) {
-      const int k = threadIdx.x * 8 + it * kStep;
-      if (k < kpad) store8(k, v[it], up);
-    }
-    return;
-  }
-  float amax = 0.f;
-  for (int k = threadIdx.x * 8; k < dim; k += kStep) {
-    float v[8];
-    load8(row, k, dim, vec_ok, v);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-  }
-  const float up = row_scale_exp(amax);
-  for (int k = threadIdx.x * 8; k < kpad; k += kStep) {
-    float v[8];
-    load8(row, k, dim, vec_ok, v);
-    store8(k, v, up);
   }
 }
 
