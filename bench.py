@@ -319,14 +319,13 @@ def run_gpu(args, wl_name=None, emit=True):
         y = torch.empty(N, dim, dtype=torch.bfloat16, device=dev)
         rw = torch.empty(N, topk, dtype=torch.float32, device=dev)
         ri = torch.empty(N, topk, dtype=torch.int32, device=dev)
-        sp = stream.cuda_stream
         ids_p = ids.data_ptr() if ids is not None else None
 
         def step(i):
             x = xs[i % n_batches]
             _lib.check(L.dsm_moe_forward(ctypes.byref(desc), x.data_ptr(), _lib.DT_BF16, ids_p, _lib.DT_I32,
                                          N if ids is not None else 0, y.data_ptr(), rw.data_ptr(), ri.data_ptr(),
-                                         wsp.data_ptr(), wsb, sp))
+                                         wsp.data_ptr(), wsb, torch.cuda.current_stream().cuda_stream))
 
         def routing(i):
             step(i)
@@ -363,17 +362,41 @@ def run_gpu(args, wl_name=None, emit=True):
             c = c[e0:e0 + el]
         touched_bytes.append(W.routed_weight_bytes(wl, c.cpu()))
     torch.cuda.synchronize()
-    _barrier(ws)
-    torch.cuda.synchronize()
-    e0_, e1_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        e0_.record(stream)
-        for i in range(args.steps):
-            step(i)
-        e1_.record(stream)
+    # one CUDA graph per token batch: the whole layer call (every launch of dsm_moe_forward,
+    # the shared expert's side stream included) replayed as one graph launch
+    graphs, graph_note = None, None
+    # launch-bound calls (decode-shaped: up to 4096 routed rows) replay as graphs; a prefill
+    # call's launches are a negligible share of its ~10 ms
+    if ws == 1 and not args.no_graph and N * topk <= 4096:
+        try:
+            graphs = []
+            for b in range(n_batches):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    step(b)
+                graphs.append(g)
+            for i in range(args.warmup):
+                graphs[i % n_batches].replay()
+            torch.cuda.synchronize()
+        except Exception as exc:  # noqa: BLE001 - report and time the eager calls instead
+            graphs, graph_note = None, f"capture failed: {exc}"
+
+    def timed(run):
+        _barrier(ws)
         torch.cuda.synchronize()
-    ms = e0_.elapsed_time(e1_) / args.steps
-    ms = _max_over_ranks(ms, ws, dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk_:
+            a.record(stream)
+            for i in range(args.steps):
+                run(i)
+            b.record(stream)
+            torch.cuda.synchronize()
+        return _max_over_ranks(a.elapsed_time(b) / args.steps, ws, dev), clk_
+
+    eager_ms, clk = timed(step)
+    ms = eager_ms
+    if graphs:
+        ms, clk = timed(lambda i: graphs[i % n_batches].replay())
     _barrier(ws)
     ep_info = ep_measure(model, step, routing, ws, rank, dev, wl) if ws > 1 else None
 
@@ -459,6 +482,10 @@ def run_gpu(args, wl_name=None, emit=True):
         }
         if ep_info is not None:
             line["expert_parallel"] = ep_info
+        if ws == 1:
+            line["launch"] = ("CUDA graph replay of the whole layer call (one graph per token batch)" if graphs
+                              else "eager C-ABI calls" + (f" ({graph_note})" if graph_note else ""))
+            line["ms_per_step_eager"] = eager_ms
         if emit:
             print(json.dumps(line))
         return line
@@ -700,7 +727,27 @@ def run_qwen3(args, emit=True):
     _barrier(ws)
     with ClockSampler(local) as clk:
         ms = timed(lambda i: mlp(xs[i % 4]))
-    ms = _max_over_ranks(ms, ws, dev)
+    eager_ms = _max_over_ranks(ms, ws, dev)
+    ms = eager_ms
+    # the same call replayed as a CUDA graph (one per token batch)
+    graph_note = None
+    if not args.no_graph:
+        try:
+            graphs = []
+            for b in range(4):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    mlp(xs[b])
+                graphs.append(g)
+            for i in range(args.warmup):
+                graphs[i % 4].replay()
+            torch.cuda.synchronize()
+            _barrier(ws)
+            with ClockSampler(local) as clk:
+                ms = _max_over_ranks(timed(lambda i: graphs[i % 4].replay()), ws, dev)
+            graph_note = "CUDA graph replay of the whole MLP call (one graph per token batch)"
+        except Exception as exc:  # noqa: BLE001 - report and keep the eager time
+            graph_note = f"eager C-ABI calls (capture failed: {exc})"
     pg, pu, pd = mlp.gate_proj.packed(), mlp.up_proj.packed(), mlp.down_proj.packed()
     weight_bytes = pg.nbytes + pu.nbytes + pd.nbytes
     step_bytes = weight_bytes + 2 * N * h * 2
@@ -768,6 +815,8 @@ def run_qwen3(args, emit=True):
                 "d2h_bytes_per_step": N * h * 2, "ms_per_step": e2e_ms},
             "gpu_launches": QWEN3_KERNELS_PER_STEP * args.steps,
             "clocks": clk.summary(),
+            "launch": graph_note or "eager C-ABI calls",
+            "ms_per_step_eager": eager_ms,
         }
         if emit:
             print(json.dumps(line))
@@ -1402,7 +1451,8 @@ SIDE_CONFIGS = ("tiny_hash", "fp4_decode", "qwen3_mlp_q8", "prefill_fp8")
 # 8 GPUs with its all-to-all GB/s and tensor-pipe figures)
 SIDE_CONFIGS_EP = ("fp4_decode", "prefill_fp8")
 CONFIG_KEYS = ("metric", "value", "unit", "ms_per_step", "higher_is_better", "dtype", "config", "hbm_gbs_step",
-               "roofline", "cpu_baseline", "e2e", "gpu_launches", "clocks", "expert_parallel")
+               "roofline", "cpu_baseline", "e2e", "gpu_launches", "clocks", "expert_parallel", "launch",
+               "ms_per_step_eager")
 
 
 def run_all(args):
@@ -1435,6 +1485,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-kernel-timing", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="time eager calls only (no CUDA graph replay)")
     ap.add_argument("--experts", type=int, default=0, help="shrink the routed expert pool (profiling)")
     ap.add_argument("--tokens", type=int, default=0, help="override a MoE workload's tokens per call (profiling)")
     ap.add_argument("--attn-kernel", default="mma", choices=["cuda", "mma"],

@@ -105,9 +105,24 @@ __device__ __forceinline__ bool ep_wait_flag(const uint32_t* flag, uint32_t epoc
 }
 
 // Copies `bytes` (a multiple of 16, both ends 16-byte aligned) with the CTA's threads.
-__device__ __forceinline__ void copy_row16(uint8_t* dst, const uint8_t* src, int bytes) {
-  for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x)
-    reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+// One row by the CTA, four 16-byte loads per thread in flight before their stores.
+__device__ __forceinline__ void copy_row16(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, int bytes) {
+  const int n = bytes / 16;
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+  for (int i0 = threadIdx.x; i0 < n; i0 += 4 * blockDim.x) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * int(blockDim.x);
+      if (i < n) v[u] = s4[i];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * int(blockDim.x);
+      if (i < n) d4[i] = v[u];
+    }
+  }
 }
 
 // The CTA that finishes last raises `flag_off` (+ 4 * index) in every peer's buffer. Every
@@ -127,15 +142,19 @@ __device__ __forceinline__ void ep_signal_peers(const uint64_t* peer_base, int w
   }
 }
 
-// grid = n_pairs + 1 CTAs: CTA i < n_pairs sends sorted row i; the last one sends the counts.
+// grid = min(n_pairs, kEpDispatchCtas) + 1 CTAs: CTA b < grid - 1 sends sorted rows b,
+// b + grid - 1, ...; the last one sends the counts. A few CTAs per SM that each loop over
+// rows keep the NVLink stores flowing, and the system-scope fence and the completion count
+// are paid once per CTA, not once per row.
+constexpr int64_t kEpDispatchCtas = 1024;
 __global__ void __launch_bounds__(kEpCopyThreads) ep_dispatch_kernel(
     EpGeom g, const uint8_t* __restrict__ x, int64_t n_tokens, const int32_t* __restrict__ indices,
     const int32_t* __restrict__ perm, const int32_t* __restrict__ offsets, const int32_t* __restrict__ counts,
     int64_t n_pairs, int topk, const uint64_t* __restrict__ peer_base, int32_t* __restrict__ row_map,
     uint32_t* done, uint32_t epoch) {
   const int set = int(epoch & 1u);
-  const int64_t i = blockIdx.x;
-  if (i < n_pairs) {
+  const int64_t row_ctas = int64_t(gridDim.x) - 1;
+  for (int64_t i = blockIdx.x; i < n_pairs && int64_t(blockIdx.x) < row_ctas; i += row_ctas) {
     const int32_t pair = perm[i];
     const int e = (pair >= 0 && pair < n_pairs) ? indices[pair] : -1;
     const int d = e >= 0 ? e / g.e_local : -1;
@@ -153,7 +172,8 @@ __global__ void __launch_bounds__(kEpCopyThreads) ep_dispatch_kernel(
       copy_row16(dst, x + t * row_bytes, int(row_bytes));
       if (threadIdx.x == 0) row_map[pair] = int32_t(d * g.cap + j);
     }
-  } else {
+  }
+  if (int64_t(blockIdx.x) == row_ctas) {
     for (int c = threadIdx.x; c < g.world * g.e_local; c += blockDim.x) {
       const int d = c / g.e_local, e = c % g.e_local;
       int32_t* dst = reinterpret_cast<int32_t*>(peer_base[d] + g.off_counts) +
@@ -239,20 +259,22 @@ __global__ void __launch_bounds__(1024) ep_receive_kernel(EpGeom g, const uint8_
   }
 }
 
-// grid = W * kEpReturnCtas CTAs: CTA (s, c) sends rows q = c, c + kEpReturnCtas, ... of the
-// rows that arrived from sender s (arrival row s * cap + q) back to s, at slot q.
-constexpr int kEpReturnCtas = 32;
+// grid = W * per CTAs: CTA (s, c) sends rows q = c, c + per, ... of the rows that arrived
+// from sender s (arrival row s * cap + q) back to s, at slot q. per = kEpReturnCtas / W (at
+// least 32): about as many CTAs in all as the dispatch uses, whatever the world size.
+constexpr int kEpReturnCtas = 1024;
+inline int ep_return_per_sender(int world) { return std::max(32, kEpReturnCtas / world); }
 __global__ void __launch_bounds__(kEpCopyThreads) ep_return_kernel(EpGeom g, const float* __restrict__ o_rows,
                                                                    const int32_t* __restrict__ n_valid,
                                                                    const uint64_t* __restrict__ peer_base,
-                                                                   uint32_t* done, uint32_t epoch) {
+                                                                   uint32_t* done, uint32_t epoch, int per) {
   const int set = int(epoch & 1u);
-  const int s = int(blockIdx.x) / kEpReturnCtas;
+  const int s = int(blockIdx.x) / per;
   const int64_t row_bytes = int64_t(g.dim) * 4;
   uint8_t* dst0 = reinterpret_cast<uint8_t*>(peer_base[s]) + g.off_back +
                   (int64_t(set) * g.world + g.rank) * g.cap * row_bytes;
   const int64_t n = n_valid[1 + s];
-  for (int64_t q = blockIdx.x % kEpReturnCtas; q < n; q += kEpReturnCtas)
+  for (int64_t q = blockIdx.x % per; q < n; q += per)
     copy_row16(dst0 + q * row_bytes, reinterpret_cast<const uint8_t*>(o_rows + (int64_t(s) * g.cap + q) * g.dim),
                int(row_bytes));
   ep_signal_peers(peer_base, g.world, g.off_bflags + (int64_t(set) * g.world + g.rank) * 4, done, epoch);
@@ -331,7 +353,7 @@ extern "C" int dsm_ep_dispatch(const dsm_ep_desc* d, const void* x, int64_t n_to
   DSM_REQUIRE(n_tokens == 0 || (x && indices && perm && offsets && row_map), "dsm_ep_dispatch: NULL pointer");
   DSM_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15) == 0, "dsm_ep_dispatch: x must be 16-byte aligned");
   const int64_t pairs = n_tokens * topk;
-  ep_dispatch_kernel<<<unsigned(pairs + 1), kEpCopyThreads, 0, as_stream(stream)>>>(
+  ep_dispatch_kernel<<<unsigned(std::min(pairs, kEpDispatchCtas) + 1), kEpCopyThreads, 0, as_stream(stream)>>>(
       geom_of(d), static_cast<const uint8_t*>(x), n_tokens, indices, perm, offsets, counts, pairs, topk, peer_base,
       row_map, done, epoch);
   return check_launch("ep_dispatch");
@@ -356,8 +378,9 @@ extern "C" int dsm_ep_return(const dsm_ep_desc* d, const float* o_rows, const in
   DSM_REQUIRE(o_rows && n_valid && peer_base && done && epoch != 0, "dsm_ep_return: NULL pointer or epoch 0");
   DSM_REQUIRE((int64_t(d->dim) * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(o_rows) & 15) == 0,
               "dsm_ep_return: rows must be 16-byte aligned");
-  ep_return_kernel<<<unsigned(d->world * kEpReturnCtas), kEpCopyThreads, 0, as_stream(stream)>>>(
-      geom_of(d), o_rows, n_valid, peer_base, done, epoch);
+  const int per = ep_return_per_sender(d->world);
+  ep_return_kernel<<<unsigned(d->world * per), kEpCopyThreads, 0, as_stream(stream)>>>(geom_of(d), o_rows, n_valid,
+                                                                                        peer_base, done, epoch, per);
   return check_launch("ep_return");
 }
 
