@@ -154,7 +154,11 @@ __global__ void __launch_bounds__(kEpCopyThreads) ep_dispatch_kernel(
     uint32_t* done, uint32_t epoch) {
   const int set = int(epoch & 1u);
   const int64_t row_ctas = int64_t(gridDim.x) - 1;
-  for (int64_t i = blockIdx.x; i < n_pairs && int64_t(blockIdx.x) < row_ctas; i += row_ctas) {
+  // The sorted rows go out in owner order, starting at owner rank + 1: at any moment the
+  // ranks' CTAs store into different owners instead of all into owner 0, then all into 1...
+  const int64_t start = n_pairs > 0 ? offsets[((g.rank + 1) % g.world) * g.e_local] : 0;
+  for (int64_t k = blockIdx.x; k < n_pairs && int64_t(blockIdx.x) < row_ctas; k += row_ctas) {
+    const int64_t i = k + start < n_pairs ? k + start : k + start - n_pairs;
     const int32_t pair = perm[i];
     const int e = (pair >= 0 && pair < n_pairs) ? indices[pair] : -1;
     const int d = e >= 0 ? e / g.e_local : -1;
@@ -259,9 +263,11 @@ __global__ void __launch_bounds__(1024) ep_receive_kernel(EpGeom g, const uint8_
   }
 }
 
-// grid = W * per CTAs: CTA (s, c) sends rows q = c, c + per, ... of the rows that arrived
-// from sender s (arrival row s * cap + q) back to s, at slot q. per = kEpReturnCtas / W (at
-// least 32): about as many CTAs in all as the dispatch uses, whatever the world size.
+// grid = W * per CTAs: CTA b serves sender s = (b + rank + 1) % W (so the CTAs that start
+// first store into every sender, each rank beginning with a different one) and sends rows
+// q = c, c + per, ... (c = b / W) of the rows that arrived from s (arrival row s * cap + q)
+// back to s, at slot q. per = kEpReturnCtas / W (at least 32): about as many CTAs in all as
+// the dispatch uses, whatever the world size.
 constexpr int kEpReturnCtas = 1024;
 inline int ep_return_per_sender(int world) { return std::max(32, kEpReturnCtas / world); }
 __global__ void __launch_bounds__(kEpCopyThreads) ep_return_kernel(EpGeom g, const float* __restrict__ o_rows,
@@ -269,12 +275,12 @@ __global__ void __launch_bounds__(kEpCopyThreads) ep_return_kernel(EpGeom g, con
                                                                    const uint64_t* __restrict__ peer_base,
                                                                    uint32_t* done, uint32_t epoch, int per) {
   const int set = int(epoch & 1u);
-  const int s = int(blockIdx.x) / per;
+  const int s = (int(blockIdx.x) + g.rank + 1) % g.world;
   const int64_t row_bytes = int64_t(g.dim) * 4;
   uint8_t* dst0 = reinterpret_cast<uint8_t*>(peer_base[s]) + g.off_back +
                   (int64_t(set) * g.world + g.rank) * g.cap * row_bytes;
   const int64_t n = n_valid[1 + s];
-  for (int64_t q = blockIdx.x % per; q < n; q += per)
+  for (int64_t q = blockIdx.x / g.world; q < n; q += per)
     copy_row16(dst0 + q * row_bytes, reinterpret_cast<const uint8_t*>(o_rows + (int64_t(s) * g.cap + q) * g.dim),
                int(row_bytes));
   ep_signal_peers(peer_base, g.world, g.off_bflags + (int64_t(set) * g.world + g.rank) * 4, done, epoch);
