@@ -76,3 +76,64 @@ def test_moe_forward_replays_in_a_cuda_graph(name):
     assert torch.equal(i_graph, ri)
     assert torch.equal(y_graph, y)
     del g
+
+
+def _graph_matches_eager(call, inputs):
+    """``call(x)`` captured once on the first input; each replay after new data is written into
+    that input equals the eager call on the same data, bit for bit."""
+    x0 = inputs[0]
+    call(x0)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = call(x0)
+    outs = out if isinstance(out, tuple) else (out,)
+    for x in inputs:
+        x0.copy_(x)
+        g.replay()
+        torch.cuda.synchronize()
+        got = [o.clone() for o in outs]
+        want = call(x0)
+        want = want if isinstance(want, tuple) else (want,)
+        torch.cuda.synchronize()
+        assert len(got) == len(want)
+        for a, b in zip(got, want):
+            assert torch.equal(a, b)
+    del g
+
+
+def _variants(x, n=2, seed=9):
+    gen = torch.Generator(device=x.device).manual_seed(seed)
+    return [x.clone()] + [torch.randn(x.shape, generator=gen, device=x.device).to(x.dtype) for _ in range(n)]
+
+
+def test_qwen3_attention_replays_in_a_cuda_graph():
+    from dsm.qwen3_attention import rope_tables
+
+    wl = W.WORKLOADS["qwen3_attn_q8"]
+    t = W.make_gqa_tensors(wl, device=DEV, seed=0)
+    attn = W.build_gqa(wl, t, DEV)
+    a = wl.args
+    cos, sin = rope_tables(torch.arange(wl.extra["ctx"], wl.extra["ctx"] + wl.block), a["head_dim"], a["rope_theta"])
+    cos, sin = cos.to(DEV), sin.to(DEV)
+    kc, vc = t["ctx_k"], t["ctx_v"]
+    _graph_matches_eager(lambda x: attn.attend_cached(x, kc, vc, cos, sin), _variants(t["x"]))
+
+
+def test_draft_attention_replays_in_a_cuda_graph():
+    wl = W.WORKLOADS["draft_attn_dsv4"]
+    t = W.make_dsattn_tensors(wl, device=DEV, seed=0)
+    attn = W.build_dsattn(wl, t, DEV)
+    pos = wl.extra["prefill"]
+    attn(t["x"], 0, t["prefill_main"])  # the window holds the prefill's last positions
+    main = t["main"]
+    _graph_matches_eager(lambda x: attn(x, pos, main), _variants(t["x"]))
+
+
+def test_draft_head_replays_in_a_cuda_graph():
+    wl = W.WORKLOADS["draft_head"]
+    t = W.make_head_tensors(wl, device=DEV, seed=0)
+    head = W.build_head(wl, t, DEV)
+    anchor = t["anchor"]
+
+    _graph_matches_eager(lambda x: tuple(head(x, anchor)), _variants(t["x"]))
