@@ -468,7 +468,7 @@ def run_gpu(args, wl_name=None, emit=True):
             "vs_baseline": None, "dtype": DTYPE_DESC.get(wl.wfmt, wl.wfmt),
             "data": "synthetic",
             "config": moe_config(wl, ws),
-            "draft_block_latency_ms": ms,
+            "moe_layer_latency_ms": ms,
             "hbm_gbs_step": avg_step_bytes / (ms * 1e-3) / 1e9,
             "hbm_frac_of_8tbs_step": avg_step_bytes / (ms * 1e-3) / 1e9 / SPEC_HBM_GBS,
             "roofline": roofline_entry(ws, k_ms, k_bytes, k_touched, k_flops, k_tc, achieved, avg_step_bytes, ms,
@@ -1458,6 +1458,173 @@ def run_dsattn(args):
         print(json.dumps(line))
 
 
+BLOCK_METRIC = ("DeepSeek-V4 DSpark draft-block latency (a middle stage: hyper-connections, MLA draft attention over "
+                "a full 128-slot window, fp8 MoE; 8 sequences x 7-token blocks); tokens/s")
+# two hyper-connection halves (pre+norm, post: 2 each), the attention's launches, the MoE's
+BLOCK_KERNELS_PER_STEP = 2 * 2 + DSATTN_KERNELS_PER_STEP + KERNELS_PER_STEP
+
+
+def _block_cpu_setup(t, wl):
+    """The oracle's draft block on the first sequence: reference-named CPU tensors; the routed
+    experts are read from the device and dequantised to fp32 on first use, i.e. in the
+    untimed first call (the reference dequantises at load)."""
+    import torch
+
+    import oracle
+    from oracle.attention_oracle import AttnDims
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    a = wl.args
+
+    class _Cached(oracle.OracleWeights):
+        def __init__(self, codes, scales):
+            super().__init__("fp8", codes, scales=scales)
+            self._dense = {}
+
+        def matrix(self, e):
+            if e not in self._dense:
+                self._dense[e] = oracle.fp8_weight_dequant(self.data[e].cpu(), self.scales[e].cpu())
+            return self._dense[e]
+
+    p = {k: t[f"attn_{k}"].cpu() for k in ("wq_a", "wq_b", "wkv", "wo_a", "wo_b", "q_norm", "kv_norm", "attn_sink")}
+    dims = AttnDims(n_heads=a["n_heads"], head_dim=a["head_dim"], rope_head_dim=a["rope_head_dim"],
+                    o_groups=a["o_groups"], o_lora_rank=a["o_lora_rank"], window_size=a["window_size"],
+                    eps=a["norm_eps"])
+    cos, sin = oracle.rope_tables(a["rope_head_dim"], wl.extra["max_seq_len"], a["rope_theta"])
+    cache = oracle.KVWindow(a["window_size"])
+    oracle.attention_forward(p, dims, t["x"][:1, :, 0].cpu(), 0, t["attn_prefill_main"][:1].cpu(), cache, cos, sin)
+    ffn = dict(gate_weight=t["moe_gate_weight"].cpu(), gate_bias=t["moe_gate_bias"].cpu(),
+               topk=a["n_activated_experts"], score_func=a["score_func"], route_scale=a["route_scale"],
+               swiglu_limit=a["swiglu_limit"],
+               w1=_Cached(t["moe_w1_codes"], t["moe_w1_scale"]), w3=_Cached(t["moe_w3_codes"], t["moe_w3_scale"]),
+               w2=_Cached(t["moe_w2_codes"], t["moe_w2_scale"]),
+               shared=tuple(t[f"moe_shared_{n}"].cpu() for n in ("w1", "w2", "w3")))
+    hc = dict(hc=a["hc_mult"], iters=a["hc_sinkhorn_iters"], norm_eps=a["norm_eps"], hc_eps=a["hc_eps"])
+    halves = {h: dict(hc_fn=t[f"hc_{h}_fn"].cpu(), hc_scale=t[f"hc_{h}_scale"].cpu(),
+                      hc_base=t[f"hc_{h}_base"].cpu(), norm_weight=t[f"norm_{h}"].cpu()) for h in ("attn", "ffn")}
+    x, main = t["x"][:1].cpu(), t["attn_main"][:1].cpu()
+    pos = wl.extra["prefill"]
+
+    def call():
+        y = oracle.ffn_sublayer(x, None, moe=lambda h, _i: oracle.attention_forward(p, dims, h, pos, main, cache,
+                                                                                    cos, sin),
+                                **halves["attn"], **hc)
+        return oracle.ffn_sublayer(y, None, moe=lambda h, ids: oracle.moe_forward(h, ids, **ffn), **halves["ffn"], **hc)
+
+    call()  # untimed: dequantises the experts this sequence routes to
+    return call
+
+
+def _block_cpu_timed(call, budget_s, max_calls=20):
+    n, t0 = 0, time.perf_counter()
+    while n < max_calls and (n == 0 or time.perf_counter() - t0 < budget_s):
+        call()
+        n += 1
+    el = time.perf_counter() - t0
+    return n * 7 / el, n, el
+
+
+def run_block(args):
+    """One step = one decode call of a whole DeepSeek-V4 draft block (stage 1 of 3): 8
+    sequences x 7-token blocks over 4 hyper-connection streams, the draft attention over a
+    full window and the fp8 MoE. The step streams ~4 GB of weights, so every step reads them
+    from HBM."""
+    import torch
+
+    from dsm import _lib, workloads as W
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    _lib.check(_lib.lib().dsm_set_attn_kernel(0 if args.attn_kernel == "mma" else 1), "dsm_set_attn_kernel")
+    dev = torch.device("cuda", local)
+    _init_dist(ws, dev)
+    wl = W.WORKLOADS["draft_block_dsv4"]
+    a = wl.args
+    t = W.make_block_tensors(wl, device=dev, seed=rank)
+    blk = W.build_block(wl, t, dev)
+    b, s, pos, d, hc = wl.batch, wl.block, wl.extra["prefill"], a["dim"], a["hc_mult"]
+    blk(t["x"], 0, None, t["attn_prefill_main"])  # seeds the window with the last 128 prefill positions
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(444 + rank)
+    xs = [t["x"]] + [torch.randn(t["x"].shape, generator=gen, device=dev).to(torch.bfloat16) for _ in range(3)]
+    mains = [t["attn_main"]] + [torch.randn(t["attn_main"].shape, generator=gen, device=dev).to(torch.bfloat16)
+                                for _ in range(3)]
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        y = blk(xs[i % 4], pos, None, mains[i % 4])
+    torch.cuda.synchronize()
+    if not bool(torch.isfinite(y).all()) or _lib.device_error():
+        raise RuntimeError("draft block: non-finite output or device error word set")
+
+    def timed(fn):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            fn(i)
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+        return sum(x.elapsed_time(y) for x, y in evs) / args.steps
+
+    _barrier(ws)
+    launch_note = "eager calls"
+    with ClockSampler(local) as clk:
+        ms = timed(lambda i: blk(xs[i % 4], pos, None, mains[i % 4]))
+        eager_ms = ms
+        if not args.no_graph:
+            gms, launch_note = graph_replay(lambda bb: blk(xs[bb], pos, None, mains[bb]), timed, args.warmup)
+            ms = gms if gms is not None else ms
+    ms = _max_over_ranks(ms, ws, dev)
+    eager_ms = _max_over_ranks(eager_ms, ws, dev)
+
+    e2e_ms = None
+    if not args.no_e2e:
+        xh = [x.cpu().pin_memory() for x in xs]
+        mh = [m.cpu().pin_memory() for m in mains]
+        yh = torch.empty(b, s, hc, d, dtype=torch.bfloat16).pin_memory()
+
+        def e2e(i):
+            y = blk(xh[i % 4].to(dev, non_blocking=True), pos, None, mh[i % 4].to(dev, non_blocking=True))
+            yh.copy_(y, non_blocking=True)
+
+        for i in range(3):
+            e2e(i)
+        torch.cuda.synchronize()
+        e2e_ms = _max_over_ranks(timed(e2e), ws, dev)
+
+    if rank == 0:
+        cpu = None
+        if ws == 1 and not args.no_cpu_baseline:
+            v, calls, el = _block_cpu_timed(_block_cpu_setup(t, wl), args.cpu_seconds)
+            cpu = {"value": v, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+                   "sample": f"1 of the {b} sequences ({s} block tokens) per call, {calls} calls in {el:.1f} s; the "
+                             f"experts it routes to dequantised to fp32 before timing; CPU restatement of "
+                             f"DSparkBlock.__call__ in PyTorch"}
+        line = {
+            "metric": BLOCK_METRIC, "value": ws * b * s / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp8 e4m3 experts, bf16 attention weights and activations (f16 MMA, fp32 accumulate)",
+            "data": "synthetic",
+            "config": {"workload": wl.name, "tokens_per_step_per_gpu": b * s, "batch": b, "draft_block": s,
+                       "dim": d, "hc_mult": hc, "heads": a["n_heads"], "window": a["window_size"],
+                       "n_experts": a["n_routed_experts"], "topk": a["n_activated_experts"], "weights": wl.wfmt,
+                       "attn_kernel": args.attn_kernel, "parallelism": f"replicas{ws}" if ws > 1 else "single",
+                       "l2": "inputs larger than L2 (~4 GB of weights streamed every step)"},
+            "draft_block_latency_ms": ms,
+            "roofline": None,
+            "cpu_baseline": cpu,
+            "e2e": None if e2e_ms is None else {
+                "value": ws * b * s / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": (xs[0].numel() + mains[0].numel()) * 2, "d2h_bytes_per_step": xs[0].numel() * 2,
+                "ms_per_step": e2e_ms},
+            "gpu_launches": BLOCK_KERNELS_PER_STEP * args.steps,
+            "clocks": clk.summary(),
+            "launch": launch_note,
+            "ms_per_step_eager": eager_ms,
+        }
+        print(json.dumps(line))
+
+
 def run_reference_dsattn(args):
     ws, rank, _ = _dist()
     if rank != 0:
@@ -1554,6 +1721,12 @@ def main():
         (run_reference_gqa if args.impl == "reference" else run_gqa)(args)
     elif args.workload == "draft_attn_dsv4":
         (run_reference_dsattn if args.impl == "reference" else run_dsattn)(args)
+    elif args.workload == "draft_block_dsv4":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the whole-block reference arm is not separate: "
+                              "the draft_block_dsv4 GPU line carries its own CPU baseline"}))
+        else:
+            run_block(args)
     elif args.impl == "reference":
         (run_reference_qwen3 if qwen3 else run_reference)(args)
     else:

@@ -103,6 +103,19 @@ WORKLOADS = {
         "draft_attn_dsv4", dict(dim=4096, n_heads=64, head_dim=512, rope_head_dim=64, q_lora_rank=1024, o_groups=8,
                                 o_lora_rank=1024, window_size=128, norm_eps=1e-6, rope_theta=10000.0),
         n_tokens=56, wfmt="bf16", batch=8, block=7, extra={"prefill": 160, "max_seq_len": 4096}),
+    # the whole DeepSeek-V4 DSpark draft block, a middle stage: over 4 hyper-connection
+    # streams, hc_pre -> attn_norm -> the draft attention above -> hc_post, then hc_pre ->
+    # ffn_norm -> the fp8 MoE of the decode workload -> hc_post; 8 sequences x 7-token
+    # blocks after a 160-token prefill (full window)
+    "draft_block_dsv4": Workload(
+        "draft_block_dsv4", _args(vocab_size=129280, dim=4096, moe_inter_dim=2048, n_routed_experts=256,
+                                  n_activated_experts=6, score_func="sigmoid", route_scale=2.5, n_heads=64,
+                                  head_dim=512, rope_head_dim=64, q_lora_rank=1024, o_groups=8, o_lora_rank=1024,
+                                  window_size=128, norm_eps=1e-6, rope_theta=10000.0, hc_mult=4,
+                                  hc_sinkhorn_iters=20, hc_eps=1e-6, n_layers=43, n_mtp_layers=3,
+                                  dspark_block_size=7),
+        n_tokens=56, wfmt="fp8", layer_id=44, batch=8, block=7,
+        extra={"prefill": 160, "max_seq_len": 4096, "stage": 1}),
 }
 
 
@@ -386,6 +399,49 @@ def make_dsattn_tensors(wl: Workload, device="cpu", seed: Optional[int] = None) 
             "wo_b": r(d, og * orank, std=(og * orank) ** -0.5).to(bf),
             "q_norm": 1 + r(ql, std=0.1), "kv_norm": 1 + r(hd, std=0.1), "attn_sink": r(h),
             "prefill_main": r(b, pre, d).to(bf), "x": r(b, s, d).to(bf), "main": r(b, 1, d).to(bf)}
+
+
+def make_block_tensors(wl: Workload, device="cpu", seed: Optional[int] = None) -> Dict[str, torch.Tensor]:
+    """Inputs and weights of the whole draft block workload: the draft attention's tensors
+    (``attn_*``), the fp8 MoE's (``moe_*``), the hyper-connection mixers (``hc_*``), the two
+    norms (``norm_attn``, ``norm_ffn``) and the block input ``x [b, s, hc, dim]``."""
+    a = wl.args
+    sd = wl.seed if seed is None else seed
+    t = {f"attn_{k}": v for k, v in make_dsattn_tensors(wl, device, sd).items()}
+    t.update({f"moe_{k}": v for k, v in make_moe_tensors(wl, device, seed=sd + 1).items()})
+    g = torch.Generator(device=device)
+    g.manual_seed(sd + 2)
+    d, hc = a["dim"], a["hc_mult"]
+    mix = (2 + hc) * hc
+    r = lambda *shape, std=1.0: torch.randn(shape, generator=g, device=device) * std  # noqa: E731
+    for half in ("attn", "ffn"):
+        t[f"hc_{half}_fn"] = r(mix, hc * d, std=(hc * d) ** -0.5)
+        t[f"hc_{half}_base"] = r(mix, std=0.1)
+        t[f"hc_{half}_scale"] = 1 + r(3, std=0.1)
+        t[f"norm_{half}"] = 1 + r(d, std=0.1)
+    t["x"] = r(wl.batch, wl.block, hc, d).to(torch.bfloat16)
+    return t
+
+
+def build_block(wl: Workload, t: Dict[str, torch.Tensor], device="cuda"):
+    """A :class:`dsm.draft_block.DSparkBlock` (stage ``wl.extra["stage"]``) holding ``t``'s
+    weights; its MoE is the one :func:`build_moe` makes from the ``moe_*`` tensors."""
+    from .config import DSparkArgs
+    from .draft_block import DSparkBlock
+
+    blk = DSparkBlock(DSparkArgs.from_dict(wl.args), wl.extra["stage"], max_seq_len=wl.extra["max_seq_len"])
+    blk = blk.to(device)
+    at = {k[5:]: v for k, v in t.items() if k.startswith("attn_")}
+    ref = build_dsattn(wl, at, device)
+    blk.attn = ref
+    blk.ffn = build_moe(wl, {k[4:]: v for k, v in t.items() if k.startswith("moe_")}, device)
+    with torch.no_grad():
+        for half in ("attn", "ffn"):
+            getattr(blk, f"hc_{half}_fn").copy_(t[f"hc_{half}_fn"])
+            getattr(blk, f"hc_{half}_base").copy_(t[f"hc_{half}_base"])
+            getattr(blk, f"hc_{half}_scale").copy_(t[f"hc_{half}_scale"])
+            getattr(blk, f"{half}_norm").weight.copy_(t[f"norm_{half}"])
+    return blk
 
 
 def build_dsattn(wl: Workload, t: Dict[str, torch.Tensor], device="cuda"):

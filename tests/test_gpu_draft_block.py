@@ -89,3 +89,49 @@ def test_draft_block_matches_reference_goldens(name, attn_kernel):
     n = _compare_walk(out_ids.cpu(), biased.cpu(), conf.cpu(), ref_ids, _t(z["head_logits"]), _t(z["head_conf"]), 2e-3)
     assert n >= ref_ids.shape[0]
     assert _lib.device_error() == 0
+
+
+def test_draft_block_full_width_matches_oracle():
+    """The bench's whole-block workload at its own widths (DeepSeek-V4: dim 4096, 64 heads of
+    512, 4 hyper-connection streams, 256 fp8 experts top-6): one decode step of 8 sequences
+    after a 160-token prefill, the first sequence against the oracle's block (the experts it
+    routes to dequantised on the CPU)."""
+    import oracle
+    from dsm import workloads as W
+    from oracle.attention_oracle import AttnDims
+
+    wl = W.WORKLOADS["draft_block_dsv4"]
+    a = wl.args
+    t = W.make_block_tensors(wl, device=DEV, seed=3)
+    blk = W.build_block(wl, t, DEV)
+    pos = wl.extra["prefill"]
+    blk(t["x"], 0, None, t["attn_prefill_main"])
+    y = blk(t["x"], pos, None, t["attn_main"])
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+
+    class _Lazy(oracle.OracleWeights):
+        def matrix(self, e):
+            return oracle.fp8_weight_dequant(self.data[e].cpu(), self.scales[e].cpu())
+
+    p = {k: t[f"attn_{k}"].cpu() for k in ("wq_a", "wq_b", "wkv", "wo_a", "wo_b", "q_norm", "kv_norm", "attn_sink")}
+    dims = AttnDims(n_heads=a["n_heads"], head_dim=a["head_dim"], rope_head_dim=a["rope_head_dim"],
+                    o_groups=a["o_groups"], o_lora_rank=a["o_lora_rank"], window_size=a["window_size"],
+                    eps=a["norm_eps"])
+    cos, sin = oracle.rope_tables(a["rope_head_dim"], wl.extra["max_seq_len"], a["rope_theta"])
+    cache = oracle.KVWindow(a["window_size"])
+    oracle.attention_forward(p, dims, t["x"][:1, :, 0].cpu(), 0, t["attn_prefill_main"][:1].cpu(), cache, cos, sin)
+    ffn = dict(gate_weight=t["moe_gate_weight"].cpu(), gate_bias=t["moe_gate_bias"].cpu(),
+               topk=a["n_activated_experts"], score_func=a["score_func"], route_scale=a["route_scale"],
+               swiglu_limit=a["swiglu_limit"],
+               **{n: _Lazy("fp8", t[f"moe_{n}_codes"], scales=t[f"moe_{n}_scale"]) for n in ("w1", "w3", "w2")},
+               shared=tuple(t[f"moe_shared_{n}"].cpu() for n in ("w1", "w2", "w3")))
+    hc = dict(hc=a["hc_mult"], iters=a["hc_sinkhorn_iters"], norm_eps=a["norm_eps"], hc_eps=a["hc_eps"])
+    halves = {h: dict(hc_fn=t[f"hc_{h}_fn"].cpu(), hc_scale=t[f"hc_{h}_scale"].cpu(),
+                      hc_base=t[f"hc_{h}_base"].cpu(), norm_weight=t[f"norm_{h}"].cpu()) for h in ("attn", "ffn")}
+    x, main = t["x"][:1].cpu(), t["attn_main"][:1].cpu()
+    h = oracle.ffn_sublayer(x, None, moe=lambda v, _i: oracle.attention_forward(p, dims, v, pos, main, cache, cos, sin),
+                            **halves["attn"], **hc)
+    ref = oracle.ffn_sublayer(h, None, moe=lambda v, ids: oracle.moe_forward(v, ids, **ffn), **halves["ffn"], **hc)
+    assert ref.shape == y[:1].shape and ref.dtype == y.dtype
+    assert max_rel_err(y[:1], ref) < 2e-2, max_rel_err(y[:1], ref)
