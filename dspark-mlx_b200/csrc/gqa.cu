@@ -20,7 +20,7 @@
 // and range. A second kernel combines the ranges in order. The output is rounded once to the
 // activation dtype. Two CTA kernels:
 //   gqa_attn_kernel  fp32 CUDA-core products, any dtype and head_dim 32..256;
-//   gqa_mma_kernel   bf16 with head_dim 64 or 128: K/V tiles double-buffered by cp.async,
+//   gqa_mma_kernel   bf16 with head_dim 64 or 128: K/V tiles in a three-slot cp.async ring,
 //                    q.k and p.v on mma.m16n8k16 (bf16 in, fp32 accumulate; p rounded to
 //                    bf16 for the second product), each warp an online softmax over half of
 //                    every tile, so each key range leaves two partials.
@@ -41,9 +41,9 @@ constexpr int kMaxSplits = 64;  // key ranges per KV head
 constexpr int kMaxParts = 2 * kMaxSplits;  // partials per query row (two per range on the mma path)
 constexpr int kMaxHeadDim = 256;
 constexpr int kMmaThreads = 128;  // 4 warps: 2 row tiles of 16 x 2 key halves of 32
-constexpr int kMmaStages = 2;
-
-
+// K/V tiles in flight: two loads ahead of the tile being multiplied. At head_dim 128 a CTA
+// holds (32 + 3 x 2 x 64) padded rows = 113,152 B, so two CTAs still share an SM.
+constexpr int kMmaStages = 3;
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -296,6 +296,20 @@ __global__ void __launch_bounds__(kMmaThreads) gqa_mma_kernel(
     const int kt0 = k0 + tile * kKeyTile;
     __nv_bfloat16* ks = Ks + stage * kKeyTile * RS;
     __nv_bfloat16* vs = Vs + stage * kKeyTile * RS;
+    if (kt0 + kKeyTile <= min(k1, n_ctx)) {
+      // a whole tile of context rows (every tile but a range's last): fixed column chunk per
+      // thread, rows RPP apart, no per-chunk bounds or source choice
+      constexpr int RPP = kMmaThreads / CPR;
+      const int c = tid % CPR, jr = tid / CPR;
+      const int64_t src0 = ctx_base + int64_t(kt0 + jr) * HD + c * 8;
+      const uint32_t kd = smem_u32(ks + jr * RS + c * 8), vd = smem_u32(vs + jr * RS + c * 8);
+#pragma unroll
+      for (int it = 0; it < kKeyTile / RPP; ++it) {
+        cp_async16(kd + uint32_t(it * RPP * RS * 2), ctx_k + src0 + int64_t(it) * RPP * HD, true);
+        cp_async16(vd + uint32_t(it * RPP * RS * 2), ctx_v + src0 + int64_t(it) * RPP * HD, true);
+      }
+      return;
+    }
     for (int i = tid; i < kKeyTile * CPR; i += kMmaThreads) {
       const int j = i / CPR, c = i % CPR;
       const int k = kt0 + j;
@@ -316,6 +330,8 @@ __global__ void __launch_bounds__(kMmaThreads) gqa_mma_kernel(
   };
   load_tile(0, 0);  // every range holds at least one key
   cp_async_commit();
+  if (n_tiles > 1) load_tile(1, 1);
+  cp_async_commit();  // one group per tile slot, empty or not, so the wait count below holds
   __syncthreads();  // Qs
   uint32_t qa[KS][4];
 #pragma unroll
@@ -326,15 +342,18 @@ __global__ void __launch_bounds__(kMmaThreads) gqa_mma_kernel(
   float o[NT][4];
 #pragma unroll
   for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};  // m_run in base-2 units
+  const float scale2 = scale * 1.4426950408889634f;  // log2(e)
   for (int tile = 0; tile < n_tiles; ++tile) {
-    if (tile + 1 < n_tiles) load_tile(tile + 1, (tile + 1) & 1);
+    const int stage = tile % kMmaStages;
+    // the slot refilled here held tile - 1, released by the barrier that ended its iteration
+    if (tile + 2 < n_tiles) load_tile(tile + 2, (tile + 2) % kMmaStages);
     cp_async_commit();
-    cp_async_wait1();  // this tile's group has landed
+    cp_async_wait2();  // this tile's group has landed
     __syncthreads();
     const int kt = min(kKeyTile, k1 - (k0 + tile * kKeyTile));
-    const __nv_bfloat16* ks = Ks + ((tile & 1) * kKeyTile + 32 * kh) * RS;
-    const __nv_bfloat16* vs = Vs + ((tile & 1) * kKeyTile + 32 * kh) * RS;
+    const __nv_bfloat16* ks = Ks + (stage * kKeyTile + 32 * kh) * RS;
+    const __nv_bfloat16* vs = Vs + (stage * kKeyTile + 32 * kh) * RS;
     float s[4][4];
 #pragma unroll
     for (int n = 0; n < 4; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
@@ -349,16 +368,27 @@ __global__ void __launch_bounds__(kMmaThreads) gqa_mma_kernel(
         mma_16816(s[2 * p + 1], qa[kk], b2, b3);
       }
     }
+    // scores in base-2 units (scale * log2 e folded in): the softmax weights are exp2 of them
     float mx[2] = {-INFINITY, -INFINITY};
+    if (kt == kKeyTile) {
 #pragma unroll
-    for (int n = 0; n < 4; ++n)
+      for (int n = 0; n < 4; ++n)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int key = 32 * kh + 8 * n + 2 * t4 + (c & 1);
-        const float v = key < kt ? s[n][c] * scale : -INFINITY;
-        s[n][c] = v;
-        mx[c >> 1] = fmaxf(mx[c >> 1], v);
-      }
+        for (int c = 0; c < 4; ++c) {
+          s[n][c] *= scale2;
+          mx[c >> 1] = fmaxf(mx[c >> 1], s[n][c]);
+        }
+    } else {
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int key = 32 * kh + 8 * n + 2 * t4 + (c & 1);
+          const float v = key < kt ? s[n][c] * scale2 : -INFINITY;
+          s[n][c] = v;
+          mx[c >> 1] = fmaxf(mx[c >> 1], v);
+        }
+    }
     float alpha[2];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
@@ -366,7 +396,7 @@ __global__ void __launch_bounds__(kMmaThreads) gqa_mma_kernel(
       mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
       const float m_new = fmaxf(m_run[i], mx[i]);
       const float mref = m_new == -INFINITY ? 0.f : m_new;  // a row with no key yet stays empty
-      alpha[i] = expf(m_run[i] - mref);
+      alpha[i] = exp2f(m_run[i] - mref);
       m_run[i] = m_new;
       mx[i] = mref;
     }
@@ -376,7 +406,7 @@ __global__ void __launch_bounds__(kMmaThreads) gqa_mma_kernel(
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         // rounded to bf16 here, so the denominator sums the weights the p.v products use
-        const float pv = __bfloat162float(__float2bfloat16_rn(expf(s[n][c] - mx[c >> 1])));
+        const float pv = __bfloat162float(__float2bfloat16_rn(exp2f(s[n][c] - mx[c >> 1])));
         s[n][c] = pv;
         ls[c >> 1] += pv;
       }
@@ -426,7 +456,7 @@ __global__ void __launch_bounds__(kMmaThreads) gqa_mma_kernel(
         dst[8 * n + 2 * t4 + 1] = o[n][2 * i + 1];
       }
       if (t4 == 0) {
-        ml[(row * n_parts + pi) * 2] = m_run[i];
+        ml[(row * n_parts + pi) * 2] = m_run[i] * 0.6931471805599453f;  // back to natural units: ln(2)
         ml[(row * n_parts + pi) * 2 + 1] = l_run[i];
       }
     }
@@ -462,10 +492,36 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_combine_kernel(const float* _
   const int64_t b = bh / n_heads;
   T* dst = out + ((b * block + t) * n_heads + h) * int64_t(head_dim);
   const float* pr = part + row * n_parts * int64_t(head_dim);
-  for (int d = lane; d < head_dim; d += 32) {
-    float o = 0.f;
-    for (int s = 0; s < n_parts; ++s) o = fmaf(pr[int64_t(s) * head_dim + d], wts[warp][s], o);
-    dst[d] = st_f<T>(o / l);
+  // four columns per lane (head_dim is a multiple of 4, the partial rows 16-byte aligned); four
+  // partials' loads in flight before their adds, which keep range order
+  for (int d = 4 * lane; d < head_dim; d += 128) {
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    int s = 0;
+    for (; s + 4 <= n_parts; s += 4) {
+      float4 v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = *reinterpret_cast<const float4*>(pr + int64_t(s + i) * head_dim + d);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float w = wts[warp][s + i];
+        o.x = fmaf(v[i].x, w, o.x);
+        o.y = fmaf(v[i].y, w, o.y);
+        o.z = fmaf(v[i].z, w, o.z);
+        o.w = fmaf(v[i].w, w, o.w);
+      }
+    }
+    for (; s < n_parts; ++s) {
+      const float4 v = *reinterpret_cast<const float4*>(pr + int64_t(s) * head_dim + d);
+      const float w = wts[warp][s];
+      o.x = fmaf(v.x, w, o.x);
+      o.y = fmaf(v.y, w, o.y);
+      o.z = fmaf(v.z, w, o.z);
+      o.w = fmaf(v.w, w, o.w);
+    }
+    dst[d] = st_f<T>(o.x / l);
+    dst[d + 1] = st_f<T>(o.y / l);
+    dst[d + 2] = st_f<T>(o.z / l);
+    dst[d + 3] = st_f<T>(o.w / l);
   }
 }
 
@@ -473,14 +529,17 @@ struct GqaPlan {
   int row_blocks, chunk, n_splits;
 };
 
-// Key ranges: enough CTAs for two per SM, whole tiles per range, no empty range.
+// Key ranges: as many as keep every CTA in one wave of two per SM (both kernels fit two per
+// SM at head_dim 128), whole tiles per range, no empty range. Rounding the range count up
+// instead would leave a second, partial wave: 16 sequences x 8 KV heads at 3 ranges are 384
+// CTAs for 296 slots.
 GqaPlan gqa_plan(int batch, int block, int n_heads, int n_kv, int n_ctx) {
   GqaPlan p;
   p.row_blocks = int(ceil_div(int64_t(n_heads / n_kv) * block, kRowBlock));
   const int64_t nk = int64_t(n_ctx) + block;
   const int64_t base = int64_t(batch) * n_kv * p.row_blocks;
   const int64_t tiles = ceil_div(nk, kKeyTile);
-  int64_t want = ceil_div(2 * int64_t(num_sms()), base);
+  int64_t want = 2 * int64_t(num_sms()) / base;
   want = want < 1 ? 1 : (want > kMaxSplits ? kMaxSplits : want);
   if (want > tiles) want = tiles;
   const int64_t per = ceil_div(tiles, want);
@@ -614,6 +673,7 @@ extern "C" int dsm_gqa_attn(const void* q, const void* ctx_k, const void* ctx_v,
   DSM_REQUIRE(dtype == DSM_DT_F32 || dtype == DSM_DT_BF16, "dsm_gqa_attn: dtype must be F32 or BF16");
   if (batch == 0) return DSM_OK;
   DSM_REQUIRE(q && blk_k && blk_v && out && ws && (n_ctx == 0 || (ctx_k && ctx_v)), "dsm_gqa_attn: NULL pointer");
+  DSM_REQUIRE(aligned16(ws), "dsm_gqa_attn: workspace must be 16-byte aligned");
   const GqaPlan p = gqa_plan(batch, block, n_heads, n_kv, n_ctx);
   DSM_REQUIRE(int64_t(batch) * p.row_blocks <= 65535 && n_kv <= 65535, "dsm_gqa_attn: batch or n_kv too large");
   const size_t need = gqa_ws_bytes(batch, block, n_heads, head_dim, p);

@@ -330,7 +330,7 @@ int dsm_round_rows(const float* in, const float* in_lo, int64_t n, void* out, in
  *   b * ctx_batch_stride + g * ctx_head_stride + row * head_dim) and then the block's rows
  *   blk_k / blk_v [batch, n_kv, block, head_dim]; q is [batch, block, n_heads, head_dim].
  *   head_dim 32, 64, 128 or 256. workspace: dsm_gqa_attn_workspace_bytes (fp32 partials of
- *   the key ranges).
+ *   the key ranges), 16-byte aligned.
  * set_attn_kernel: 0 (the default) runs bf16 attention on the tensor-core kernels (mma.m16n8k16) where
  *   they apply: dsm_gqa_attn with head_dim 64 / 128, every pointer 16-byte aligned and the
  *   context strides multiples of 8; dsm_sparse_attn with head_dim 64..512 (a multiple of 64),
