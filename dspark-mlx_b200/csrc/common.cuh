@@ -171,6 +171,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// mbar_wait for a waiter that is off the critical path while it waits (epilogue warps that
+// wait out a whole unit's main loop): between tries it sleeps ns, so its warps leave the issue
+// slots to the converters and the MMA issuers. Same ~2 s bound.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, unsigned ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    __nanosleep(ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if (global_timer_ns() - t0 > 2000000000ull) {
+      raise_device_error(DSM_DEV_ERR_PIPELINE_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

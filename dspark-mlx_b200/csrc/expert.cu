@@ -346,7 +346,11 @@ int dispatch(int wfmt, int nt, const ExpertArgs& a, cudaStream_t s) {
 #define DSM_NT_CASES(F)                                    \
   if (nt == 1) return launch_expert<F, DUAL, 1>(a, s);     \
   if (nt == 2) return launch_expert<F, DUAL, 2>(a, s);     \
-  return launch_expert<F, DUAL, 4>(a, s);
+  if (nt == 4) return launch_expert<F, DUAL, 4>(a, s);     \
+  if constexpr (DUAL && F == DSM_WFMT_FP8_B128)            \
+    return launch_expert<F, DUAL, 4>(a, s);                \
+  else                                                     \
+    return launch_expert<F, DUAL, 8>(a, s);
   switch (wfmt) {
     case DSM_WFMT_F16: { DSM_NT_CASES(DSM_WFMT_F16) }
     case DSM_WFMT_FP8_B128: { DSM_NT_CASES(DSM_WFMT_FP8_B128) }
@@ -361,11 +365,14 @@ int dispatch(int wfmt, int nt, const ExpertArgs& a, cudaStream_t s) {
 // with few busy experts (the shared expert is one group holding every token) narrower
 // tiles give more work units, and the re-reads of a tile are served from L2. The grid is
 // this launch's persistent grid: a slice of the SMs when the shared expert runs beside the
-// routed products, where wider tiles (fewer re-reads per SM) win.
+// routed products, where wider tiles (fewer re-reads per SM) win. Eight n8 tiles (64 rows)
+// serve one large matrix over a whole draft step's rows, such as the draft head's LM head
+// (56 rows over 1,010 row tiles), whose weight tiles are then streamed once instead of once
+// per 32-row chunk. The fp8 gate/up pair stops at four: eight would spill registers.
 int pick_nt(int64_t n_rows, int n_experts, int rt_count) {
   const int64_t busy = std::max<int64_t>(1, std::min<int64_t>(n_rows, n_experts));
   const double avg = double(n_rows) / double(busy);
-  int nt = avg <= 8.0 ? 1 : (avg <= 16.0 ? 2 : 4);
+  int nt = avg <= 8.0 ? 1 : (avg <= 16.0 ? 2 : (avg <= 32.0 ? 4 : 8));
   while (nt > 1) {
     const int64_t units = busy * int64_t(std::ceil(avg / (8.0 * nt))) * rt_count;
     if (units >= 2 * int64_t(persistent_ctas())) break;

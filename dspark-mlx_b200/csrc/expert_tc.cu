@@ -411,7 +411,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
       const int rt = local / nch, chunk = local % nch;
       const int rows = min(BN, cnt - chunk * BN);
       const int buf = j % C::kNBuf;
-      if (*abort_flag || !mbar_wait(&tfull[buf], (j / C::kNBuf) & 1)) {
+      if (*abort_flag || !mbar_wait_backoff(&tfull[buf], (j / C::kNBuf) & 1, 200)) {
         *abort_flag = 1;
         break;
       }

@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
     const int rows = min(BN, w.cnt - chunk * BN);
     float* const o_out = a.o_out + w.ks * a.o_split_stride;
     const int buf = j % C::DB;
-    if (*abort_flag || !mbar_wait(&tfull[buf], (j / C::DB) & 1)) {
+    if (*abort_flag || !mbar_wait_backoff(&tfull[buf], (j / C::DB) & 1, 200)) {
       *abort_flag = 1;
       return false;
     }
