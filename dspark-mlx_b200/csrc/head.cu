@@ -318,33 +318,9 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
       for (int tile = warp; v0 + tile * 16 < v1; tile += kWalkWarps) {
         const int ra = v0 + tile * 16 + g, rb = ra + 8;
         const bool oka = ra < v1, okb = rb < v1;
-        float d[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
-        for (int k4 = 0; k4 < R; k4 += 128) {  // four 32-entry blocks: their 8 loads in flight together
-          const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-          uint4 A0[4], A1[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int k2 = k4 + 32 * u;
-            A0[u] = (oka && k2 < R) ? __ldg(reinterpret_cast<const uint4*>(w2b + int64_t(ra) * R + k2 + 8 * q)) : z;
-            A1[u] = (okb && k2 < R) ? __ldg(reinterpret_cast<const uint4*>(w2b + int64_t(rb) * R + k2 + 8 * q)) : z;
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int k2 = k4 + 32 * u;
-            if (k2 >= R) break;
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-              if (nt * 8 >= B) break;
-              const uint4 Bv = *reinterpret_cast<const uint4*>(eb + (nt * 8 + g) * RP + k2 + 8 * q);
-              mma_bf16_16816(d[nt], A0[u].x, A1[u].x, A0[u].y, A1[u].y, Bv.x, Bv.y);
-              mma_bf16_16816(d[nt], A0[u].z, A1[u].z, A0[u].w, A1[u].w, Bv.z, Bv.w);
-            }
-          }
-        }
-        // D fragment: d0, d1 row ra; d2, d3 row rb; batch nt*8 + 2q + {0, 1}. The tile's base
-        // logits are read first, so no load waits behind a store of a biased logit
+        // The tile's base logits and its Markov rows for up to 256 rank entries are all
+        // requested before the first product: one memory latency per tile, not one per
+        // 128 entries plus one for the logits.
         float lg[NT][4];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -359,6 +335,32 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
             if (okb) lg[nt][2 + c] = __ldg(&a.logits[t * V + rb]) + (a.lo_offset ? __ldg(&a.logits[(a.lo_offset + t) * V + rb]) : 0.f);
           }
         }
+        float d[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+        for (int k8 = 0; k8 < R; k8 += 256) {  // eight 32-entry blocks: their 16 loads in flight together
+          const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+          uint4 A0[8], A1[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int k2 = k8 + 32 * u;
+            A0[u] = (oka && k2 < R) ? __ldg(reinterpret_cast<const uint4*>(w2b + int64_t(ra) * R + k2 + 8 * q)) : z;
+            A1[u] = (okb && k2 < R) ? __ldg(reinterpret_cast<const uint4*>(w2b + int64_t(rb) * R + k2 + 8 * q)) : z;
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int k2 = k8 + 32 * u;
+            if (k2 >= R) break;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              if (nt * 8 >= B) break;
+              const uint4 Bv = *reinterpret_cast<const uint4*>(eb + (nt * 8 + g) * RP + k2 + 8 * q);
+              mma_bf16_16816(d[nt], A0[u].x, A1[u].x, A0[u].y, A1[u].y, Bv.x, Bv.y);
+              mma_bf16_16816(d[nt], A0[u].z, A1[u].z, A0[u].w, A1[u].w, Bv.z, Bv.w);
+            }
+          }
+        }
+        // D fragment: d0, d1 row ra; d2, d3 row rb; batch nt*8 + 2q + {0, 1}
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           if (nt * 8 >= B) break;
