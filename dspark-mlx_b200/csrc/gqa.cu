@@ -475,6 +475,15 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_combine_kernel(const float* _
   const int64_t row = int64_t(blockIdx.x) * kGqaWarps + warp;
   if (row >= n_rows) return;  // whole warps leave; only warp-level syncs follow
   const float* mlr = ml + row * n_parts * 2;
+  const float* pr = part + row * n_parts * int64_t(head_dim);
+  // the first four partials of this lane's first four columns are requested before the range
+  // weights are worked out: their load latency overlaps that of the (m, l) pairs
+  const int d0 = 4 * lane;
+  float4 v0[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    v0[i] = (d0 < head_dim && i < n_parts) ? *reinterpret_cast<const float4*>(pr + int64_t(i) * head_dim + d0)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
   float m = -INFINITY;
   for (int s = lane; s < n_parts; s += 32) m = fmaxf(m, mlr[2 * s]);
   m = warp_max(m);
@@ -491,16 +500,16 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_combine_kernel(const float* _
   const int h = int(bh % n_heads);
   const int64_t b = bh / n_heads;
   T* dst = out + ((b * block + t) * n_heads + h) * int64_t(head_dim);
-  const float* pr = part + row * n_parts * int64_t(head_dim);
   // four columns per lane (head_dim is a multiple of 4, the partial rows 16-byte aligned); four
   // partials' loads in flight before their adds, which keep range order
-  for (int d = 4 * lane; d < head_dim; d += 128) {
+  for (int d = d0; d < head_dim; d += 128) {
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
     int s = 0;
     for (; s + 4 <= n_parts; s += 4) {
       float4 v[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v[i] = *reinterpret_cast<const float4*>(pr + int64_t(s + i) * head_dim + d);
+      for (int i = 0; i < 4; ++i)
+        v[i] = (d == d0 && s == 0) ? v0[i] : *reinterpret_cast<const float4*>(pr + int64_t(s + i) * head_dim + d);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float w = wts[warp][s + i];
@@ -510,9 +519,12 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_combine_kernel(const float* _
         o.w = fmaf(v[i].w, w, o.w);
       }
     }
-    for (; s < n_parts; ++s) {
-      const float4 v = *reinterpret_cast<const float4*>(pr + int64_t(s) * head_dim + d);
-      const float w = wts[warp][s];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {  // the last n_parts % 4 ranges (s + i < 4 only when s == 0)
+      if (s + i >= n_parts) break;
+      const float4 v =
+          (d == d0 && s == 0) ? v0[i] : *reinterpret_cast<const float4*>(pr + int64_t(s + i) * head_dim + d);
+      const float w = wts[warp][s + i];
       o.x = fmaf(v.x, w, o.x);
       o.y = fmaf(v.y, w, o.y);
       o.z = fmaf(v.z, w, o.z);

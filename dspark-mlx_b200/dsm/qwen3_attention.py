@@ -17,7 +17,8 @@ Same constructor (``Qwen3DSparkAttention(args)``), parameter names (``q_proj``, 
 The projections are ``Projection``s, dense or MLX affine after ``quantize`` as
 ``quantize_drafter`` leaves them, on ``dsm_linear`` (quantised ones on
 ``dsm_linear_splitk``, which spreads K over the GPU). q, k and v share one staging of the
-input and one fp32 output slab. The head norms, NeoX RoPE and the cache layout are one
+input and one fp32 output slab; quantised alike, they are one packed matrix of stacked rows
+and one product. The head norms, NeoX RoPE and the cache layout are one
 ``dsm_qkv_norm_rope``; the attention is ``dsm_gqa_attn``; ``o_proj`` is one more
 ``dsm_linear``. The activation dtype is the projections' MLX product dtype (bf16 or fp32).
 CPU tensors are rejected.
@@ -33,6 +34,7 @@ from torch import nn
 from ._lib import check, dtype_code, lib, ptr, stream_ptr
 from .block import RMSNorm
 from .qwen3 import Projection
+from .weights import pack
 
 
 def rope_tables(position_ids, head_dim: int, theta: float) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -66,6 +68,7 @@ class Qwen3DSparkAttention(nn.Module):
         self.o_proj = Projection(nh * hd, h)
         self.q_norm = RMSNorm(hd, eps)
         self.k_norm = RMSNorm(hd, eps)
+        self._fused = {}  # with_q -> (source key, packed q/k/v rows): see _fused_packed
 
     # ---------------------------------------------------------------- helpers
     def _act_dtype(self, x: torch.Tensor) -> torch.dtype:
@@ -95,12 +98,34 @@ class Qwen3DSparkAttention(nn.Module):
                                    stream_ptr()), "dsm_stage_rows")
         return staged, xscale, cap, rows, k
 
+    def _fused_packed(self, with_q: bool):
+        """k_proj and v_proj (after q_proj when with_q) as one packed matrix of their stacked
+        output rows, when all of them are quantised alike; else None. One product then fills
+        the q/k/v slab, instead of one launch per projection with its own pipeline fill and
+        split sum. The packed rows are cached and rebuilt when a source tensor changes."""
+        projs = ((self.q_proj,) if with_q else ()) + (self.k_proj, self.v_proj)
+        quant = projs[0].quant
+        if quant is None or any(p.quant != quant for p in projs):
+            return None
+        srcs = [t for p in projs for t in (p.q, p.scales, p.biases)]
+        key = tuple((t.data_ptr(), t._version, t.dtype, t.device) for t in srcs)
+        hit = self._fused.get(with_q)
+        if hit is None or hit[0] != key:
+            bits, gs = quant
+            q = torch.cat([p.q for p in projs], 0)
+            sc = torch.cat([p.scales for p in projs], 0)
+            bi = torch.cat([p.biases for p in projs], 0)
+            hit = (key, pack("affine", data=q, scales=sc, biases=bi, group_size=gs, bits=bits, device=q.device))
+            self._fused[with_q] = hit
+        return hit[1]
+
     @staticmethod
-    def _project(st, proj: Projection, out: torch.Tensor, ldo: int) -> None:
-        """out[:, :proj.out_dim] (row stride ldo) = the staged rows times the projection. Quantised
-        projections split K across the GPU (``dsm_linear_splitk``)."""
+    def _project(st, proj: Projection, out: torch.Tensor, ldo: int, pm=None) -> None:
+        """out[:, :proj.out_dim] (row stride ldo) = the staged rows times the projection (or times
+        the packed matrix pm, quantised like proj). Quantised projections split K across the GPU
+        (``dsm_linear_splitk``)."""
         staged, xscale, cap, rows, k = st
-        pm = proj.packed()
+        pm = proj.packed() if pm is None else pm
         L = lib()
         if proj.quant is None:
             check(L.dsm_linear(ptr(staged), ptr(xscale), cap, k, pm.wfmt, pm.group_size, ptr(pm.packed), pm.rows,
@@ -137,11 +162,15 @@ class Qwen3DSparkAttention(nn.Module):
         st = self._stage(x.reshape(n, -1))
         rows = st[3]
         slab = torch.empty(rows, cols, dtype=torch.float32, device=x.device)
-        c = 0
-        for proj, used in ((self.q_proj, with_q), (self.k_proj, True), (self.v_proj, True)):
-            if used:
-                self._project(st, proj, slab[:, c:], cols)
-                c += proj.out_dim
+        fused = self._fused_packed(with_q)
+        if fused is not None:
+            self._project(st, self.k_proj, slab, cols, pm=fused)
+        else:
+            c = 0
+            for proj, used in ((self.q_proj, with_q), (self.k_proj, True), (self.v_proj, True)):
+                if used:
+                    self._project(st, proj, slab[:, c:], cols)
+                    c += proj.out_dim
         lo = slab[n:] if rows == 2 * n else None
         q = torch.empty(b, s, self.nh, self.hd, dtype=dt, device=x.device) if with_q else None
         qw = self.q_norm.weight.detach().to(device=x.device, dtype=torch.float32).contiguous()
