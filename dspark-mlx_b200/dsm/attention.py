@@ -11,8 +11,8 @@ The five projections run on ``dsm_linear`` over packed weights. A bf16 activatio
 exactly. An fp32 activation is staged as two f16 rows (hi + lo), so its products keep fp32
 precision. The norms, RoPE, the window ring, the gathered attention with its sink and the
 output's inverse rotation are the ``dsm_*`` kernels of ``csrc/attn.cu``. The grouped output
-projection is one ``dsm_linear`` per group over group-major attention output. CPU tensors
-are rejected.
+projection is one ``dsm_grouped_linear`` launch over the group-major attention output (bf16;
+fp32 rows, staged hi + lo, take one ``dsm_linear`` per group). CPU tensors are rejected.
 """
 
 from __future__ import annotations
@@ -64,7 +64,7 @@ class DSparkAttention(nn.Module):
         self.register_buffer("_cos", cos, persistent=False)
         self.register_buffer("_sin", sin, persistent=False)
         self.window: Optional[torch.Tensor] = None  # [b, window, head_dim], slot p % window = position p
-        self._packed: Dict[str, Tuple[tuple, PackedMatrix]] = {}
+        self._packed: Dict[object, tuple] = {}  # packed weights and row maps, by name
 
     # ---------------------------------------------------------------- projections
     def _pm(self, name: str, w: torch.Tensor) -> PackedMatrix:
@@ -96,6 +96,37 @@ class DSparkAttention(nn.Module):
         check(L.dsm_linear(ptr(staged), ptr(xscale), cap, k, pm.wfmt, pm.group_size, ptr(pm.packed), pm.rows, ptr(out),
                            ldo, rows, s), "dsm_linear")
         return out
+
+    def _grouped_wo_a(self, o: torch.Tensor, wo_a: torch.Tensor, y1: torch.Tensor) -> None:
+        """y1[t, gi * rank + c] = o[gi, t] . wo_a[gi, c] for every group in one staging and one
+        ``dsm_grouped_linear`` launch: the groups are the packed matrix's experts over group-major
+        rows, and row gi * n + t goes to y1's row t * groups + gi seen as rows of rank values."""
+        g, n, dg = o.shape
+        rank = wo_a.shape[1]
+        key = (wo_a.data_ptr(), wo_a._version, wo_a.dtype, wo_a.device)
+        hit = self._packed.get("wo_a")
+        if hit is None or hit[0] != key:
+            hit = (key, pack("dense", data=wo_a.detach(), device=wo_a.device))
+            self._packed["wo_a"] = hit
+        pm = hit[1]
+        maps = self._packed.get(("wo_a_rows", g, n))
+        if maps is None or maps[0].device != o.device:
+            offsets = torch.arange(0, g * n + 1, n, dtype=torch.int32, device=o.device)
+            t = torch.arange(n, dtype=torch.int32, device=o.device)
+            gi = torch.arange(g, dtype=torch.int32, device=o.device)
+            row_map = (t.unsqueeze(0) * g + gi.unsqueeze(1)).reshape(-1).contiguous()
+            maps = (offsets, row_map)
+            self._packed[("wo_a_rows", g, n)] = maps
+        L = lib()
+        x_all = o.reshape(g * n, dg)
+        cap = L.dsm_stage_rows_cap(g * n)
+        staged = torch.empty(L.dsm_stage_bytes(cap, dg), dtype=torch.uint8, device=o.device)
+        xscale = torch.empty(cap, dtype=torch.float32, device=o.device)
+        s = stream_ptr()
+        check(L.dsm_stage_rows(ptr(x_all), dtype_code(x_all.dtype), g * n, dg, None, g * n, 1, ptr(staged), cap,
+                               ptr(xscale), s), "dsm_stage_rows")
+        check(L.dsm_grouped_linear(ptr(staged), ptr(xscale), cap, dg, pm.wfmt, pm.group_size, ptr(pm.packed), g,
+                                   ptr(maps[0]), rank, ptr(y1), rank, ptr(maps[1]), g * n, s), "dsm_grouped_linear")
 
     @staticmethod
     def _hilo(o: torch.Tensor, n: int):
@@ -171,8 +202,11 @@ class DSparkAttention(nn.Module):
         rows = 2 * n if dt == torch.float32 else n
         y1 = torch.empty(rows, g * rank, dtype=torch.float32, device=x.device)
         wo_a = self.wo_a.weight.reshape(g, rank, dg)
-        for gi in range(g):
-            self._linear(o[gi], self._pm(f"wo_a{gi}", wo_a[gi]), out=y1[:, gi * rank:], ldo=g * rank)
+        if dt == torch.bfloat16:
+            self._grouped_wo_a(o, wo_a, y1)
+        else:  # fp32 rows are staged hi + lo per group: one product per group
+            for gi in range(g):
+                self._linear(o[gi], self._pm(f"wo_a{gi}", wo_a[gi]), out=y1[:, gi * rank:], ldo=g * rank)
         y1h, y1l = self._hilo(y1, n)
         y1t = torch.empty(n, g * rank, dtype=dt, device=x.device)
         check(L.dsm_round_rows(ptr(y1h), ptr(y1l), y1t.numel(), ptr(y1t), dtype_code(dt), stream_ptr()),
