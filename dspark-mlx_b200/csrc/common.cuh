@@ -68,6 +68,14 @@ int tm_down_splits(int inter, int dim, int64_t n_rows, int max_splits);
 int expert_tm_down_split(int wfmt, int group_size, const void* h_staged, float h_scale, int64_t rows_cap,
                          int inter, const void* w2, int dim, int k_splits, float* partials, int64_t n_rows,
                          void* stream, const float* x_row_scale = nullptr);
+// The streaming kernel's single-matrix product (f16, fp8) with K split into ranges, each
+// writing an fp32 partial slab parts[split][n_rows][out_dim] in staged-row order: for a product
+// whose row tiles alone would leave SMs idle or re-read each tile once per 8-64-row chunk.
+// *splits_used = the ranges launched; 1: nothing was launched (another kernel fits better, or
+// one range fills the GPU) and the caller runs the unsplit product.
+int expert_stream_split(int wfmt, int group_size, const void* x_staged, const float* x_row_scale, int64_t rows_cap,
+                        int k_dim, const int32_t* offsets, int n_groups, const void* w_packed, int out_dim,
+                        int64_t n_rows, int max_splits, float* parts, void* stream, int* splits_used);
 // h staging scale of the SwiGLU output: 1 when the clamp bounds |h| by limit^2, else 2^-8
 float h_scale_for(int act, float limit);
 // 0 = choose by rows per expert, 1 = always the decode kernel, 2 = tcgen05 where supported

@@ -94,9 +94,12 @@ DenseLayout dense_layout(int64_t n_tokens, int dim, int inter, void* base) {
   return L;
 }
 
-// o[r * ldo + c] = sum over s of parts[s][r][c], in split order: the split-K linear's fp32 rows
+// o[row_map[r] * ldo + c] (row_map NULL: row r) = sum over s of parts[s][r][c], in split order:
+// the split-K linear's fp32 rows
 __global__ void __launch_bounds__(256) sum_splits_rows_kernel(const float* __restrict__ parts, int n_splits,
-                                                              int64_t n_rows, int dim, int ldo, float* __restrict__ o) {
+                                                              int64_t n_rows, int dim, int ldo,
+                                                              const int32_t* __restrict__ row_map,
+                                                              float* __restrict__ o) {
   // four consecutive columns per thread: dim, ldo and the pointers are 16-byte multiples
   const int64_t count = n_rows * dim;
   for (int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < count;
@@ -117,7 +120,8 @@ __global__ void __launch_bounds__(256) sum_splits_rows_kernel(const float* __res
     }
     const int64_t r = i / dim;
     const int c = int(i % dim);
-    *reinterpret_cast<float4*>(o + r * ldo + c) = acc;
+    const int64_t orow = row_map ? int64_t(row_map[r]) : r;
+    *reinterpret_cast<float4*>(o + orow * ldo + c) = acc;
   }
 }
 
@@ -186,19 +190,62 @@ extern "C" int dsm_linear_splitk(const void* x_staged, const float* x_row_scale,
   DSM_REQUIRE(x_staged && x_row_scale && w_packed && o_rows, "dsm_linear_splitk: NULL pointer");
   if (n_rows == 0) return DSM_OK;
   const bool aligned = (reinterpret_cast<uintptr_t>(o_rows) & 15) == 0 && (reinterpret_cast<uintptr_t>(ws) & 15) == 0;
-  const int splits = tm_supports(wfmt) ? tm_down_splits(k_dim, out_dim, n_rows, kMaxSplits) : 1;
-  if (splits <= 1 || !ws || !aligned || out_dim % 4 || ldo % 4)
+  const bool can_split = ws && aligned && out_dim % 4 == 0 && ldo % 4 == 0;
+  float* parts = static_cast<float*>(ws);
+  int splits = 1;
+  if (can_split && !tm_supports(wfmt)) {  // the streaming kernel (f16, fp8) takes its own split
+    DSM_REQUIRE(rows_cap >= dsm_stage_rows_cap(n_rows), "dsm_linear_splitk: rows_cap too small");
+    if (ws_bytes < dsm_linear_splitk_workspace_bytes(n_rows, out_dim))
+      return fail(DSM_ERR_WORKSPACE, "dsm_linear_splitk: workspace too small");
+    int rc = expert_stream_split(wfmt, group_size, x_staged, x_row_scale, rows_cap, k_dim, nullptr, 1, w_packed,
+                                 out_dim, n_rows, kMaxSplits, parts, stream, &splits);
+    if (rc != DSM_OK) return rc;
+  } else if (can_split) {
+    splits = tm_down_splits(k_dim, out_dim, n_rows, kMaxSplits);
+    if (splits > 1) {
+      DSM_REQUIRE(rows_cap >= dsm_stage_rows_cap(n_rows), "dsm_linear_splitk: rows_cap too small");
+      const size_t need = size_t(splits) * size_t(n_rows) * size_t(out_dim) * 4;
+      if (ws_bytes < need) return fail(DSM_ERR_WORKSPACE, "dsm_linear_splitk: workspace too small");
+      int rc = expert_tm_down_split(wfmt, group_size, x_staged, 1.f, rows_cap, k_dim, w_packed, out_dim, splits,
+                                    parts, n_rows, stream, x_row_scale);
+      if (rc != DSM_OK) return rc;
+    }
+  }
+  if (splits <= 1)
     return dsm_linear(x_staged, x_row_scale, rows_cap, k_dim, wfmt, group_size, w_packed, out_dim, o_rows, ldo,
                       n_rows, stream);
-  DSM_REQUIRE(rows_cap >= dsm_stage_rows_cap(n_rows), "dsm_linear_splitk: rows_cap too small");
-  const size_t need = size_t(splits) * size_t(n_rows) * size_t(out_dim) * 4;
-  if (ws_bytes < need) return fail(DSM_ERR_WORKSPACE, "dsm_linear_splitk: workspace too small");
-  float* parts = static_cast<float*>(ws);
-  int rc = expert_tm_down_split(wfmt, group_size, x_staged, 1.f, rows_cap, k_dim, w_packed, out_dim, splits, parts,
-                                n_rows, stream, x_row_scale);
-  if (rc != DSM_OK) return rc;
   const int64_t count = n_rows * out_dim;
   const int grid = int(std::min<int64_t>(ceil_div(count, 4 * 256), 4 * num_sms()));
-  sum_splits_rows_kernel<<<grid, 256, 0, as_stream(stream)>>>(parts, splits, n_rows, out_dim, ldo, o_rows);
+  sum_splits_rows_kernel<<<grid, 256, 0, as_stream(stream)>>>(parts, splits, n_rows, out_dim, ldo, nullptr, o_rows);
+  return check_launch("sum_splits_rows");
+}
+
+extern "C" int dsm_grouped_linear_splitk(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int k_dim,
+                                         int wfmt, int group_size, const void* w_packed, int n_groups,
+                                         const int32_t* offsets, int out_dim, float* o_rows, int ldo,
+                                         const int32_t* o_row_map, int64_t n_rows, void* ws, size_t ws_bytes,
+                                         void* stream) {
+  DSM_REQUIRE(out_dim > 0 && k_dim > 0 && n_rows >= 0 && ldo >= out_dim && n_groups >= 1 && n_groups <= 4096,
+              "dsm_grouped_linear_splitk: bad shape");
+  DSM_REQUIRE(x_staged && x_row_scale && w_packed && o_rows && offsets, "dsm_grouped_linear_splitk: NULL pointer");
+  if (n_rows == 0) return DSM_OK;
+  const bool aligned = (reinterpret_cast<uintptr_t>(o_rows) & 15) == 0 && (reinterpret_cast<uintptr_t>(ws) & 15) == 0;
+  int splits = 1;
+  if (ws && aligned && out_dim % 4 == 0 && ldo % 4 == 0 && !tm_supports(wfmt) &&
+      (wfmt == DSM_WFMT_F16 || wfmt == DSM_WFMT_FP8_B128)) {
+    DSM_REQUIRE(rows_cap >= dsm_stage_rows_cap(n_rows), "dsm_grouped_linear_splitk: rows_cap too small");
+    if (ws_bytes < dsm_linear_splitk_workspace_bytes(n_rows, out_dim))
+      return fail(DSM_ERR_WORKSPACE, "dsm_grouped_linear_splitk: workspace too small");
+    int rc = expert_stream_split(wfmt, group_size, x_staged, x_row_scale, rows_cap, k_dim, offsets, n_groups,
+                                 w_packed, out_dim, n_rows, kMaxSplits, static_cast<float*>(ws), stream, &splits);
+    if (rc != DSM_OK) return rc;
+  }
+  if (splits <= 1)
+    return dsm_grouped_linear(x_staged, x_row_scale, rows_cap, k_dim, wfmt, group_size, w_packed, n_groups, offsets,
+                              out_dim, o_rows, ldo, o_row_map, n_rows, stream);
+  const int64_t count = n_rows * out_dim;
+  const int grid = int(std::min<int64_t>(ceil_div(count, 4 * 256), 4 * num_sms()));
+  sum_splits_rows_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<const float*>(ws), splits, n_rows, out_dim,
+                                                                ldo, o_row_map, o_rows);
   return check_launch("sum_splits_rows");
 }

@@ -62,7 +62,14 @@ struct ExpertArgs {
   int ldo;
   int round_o;
   int64_t n_rows;  // rows of the single group when offsets is NULL
+  // single-matrix product only: K ranges per (row tile, row chunk), each writing an fp32
+  // partial slab o_out + split * o_split_stride (rows [n_rows][ldo], staged-row order, no row
+  // map); 0 or 1 = no split. k_per: 128-K chunks per range.
+  int k_splits;
+  int k_per;
+  int64_t o_split_stride;
 };
+__host__ __device__ __forceinline__ int n_ksplit(const ExpertArgs& a) { return a.k_splits > 1 ? a.k_splits : 1; }
 
 // rows [first, first + count) of group e (offsets == NULL: one group holding every row)
 __device__ __forceinline__ int group_first(const ExpertArgs& a, int e) { return a.offsets ? a.offsets[e] : 0; }
@@ -118,7 +125,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
       int v = 0;
       if (e < E) {
         const int cnt = group_count(a, e);
-        v = cnt > 0 ? a.rt_count * ((cnt + BN - 1) / BN) : 0;
+        v = cnt > 0 ? a.rt_count * ((cnt + BN - 1) / BN) * n_ksplit(a) : 0;
       }
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -150,10 +157,13 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
         const int cnt = group_count(a, e);
         const int nch = (cnt + BN - 1) / BN;
         const int local = u - pre[e];
-        const int rt = local / nch, chunk = local % nch;
+        const int rt = local / (nch * n_ksplit(a)), r2 = local % (nch * n_ksplit(a));
+        const int chunk = r2 % nch;
+        const int kc0 = a.k_splits > 1 ? (r2 / nch) * a.k_per : 0;
+        const int kc1 = a.k_splits > 1 ? min(a.kc_count, kc0 + a.k_per) : a.kc_count;
         const int64_t row0 = int64_t(group_first(a, e)) + int64_t(chunk) * BN;
         const int64_t tile0 = (int64_t(e) * a.rt_count + rt) * a.kc_count;
-        for (int kc = 0; kc < a.kc_count; ++kc) {
+        for (int kc = kc0; kc < kc1; ++kc) {
           if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u)) {
             *abort_flag = 1;
             ok = false;
@@ -189,7 +199,10 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
     const int cnt = group_count(a, e);
     const int nch = (cnt + BN - 1) / BN;
     const int local = u - pre[e];
-    const int rt = local / nch, chunk = local % nch;
+    const int rt = local / (nch * n_ksplit(a)), r2 = local % (nch * n_ksplit(a));
+    const int chunk = r2 % nch, ks = r2 / nch;
+    const int kc0 = a.k_splits > 1 ? ks * a.k_per : 0;
+    const int kc1 = a.k_splits > 1 ? min(a.kc_count, kc0 + a.k_per) : a.kc_count;
 
     float acc[NM][kMt][NT][4];
     float tmp[kTmp ? NM : 1][kMt][NT][4];
@@ -206,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
           }
 
     bool ok = true;
-    for (int kc = 0; kc < a.kc_count; ++kc) {
+    for (int kc = kc0; kc < kc1; ++kc) {
       if (*abort_flag || !mbar_wait(&full[s], ph)) {
         *abort_flag = 1;
         ok = false;
@@ -317,6 +330,10 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
             const int d = rt * kTileRows + rloc;
             if (d >= a.out_rows) continue;
             float v = acc[0][i][j][c] * xs * wmul_a;
+            if (a.k_splits > 1) {  // a partial of the K range: summed and rounded by the split sum
+              a.o_out[int64_t(ks) * a.o_split_stride + r * a.ldo + d] = v;
+              continue;
+            }
             if (a.round_o) v = bf16_round(v);
             const int64_t orow = a.o_row_map ? int64_t(a.o_row_map[r]) : r;
             a.o_out[orow * a.ldo + d] = v;
@@ -562,6 +579,50 @@ extern "C" int dsm_grouped_linear(const void* x_staged, const float* x_row_scale
 
 namespace dsm {
 int expert_regime() { return g_regime; }
+
+int expert_stream_split(int wfmt, int group_size, const void* x_staged, const float* x_row_scale, int64_t rows_cap,
+                        int k_dim, const int32_t* offsets, int n_groups, const void* w_packed, int out_dim,
+                        int64_t n_rows, int max_splits, float* parts, void* stream, int* splits_used) {
+  *splits_used = 1;
+  if ((wfmt != DSM_WFMT_F16 && wfmt != DSM_WFMT_FP8_B128) || n_rows <= 0 || use_tc(wfmt, n_rows, n_groups))
+    return DSM_OK;
+  const int rt = int(ceil_div(out_dim, kTileRows)), kcs = int(ceil_div(k_dim, kChunkK));
+  const int64_t busy = std::max<int64_t>(1, std::min<int64_t>(n_rows, n_groups));
+  const double avg = double(n_rows) / double(busy);
+  // the narrowest unit holding a group's rows: each weight tile is then streamed once per K
+  // range, and the K ranges, not row chunks, fill the SMs
+  const int nt = avg <= 8.0 ? 1 : (avg <= 16.0 ? 2 : (avg <= 32.0 ? 4 : 8));
+  const int64_t units = busy * int64_t(std::ceil(avg / (8.0 * nt))) * rt;
+  int splits = int(std::min<int64_t>({int64_t(max_splits), int64_t(kcs), int64_t(persistent_ctas()) / units}));
+  if (splits <= 1) return DSM_OK;
+  const int k_per = int(ceil_div(kcs, splits));
+  splits = int(ceil_div(kcs, k_per));  // no empty range
+  if (splits <= 1) return DSM_OK;
+  ExpertArgs a{};
+  a.wa = static_cast<const uint8_t*>(w_packed);
+  a.wb = nullptr;
+  a.xin = static_cast<const __half*>(x_staged);
+  a.act_scale = x_row_scale;
+  a.act_scale_const = 1.f;
+  a.rows_cap = rows_cap;
+  a.offsets = offsets;
+  a.n_rows = n_rows;
+  a.n_experts = n_groups;
+  a.out_rows = out_dim;
+  a.rt_count = rt;
+  a.kc_count = kcs;
+  a.group_size = group_size > 0 ? group_size : 64;
+  a.o_out = parts;
+  a.o_row_map = nullptr;
+  a.ldo = out_dim;
+  a.round_o = 0;
+  a.k_splits = splits;
+  a.k_per = k_per;
+  a.o_split_stride = n_rows * int64_t(out_dim);
+  const int rc = dispatch<false>(wfmt, nt, a, as_stream(stream));
+  if (rc == DSM_OK) *splits_used = splits;
+  return rc;
+}
 }  // namespace dsm
 
 extern "C" int dsm_set_expert_regime(int regime) {

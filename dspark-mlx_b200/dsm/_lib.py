@@ -41,7 +41,7 @@ EXPORTED = (
     "dsm_sparse_attn_scratch_bytes", "dsm_sparse_attn", "dsm_round_rows", "dsm_stage_rows_hilo",
     "dsm_qkv_norm_rope", "dsm_gqa_attn_workspace_bytes", "dsm_gqa_attn", "dsm_set_attn_kernel",
     "dsm_linear_splitk_workspace_bytes", "dsm_linear_splitk", "dsm_add_rms_norm",
-    "dsm_grouped_linear",
+    "dsm_grouped_linear", "dsm_grouped_linear_splitk",
 )
 
 
@@ -154,6 +154,7 @@ def _declare(lib):
         "dsm_linear_splitk": (I, [V, V, I64, I, I, I, V, I, V, I, I64, V, S, V]),
         "dsm_add_rms_norm": (I, [V, V, I, I64, I, V, F, V, V, V]),
         "dsm_grouped_linear": (I, [V, V, I64, I, I, I, V, I, V, I, V, I, V, I64, V]),
+        "dsm_grouped_linear_splitk": (I, [V, V, I64, I, I, I, V, I, V, I, V, I, V, I64, V, S, V]),
         "dsm_stage_rows_hilo": (I, [V, I64, I, V, I64, V, V]),
         "dsm_moe_workspace_bytes": (S, [POINTER(MoEDesc)]),
         "dsm_moe_forward": (I, [POINTER(MoEDesc), V, I, V, I, I64, V, V, V, V, S, V]),

@@ -7,7 +7,8 @@ reference, and the same parameter names. Those are ``wq_a``, ``q_norm``, ``wq_b`
 ``kv_norm``, ``wo_a``, ``wo_b`` and ``attn_sink``. A prefill call (``start_pos == 0``) seeds
 the sliding KV window and returns x. A decode call drafts the block.
 
-The five projections run on ``dsm_linear`` over packed weights. A bf16 activation is staged
+The five projections run on ``dsm_linear_splitk`` over packed weights (K split where the row
+tiles alone would leave SMs idle). A bf16 activation is staged
 exactly. An fp32 activation is staged as two f16 rows (hi + lo), so its products keep fp32
 precision. The norms, RoPE, the window ring, the gathered attention with its sink and the
 output's inverse rotation are the ``dsm_*`` kernels of ``csrc/attn.cu``. The grouped output
@@ -93,8 +94,11 @@ class DSparkAttention(nn.Module):
         if out is None:
             out = torch.empty(rows, pm.rows, dtype=torch.float32, device=x2.device)
             ldo = pm.rows
-        check(L.dsm_linear(ptr(staged), ptr(xscale), cap, k, pm.wfmt, pm.group_size, ptr(pm.packed), pm.rows, ptr(out),
-                           ldo, rows, s), "dsm_linear")
+        # K split across the GPU where the row tiles alone leave SMs idle (wq_a, wkv, wo_b)
+        ws_bytes = L.dsm_linear_splitk_workspace_bytes(rows, pm.rows)
+        ws = torch.empty(max(1, ws_bytes), dtype=torch.uint8, device=x2.device)
+        check(L.dsm_linear_splitk(ptr(staged), ptr(xscale), cap, k, pm.wfmt, pm.group_size, ptr(pm.packed), pm.rows,
+                                  ptr(out), ldo, rows, ptr(ws), ws_bytes, s), "dsm_linear_splitk")
         return out
 
     def _grouped_wo_a(self, o: torch.Tensor, wo_a: torch.Tensor, y1: torch.Tensor) -> None:
@@ -125,8 +129,11 @@ class DSparkAttention(nn.Module):
         s = stream_ptr()
         check(L.dsm_stage_rows(ptr(x_all), dtype_code(x_all.dtype), g * n, dg, None, g * n, 1, ptr(staged), cap,
                                ptr(xscale), s), "dsm_stage_rows")
-        check(L.dsm_grouped_linear(ptr(staged), ptr(xscale), cap, dg, pm.wfmt, pm.group_size, ptr(pm.packed), g,
-                                   ptr(maps[0]), rank, ptr(y1), rank, ptr(maps[1]), g * n, s), "dsm_grouped_linear")
+        ws_bytes = L.dsm_linear_splitk_workspace_bytes(g * n, rank)
+        ws = torch.empty(max(1, ws_bytes), dtype=torch.uint8, device=o.device)
+        check(L.dsm_grouped_linear_splitk(ptr(staged), ptr(xscale), cap, dg, pm.wfmt, pm.group_size, ptr(pm.packed), g,
+                                          ptr(maps[0]), rank, ptr(y1), rank, ptr(maps[1]), g * n, ptr(ws), ws_bytes,
+                                          s), "dsm_grouped_linear_splitk")
 
     @staticmethod
     def _hilo(o: torch.Tensor, n: int):

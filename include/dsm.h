@@ -236,12 +236,22 @@ int dsm_linear(const void* x_staged, const float* x_row_scale, int64_t rows_cap,
 int dsm_grouped_linear(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int k_dim, int wfmt,
                        int group_size, const void* w_packed, int n_groups, const int32_t* offsets, int out_dim,
                        float* o_rows, int ldo, const int32_t* o_row_map, int64_t n_rows, void* stream);
-/* dsm_linear with K split across the GPU for the tensor-memory formats (fp4, affine), whose
- * units hold up to 128 rows each: a few row tiles of a decode-sized product would leave most
- * SMs idle. fp32 partial slabs per K range go to the workspace
- * (dsm_linear_splitk_workspace_bytes) and are summed in range order into o_rows. Other
- * formats, one-range products, out_dim or ldo not a multiple of 4, or pointers off 16 bytes
- * run dsm_linear. */
+/* grouped_linear_splitk: dsm_grouped_linear with K split as dsm_linear_splitk splits it, for
+ * the streaming formats (f16, fp8); workspace dsm_linear_splitk_workspace_bytes(n_rows,
+ * out_dim), the partial rows summed in range order into o_rows through o_row_map. Other
+ * formats, one-range products and unaligned pointers run dsm_grouped_linear. Same product as
+ * grouped_linear (model/attention.py:124-128), with no reference counterpart of its own. */
+int dsm_grouped_linear_splitk(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int k_dim,
+                              int wfmt, int group_size, const void* w_packed, int n_groups, const int32_t* offsets,
+                              int out_dim, float* o_rows, int ldo, const int32_t* o_row_map, int64_t n_rows,
+                              void* ws, size_t ws_bytes, void* stream);
+/* dsm_linear with K split across the GPU, where a product's row tiles alone would leave most
+ * SMs idle: the tensor-memory formats (fp4, affine; units of up to 128 rows), and the
+ * streaming formats (f16, fp8) below the tcgen05 row count, whose units then hold a whole
+ * draft step's rows (up to 64) so that each weight tile is streamed once per K range. fp32
+ * partial slabs per K range go to the workspace (dsm_linear_splitk_workspace_bytes) and are
+ * summed in range order into o_rows. One-range products, out_dim or ldo not a multiple of 4,
+ * or pointers off 16 bytes run dsm_linear. */
 size_t dsm_linear_splitk_workspace_bytes(int64_t n_rows, int out_dim);
 int dsm_linear_splitk(const void* x_staged, const float* x_row_scale, int64_t rows_cap, int k_dim, int wfmt,
                       int group_size, const void* w_packed, int out_dim, float* o_rows, int ldo, int64_t n_rows,

@@ -1,14 +1,15 @@
 """The linear entry points beside ``dsm_linear``, through the C ABI.
 
-``dsm_linear_splitk`` (K split across the GPU for the tensor-memory weight formats) against
-``dsm_linear`` on the same staged rows and packed weights.
+``dsm_linear_splitk`` (K split across the GPU: the tensor-memory weight formats, and bf16 weights
+on the streaming kernel) against ``dsm_linear`` on the same staged rows and packed weights.
 
 Both multiply the same products; the split one sums fp32 partial slabs over K ranges in range
 order, so the two agree to fp32 rounding (1e-5 relative). Outputs go to a column slice of a
 wider buffer (row stride ``ldo``): the columns outside the slice must keep their contents.
 
-``dsm_grouped_linear`` (several weight matrices over row groups, one launch, scattered output
-rows) against fp32 products of the same rows and (dequantised) weights."""
+``dsm_grouped_linear`` and ``dsm_grouped_linear_splitk`` (several weight matrices over row groups,
+one launch, scattered output rows) against fp32 products of the same rows and (dequantised)
+weights."""
 
 from __future__ import annotations
 
@@ -25,12 +26,18 @@ DEV = "cuda"
 
 
 @pytest.mark.parametrize("bits,n,k,out", [(8, 112, 2560, 1024), (8, 300, 2560, 2560), (4, 56, 4096, 512),
-                                          (8, 14, 4096, 4096)])
+                                          (8, 14, 4096, 4096),
+                                          # bf16 weights on the streaming kernel: the draft attention's
+                                          # wo_b, wq_a and wkv over a 56-row draft step, and 9 rows
+                                          (0, 56, 8192, 4096), (0, 56, 4096, 1024), (0, 9, 4096, 512)])
 def test_splitk_matches_whole_k_linear(bits, n, k, out):
     g = torch.Generator().manual_seed(n + k + out)
     w = (torch.randn(out, k, generator=g) * k ** -0.5).to(torch.bfloat16).to(DEV)
-    q, s, b = affine_quantize(w, group_size=64, bits=bits)
-    pm = pack("affine", data=q, scales=s, biases=b, group_size=64, bits=bits, device=DEV)
+    if bits:
+        q, s, b = affine_quantize(w, group_size=64, bits=bits)
+        pm = pack("affine", data=q, scales=s, biases=b, group_size=64, bits=bits, device=DEV)
+    else:
+        pm = pack("dense", data=w, device=DEV)
     x = torch.randn(n, k, generator=g).to(torch.bfloat16).to(DEV)
     L = lib()
     cap = L.dsm_stage_rows_cap(n)
@@ -55,11 +62,13 @@ def test_splitk_matches_whole_k_linear(bits, n, k, out):
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("split", [False, True])
 @pytest.mark.parametrize("fmt", ["dense", "affine8"])
-def test_grouped_linear_matches_per_group_products(fmt):
+def test_grouped_linear_matches_per_group_products(fmt, split):
     """The draft attention's grouped output projection as one call: 4 groups of rank 256 over
     group-major rows (56 tokens x 512 values per group), row r = (g, t) written to output row
-    t * 4 + g of a [56, 4 * 256] buffer."""
+    t * 4 + g of a [56, 4 * 256] buffer. split: through dsm_grouped_linear_splitk (K split for
+    the dense weights: four ranges of 128; the affine weights take the unsplit product)."""
     from oracle.formats import affine_dequantize
 
     g = torch.Generator().manual_seed(9)
@@ -85,10 +94,18 @@ def test_grouped_linear_matches_per_group_products(fmt):
     gi, t = torch.meshgrid(torch.arange(groups), torch.arange(n), indexing="ij")
     row_map = (t * groups + gi).reshape(-1).to(torch.int32).to(DEV)
     y = torch.full((n, groups * rank), 7.0, device=DEV)
+    ws_bytes = L.dsm_linear_splitk_workspace_bytes(rows, rank)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=DEV)
     for _ in range(2):
-        _lib.check(L.dsm_grouped_linear(ptr(staged), ptr(xs), cap, d, pm.wfmt, pm.group_size, ptr(pm.packed), groups,
-                                        ptr(offsets), rank, ptr(y), rank, ptr(row_map), rows, stream_ptr()),
-                   "dsm_grouped_linear")
+        if split:
+            _lib.check(L.dsm_grouped_linear_splitk(ptr(staged), ptr(xs), cap, d, pm.wfmt, pm.group_size,
+                                                   ptr(pm.packed), groups, ptr(offsets), rank, ptr(y), rank,
+                                                   ptr(row_map), rows, ptr(ws), ws_bytes, stream_ptr()),
+                       "dsm_grouped_linear_splitk")
+        else:
+            _lib.check(L.dsm_grouped_linear(ptr(staged), ptr(xs), cap, d, pm.wfmt, pm.group_size, ptr(pm.packed),
+                                            groups, ptr(offsets), rank, ptr(y), rank, ptr(row_map), rows,
+                                            stream_ptr()), "dsm_grouped_linear")
     torch.cuda.synchronize()
     ref = torch.einsum("gtd,grd->tgr", o.float(), wf.reshape(groups, rank, d)).reshape(n, groups * rank)
     # bf16 weights are exact in the f16 tiles; dequantised 8-bit weights are formed in f16 in
