@@ -20,7 +20,7 @@
 // and range. A second kernel combines the ranges in order. The output is rounded once to the
 // activation dtype. Two CTA kernels:
 //   gqa_attn_kernel  fp32 CUDA-core products, any dtype and head_dim 32..256;
-//   gqa_mma_kernel   bf16 with head_dim 64 or 128: K/V tiles in a three-slot cp.async ring,
+//   gqa_mma_kernel   bf16 with head_dim 64 or 128: K/V tiles double-buffered by cp.async,
 //                    q.k and p.v on mma.m16n8k16 (bf16 in, fp32 accumulate; p rounded to
 //                    bf16 for the second product), each warp an online softmax over half of
 //                    every tile, so each key range leaves two partials.
@@ -41,9 +41,11 @@ constexpr int kMaxSplits = 64;  // key ranges per KV head
 constexpr int kMaxParts = 2 * kMaxSplits;  // partials per query row (two per range on the mma path)
 constexpr int kMaxHeadDim = 256;
 constexpr int kMmaThreads = 128;  // 4 warps: 2 row tiles of 16 x 2 key halves of 32
-// K/V tiles in flight: two loads ahead of the tile being multiplied. At head_dim 128 a CTA
-// holds (32 + 3 x 2 x 64) padded rows = 113,152 B, so two CTAs still share an SM.
-constexpr int kMmaStages = 3;
+// K/V tile slots: one load ahead of the tile being multiplied. At head_dim 128 a CTA holds
+// (32 + 2 x 2 x 64) rows of 256 B = 73,728 B of shared memory, so three CTAs share an SM
+// (12 warps: the warps' dependency chains, not the loads, bound this kernel).
+constexpr int kMmaStages = 2;
+constexpr int kMmaCtasPerSm = 3;
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -250,24 +252,30 @@ __global__ void __launch_bounds__(kGqaThreads) gqa_attn_kernel(
 // ..) and key half w >> 1 (keys 32 (w >> 1) .. of every 64-key tile), keeps its own running
 // max / denominator / output, and leaves partial 2 * split + (w >> 1). Fragment layouts are
 // those of mma.m16n8k16: thread (g, t) = (lane / 4, lane % 4) holds rows g and g + 8,
-// columns 2t and 2t + 1 of each 8-wide accumulator tile. Shared rows are padded by 8
-// elements so the ldmatrix row addresses of one 8x8 matrix fall in distinct banks.
+// columns 2t and 2t + 1 of each 8-wide accumulator tile. Shared rows are unpadded, with the
+// 16-byte chunks of row r XOR-swizzled by r % 8, so the eight rows that one 8x8 ldmatrix
+// reads at a logical chunk sit in eight different bank groups. Without padding, and with
+// the q fragments loaded per tile instead of held in registers, three CTAs share an SM.
 template <int HD>
-__global__ void __launch_bounds__(kMmaThreads) gqa_mma_kernel(
+__global__ void __launch_bounds__(kMmaThreads, kMmaCtasPerSm) gqa_mma_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ ctx_k,
     const __nv_bfloat16* __restrict__ ctx_v, int64_t ctx_sb, int64_t ctx_sh, int n_ctx,
     const __nv_bfloat16* __restrict__ blk_k, const __nv_bfloat16* __restrict__ blk_v, int block, int n_heads,
     int n_kv, int row_blocks, int chunk, int n_parts, float scale, float* __restrict__ part,
     float* __restrict__ ml) {
-  constexpr int RS = HD + 8;   // shared row stride (elements)
-  constexpr int CPR = HD / 8;  // 16-byte chunks per row
+  constexpr int ROWB = HD * 2;  // shared row (bytes)
+  constexpr int CPR = HD / 8;    // 16-byte chunks per row
   constexpr int KS = HD / 16;  // k-steps of q.k
   constexpr int NT = HD / 8;   // 8-wide output tiles
   static_assert(HD == 64 || HD == 128, "head_dim");
-  extern __shared__ __align__(16) unsigned char gqa_smem[];
-  __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(gqa_smem);  // [32][RS]
-  __nv_bfloat16* Ks = Qs + kRowBlock * RS;                          // [stage][64][RS]
-  __nv_bfloat16* Vs = Ks + kMmaStages * kKeyTile * RS;              // [stage][64][RS]
+  extern __shared__ __align__(128) unsigned char gqa_smem[];
+  // byte offsets: q [32 rows], K [stage][64 rows], V [stage][64 rows]
+  constexpr uint32_t kQ0 = 0, kK0 = kRowBlock * ROWB, kV0 = kK0 + kMmaStages * kKeyTile * ROWB;
+  const uint32_t sm0 = smem_u32(gqa_smem);
+  // chunk c of row r of a region at byte offset base
+  auto swz = [](uint32_t base, int r, int c) -> uint32_t {
+    return base + uint32_t(r * ROWB) + (uint32_t(c ^ (r & 7)) << 4);
+  };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, t4 = lane & 3;
@@ -290,23 +298,23 @@ __global__ void __launch_bounds__(kMmaThreads) gqa_mma_kernel(
       const int h = g * G + ri / block, t = ri % block;
       v = *reinterpret_cast<const uint4*>(q + ((int64_t(b) * block + t) * n_heads + h) * HD + c * 8);
     }
-    *reinterpret_cast<uint4*>(Qs + r * RS + c * 8) = v;
+    *reinterpret_cast<uint4*>(gqa_smem + swz(kQ0, r, c)) = v;
   }
   auto load_tile = [&](int tile, int stage) {
     const int kt0 = k0 + tile * kKeyTile;
-    __nv_bfloat16* ks = Ks + stage * kKeyTile * RS;
-    __nv_bfloat16* vs = Vs + stage * kKeyTile * RS;
+    const uint32_t ks = kK0 + uint32_t(stage * kKeyTile * ROWB), vs = kV0 + uint32_t(stage * kKeyTile * ROWB);
     if (kt0 + kKeyTile <= min(k1, n_ctx)) {
       // a whole tile of context rows (every tile but a range's last): fixed column chunk per
       // thread, rows RPP apart, no per-chunk bounds or source choice
       constexpr int RPP = kMmaThreads / CPR;
       const int c = tid % CPR, jr = tid / CPR;
       const int64_t src0 = ctx_base + int64_t(kt0 + jr) * HD + c * 8;
-      const uint32_t kd = smem_u32(ks + jr * RS + c * 8), vd = smem_u32(vs + jr * RS + c * 8);
+      // RPP is a multiple of 8: the thread's rows share one swizzle
+      const uint32_t kd = sm0 + swz(ks, jr, c), vd = sm0 + swz(vs, jr, c);
 #pragma unroll
       for (int it = 0; it < kKeyTile / RPP; ++it) {
-        cp_async16(kd + uint32_t(it * RPP * RS * 2), ctx_k + src0 + int64_t(it) * RPP * HD, true);
-        cp_async16(vd + uint32_t(it * RPP * RS * 2), ctx_v + src0 + int64_t(it) * RPP * HD, true);
+        cp_async16(kd + uint32_t(it * RPP * ROWB), ctx_k + src0 + int64_t(it) * RPP * HD, true);
+        cp_async16(vd + uint32_t(it * RPP * ROWB), ctx_v + src0 + int64_t(it) * RPP * HD, true);
       }
       return;
     }
@@ -324,20 +332,18 @@ __global__ void __launch_bounds__(kMmaThreads) gqa_mma_kernel(
         ksrc = blk_k + (blk_base + kb) * HD + c * 8;
         vsrc = blk_v + (blk_base + kb) * HD + c * 8;
       }
-      cp_async16(smem_u32(ks + j * RS + c * 8), ksrc, valid);
-      cp_async16(smem_u32(vs + j * RS + c * 8), vsrc, valid);
+      cp_async16(sm0 + swz(ks, j, c), ksrc, valid);
+      cp_async16(sm0 + swz(vs, j, c), vsrc, valid);
     }
   };
-  load_tile(0, 0);  // every range holds at least one key
-  cp_async_commit();
-  if (n_tiles > 1) load_tile(1, 1);
-  cp_async_commit();  // one group per tile slot, empty or not, so the wait count below holds
-  __syncthreads();  // Qs
-  uint32_t qa[KS][4];
+  // tiles 0 .. kMmaStages - 2 ahead; one commit group per tile slot, empty or not, so the
+  // wait count below holds (every range holds at least one key)
 #pragma unroll
-  for (int kk = 0; kk < KS; ++kk)
-    ldsm_x4(smem_u32(Qs + (16 * mt + (lane & 7) + 8 * ((lane >> 3) & 1)) * RS + 16 * kk + 8 * (lane >> 4)),
-            qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+  for (int t = 0; t < kMmaStages - 1; ++t) {
+    if (t < n_tiles) load_tile(t, t);
+    cp_async_commit();
+  }
+  const int q_row = 16 * mt + (lane & 7) + 8 * ((lane >> 3) & 1);  // this lane's ldmatrix row of q
 
   float o[NT][4];
 #pragma unroll
@@ -347,25 +353,27 @@ __global__ void __launch_bounds__(kMmaThreads) gqa_mma_kernel(
   for (int tile = 0; tile < n_tiles; ++tile) {
     const int stage = tile % kMmaStages;
     // the slot refilled here held tile - 1, released by the barrier that ended its iteration
-    if (tile + 2 < n_tiles) load_tile(tile + 2, (tile + 2) % kMmaStages);
+    if (tile + kMmaStages - 1 < n_tiles) load_tile(tile + kMmaStages - 1, (tile + kMmaStages - 1) % kMmaStages);
     cp_async_commit();
-    cp_async_wait2();  // this tile's group has landed
+    cp_async_wait<kMmaStages - 1>();  // this tile's group has landed (and, at tile 0, q)
     __syncthreads();
     const int kt = min(kKeyTile, k1 - (k0 + tile * kKeyTile));
-    const __nv_bfloat16* ks = Ks + (stage * kKeyTile + 32 * kh) * RS;
-    const __nv_bfloat16* vs = Vs + (stage * kKeyTile + 32 * kh) * RS;
+    const uint32_t ks = kK0 + uint32_t(stage * kKeyTile * ROWB), vs = kV0 + uint32_t(stage * kKeyTile * ROWB);
+    const int kr0 = 32 * kh;  // this warp's key half
     float s[4][4];
 #pragma unroll
     for (int n = 0; n < 4; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < KS; ++kk) {
+      uint32_t qa[4];  // q's A fragment of k-step kk
+      ldsm_x4(sm0 + swz(kQ0, q_row, 2 * kk + (lane >> 4)), qa[0], qa[1], qa[2], qa[3]);
 #pragma unroll
       for (int p = 0; p < 2; ++p) {  // keys 16p .. 16p + 15 of this warp's half: two 8-key tiles
         uint32_t b0, b1, b2, b3;
-        ldsm_x4(smem_u32(ks + (16 * p + (lane & 7) + 8 * (lane >> 4)) * RS + 16 * kk + 8 * ((lane >> 3) & 1)), b0,
-                b1, b2, b3);
-        mma_16816(s[2 * p], qa[kk], b0, b1);
-        mma_16816(s[2 * p + 1], qa[kk], b2, b3);
+        ldsm_x4(sm0 + swz(ks, kr0 + 16 * p + (lane & 7) + 8 * (lane >> 4), 2 * kk + ((lane >> 3) & 1)), b0, b1,
+                b2, b3);
+        mma_16816(s[2 * p], qa, b0, b1);
+        mma_16816(s[2 * p + 1], qa, b2, b3);
       }
     }
     // scores in base-2 units (scale * log2 e folded in): the softmax weights are exp2 of them
@@ -429,8 +437,8 @@ __global__ void __launch_bounds__(kMmaThreads) gqa_mma_kernel(
 #pragma unroll
       for (int dp = 0; dp < HD / 16; ++dp) {  // output columns 16dp .. 16dp + 15
         uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(smem_u32(vs + (16 * j + (lane & 7) + 8 * ((lane >> 3) & 1)) * RS + 16 * dp + 8 * (lane >> 4)), b0,
-                  b1, b2, b3);
+        ldsm_x4_t(sm0 + swz(vs, kr0 + 16 * j + (lane & 7) + 8 * ((lane >> 3) & 1), 2 * dp + (lane >> 4)), b0, b1,
+                  b2, b3);
         mma_16816(o[2 * dp], pa, b0, b1);
         mma_16816(o[2 * dp + 1], pa, b2, b3);
       }
@@ -541,17 +549,17 @@ struct GqaPlan {
   int row_blocks, chunk, n_splits;
 };
 
-// Key ranges: as many as keep every CTA in one wave of two per SM (both kernels fit two per
-// SM at head_dim 128), whole tiles per range, no empty range. Rounding the range count up
-// instead would leave a second, partial wave: 16 sequences x 8 KV heads at 3 ranges are 384
-// CTAs for 296 slots.
-GqaPlan gqa_plan(int batch, int block, int n_heads, int n_kv, int n_ctx) {
+// Key ranges: as many as keep every CTA in one wave of per_sm CTAs per SM (the CUDA-core
+// kernel fits two at head_dim 128, the tensor-core kernel three), whole tiles per range, no
+// empty range. Rounding the range count up instead would leave a second, partial wave:
+// 16 sequences x 8 KV heads at 3 ranges are 384 CTAs for 296 slots of two per SM.
+GqaPlan gqa_plan(int batch, int block, int n_heads, int n_kv, int n_ctx, int per_sm) {
   GqaPlan p;
   p.row_blocks = int(ceil_div(int64_t(n_heads / n_kv) * block, kRowBlock));
   const int64_t nk = int64_t(n_ctx) + block;
   const int64_t base = int64_t(batch) * n_kv * p.row_blocks;
   const int64_t tiles = ceil_div(nk, kKeyTile);
-  int64_t want = 2 * int64_t(num_sms()) / base;
+  int64_t want = int64_t(per_sm) * num_sms() / base;
   want = want < 1 ? 1 : (want > kMaxSplits ? kMaxSplits : want);
   if (want > tiles) want = tiles;
   const int64_t per = ceil_div(tiles, want);
@@ -608,7 +616,7 @@ size_t gqa_ws_bytes(int batch, int block, int n_heads, int head_dim, const GqaPl
   return rows * size_t(2 * p.n_splits) * (size_t(head_dim) + 2) * 4;
 }
 
-size_t gqa_mma_smem_bytes(int hd) { return size_t(kRowBlock + 2 * kMmaStages * kKeyTile) * (hd + 8) * 2; }
+size_t gqa_mma_smem_bytes(int hd) { return size_t(kRowBlock + 2 * kMmaStages * kKeyTile) * hd * 2; }
 
 template <int HD>
 int launch_gqa_mma(const void* q, const void* ctx_k, const void* ctx_v, int64_t sb, int64_t sh, int n_ctx,
@@ -669,7 +677,8 @@ extern "C" size_t dsm_gqa_attn_workspace_bytes(int batch, int block, int n_heads
                                                int n_ctx) {
   if (batch <= 0 || block <= 0 || n_kv <= 0 || n_heads <= 0 || n_heads % n_kv != 0 || n_ctx < 0 || head_dim <= 0)
     return 0;
-  return gqa_ws_bytes(batch, block, n_heads, head_dim, gqa_plan(batch, block, n_heads, n_kv, n_ctx));
+  // the larger of the two kernels' plans: the workspace serves either
+  return gqa_ws_bytes(batch, block, n_heads, head_dim, gqa_plan(batch, block, n_heads, n_kv, n_ctx, kMmaCtasPerSm));
 }
 
 extern "C" int dsm_gqa_attn(const void* q, const void* ctx_k, const void* ctx_v, int64_t ctx_batch_stride,
@@ -686,16 +695,16 @@ extern "C" int dsm_gqa_attn(const void* q, const void* ctx_k, const void* ctx_v,
   if (batch == 0) return DSM_OK;
   DSM_REQUIRE(q && blk_k && blk_v && out && ws && (n_ctx == 0 || (ctx_k && ctx_v)), "dsm_gqa_attn: NULL pointer");
   DSM_REQUIRE(aligned16(ws), "dsm_gqa_attn: workspace must be 16-byte aligned");
-  const GqaPlan p = gqa_plan(batch, block, n_heads, n_kv, n_ctx);
-  DSM_REQUIRE(int64_t(batch) * p.row_blocks <= 65535 && n_kv <= 65535, "dsm_gqa_attn: batch or n_kv too large");
-  const size_t need = gqa_ws_bytes(batch, block, n_heads, head_dim, p);
-  if (ws_bytes < need) return fail(DSM_ERR_WORKSPACE, "dsm_gqa_attn: workspace too small");
   const int64_t rows = int64_t(batch) * n_heads * block;
   const int64_t sb = n_ctx ? ctx_batch_stride : 0, sh = n_ctx ? ctx_head_stride : 0;
   // the mma kernel moves 16-byte chunks: every row and base it reads must sit on 16 bytes
   const bool mma = attn_kernel() == 0 && dtype == DSM_DT_BF16 &&
                    (head_dim == 64 || head_dim == 128) && aligned16(q) && aligned16(blk_k) && aligned16(blk_v) &&
                    (n_ctx == 0 || (aligned16(ctx_k) && aligned16(ctx_v) && sb % 8 == 0 && sh % 8 == 0));
+  const GqaPlan p = gqa_plan(batch, block, n_heads, n_kv, n_ctx, mma ? kMmaCtasPerSm : 2);
+  DSM_REQUIRE(int64_t(batch) * p.row_blocks <= 65535 && n_kv <= 65535, "dsm_gqa_attn: batch or n_kv too large");
+  const size_t need = gqa_ws_bytes(batch, block, n_heads, head_dim, p);
+  if (ws_bytes < need) return fail(DSM_ERR_WORKSPACE, "dsm_gqa_attn: workspace too small");
   const int n_parts = mma ? 2 * p.n_splits : p.n_splits;
   float* part = static_cast<float*>(ws);
   float* ml = part + rows * n_parts * int64_t(head_dim);
