@@ -26,8 +26,7 @@
 namespace dsm {
 namespace {
 
-constexpr int kWalkThreads = 256;
-constexpr int kWalkWarps = kWalkThreads / 32;
+constexpr int kWalkThreads = 256;  // the Markov head kernel's block; the walk gives each CTA at least this many words
 constexpr int kWalkCtaBound = 160;  // at least the SM count: sizes the candidate buffers
 constexpr size_t kWalkHeader = 256;
 
@@ -152,14 +151,14 @@ __device__ __forceinline__ void warp_best(const float (&bv)[MAXB], const int (&b
 }
 
 // the warps' candidates in sv/si combined: threads b < batch return row b's winner
-template <int MAXB>
+template <int MAXB, int WARPS>
 __device__ __forceinline__ void warps_best(int batch, float (*sv)[MAXB], int (*si)[MAXB], float& out_v, int& out_i) {
   __syncthreads();
   if (int(threadIdx.x) < batch) {
     const int b = threadIdx.x;
     float v = sv[0][b];
     int ix = si[0][b];
-    for (int w = 1; w < kWalkWarps; ++w)
+    for (int w = 1; w < WARPS; ++w)
       if (better(sv[w][b], si[w][b], v, ix)) {
         v = sv[w][b];
         ix = si[w][b];
@@ -169,7 +168,7 @@ __device__ __forceinline__ void warps_best(int batch, float (*sv)[MAXB], int (*s
   }
 }
 
-template <int MAXB>
+template <int MAXB, int WARPS>
 __device__ __forceinline__ void block_sum_b(const float (&s)[MAXB], int batch, float (*sv)[MAXB], float& out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
@@ -183,7 +182,7 @@ __device__ __forceinline__ void block_sum_b(const float (&s)[MAXB], int batch, f
   __syncthreads();
   if (int(threadIdx.x) < batch) {
     float v = 0.f;
-    for (int w = 0; w < kWalkWarps; ++w) v += sv[w][threadIdx.x];
+    for (int w = 0; w < WARPS; ++w) v += sv[w][threadIdx.x];
     out = v;
   }
 }
@@ -230,8 +229,9 @@ __host__ __device__ __forceinline__ int walk_e_floats(int batch, int rank, int m
   return f32 > bf ? f32 : bf;
 }
 
-template <int MAXB>
-__global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs a) {
+template <int MAXB, int THREADS>
+__global__ void __launch_bounds__(THREADS) head_walk_kernel(const WalkArgs a) {
+  constexpr int kWarps = THREADS / 32;
   extern __shared__ float sm[];
   const int B = a.batch, R = a.rank, V = a.vocab, S = a.block;
   // Markov embeddings of the previous tokens: [B][R] fp32, or [MAXB][R + 8] bf16 (tensor-core
@@ -240,8 +240,8 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
   float* li_sm = sm + walk_e_floats(B, R, MAXB);
   __shared__ int prev_s[MAXB];
   __shared__ float stat_m[MAXB], stat_z[MAXB];
-  __shared__ float sv[kWalkWarps][MAXB];
-  __shared__ int si[kWalkWarps][MAXB];
+  __shared__ float sv[kWarps][MAXB];
+  __shared__ int si[kWarps][MAXB];
   const int G = gridDim.x;
   const int v0 = blockIdx.x * a.slice, v1 = min(V, v0 + a.slice);
   const bool sampled = a.temperature > 0.f;
@@ -275,12 +275,12 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
   for (int i = 0; i < S; ++i) {
     if (use_mma) {
       const __nv_bfloat16* w1b = static_cast<const __nv_bfloat16*>(a.w1);
-      for (int k = threadIdx.x; k < NT * 8 * RP; k += kWalkThreads) {
+      for (int k = threadIdx.x; k < NT * 8 * RP; k += THREADS) {
         const int b = k / RP, r = k - b * RP;
         eb[k] = (b < B && r < R) ? w1b[int64_t(prev_s[b]) * R + r] : __float2bfloat16_rn(0.f);
       }
     } else {
-      for (int k = threadIdx.x; k < B * R; k += kWalkThreads) {
+      for (int k = threadIdx.x; k < B * R; k += THREADS) {
         const int b = k / R;
         e_sm[k] = wload(a.w1, a.w_bf16, int64_t(prev_s[b]) * R + (k - b * R));
       }
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
           bv2[nt][c] = -INFINITY;
           bi2[nt][c] = INT_MAX;
         }
-      for (int tile = warp; v0 + tile * 16 < v1; tile += kWalkWarps) {
+      for (int tile = warp; v0 + tile * 16 < v1; tile += kWarps) {
         const int ra = v0 + tile * 16 + g, rb = ra + 8;
         const bool oka = ra < v1, okb = rb < v1;
         // The tile's base logits and its Markov rows for up to 256 rank entries are all
@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
         best[b] = -INFINITY;
         bidx[b] = INT_MAX;
       }
-      for (int v = v0 + threadIdx.x; v < v1; v += kWalkThreads) {
+      for (int v = v0 + threadIdx.x; v < v1; v += THREADS) {
         float acc[MAXB];
 #pragma unroll
         for (int b = 0; b < MAXB; ++b) acc[b] = 0.f;
@@ -429,14 +429,14 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
     }
     float cv = 0.f;
     int ci = 0;
-    warps_best<MAXB>(B, sv, si, cv, ci);
+    warps_best<MAXB, kWarps>(B, sv, si, cv, ci);
     if (int(threadIdx.x) < B) {
       a.cand_v[(int64_t(buf) * G + blockIdx.x) * B + threadIdx.x] = cv;
       a.cand_i[(int64_t(buf) * G + blockIdx.x) * B + threadIdx.x] = ci;
       __threadfence();
     }
     if (!walk_sync(a, gen)) return;
-    for (int b = warp; b < B; b += kWalkWarps) {  // every CTA takes the same winner
+    for (int b = warp; b < B; b += kWarps) {  // every CTA takes the same winner
       float v;
       int ix;
       combine_best(a, buf, b, v, ix);
@@ -454,20 +454,20 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
       float sum[MAXB];
 #pragma unroll
       for (int b = 0; b < MAXB; ++b) sum[b] = 0.f;
-      for (int v = v0 + threadIdx.x; v < v1; v += kWalkThreads)
+      for (int v = v0 + threadIdx.x; v < v1; v += THREADS)
 #pragma unroll
         for (int b = 0; b < MAXB; ++b) {
           if (b >= B) break;
           sum[b] += expf(li_sm[b * a.slice + (v - v0)] / tp - stat_m[b]);
         }
       float bs = 0.f;
-      block_sum_b<MAXB>(sum, B, sv, bs);
+      block_sum_b<MAXB, kWarps>(sum, B, sv, bs);
       if (int(threadIdx.x) < B) {
         a.cand_v[(int64_t(buf) * G + blockIdx.x) * B + threadIdx.x] = bs;
         __threadfence();
       }
       if (!walk_sync(a, gen)) return;
-      for (int b = warp; b < B; b += kWalkWarps) {
+      for (int b = warp; b < B; b += kWarps) {
         const float z = combine_sum(a, buf, b);
         if (lane == 0) stat_z[b] = z;
       }
@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
         best[b] = -INFINITY;
         bidx[b] = INT_MAX;
       }
-      for (int v = v0 + threadIdx.x; v < v1; v += kWalkThreads)
+      for (int v = v0 + threadIdx.x; v < v1; v += THREADS)
 #pragma unroll
         for (int b = 0; b < MAXB; ++b) {
           if (b >= B) break;
@@ -494,14 +494,14 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
           }
         }
       warp_best<MAXB>(best, bidx, B, sv, si);
-      warps_best<MAXB>(B, sv, si, cv, ci);
+      warps_best<MAXB, kWarps>(B, sv, si, cv, ci);
       if (int(threadIdx.x) < B) {
         a.cand_v[(int64_t(buf) * G + blockIdx.x) * B + threadIdx.x] = cv;
         a.cand_i[(int64_t(buf) * G + blockIdx.x) * B + threadIdx.x] = ci;
         __threadfence();
       }
       if (!walk_sync(a, gen)) return;
-      for (int b = warp; b < B; b += kWalkWarps) {
+      for (int b = warp; b < B; b += kWarps) {
         float v;
         int ix;
         combine_best(a, buf, b, v, ix);
@@ -519,7 +519,7 @@ __global__ void __launch_bounds__(kWalkThreads) head_walk_kernel(const WalkArgs 
 
   // confidence (CTA 0): hidden half from hc_head_norm plus the Markov half, w1[tok] . wc_r
   if (blockIdx.x == 0 && a.confidence) {
-    for (int p = warp; p < B * S; p += kWalkWarps) {
+    for (int p = warp; p < B * S; p += kWarps) {
       const int b = p / S, i = p - b * S;
       const int tok = a.out_ids[int64_t(b) * (S + 1) + i];
       float s = 0.f;
@@ -624,17 +624,20 @@ int launch_walk(const WalkArgs& a0, void* walk_ws, cudaStream_t s) {
   const size_t smem =
       (size_t(walk_e_floats(a.batch, a.rank, maxb)) + (a.temperature > 0.f ? size_t(a.batch) * a.slice : 0)) * 4;
   void* args[] = {&a};
-  auto go = [&](auto kern) {
+  auto go = [&](auto kern, int threads) {
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
       return check_launch("draft head walk smem attribute");
-    if (cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kern), dim3(G), dim3(kWalkThreads), args, smem, s) !=
+    if (cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kern), dim3(G), dim3(threads), args, smem, s) !=
         cudaSuccess)
       return check_launch("draft head walk (cooperative launch)");
     return check_launch("draft head walk");
   };
-  if (a.batch <= 8) return go(head_walk_kernel<8>);
-  return go(head_walk_kernel<32>);
+  // up to 8 batch rows: 16 warps per CTA (128 registers each), twice the Markov-row and logit
+  // loads in flight of 8 warps, which left the walk waiting on L2; the 32-row form needs its
+  // registers at 8 warps
+  if (a.batch <= 8) return go(head_walk_kernel<8, 512>, 512);
+  return go(head_walk_kernel<32, 256>, 256);
 }
 
 }  // namespace
