@@ -992,7 +992,7 @@ def run_head(args):
                                                        hp.packed.data_ptr(), vocab, out.data_ptr(), vocab, n, sp)))
         k_bytes = hp.nbytes + n * dim * 2 + n * vocab * 4
         achieved = k_bytes / (k_ms * 1e-3) / 1e9
-        roofline = {"bound": "hbm", "kernel": "expert_kernel<f16, down> (LM head, weight streaming)",
+        roofline = {"bound": "hbm", "kernel": "expert_tc_kernel<f16, down> (LM head over 56 rows, tcgen05)",
                     "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                     "peak_kind": peak_kind, "frac_of_8tbs": achieved / SPEC_HBM_GBS,
                     "algorithmic_bytes_per_launch": k_bytes, "launch_ms": k_ms, "traffic": None}
@@ -1405,7 +1405,7 @@ def run_dsattn(args):
                                                        pm.packed.data_ptr(), pm.rows, out.data_ptr(), pm.rows, n, sp)))
         k_bytes = pm.nbytes + n * k * 2 + n * pm.rows * 4
         achieved = k_bytes / (k_ms * 1e-3) / 1e9
-        roofline = {"bound": "hbm", "kernel": "expert_kernel<f16, down> (wq_b, weight streaming)",
+        roofline = {"bound": "hbm", "kernel": "expert_tc_kernel<f16, down> (wq_b over 56 rows, tcgen05)",
                     "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                     "peak_kind": peak_kind, "frac_of_8tbs": achieved / SPEC_HBM_GBS,
                     "algorithmic_bytes_per_launch": k_bytes, "launch_ms": k_ms, "traffic": None}

@@ -403,13 +403,18 @@ thread_local int g_regime = 0;
 
 // The tcgen05 kernel pays off once an expert's weight tile is reused by many rows: with
 // 128-row MMA tiles, from about 64 rows per busy expert on average.
-bool use_tc(int wfmt, int64_t n_rows, int n_experts) {
+// min_rows: rows per busy expert from which the tcgen05 kernel runs. A single matrix with
+// many row tiles (dsm_linear: an LM head, a wide projection) switches above 32 rows: there
+// the streaming kernel needs its eight-tile units, whose mma.sync work per weight byte is
+// the bound (measured on a 129,280 x 4096 bf16 LM head: 32 rows streaming 182 us, 56 rows
+// streaming 315 us, 64 rows on tcgen05 235 us).
+bool use_tc(int wfmt, int64_t n_rows, int n_experts, int min_rows = 64) {
   if (!tc_supports(wfmt)) return false;
   const int r = g_regime;
   if (r == 1) return false;
   if (r == 2) return true;
   const int64_t busy = std::max<int64_t>(1, std::min<int64_t>(n_rows, n_experts));
-  return n_rows >= 64 * busy;
+  return n_rows >= int64_t(min_rows) * busy;
 }
 
 int check_common(int wfmt, int group_size, const int32_t* offsets, int n_experts) {
@@ -516,7 +521,7 @@ extern "C" int dsm_linear(const void* x_staged, const float* x_row_scale, int64_
   if (tm_supports(wfmt))
     return expert_tm_down(wfmt, group_size, x_staged, 1.f, rows_cap, k_dim, nullptr, 1, w_packed, out_dim, 0, o_rows,
                           ldo, nullptr, n_rows, stream, x_row_scale);
-  if (use_tc(wfmt, n_rows, 1))
+  if (use_tc(wfmt, n_rows, 1, 33))
     return expert_tc_down(wfmt, x_staged, 1.f, rows_cap, k_dim, nullptr, 1, w_packed, out_dim, 0, o_rows, ldo, nullptr,
                           n_rows, stream, x_row_scale);
   ExpertArgs a{};
