@@ -50,6 +50,11 @@ int expert_tc_gate_up(int wfmt, const void* x_staged, const float* x_row_scale, 
 int expert_tc_down(int wfmt, const void* h_staged, float h_scale, int64_t rows_cap, int inter, const int32_t* offsets,
                    int n_experts, const void* w2, int dim, int round_o, float* o_rows, int ldo,
                    const int32_t* o_row_map, int64_t n_rows, void* stream, const float* x_row_scale = nullptr);
+// the single-matrix (grouped) product with K split into k_splits ranges of k_per 128-K chunks,
+// fp32 partial slabs parts[split][n_rows][out_dim] in staged-row order
+int expert_tc_split(int wfmt, const void* x_staged, const float* x_row_scale, int64_t rows_cap, int k_dim,
+                    const int32_t* offsets, int n_groups, const void* w_packed, int out_dim, int64_t n_rows,
+                    int k_splits, int k_per, float* parts, void* stream);
 // fp4 and affine experts at every token count (expert_tm.cu): weights dequantised into
 // tensor memory
 bool tm_supports(int wfmt);

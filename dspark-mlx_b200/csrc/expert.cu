@@ -589,20 +589,28 @@ int expert_stream_split(int wfmt, int group_size, const void* x_staged, const fl
                         int k_dim, const int32_t* offsets, int n_groups, const void* w_packed, int out_dim,
                         int64_t n_rows, int max_splits, float* parts, void* stream, int* splits_used) {
   *splits_used = 1;
-  if ((wfmt != DSM_WFMT_F16 && wfmt != DSM_WFMT_FP8_B128) || n_rows <= 0 || use_tc(wfmt, n_rows, n_groups))
-    return DSM_OK;
+  if ((wfmt != DSM_WFMT_F16 && wfmt != DSM_WFMT_FP8_B128) || n_rows <= 0) return DSM_OK;
   const int rt = int(ceil_div(out_dim, kTileRows)), kcs = int(ceil_div(k_dim, kChunkK));
   const int64_t busy = std::max<int64_t>(1, std::min<int64_t>(n_rows, n_groups));
   const double avg = double(n_rows) / double(busy);
-  // the narrowest unit holding a group's rows: each weight tile is then streamed once per K
-  // range, and the K ranges, not row chunks, fill the SMs
+  // Above 32 rows per group the tcgen05 kernel takes the ranges (units of up to 256 rows);
+  // below, the streaming kernel in the narrowest unit holding a group's rows. Either way each
+  // weight tile is streamed once per K range, and the K ranges, not row chunks, fill the SMs.
+  const bool tc = use_tc(wfmt, n_rows, n_groups, 33);
   const int nt = avg <= 8.0 ? 1 : (avg <= 16.0 ? 2 : (avg <= 32.0 ? 4 : 8));
-  const int64_t units = busy * int64_t(std::ceil(avg / (8.0 * nt))) * rt;
+  const double unit_rows = tc ? 256.0 : 8.0 * nt;
+  const int64_t units = busy * int64_t(std::ceil(avg / unit_rows)) * rt;
   int splits = int(std::min<int64_t>({int64_t(max_splits), int64_t(kcs), int64_t(persistent_ctas()) / units}));
   if (splits <= 1) return DSM_OK;
   const int k_per = int(ceil_div(kcs, splits));
   splits = int(ceil_div(kcs, k_per));  // no empty range
   if (splits <= 1) return DSM_OK;
+  if (tc) {
+    const int rc = expert_tc_split(wfmt, x_staged, x_row_scale, rows_cap, k_dim, offsets, n_groups, w_packed, out_dim,
+                                   n_rows, splits, k_per, parts, stream);
+    if (rc == DSM_OK) *splits_used = splits;
+    return rc;
+  }
   ExpertArgs a{};
   a.wa = static_cast<const uint8_t*>(w_packed);
   a.wb = nullptr;

@@ -108,6 +108,18 @@ struct TcArgs {
   const int32_t* o_row_map;
   int ldo;
   int round_o;
+  // single-matrix, unpaired product only: K ranges per (row tile, row chunk), each writing an
+  // fp32 partial slab o_out + split * o_split_stride (rows [n_rows][ldo], staged-row order, no
+  // row map or rounding); 0 or 1 = no split. k_per: 128-K chunks per range.
+  int k_splits;
+  int k_per;
+  int64_t o_split_stride;
+};
+
+// Unit u's place: expert e, row tile rt, row chunk, K range ksp covering 64-K stages
+// [ks0, ks1). K ranges sit between the row tiles and the row chunks.
+struct TcUnit {
+  int e, rt, chunk, ksp, ks0, ks1;
 };
 
 __device__ __forceinline__ int tc_group_first(const TcArgs& a, int e) { return a.offsets ? a.offsets[e] : 0; }
@@ -186,7 +198,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
       int v = 0;
       if (e < E) {
         const int cnt = tc_group_count(a, e);
-        v = cnt > 0 ? rtu * ((cnt + BN - 1) / BN) : 0;
+        v = cnt > 0 ? rtu * ((cnt + BN - 1) / BN) * (a.k_splits > 1 ? a.k_splits : 1) : 0;
       }
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -205,7 +217,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
   const int64_t hdr_bytes = ceil_div(int64_t(E) * 4, kPackHeader) * kPackHeader;
   const int tile_b = tile_bytes(FMT, 0);
   const uint8_t* tiles[2] = {a.wa + hdr_bytes, DUAL ? a.wb + hdr_bytes : a.wa + hdr_bytes};
-  const int nks = 2 * a.kc_count;  // 64-wide K stages per unit
+  const int nks = 2 * a.kc_count;  // 64-wide K stages per unsplit unit
+  const int nsp = a.k_splits > 1 ? a.k_splits : 1;
+  auto unit = [&](int u) {
+    TcUnit w;
+    w.e = tc_find_expert(pre, E, u);
+    const int nch = (tc_group_count(a, w.e) + BN - 1) / BN;
+    const int local = u - pre[w.e];
+    w.rt = local / (nch * nsp);
+    const int r2 = local % (nch * nsp);
+    w.chunk = r2 % nch;
+    w.ksp = r2 / nch;
+    w.ks0 = nsp > 1 ? 2 * w.ksp * a.k_per : 0;
+    w.ks1 = nsp > 1 ? min(nks, w.ks0 + 2 * a.k_per) : nks;
+    return w;
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
@@ -215,15 +241,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
       uint32_t ph = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-        const int e = tc_find_expert(pre, E, u);
-        const int cnt = tc_group_count(a, e);
-        const int nch = (cnt + BN - 1) / BN;
-        const int local = u - pre[e];
-        const int rt = local / nch, chunk = local % nch;
-        const int row0 = tc_group_first(a, e) + chunk * BN;
+        const TcUnit w = unit(u);
+        const int e = w.e, rt = w.rt;
+        const int row0 = tc_group_first(a, e) + w.chunk * BN;
         // first row tile of the unit: rt (gate/up pair, both matrices) or 2 rt, 2 rt + 1 (PAIR)
         const int64_t tile0 = (int64_t(e) * a.rt_count + (PAIR ? 2 * rt : rt)) * a.kc_count;
-        for (int ks = 0; ks < nks; ++ks) {
+        for (int ks = w.ks0; ks < w.ks1; ++ks) {
           if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u)) {
             *abort_flag = 1;
             ok = false;
@@ -256,11 +279,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
       bool ok = true;
       int j = 0;
       for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++j) {
-        const int e = tc_find_expert(pre, E, u);
-        const int cnt = tc_group_count(a, e);
-        const int nch = (cnt + BN - 1) / BN;
-        const int chunk = (u - pre[e]) % nch;
-        const int rows = min(BN, cnt - chunk * BN);
+        const TcUnit w = unit(u);
+        const int rows = min(BN, tc_group_count(a, w.e) - w.chunk * BN);
         const int n_mma = min(BN, (rows + 15) / 16 * 16);
         const uint32_t idesc = umma_idesc_f16(kTcM, n_mma);
         const int buf = j % C::kNBuf;
@@ -270,7 +290,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
           break;
         }
         tc_fence_after();
-        for (int ks = 0; ks < nks; ++ks) {
+        for (int ks = w.ks0; ks < w.ks1; ++ks) {
           if (*abort_flag || !mbar_wait(&conv[ab], aph) || !mbar_wait(&full[s], ph)) {
             *abort_flag = 1;
             ok = false;
@@ -286,7 +306,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
             for (int m = 0; m < NM; ++m) {
               const uint64_t adesc = umma_desc_sw128(sa + m * kABytes) + uint64_t(kk * 2);
               const uint32_t d = tmem + uint32_t((buf * NM + m) * BN);
-              umma_f16(d, adesc, bdesc, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+              umma_f16(d, adesc, bdesc, idesc, (ks > w.ks0 || kk > 0) ? 1u : 0u);
             }
           }
           umma_commit(&empty[s]);    // load slot free once these MMAs have read B (the
@@ -315,7 +335,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
     uint32_t ph = 0, aph = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x) {
       bool ok = true;
-      for (int ks = 0; ks < nks; ++ks) {
+      const TcUnit w = unit(u);
+      for (int ks = w.ks0; ks < w.ks1; ++ks) {
         // the stage's codes have landed, and the MMAs two stages back have released A slot ab
         if (*abort_flag || !mbar_wait(&full[s], ph) || !mbar_wait(&aempty[ab], aph ^ 1u)) {
           *abort_flag = 1;
@@ -403,13 +424,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
     const int rloc = 32 * sp + lane;
     int j = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x, ++j) {
-      const int e = tc_find_expert(pre, E, u);
+      const TcUnit w = unit(u);
+      const int e = w.e, rt = w.rt, chunk = w.chunk;
       const int off = tc_group_first(a, e);
-      const int cnt = tc_group_count(a, e);
-      const int nch = (cnt + BN - 1) / BN;
-      const int local = u - pre[e];
-      const int rt = local / nch, chunk = local % nch;
-      const int rows = min(BN, cnt - chunk * BN);
+      const int rows = min(BN, tc_group_count(a, e) - chunk * BN);
       const int buf = j % C::kNBuf;
       if (*abort_flag || !mbar_wait_backoff(&tfull[buf], (j / C::kNBuf) & 1, 200)) {
         *abort_flag = 1;
@@ -467,6 +485,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
               const float xs = __shfl_sync(0xffffffffu, xs_b, i);
               const int orow = __shfl_sync(0xffffffffu, or_b, i);
               float v = __uint_as_float(m ? uv[i] : gv[i]) * xs * wmul_a;
+              if (nsp > 1) {  // a partial of the K range, in staged-row order: the split sum rounds
+                if (cb + i < rows && d < a.out_rows)
+                  a.o_out[int64_t(w.ksp) * a.o_split_stride + int64_t(off + chunk * BN + cb + i) * a.ldo + d] = v;
+                continue;
+              }
               v = a.round_o ? bf16_round(v) : v;
               if (cb + i < rows && d < a.out_rows) a.o_out[int64_t(orow) * a.ldo + d] = v;
             }
@@ -588,6 +611,31 @@ int expert_tc_down(int wfmt, const void* h_staged, float h_scale, int64_t rows_c
   // two load slots, and the shared expert's down product measured slower that way.
   if (a.rt_count % 2 == 0) return launch_tc<DSM_WFMT_FP8_B128, false, true>(a, h_staged, rows_cap, as_stream(stream));
   return launch_tc<DSM_WFMT_FP8_B128, false>(a, h_staged, rows_cap, as_stream(stream));
+}
+
+int expert_tc_split(int wfmt, const void* x_staged, const float* x_row_scale, int64_t rows_cap, int k_dim,
+                    const int32_t* offsets, int n_groups, const void* w_packed, int out_dim, int64_t n_rows,
+                    int k_splits, int k_per, float* parts, void* stream) {
+  TcArgs a{};
+  a.wa = static_cast<const uint8_t*>(w_packed);
+  a.wb = nullptr;
+  a.act_scale = x_row_scale;
+  a.act_scale_const = 1.f;
+  a.offsets = offsets;
+  a.n_rows = n_rows;
+  a.n_experts = n_groups;
+  a.out_rows = out_dim;
+  a.rt_count = int(ceil_div(out_dim, kTcM));
+  a.kc_count = int(ceil_div(k_dim, kChunkK));
+  a.o_out = parts;
+  a.o_row_map = nullptr;
+  a.ldo = out_dim;
+  a.round_o = 0;
+  a.k_splits = k_splits;
+  a.k_per = k_per;
+  a.o_split_stride = n_rows * int64_t(out_dim);
+  if (wfmt == DSM_WFMT_F16) return launch_tc<DSM_WFMT_F16, false>(a, x_staged, rows_cap, as_stream(stream));
+  return launch_tc<DSM_WFMT_FP8_B128, false>(a, x_staged, rows_cap, as_stream(stream));
 }
 
 }  // namespace dsm
