@@ -69,7 +69,6 @@ struct ExpertArgs {
   int k_per;
   int64_t o_split_stride;
 };
-__host__ __device__ __forceinline__ int n_ksplit(const ExpertArgs& a) { return a.k_splits > 1 ? a.k_splits : 1; }
 
 // rows [first, first + count) of group e (offsets == NULL: one group holding every row)
 __device__ __forceinline__ int group_first(const ExpertArgs& a, int e) { return a.offsets ? a.offsets[e] : 0; }
@@ -90,8 +89,11 @@ __device__ __forceinline__ int find_expert(const int* pre, int n_experts, int u)
   return lo;
 }
 
-template <int FMT, bool DUAL, int NT>
+// SPLIT: the single-matrix product over K ranges (k_splits, k_per), each unit writing an fp32
+// partial slab; a separate instance, so the unsplit kernels keep their code as it was.
+template <int FMT, bool DUAL, int NT, bool SPLIT = false>
 __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a, int n_stages) {
+  static_assert(!(SPLIT && DUAL), "K split: single-matrix products only");
   constexpr int BN = 8 * NT;
   constexpr int NM = DUAL ? 2 : 1;
   static_assert(FMT == DSM_WFMT_F16 || FMT == DSM_WFMT_FP8_B128, "f16 and fp8 tiles only");
@@ -125,7 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
       int v = 0;
       if (e < E) {
         const int cnt = group_count(a, e);
-        v = cnt > 0 ? a.rt_count * ((cnt + BN - 1) / BN) * n_ksplit(a) : 0;
+        v = cnt > 0 ? a.rt_count * ((cnt + BN - 1) / BN) * (SPLIT ? a.k_splits : 1) : 0;
       }
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -157,10 +159,11 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
         const int cnt = group_count(a, e);
         const int nch = (cnt + BN - 1) / BN;
         const int local = u - pre[e];
-        const int rt = local / (nch * n_ksplit(a)), r2 = local % (nch * n_ksplit(a));
+        const int nsp = SPLIT ? a.k_splits : 1;
+        const int rt = local / (nch * nsp), r2 = local % (nch * nsp);
         const int chunk = r2 % nch;
-        const int kc0 = a.k_splits > 1 ? (r2 / nch) * a.k_per : 0;
-        const int kc1 = a.k_splits > 1 ? min(a.kc_count, kc0 + a.k_per) : a.kc_count;
+        const int kc0 = SPLIT ? (r2 / nch) * a.k_per : 0;
+        const int kc1 = SPLIT ? min(a.kc_count, kc0 + a.k_per) : a.kc_count;
         const int64_t row0 = int64_t(group_first(a, e)) + int64_t(chunk) * BN;
         const int64_t tile0 = (int64_t(e) * a.rt_count + rt) * a.kc_count;
         for (int kc = kc0; kc < kc1; ++kc) {
@@ -199,10 +202,11 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
     const int cnt = group_count(a, e);
     const int nch = (cnt + BN - 1) / BN;
     const int local = u - pre[e];
-    const int rt = local / (nch * n_ksplit(a)), r2 = local % (nch * n_ksplit(a));
+    const int nsp = SPLIT ? a.k_splits : 1;
+    const int rt = local / (nch * nsp), r2 = local % (nch * nsp);
     const int chunk = r2 % nch, ks = r2 / nch;
-    const int kc0 = a.k_splits > 1 ? ks * a.k_per : 0;
-    const int kc1 = a.k_splits > 1 ? min(a.kc_count, kc0 + a.k_per) : a.kc_count;
+    const int kc0 = SPLIT ? ks * a.k_per : 0;
+    const int kc1 = SPLIT ? min(a.kc_count, kc0 + a.k_per) : a.kc_count;
 
     float acc[NM][kMt][NT][4];
     float tmp[kTmp ? NM : 1][kMt][NT][4];
@@ -330,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
             const int d = rt * kTileRows + rloc;
             if (d >= a.out_rows) continue;
             float v = acc[0][i][j][c] * xs * wmul_a;
-            if (a.k_splits > 1) {  // a partial of the K range: summed and rounded by the split sum
+            if constexpr (SPLIT) {  // a partial of the K range: summed and rounded by the split sum
               a.o_out[int64_t(ks) * a.o_split_stride + r * a.ldo + d] = v;
               continue;
             }
@@ -342,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const ExpertArgs a,
   }
 }
 
-template <int FMT, bool DUAL, int NT>
+template <int FMT, bool DUAL, int NT, bool SPLIT = false>
 int launch_expert(const ExpertArgs& a, cudaStream_t stream) {
   const int tile_b = tile_bytes(FMT, a.group_size);
   const int act_b = 8 * NT * kStagePitch * 2;
@@ -351,7 +355,7 @@ int launch_expert(const ExpertArgs& a, cudaStream_t stream) {
   int n_stages = std::min(8, budget / stage_b);
   if (n_stages < 2) return fail(DSM_ERR_UNSUPPORTED, "expert kernel: tile too large for the shared-memory ring");
   const size_t smem = size_t(n_stages) * stage_b + size_t(2 * n_stages) * 8 + size_t(a.n_experts + 2) * 4;
-  auto kern = expert_kernel<FMT, DUAL, NT>;
+  auto kern = expert_kernel<FMT, DUAL, NT, SPLIT>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return check_launch("expert kernel smem attribute");
   kern<<<persistent_ctas(), kThreads, smem, stream>>>(a, n_stages);
@@ -363,11 +367,22 @@ int dispatch(int wfmt, int nt, const ExpertArgs& a, cudaStream_t s) {
 #define DSM_NT_CASES(F)                                    \
   if (nt == 1) return launch_expert<F, DUAL, 1>(a, s);     \
   if (nt == 2) return launch_expert<F, DUAL, 2>(a, s);     \
-  if (nt == 4) return launch_expert<F, DUAL, 4>(a, s);     \
-  if constexpr (DUAL && F == DSM_WFMT_FP8_B128)            \
-    return launch_expert<F, DUAL, 4>(a, s);                \
-  else                                                     \
-    return launch_expert<F, DUAL, 8>(a, s);
+  return launch_expert<F, DUAL, 4>(a, s);
+  switch (wfmt) {
+    case DSM_WFMT_F16: { DSM_NT_CASES(DSM_WFMT_F16) }
+    case DSM_WFMT_FP8_B128: { DSM_NT_CASES(DSM_WFMT_FP8_B128) }
+    default: return fail(DSM_ERR_INVALID_ARGUMENT, "expert kernel: unknown weight format");
+  }
+#undef DSM_NT_CASES
+}
+
+// the K-split instances: single matrix, up to eight n8 tiles (a group's rows whole)
+int dispatch_split(int wfmt, int nt, const ExpertArgs& a, cudaStream_t s) {
+#define DSM_NT_CASES(F)                                          \
+  if (nt == 1) return launch_expert<F, false, 1, true>(a, s);    \
+  if (nt == 2) return launch_expert<F, false, 2, true>(a, s);    \
+  if (nt == 4) return launch_expert<F, false, 4, true>(a, s);    \
+  return launch_expert<F, false, 8, true>(a, s);
   switch (wfmt) {
     case DSM_WFMT_F16: { DSM_NT_CASES(DSM_WFMT_F16) }
     case DSM_WFMT_FP8_B128: { DSM_NT_CASES(DSM_WFMT_FP8_B128) }
@@ -382,14 +397,15 @@ int dispatch(int wfmt, int nt, const ExpertArgs& a, cudaStream_t s) {
 // with few busy experts (the shared expert is one group holding every token) narrower
 // tiles give more work units, and the re-reads of a tile are served from L2. The grid is
 // this launch's persistent grid: a slice of the SMs when the shared expert runs beside the
-// routed products, where wider tiles (fewer re-reads per SM) win. Eight n8 tiles (64 rows)
-// serve one large matrix over a whole draft step's rows, such as the draft head's LM head
-// (56 rows over 1,010 row tiles), whose weight tiles are then streamed once instead of once
-// per 32-row chunk. The fp8 gate/up pair stops at four: eight would spill registers.
+// routed products, where wider tiles (fewer re-reads per SM) win. Four n8 tiles at most:
+// eight-tile units are bound by their mma.sync work per weight byte (a 56-row LM head ran
+// 0.344 ms in 32-row units, 0.311 ms in 64-row units and 0.231 ms on the tcgen05 kernel), so
+// single matrices above 32 rows take the tcgen05 kernel (dsm_linear), and eight-tile units
+// serve only the K-split products when the tcgen05 kernel is switched off.
 int pick_nt(int64_t n_rows, int n_experts, int rt_count) {
   const int64_t busy = std::max<int64_t>(1, std::min<int64_t>(n_rows, n_experts));
   const double avg = double(n_rows) / double(busy);
-  int nt = avg <= 8.0 ? 1 : (avg <= 16.0 ? 2 : (avg <= 32.0 ? 4 : 8));
+  int nt = avg <= 8.0 ? 1 : (avg <= 16.0 ? 2 : 4);
   while (nt > 1) {
     const int64_t units = busy * int64_t(std::ceil(avg / (8.0 * nt))) * rt_count;
     if (units >= 2 * int64_t(persistent_ctas())) break;
@@ -632,7 +648,7 @@ int expert_stream_split(int wfmt, int group_size, const void* x_staged, const fl
   a.k_splits = splits;
   a.k_per = k_per;
   a.o_split_stride = n_rows * int64_t(out_dim);
-  const int rc = dispatch<false>(wfmt, nt, a, as_stream(stream));
+  const int rc = dispatch_split(wfmt, nt, a, as_stream(stream));
   if (rc == DSM_OK) *splits_used = splits;
   return rc;
 }
