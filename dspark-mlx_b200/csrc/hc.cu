@@ -78,7 +78,28 @@ __global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(const T* __rest
   float acc[MIX + 1];
 #pragma unroll
   for (int i = 0; i <= MIX; ++i) acc[i] = 0.f;
-  for (int k = threadIdx.x; k < hcd; k += kHcThreads) {
+  // kU of the thread's columns per step: all their loads (x and the MIX projection rows,
+  // which stay in L2 across tokens) are issued before the multiply-adds, so a step waits on
+  // one L2 round trip instead of kU; the adds keep the thread's column order.
+  constexpr int kU = 4;
+  int k = threadIdx.x;
+  for (; k + (kU - 1) * kHcThreads < hcd; k += kU * kHcThreads) {
+    float v[kU], f[kU][MIX];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int ku = k + u * kHcThreads;
+      v[u] = to_f(xt[ku]);
+#pragma unroll
+      for (int j = 0; j < MIX; ++j) f[u][j] = fn[int64_t(j) * hcd + ku];
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      acc[MIX] = fmaf(v[u], v[u], acc[MIX]);
+#pragma unroll
+      for (int j = 0; j < MIX; ++j) acc[j] = fmaf(v[u], f[u][j], acc[j]);
+    }
+  }
+  for (; k < hcd; k += kHcThreads) {
     const float v = to_f(xt[k]);
     acc[MIX] = fmaf(v, v, acc[MIX]);
 #pragma unroll
