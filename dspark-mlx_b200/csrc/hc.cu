@@ -233,7 +233,26 @@ __global__ void __launch_bounds__(kHcThreads) hc_head_norm_kernel(const T* __res
   float acc[HC + 1];
 #pragma unroll
   for (int i = 0; i <= HC; ++i) acc[i] = 0.f;
-  for (int k = threadIdx.x; k < hcd; k += kHcThreads) {
+  // as in hc_pre_norm_kernel: kU columns' loads in flight per step, adds in column order
+  constexpr int kU = 8;
+  int k = threadIdx.x;
+  for (; k + (kU - 1) * kHcThreads < hcd; k += kU * kHcThreads) {
+    float v[kU], f[kU][HC];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int ku = k + u * kHcThreads;
+      v[u] = to_f(xt[ku]);
+#pragma unroll
+      for (int j = 0; j < HC; ++j) f[u][j] = fn[int64_t(j) * hcd + ku];
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      acc[HC] = fmaf(v[u], v[u], acc[HC]);
+#pragma unroll
+      for (int j = 0; j < HC; ++j) acc[j] = fmaf(v[u], f[u][j], acc[j]);
+    }
+  }
+  for (; k < hcd; k += kHcThreads) {
     const float v = to_f(xt[k]);
     acc[HC] = fmaf(v, v, acc[HC]);
 #pragma unroll
