@@ -183,3 +183,28 @@ def test_grouped_linear_rejects_bad_arguments_on_the_host():
     assert L.dsm_grouped_linear(1, 1, 1 << 10, 512, _lib.WFMT_F16, 0, 1, 4, 1, 256, 1, 128, None, 224, None) != 0
     assert L.dsm_grouped_linear(1, 1, 1 << 10, 512, 9, 0, 1, 4, 1, 256, 1, 256, None, 224, None) != 0
     assert L.dsm_last_error_message().decode()
+
+
+def test_split_linear_entry_points_reject_bad_arguments_on_the_host():
+    """The K-split products check their shapes and pointers before touching the GPU."""
+    L = _lib.lib()
+    f16 = _lib.WFMT_F16
+    cases = [
+        # ldo below out_dim
+        lambda: L.dsm_grouped_linear_splitk(1, 1, 128, 512, f16, 0, 1, 4, 1, 256, 1, 128, None, 56, None, 0, None),
+        # no offsets for the groups
+        lambda: L.dsm_grouped_linear_splitk(1, 1, 128, 512, f16, 0, 1, 4, None, 256, 1, 256, None, 56, None, 0,
+                                            None),
+        # NULL weights
+        lambda: L.dsm_grouped_linear_splitk(1, 1, 128, 512, f16, 0, None, 4, 1, 256, 1, 256, None, 56, None, 0,
+                                            None),
+        # too many groups
+        lambda: L.dsm_grouped_linear_splitk(1, 1, 128, 512, f16, 0, 1, 5000, 1, 256, 1, 256, None, 56, None, 0,
+                                            None),
+        # ldo below out_dim
+        lambda: L.dsm_linear_splitk(1, 1, 128, 512, f16, 0, 1, 256, 1, 128, 56, None, 0, None),
+    ]
+    for i, call in enumerate(cases):
+        assert call() != 0, i
+        assert L.dsm_last_error_message().decode()
+    assert L.dsm_linear_splitk_workspace_bytes(56, 4096) == 8 * 56 * 4096 * 4
