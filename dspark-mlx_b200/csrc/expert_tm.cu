@@ -54,19 +54,23 @@ constexpr int kTmProducer = 4;
 constexpr int kTmConv0 = 8;       // first converter warp (a multiple of 4: warp % 4 = TMEM sub-partition)
 constexpr int kTmBoxRows = 16;
 
-template <int FMT, bool DUAL, int BN, int CW, int P>
+// PAIR: the single-matrix (down) product over two adjacent row tiles per unit, built like the
+// gate/up pair (two A matrices, one activation tile per stage feeding both), so each staged
+// activation tile serves 256 weight rows instead of 128.
+template <int FMT, bool DUAL, int BN, int CW, int P, bool PAIR = false>
 struct TmCfg {
+  static_assert(!(DUAL && PAIR), "PAIR is the single-matrix product");
   static constexpr bool kAffine = FMT != DSM_WFMT_FP4_G32;
   static constexpr bool kB8 = FMT == DSM_WFMT_AFFINE8;
   static constexpr int kCodeBytes = kB8 ? 16384 : 8192;
   static constexpr int kChunkK = kB8 ? 16 : 32;         // K per 16-byte chunk
   static constexpr int kRowChunks = 128 / kChunkK;      // chunks per row of a tile
-  static constexpr int NM = DUAL ? 2 : 1;
+  static constexpr int NM = (DUAL || PAIR) ? 2 : 1;
   // 128-K chunks per stage: two for the single-matrix (down) product, whose tiles carry half
   // the bytes of a gate/up pair, so the per-stage barrier, copy and commit costs are spread
   // over the same bytes; the gate/up pair keeps one (its A buffer is already 128 columns),
   // and so do 128-row units, whose activation rows alone fill 32 KB per chunk
-  static constexpr int KS = (DUAL || BN >= 128) ? 1 : 2;
+  static constexpr int KS = (DUAL || PAIR || BN >= 128) ? 1 : 2;
   static constexpr int kMma0 = kTmConv0 + CW;  // first MMA issuer warp
   static constexpr int kThreads = 32 * (kMma0 + P);
   static constexpr int kKkStride = P / NM;     // issuer p: matrix p % NM, k16 steps p / NM + j * kKkStride
@@ -163,10 +167,10 @@ __device__ __forceinline__ int tm_find(const int* pre, int n, int u) {
   return lo;
 }
 
-template <int FMT, bool DUAL, int BN, int CW, int P>
-__global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
+template <int FMT, bool DUAL, int BN, int CW, int P, bool PAIR = false>
+__global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P, PAIR>::kThreads, 1)
     expert_tm_kernel(const TmArgs a, const __grid_constant__ CUtensorMap xmap, int n_stages) {
-  using C = TmCfg<FMT, DUAL, BN, CW, P>;
+  using C = TmCfg<FMT, DUAL, BN, CW, P, PAIR>;
   constexpr int NM = C::NM, NA = C::kABufs;
   const int S = n_stages;
   const int stage_b = a.stage_b, tile_b = a.tile_b;
@@ -210,7 +214,7 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
       int v = 0;
       if (e < E) {
         const int cnt = tm_count(a, e);
-        v = cnt > 0 ? a.rt_count * ((cnt + BN - 1) / BN) * a.k_splits : 0;
+        v = cnt > 0 ? (PAIR ? a.rt_count / 2 : a.rt_count) * ((cnt + BN - 1) / BN) * a.k_splits : 0;
       }
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -291,6 +295,26 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
         }
         continue;
       }
+      if constexpr (PAIR) {
+        // the pair's two row tiles, 2 rt and 2 rt + 1: the partials of matrix m are row tile
+        // 2 rt + m's outputs
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int col = cb + i;
+          if (col >= rows) break;
+          const int64_t r = int64_t(off) + chunk * BN + col;
+          const float xs = a.act_scale ? a.act_scale[r] : a.act_scale_const;
+          const int64_t orow = a.o_row_map ? int64_t(a.o_row_map[r]) : r;
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+            const int d = (2 * rt + m) * kTmM + rloc;
+            float v = (m ? usum[i] : gsum[i]) * xs * wmul_a;
+            v = a.round_o ? bf16_round(v) : v;
+            if (d < a.out_rows) o_out[orow * a.ldo + d] = v;
+          }
+        }
+        continue;
+      }
       // the block's 16 row scales (and output rows): one guarded load per lane, broadcast
       // with a constant source lane per column
       const int cl = cb + (lane & 15);
@@ -353,7 +377,8 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
         const TmUnit w = tm_unit<BN>(a, pre, E, u, kcs);
         const int row0 = tm_first(a, w.e) + w.chunk * BN;
         const int nbox = (min(BN, w.cnt - w.chunk * BN) + kTmBoxRows - 1) / kTmBoxRows;
-        const int64_t tile0 = (int64_t(w.e) * a.rt_count + w.rt) * kcs;
+        // first row tile: the unit's (gate/up: both matrices'), or the pair's first (PAIR)
+        const int64_t tile0 = (int64_t(w.e) * a.rt_count + (PAIR ? 2 * w.rt : w.rt)) * kcs;
         const uint32_t tx1 = uint32_t(NM * tile_b + 2 * nbox * kTmBoxRows * 128);  // per chunk
         for (int kc = w.kc0; kc < w.kc1; kc += C::KS) {
           const int nk = min(C::KS, w.kc1 - kc);
@@ -368,6 +393,8 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
             uint8_t* raw = st + C::kOffRaw + j * NM * tile_b;
             bulk_g2s(raw, tiles_a + (tile0 + kc + j) * tile_b, uint32_t(tile_b), &full[s], pol_w);
             if (DUAL) bulk_g2s(raw + tile_b, tiles_b + (tile0 + kc + j) * tile_b, uint32_t(tile_b), &full[s], pol_w);
+            if (PAIR)
+              bulk_g2s(raw + tile_b, tiles_a + (tile0 + kcs + kc + j) * tile_b, uint32_t(tile_b), &full[s], pol_w);
             for (int h = 0; h < 2; ++h)
               for (int b = 0; b < nbox; ++b)
                 tma_load_3d(smem_u32(st + (2 * j + h) * C::kBHalf + b * kTmBoxRows * 128), &xmap, h * 64,
@@ -572,9 +599,9 @@ __global__ void __launch_bounds__(TmCfg<FMT, DUAL, BN, CW, P>::kThreads, 1)
   }
 }
 
-template <int FMT, bool DUAL, int BN, int CW, int P>
+template <int FMT, bool DUAL, int BN, int CW, int P, bool PAIR = false>
 int launch_tm(TmArgs a, const void* staged, int64_t rows_cap, cudaStream_t stream) {
-  using C = TmCfg<FMT, DUAL, BN, CW, P>;
+  using C = TmCfg<FMT, DUAL, BN, CW, P, PAIR>;
   CUtensorMap map;
   if (int rc = make_stage_map(&map, staged, rows_cap, a.kc_count, kTmBoxRows)) return rc;
   a.tile_b = tile_bytes(FMT, a.group_size);
@@ -583,7 +610,7 @@ int launch_tm(TmArgs a, const void* staged, int64_t rows_cap, cudaStream_t strea
   if (n_stages < 2) return fail(DSM_ERR_UNSUPPORTED, "expert_tm: tile too large for the shared-memory ring");
   const size_t smem = 1024 + size_t(n_stages) * a.stage_b + 8 * (2 * n_stages + C::kABufs + 5) + 16 +
                       size_t(a.n_experts + 1) * 4;
-  auto kern = expert_tm_kernel<FMT, DUAL, BN, CW, P>;
+  auto kern = expert_tm_kernel<FMT, DUAL, BN, CW, P, PAIR>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return check_launch("expert_tm smem attribute");
   kern<<<persistent_ctas(), C::kThreads, smem, stream>>>(a, map, n_stages);
@@ -616,8 +643,14 @@ int launch_width(const TmArgs& a, const void* staged, int64_t rows_cap, cudaStre
     if (a.n_rows > 96 * busy && units128 <= persistent_ctas())
       return launch_tm<FMT, DUAL, 128, kTmCW, 2>(a, staged, rows_cap, s);
   }
-  if (a.n_rows > 32 * busy && units64 >= persistent_ctas())
+  // the down product in row-tile pairs where the tiles pair up: each staged activation tile
+  // then feeds 256 weight rows, as in the gate/up pair, instead of 128
+  const bool pair = !DUAL && a.k_splits <= 1 && a.rt_count % 2 == 0;
+  if (a.n_rows > 32 * busy && units64 >= persistent_ctas()) {
+    if (pair) return launch_tm<FMT, DUAL, 64, kTmCW, 2, !DUAL>(a, staged, rows_cap, s);
     return launch_tm<FMT, DUAL, 64, kTmCW, 2>(a, staged, rows_cap, s);
+  }
+  if (pair) return launch_tm<FMT, DUAL, 32, kTmCW, 4, !DUAL>(a, staged, rows_cap, s);
   return launch_tm<FMT, DUAL, 32, kTmCW, 4>(a, staged, rows_cap, s);
 }
 
