@@ -114,6 +114,10 @@ struct TcArgs {
   int k_splits;
   int k_per;
   int64_t o_split_stride;
+  // activation rows per TMA box (a multiple of 16, at most the unit width; 0 = the unit
+  // width): a single group of few rows loads only the rows it has, not a 256-row box of
+  // which the rows past the group are read for nothing
+  int box_rows;
 };
 
 // Unit u's place: expert e, row tile rt, row chunk, K range ksp covering 64-K stages
@@ -235,6 +239,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
+    const int box = a.box_rows > 0 ? a.box_rows : BN;
+    const uint32_t tx_bytes = uint32_t(C::kTxBytes - C::kBBytes + box * kTcK * 2);
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       int s = 0;
@@ -254,7 +260,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
           }
           uint8_t* st = lbase + size_t(s) * C::kLoadBytes;
           const int kc = ks >> 1, half = ks & 1;
-          mbar_arrive_expect_tx(&full[s], uint32_t(C::kTxBytes));
+          mbar_arrive_expect_tx(&full[s], tx_bytes);
 #pragma unroll
           for (int m = 0; m < NM; ++m) {
             const uint8_t* tile = tiles[m] + (tile0 + (PAIR ? m * a.kc_count : 0) + kc) * tile_b;
@@ -510,10 +516,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) expert_tc_kernel(const TcArgs a
 }
 
 template <int FMT, bool DUAL, bool PAIR = false>
-int launch_tc(const TcArgs& a, const void* staged, int64_t rows_cap, cudaStream_t stream) {
+int launch_tc(TcArgs a, const void* staged, int64_t rows_cap, cudaStream_t stream) {
   using C = TcCfg<FMT, DUAL, PAIR>;
+  // one group of rows (offsets NULL): the box covers its rows only (whole units of 256 rows
+  // above that). Grouped calls keep the unit width: their counts are on the device.
+  a.box_rows = a.offsets ? 0 : int(std::min<int64_t>(C::BN, (a.n_rows + 15) / 16 * 16));
   CUtensorMap map;
-  if (int rc = make_stage_map(&map, staged, rows_cap, a.kc_count, C::BN)) return rc;
+  if (int rc = make_stage_map(&map, staged, rows_cap, a.kc_count, a.box_rows > 0 ? a.box_rows : C::BN)) return rc;
   int dev = 0, optin = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
