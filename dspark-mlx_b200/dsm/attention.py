@@ -76,8 +76,9 @@ class DSparkAttention(nn.Module):
             self._packed[name] = hit
         return hit[1]
 
-    def _linear(self, x2: torch.Tensor, pm: PackedMatrix, out: Optional[torch.Tensor] = None, ldo: int = 0):
-        """fp32 rows of x2 W^T: ``(hi, lo)``; lo is the product of an fp32 input's residual rows."""
+    @staticmethod
+    def _stage(x2: torch.Tensor):
+        """x2's rows staged for the products (fp32 rows as hi + lo): (staged, xscale, cap, rows, k)."""
         L = lib()
         n, k = x2.shape
         f32 = x2.dtype == torch.float32
@@ -91,6 +92,14 @@ class DSparkAttention(nn.Module):
         else:
             check(L.dsm_stage_rows(ptr(x2), dtype_code(x2.dtype), n, k, None, n, 1, ptr(staged), cap, ptr(xscale), s),
                   "dsm_stage_rows")
+        return staged, xscale, cap, rows, k
+
+    def _linear(self, x2: torch.Tensor, pm: PackedMatrix, out: Optional[torch.Tensor] = None, ldo: int = 0, st=None):
+        """fp32 rows of x2 W^T: ``(hi, lo)``; lo is the product of an fp32 input's residual rows.
+        st: x2 already staged by ``_stage`` (one staging serves several products of x2)."""
+        L = lib()
+        staged, xscale, cap, rows, k = self._stage(x2) if st is None else st
+        s = stream_ptr()
         if out is None:
             out = torch.empty(rows, pm.rows, dtype=torch.float32, device=x2.device)
             ldo = pm.rows
@@ -139,9 +148,10 @@ class DSparkAttention(nn.Module):
     def _hilo(o: torch.Tensor, n: int):
         return (o[:n], o[n:]) if o.shape[0] == 2 * n else (o, None)
 
-    def _norm_rope(self, x2: torch.Tensor, pm: PackedMatrix, weight: torch.Tensor, rope: bool, pos0: int, period: int):
+    def _norm_rope(self, x2: torch.Tensor, pm: PackedMatrix, weight: torch.Tensor, rope: bool, pos0: int, period: int,
+                   st=None):
         n = x2.shape[0]
-        hi, lo = self._hilo(self._linear(x2, pm), n)
+        hi, lo = self._hilo(self._linear(x2, pm, st=st), n)
         out = torch.empty(n, pm.rows, dtype=x2.dtype, device=x2.device)
         w = weight.detach().to(device=x2.device, dtype=torch.float32).contiguous()
         cos, sin = (self._cos, self._sin) if rope else (None, None)
@@ -186,13 +196,14 @@ class DSparkAttention(nn.Module):
         pos_b = start_pos + seqlen  # positions of the block's rows
         h, hd, g = self.n_heads, self.head_dim, self.n_groups
         # q: wq_b(q_norm(wq_a(x))), per-head RMS, RoPE
-        q_lat = self._norm_rope(x2, self._pm("wq_a", self.wq_a.weight), self.q_norm.weight, False, 0, 1)
+        st = self._stage(x2)  # one staging of x for wq_a and wkv
+        q_lat = self._norm_rope(x2, self._pm("wq_a", self.wq_a.weight), self.q_norm.weight, False, 0, 1, st=st)
         qh, ql = self._hilo(self._linear(q_lat, self._pm("wq_b", self.wq_b.weight)), n)
         q = torch.empty(n, h * hd, dtype=dt, device=x.device)
         check(lib().dsm_q_head_norm_rope(ptr(qh), ptr(ql), n, h, hd, float(self.eps), self.rope_head_dim,
                                          ptr(self._cos), ptr(self._sin), pos_b, block, ptr(q), dtype_code(dt),
                                          stream_ptr()), "dsm_q_head_norm_rope")
-        kv = self._norm_rope(x2, self._pm("wkv", self.wkv.weight), self.kv_norm.weight, True, pos_b, block)
+        kv = self._norm_rope(x2, self._pm("wkv", self.wkv.weight), self.kv_norm.weight, True, pos_b, block, st=st)
         self._write_window(main_kv[:, :1].contiguous(), start_pos)  # cache.update(start_pos, main_kv[:, 0])
         n_win = min(win, start_pos + 1)
         dg = h * hd // g
