@@ -57,22 +57,28 @@ __device__ __forceinline__ void block_sum(float (&v)[NV], float* red) {
   }
 }
 
-template <typename T, int HC>
-__global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(const T* __restrict__ x, int dim,
-                                                                   const float* __restrict__ fn,
-                                                                   const float* __restrict__ scale,
-                                                                   const float* __restrict__ base, int iters,
-                                                                   float norm_eps, float hc_eps,
-                                                                   const float* __restrict__ weight, T* __restrict__ xn,
-                                                                   float* __restrict__ post_out,
-                                                                   float* __restrict__ comb_out) {
+// PAIR: the token's pass 1 split between the two CTAs of a cluster, each over half of the
+// hc * dim columns (each reads half of the projection rows from L2). CTA 1 stores its sums
+// into CTA 0's shared memory (distributed shared memory), CTA 0 adds them after its own and
+// finishes the token alone.
+template <typename T, int HC, bool PAIR>
+__device__ __forceinline__ void hc_pre_norm_body(const T* __restrict__ x, int dim, const float* __restrict__ fn,
+                                                 const float* __restrict__ scale, const float* __restrict__ base,
+                                                 int iters, float norm_eps, float hc_eps,
+                                                 const float* __restrict__ weight, T* __restrict__ xn,
+                                                 float* __restrict__ post_out, float* __restrict__ comb_out) {
   constexpr int MIX = (2 + HC) * HC;
   extern __shared__ float ysm[];  // dim floats: the reduced row, rounded to T
   __shared__ float red[(kHcThreads / 32) * (MIX + 1)];
   __shared__ float pre_s[HC];
-  const int64_t t = blockIdx.x;
+  __shared__ float peer_acc[MIX + 1];  // PAIR: CTA 1's sums, written by CTA 1 into CTA 0
+  uint32_t rank = 0;
+  if constexpr (PAIR) asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  const int64_t t = PAIR ? int64_t(blockIdx.x >> 1) : int64_t(blockIdx.x);
   const int hcd = HC * dim;
   const T* xt = x + t * hcd;
+  // this CTA's columns: all of them, or half (hcd is even: dim is)
+  const int k_lo = PAIR ? int(rank) * (hcd / 2) : 0, k_hi = PAIR ? k_lo + hcd / 2 : hcd;
 
   // pass 1: sum of squares and the mix projections of the flattened copies
   float acc[MIX + 1];
@@ -82,8 +88,8 @@ __global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(const T* __rest
   // which stay in L2 across tokens) are issued before the multiply-adds, so a step waits on
   // one L2 round trip instead of kU; the adds keep the thread's column order.
   constexpr int kU = 4;
-  int k = threadIdx.x;
-  for (; k + (kU - 1) * kHcThreads < hcd; k += kU * kHcThreads) {
+  int k = k_lo + int(threadIdx.x);
+  for (; k + (kU - 1) * kHcThreads < k_hi; k += kU * kHcThreads) {
     float v[kU], f[kU][MIX];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
@@ -99,13 +105,29 @@ __global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(const T* __rest
       for (int j = 0; j < MIX; ++j) acc[j] = fmaf(v[u], f[u][j], acc[j]);
     }
   }
-  for (; k < hcd; k += kHcThreads) {
+  for (; k < k_hi; k += kHcThreads) {
     const float v = to_f(xt[k]);
     acc[MIX] = fmaf(v, v, acc[MIX]);
 #pragma unroll
     for (int j = 0; j < MIX; ++j) acc[j] = fmaf(v, fn[int64_t(j) * hcd + k], acc[j]);
   }
   block_sum(acc, red);
+  if constexpr (PAIR) {
+    if (rank == 1 && int(threadIdx.x) <= MIX) {  // this half's sums into CTA 0's peer_acc
+      uint32_t dst;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(dst) : "r"(smem_u32(&peer_acc[threadIdx.x])));
+      float mine = 0.f;
+#pragma unroll
+      for (int i = 0; i <= MIX; ++i)
+        if (i == int(threadIdx.x)) mine = acc[i];
+      asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dst), "f"(mine) : "memory");
+    }
+    // every thread of both CTAs: CTA 1's stores are visible in CTA 0 after this barrier
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (rank == 1) return;
+#pragma unroll
+    for (int i = 0; i <= MIX; ++i) acc[i] += peer_acc[i];  // first half, then second
+  }
 
   if (threadIdx.x == 0) {  // hc_split_sinkhorn on the token's mixes
     const float inv_rms = rsqrtf(acc[MIX] / float(hcd) + norm_eps);
@@ -183,6 +205,29 @@ __global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(const T* __rest
     const float v = ysm[j] * r;
     out[j] = from_f<T>(weight ? weight[j] * v : v);
   }
+}
+
+template <typename T, int HC>
+__global__ void __launch_bounds__(kHcThreads) hc_pre_norm_kernel(const T* __restrict__ x, int dim,
+                                                                   const float* __restrict__ fn,
+                                                                   const float* __restrict__ scale,
+                                                                   const float* __restrict__ base, int iters,
+                                                                   float norm_eps, float hc_eps,
+                                                                   const float* __restrict__ weight, T* __restrict__ xn,
+                                                                   float* __restrict__ post_out,
+                                                                   float* __restrict__ comb_out) {
+  hc_pre_norm_body<T, HC, false>(x, dim, fn, scale, base, iters, norm_eps, hc_eps, weight, xn, post_out, comb_out);
+}
+
+// two CTAs per token (grid 2 n, clusters of 2): few tokens, whose CTAs alone would leave most
+// SMs idle while each reads all (2 + hc) * hc projection rows
+template <typename T, int HC>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHcThreads)
+    hc_pre_norm_pair_kernel(const T* __restrict__ x, int dim, const float* __restrict__ fn,
+                            const float* __restrict__ scale, const float* __restrict__ base, int iters, float norm_eps,
+                            float hc_eps, const float* __restrict__ weight, T* __restrict__ xn,
+                            float* __restrict__ post_out, float* __restrict__ comb_out) {
+  hc_pre_norm_body<T, HC, true>(x, dim, fn, scale, base, iters, norm_eps, hc_eps, weight, xn, post_out, comb_out);
 }
 
 template <typename T, int HC>
@@ -321,14 +366,17 @@ int launch_pre(const void* x, int64_t n, int hc, int dim, const float* fn, const
   const size_t smem = size_t(dim) * sizeof(float);
   const T* xp = static_cast<const T*>(x);
   T* xo = static_cast<T*>(xn);
+  // a draft step's few tokens take two CTAs each (a cluster): one CTA per token would leave
+  // most SMs idle, each reading the whole projection matrix from L2
+  const bool pair = n <= int64_t(num_sms());
 #define DSM_HC_PRE(H)                                                                                         \
   {                                                                                                           \
-    auto k = hc_pre_norm_kernel<T, H>;                                                                        \
+    auto k = pair ? hc_pre_norm_pair_kernel<T, H> : hc_pre_norm_kernel<T, H>;                               \
     if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != \
                                 cudaSuccess)                                                                  \
       return check_launch("hc_pre_norm smem attribute");                                                      \
-    k<<<unsigned(n), kHcThreads, smem, s>>>(xp, dim, fn, scale, base, iters, norm_eps, hc_eps, weight, xo,    \
-                                            post, comb);                                                      \
+    k<<<unsigned(pair ? 2 * n : n), kHcThreads, smem, s>>>(xp, dim, fn, scale, base, iters, norm_eps, hc_eps,  \
+                                                           weight, xo, post, comb);                           \
     return check_launch("hc_pre_norm");                                                                       \
   }
   switch (hc) {
